@@ -1,0 +1,413 @@
+// gpb2_device.cuh -- per-point Vecchia numerics for sm_100a, one thread per refined point.
+//
+// Each refined point conditions on its K nearest preceding neighbours.  A thread gathers the
+// (K+1) lattice coordinates, assembles the (K+1)x(K+1) covariance by table interpolation,
+// factorises it (left-looking Cholesky with the reference's pivot floor), solves for the
+// conditional-mean weights and, for the adjoints, runs the exact reverse of the factorisation.
+// The packed lower triangle lives in registers (all loops are unrolled over the compile-time K).
+//
+// Arithmetic: every operation is an explicit round-to-nearest IEEE operation (__fmul_rn,
+// __fadd_rn, __fdiv_rn, __fsqrt_rn and the double forms) in the written order, so nothing is
+// contracted into an FMA and each point's result is the same bit pattern the scalar restatement
+// produces.  Operation order follows:
+//   cov_lookup / cov_lookup_weights     src/interp.jl:10-34, 62-83
+//   assemble_cov!                       src/linalg.jl:98-112
+//   chol_lower!                         src/linalg.jl:121-156
+//   mean_vec_solve!                     src/linalg.jl:168-186
+//   chol_pullback!                      src/linalg.jl:195-217
+//
+// Interpolation table.  The reference finds the bracketing bin with a binary search (about
+// log2(nbins) dependent loads per covariance entry).  Here the table is staged in shared memory
+// as segments {x0, x1, y0, slope} with slope = (y1 - y0) / (x1 - x0) evaluated once per segment
+// in T (the same IEEE quotient the reference forms per lookup), plus a bucket index keyed on the
+// high bits of r's IEEE representation (monotone in r for r > 0).  A lookup reads the bucket's
+// first segment and steps forward while x1 <= r: the bracket found is the unique lo with
+// bins[lo] <= r < bins[lo+1], i.e. exactly the binary search's, for any strictly increasing
+// table.  The interpolated value is y0 + slope*(r - x0) in that order, as in the reference.
+#pragma once
+#include <cfloat>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <type_traits>
+
+namespace gpb2 {
+
+// ------------------------------------------------------------------------------------------
+// IEEE round-to-nearest arithmetic that the compiler may not contract.
+// ------------------------------------------------------------------------------------------
+template <typename T> struct Num;
+
+template <> struct Num<float> {
+    using U = uint32_t;
+    static __device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
+    static __device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
+    static __device__ __forceinline__ float sub(float a, float b) { return __fsub_rn(a, b); }
+    static __device__ __forceinline__ float div(float a, float b) { return __fdiv_rn(a, b); }
+    static __device__ __forceinline__ float sqrt(float a) { return __fsqrt_rn(a); }
+    static __device__ __forceinline__ float log(float a) { return logf(a); }
+    static __device__ __forceinline__ float from_i64(long long x) { return __ll2float_rn(x); }
+    static __device__ __forceinline__ U bits(float x) { return __float_as_uint(x); }
+    static __host__ __device__ constexpr float eps() { return FLT_EPSILON; }
+};
+
+template <> struct Num<double> {
+    using U = unsigned long long;
+    static __device__ __forceinline__ double mul(double a, double b) { return __dmul_rn(a, b); }
+    static __device__ __forceinline__ double add(double a, double b) { return __dadd_rn(a, b); }
+    static __device__ __forceinline__ double sub(double a, double b) { return __dsub_rn(a, b); }
+    static __device__ __forceinline__ double div(double a, double b) { return __ddiv_rn(a, b); }
+    static __device__ __forceinline__ double sqrt(double a) { return __dsqrt_rn(a); }
+    static __device__ __forceinline__ double log(double a) { return ::log(a); }
+    static __device__ __forceinline__ double from_i64(long long x) { return __ll2double_rn(x); }
+    static __device__ __forceinline__ U bits(double x) {
+        return (unsigned long long)__double_as_longlong(x);
+    }
+    static __host__ __device__ constexpr double eps() { return DBL_EPSILON; }
+};
+
+// ------------------------------------------------------------------------------------------
+// Interpolation table (built on the host by the problem handle, see gpb2_problem.cu).
+// ------------------------------------------------------------------------------------------
+template <typename T>
+struct TableView {
+    const T* seg;              // device, 4 * (nb - 1): {x0, x1, y0, slope} per segment
+    const uint16_t* start;     // device, nkeys: first segment to probe for each bucket
+    typename Num<T>::U base;   // bucket of bins[1]
+    int nb, nkeys, shift;
+    T b0, b1, bN, v0, vN;      // bins[0], bins[1], bins[nb-1], vals[0], vals[nb-1]
+    T pivc;                    // T(1.5) * sqrt(eps(T)), evaluated in T on the host
+};
+
+// Bytes of dynamic shared memory a kernel needs for the staged table.
+template <typename T>
+__host__ __device__ inline size_t table_smem_bytes(int nb, int nkeys) {
+    size_t segb = sizeof(T) * 4 * (size_t)(nb - 1);
+    size_t keyb = ((sizeof(uint16_t) * (size_t)nkeys) + 15) & ~size_t(15);
+    return segb + keyb;
+}
+
+template <typename T>
+struct SmemTable {
+    using N = Num<T>;
+    using U = typename N::U;
+    const T* seg;
+    const uint16_t* start;
+    U base;
+    int nb, last_key, shift;
+    T b0, b1, bN, v0, vN;
+
+    // Cooperative copy of the table into shared memory; the caller synchronises afterwards.
+    __device__ __forceinline__ void stage(const TableView<T>& tv, unsigned char* smem, int tid,
+                                          int nthr) {
+        const int nseg4 = 4 * (tv.nb - 1);
+        T* s = reinterpret_cast<T*>(smem);
+        const int nvec = (int)((sizeof(T) * nseg4) / 16);
+        const int4* src = reinterpret_cast<const int4*>(tv.seg);
+        int4* dst = reinterpret_cast<int4*>(s);
+        for (int i = tid; i < nvec; i += nthr) dst[i] = __ldg(src + i);
+        uint16_t* st = reinterpret_cast<uint16_t*>(smem + sizeof(T) * nseg4);
+        for (int i = tid; i < tv.nkeys; i += nthr) st[i] = __ldg(tv.start + i);
+        seg = s;
+        start = st;
+        base = tv.base;
+        nb = tv.nb;
+        last_key = tv.nkeys - 1;
+        shift = tv.shift;
+        b0 = tv.b0; b1 = tv.b1; bN = tv.bN; v0 = tv.v0; vN = tv.vN;
+    }
+
+    // Segment index lo with bins[lo] <= r < bins[lo+1]; requires bins[0] < r < bins[nb-1].
+    __device__ __forceinline__ int locate(T r) const {
+        if (r < b1) return 0;
+        U key = (N::bits(r) >> shift) - base;
+        int ki = key > (U)last_key ? last_key : (int)key;
+        int lo = start[ki];
+        while (seg[4 * lo + 1] <= r) ++lo;  // terminates: seg[nb-2].x1 == bins[nb-1] > r
+        return lo;
+    }
+
+    // cov_lookup (src/interp.jl:10-34).
+    __device__ __forceinline__ T lookup(T r) const {
+        if (r <= b0) return v0;
+        if (r >= bN) return vN;
+        const int lo = locate(r);
+        const T x0 = seg[4 * lo + 0];
+        const T y0 = seg[4 * lo + 2];
+        const T slope = seg[4 * lo + 3];
+        return N::add(y0, N::mul(slope, N::sub(r, x0)));
+    }
+
+    // cov_lookup_weights (src/interp.jl:62-83): returns lo, writes w_lo and w_hi.
+    __device__ __forceinline__ int weights(T r, T& wlo, T& whi) const {
+        if (r <= b0) { wlo = T(1); whi = T(0); return 0; }
+        if (r >= bN) { wlo = T(0); whi = T(1); return nb - 2; }
+        const int lo = locate(r);
+        const T x0 = seg[4 * lo + 0];
+        const T x1 = seg[4 * lo + 1];
+        const T t = N::div(N::sub(r, x0), N::sub(x1, x0));
+        wlo = N::sub(T(1), t);
+        whi = t;
+        return lo;
+    }
+};
+
+// ------------------------------------------------------------------------------------------
+// Device-side layout helpers.
+// ------------------------------------------------------------------------------------------
+
+// Row stride (uint32 words) of the device coordinate copy: D = 3 is padded to 16 bytes so a
+// point's coordinates are one aligned vector load that never straddles a 32-byte sector.
+__host__ __device__ constexpr int coord_stride(int D) { return D == 3 ? 4 : D; }
+
+template <int D>
+__device__ __forceinline__ void load_coords(uint32_t (&c)[D], const uint32_t* __restrict__ coords,
+                                            int64_t p) {
+    constexpr int DS = coord_stride(D);
+    if constexpr (D == 2) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(coords) + p);
+        c[0] = v.x; c[1] = v.y;
+    } else if constexpr (DS == 4) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(coords) + p);
+        c[0] = v.x; c[1] = v.y; c[2] = v.z;
+        if constexpr (D == 4) c[3] = v.w;
+    } else {
+#pragma unroll
+        for (int d = 0; d < D; d++) c[d] = __ldg(coords + p * DS + d);
+    }
+}
+
+// K consecutive int32 (a refined point's neighbour list), vectorised when K allows.
+template <int K>
+__device__ __forceinline__ void load_row_i32(int (&o)[K], const int* __restrict__ base) {
+    if constexpr (K % 4 == 0) {
+#pragma unroll
+        for (int j = 0; j < K / 4; j++) {
+            const int4 v = __ldg(reinterpret_cast<const int4*>(base) + j);
+            o[4 * j] = v.x; o[4 * j + 1] = v.y; o[4 * j + 2] = v.z; o[4 * j + 3] = v.w;
+        }
+    } else if constexpr (K % 2 == 0) {
+#pragma unroll
+        for (int j = 0; j < K / 2; j++) {
+            const int2 v = __ldg(reinterpret_cast<const int2*>(base) + j);
+            o[2 * j] = v.x; o[2 * j + 1] = v.y;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < K; j++) o[j] = __ldg(base + j);
+    }
+}
+
+// K consecutive T (a point's conditional-mean weights).
+template <typename T, int K>
+__device__ __forceinline__ void load_row_t(T (&o)[K], const T* __restrict__ base) {
+    constexpr int PER = 16 / sizeof(T);
+    if constexpr (K % PER == 0) {
+#pragma unroll
+        for (int j = 0; j < K / PER; j++) {
+            const int4 v = __ldg(reinterpret_cast<const int4*>(base) + j);
+            const T* t = reinterpret_cast<const T*>(&v);
+#pragma unroll
+            for (int q = 0; q < PER; q++) o[PER * j + q] = t[q];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < K; j++) o[j] = __ldg(base + j);
+    }
+}
+
+template <typename T, int K>
+__device__ __forceinline__ void store_row_t(T* __restrict__ base, const T (&o)[K]) {
+    constexpr int PER = 16 / sizeof(T);
+    if constexpr (K % PER == 0) {
+#pragma unroll
+        for (int j = 0; j < K / PER; j++) {
+            int4 v;
+            T* t = reinterpret_cast<T*>(&v);
+#pragma unroll
+            for (int q = 0; q < PER; q++) t[q] = o[PER * j + q];
+            reinterpret_cast<int4*>(base)[j] = v;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < K; j++) base[j] = o[j];
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// The per-point factorisation.  Loop nests use sfor (compile-time recursion) rather than
+// `#pragma unroll`, so every index into the packed triangle is a constant and the arrays stay in
+// registers whatever the unroller's size heuristics decide.
+// ------------------------------------------------------------------------------------------
+__host__ __device__ constexpr int tri(int i, int j) { return i * (i + 1) / 2 + j; }
+
+template <int B, int E, class F>
+__device__ __forceinline__ void sfor(F&& f) {
+    if constexpr (B < E) {
+        f(std::integral_constant<int, B>{});
+        sfor<B + 1, E>(f);
+    }
+}
+// Descending: E-1, E-2, ..., B.
+template <int B, int E, class F>
+__device__ __forceinline__ void sfor_down(F&& f) {
+    if constexpr (B < E) {
+        f(std::integral_constant<int, E - 1>{});
+        sfor_down<B, E - 1>(f);
+    }
+}
+#define GPB2_CI(name) constexpr int name = decltype(name##_)::value
+
+template <typename T, int K, int D>
+struct PointMath {
+    using N = Num<T>;
+    static constexpr int KP1 = K + 1;
+    static constexpr int NT = KP1 * (KP1 + 1) / 2;
+    static constexpr int NR = NT - KP1;  // off-diagonal pairs
+
+    // Joint coordinates: rows 0..K-1 are the neighbours, row K the refined point
+    // (_gather_joint!, src/kernels.jl:9-23).
+    static __device__ __forceinline__ void gather(uint32_t (&jc)[KP1][D],
+                                                  const uint32_t* __restrict__ coords,
+                                                  const int (&nb)[K], int64_t self) {
+        sfor<0, K>([&](auto j_) {
+            GPB2_CI(j);
+            load_coords<D>(jc[j], coords, nb[j]);
+        });
+        load_coords<D>(jc[K], coords, self);
+    }
+
+    // r = sqrt(T(sq)) * scale with sq the exact Int64 squared lattice distance.
+    static __device__ __forceinline__ T radius(const uint32_t (&a)[D], const uint32_t (&b)[D],
+                                               T scale) {
+        long long sq = 0;
+        sfor<0, D>([&](auto d_) {
+            GPB2_CI(d);
+            const long long di = (long long)a[d] - (long long)b[d];
+            sq += di * di;
+        });
+        return N::mul(N::sqrt(N::from_i64(sq)), scale);
+    }
+
+    // assemble_cov! (src/linalg.jl:98-112).  With KEEP_R the radius of pair (a, b), b < a, is
+    // kept in R[tri(a-1, b)] for the adjoint's scatter.
+    template <bool KEEP_R>
+    static __device__ __forceinline__ void assemble(T (&L)[NT], T (&R)[NR],
+                                                    const uint32_t (&jc)[KP1][D], T scale,
+                                                    const SmemTable<T>& tab) {
+        const T diag = tab.lookup(T(0));
+        sfor<0, KP1>([&](auto a_) {
+            GPB2_CI(a);
+            L[tri(a, a)] = diag;
+            sfor<0, a>([&](auto b_) {
+                GPB2_CI(b);
+                const T r = radius(jc[a], jc[b], scale);
+                if constexpr (KEEP_R) R[tri(a - 1, b)] = r;
+                L[tri(a, b)] = tab.lookup(r);
+            });
+        });
+    }
+
+    // chol_lower! (src/linalg.jl:121-156).  A degenerate column (s <= eps*A11, or NaN) gets
+    // the diagonal sqrt(eps*A11) and a zeroed column; selects keep the thread branch-free.
+    static __device__ __forceinline__ void chol(T (&L)[NT]) {
+        const T pivmin = N::mul(N::eps(), L[0]);
+        sfor<0, KP1>([&](auto j_) {
+            GPB2_CI(j);
+            T s = L[tri(j, j)];
+            sfor<0, j>([&](auto p_) {
+                GPB2_CI(p);
+                s = N::sub(s, N::mul(L[tri(j, p)], L[tri(j, p)]));
+            });
+            const bool ok = s > pivmin;
+            const T d = N::sqrt(ok ? s : pivmin);
+            L[tri(j, j)] = d;
+            sfor<j + 1, KP1>([&](auto i_) {
+                GPB2_CI(i);
+                T t = L[tri(i, j)];
+                sfor<0, j>([&](auto p_) {
+                    GPB2_CI(p);
+                    t = N::sub(t, N::mul(L[tri(i, p)], L[tri(j, p)]));
+                });
+                L[tri(i, j)] = ok ? N::div(t, d) : T(0);
+            });
+        });
+    }
+
+    // mean_vec_solve! (src/linalg.jl:168-186): L[0:K,0:K]^T x = L[K,0:K], weight zeroed where
+    // the pivot sits at the clamp floor.
+    static __device__ __forceinline__ void solve(T (&x)[K], const T (&L)[NT], T pivc) {
+        const T pivfloor = N::mul(pivc, L[0]);
+        sfor_down<0, K>([&](auto i_) {
+            GPB2_CI(i);
+            const T d = L[tri(i, i)];
+            T s = L[tri(K, i)];
+            sfor<i + 1, K>([&](auto j_) {
+                GPB2_CI(j);
+                s = N::sub(s, N::mul(L[tri(j, i)], x[j]));
+            });
+            x[i] = d > pivfloor ? N::div(s, d) : T(0);
+        });
+    }
+
+    // Adjoint of mean_vec_solve!: forward substitution L[0:K,0:K] z = z_in, optionally with
+    // the pivot guard (src/kernels_adjoint.jl:520-530) or without it (src/grad.jl:574-580).
+    template <bool GUARD>
+    static __device__ __forceinline__ void forward_subst(T (&z)[K], const T (&L)[NT], T pivfloor) {
+        sfor<0, K>([&](auto i_) {
+            GPB2_CI(i);
+            T s = z[i];
+            sfor<0, i>([&](auto q_) {
+                GPB2_CI(q);
+                s = N::sub(s, N::mul(L[tri(i, q)], z[q]));
+            });
+            if constexpr (GUARD)
+                z[i] = L[tri(i, i)] > pivfloor ? N::div(s, L[tri(i, i)]) : T(0);
+            else
+                z[i] = N::div(s, L[tri(i, i)]);
+        });
+    }
+
+    // Seed of the factor cotangent from the solve's adjoint: B[K][j] += z[j],
+    // B[j][i] -= z[i]*mv[j] for i <= j (src/kernels_adjoint.jl:531-536).
+    static __device__ __forceinline__ void seed_from_solve(T (&B)[NT], const T (&z)[K],
+                                                           const T (&x)[K]) {
+        sfor<0, K>([&](auto j_) {
+            GPB2_CI(j);
+            B[tri(K, j)] = N::add(B[tri(K, j)], z[j]);
+            sfor<0, j + 1>([&](auto i_) {
+                GPB2_CI(i);
+                B[tri(j, i)] = N::sub(B[tri(j, i)], N::mul(z[i], x[j]));
+            });
+        });
+    }
+
+    // chol_pullback! (src/linalg.jl:195-217), in place: on entry B holds L-bar (lower), on
+    // exit B holds A-bar.  Each L-bar[i][j] is last read exactly where A-bar[i][j] is written,
+    // so one array serves both.
+    static __device__ __forceinline__ void pullback(T (&B)[NT], const T (&L)[NT]) {
+        sfor_down<0, KP1>([&](auto j_) {
+            GPB2_CI(j);
+            const T ljj = L[tri(j, j)];
+            sfor_down<j + 1, KP1>([&](auto i_) {
+                GPB2_CI(i);
+                const T lbij = B[tri(i, j)];
+                const T tbar = N::div(lbij, ljj);
+                B[tri(j, j)] = N::sub(B[tri(j, j)], N::div(N::mul(lbij, L[tri(i, j)]), ljj));
+                B[tri(i, j)] = tbar;
+                sfor<0, j>([&](auto p_) {
+                    GPB2_CI(p);
+                    B[tri(i, p)] = N::sub(B[tri(i, p)], N::mul(tbar, L[tri(j, p)]));
+                    B[tri(j, p)] = N::sub(B[tri(j, p)], N::mul(tbar, L[tri(i, p)]));
+                });
+            });
+            const T sbar = N::div(B[tri(j, j)], N::mul(T(2), ljj));
+            B[tri(j, j)] = sbar;
+            sfor<0, j>([&](auto p_) {
+                GPB2_CI(p);
+                B[tri(j, p)] = N::sub(B[tri(j, p)], N::mul(N::mul(T(2), sbar), L[tri(j, p)]));
+            });
+        });
+    }
+};
+
+}  // namespace gpb2

@@ -1,0 +1,502 @@
+// gpb2_kernels.cuh -- the kernels of the refine path and their launchers.
+//
+// Two shapes:
+//  * flat kernels over all M refined points (factor, inverse, logdet, the vals-gradient
+//    pullbacks): persistent grid (a multiple of the SM count, sized by occupancy), grid-stride
+//    over points, the interpolation table staged in shared memory once per CTA;
+//  * per-depth-batch kernels (the forward and reverse sweeps and the fused forward level
+//    kernel): one launch per batch, a thread per point.  Batch-mates never neighbour each
+//    other (check_graph invariant 4), so a batch reads only values finished by earlier
+//    launches on the same stream and the reverse sweep's atomics never touch the batch's own
+//    entries.
+//
+// The vals-gradients accumulate a per-CTA double histogram in shared memory and flush it into a
+// global double accumulator (one atomic per non-zero bin per CTA).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "gpb2_device.cuh"
+
+namespace gpb2 {
+
+template <typename T>
+struct PointArgs {
+    TableView<T> tab;
+    const uint32_t* coords;  // (N, coord_stride(D)) uint32
+    const int* nbrs;         // (M, K) int32, 0-based
+    int64_t n0;
+    T scale;
+};
+
+constexpr int kFlatThreads = 128;
+constexpr int kSweepThreads = 256;
+
+// Grid for a persistent flat kernel: resident CTAs per SM x SM count, capped by the work.
+int flat_grid(const void* kernel, int threads, size_t smem, int64_t work);
+cudaError_t prepare_kernel_smem(const void* kernel, size_t smem);
+
+// Launch profiler (gpb2_registry.cu): every launch is counted; with profiling enabled a CUDA
+// event pair brackets it on its stream.
+struct ProfToken {
+    const char* name;
+    cudaEvent_t a, b;
+};
+ProfToken prof_begin(const char* name, cudaStream_t s);
+void prof_end(const ProfToken& t, cudaStream_t s);
+
+// Launch `kern` bracketed by the profiler; returns the launch status.
+template <class Kern, class... Args>
+inline cudaError_t launch_prof(const char* name, Kern kern, dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t s, Args... args) {
+    const ProfToken t = prof_begin(name, s);
+    kern<<<grid, block, smem, s>>>(args...);
+    const cudaError_t e = cudaGetLastError();
+    prof_end(t, s);
+    return e;
+}
+
+__device__ __forceinline__ double block_sum_double(double v, double* red /*>= 32 doubles*/) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double s = 0.0;
+    if (threadIdx.x == 0)
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += red[w];
+    return s;  // valid on thread 0
+}
+
+// ---------------------------------------------------------------------------------------------
+// Shared per-point preamble: neighbour list, joint coords, covariance, factor.
+// ---------------------------------------------------------------------------------------------
+template <typename T, int K, int D, bool KEEP_R>
+struct PointFactor {
+    using PM = PointMath<T, K, D>;
+    int nb[K];
+    T L[PM::NT];
+    T R[PM::NR];
+
+    __device__ __forceinline__ void compute(const PointArgs<T>& a, const SmemTable<T>& tab,
+                                            int64_t m) {
+        load_row_i32<K>(nb, a.nbrs + m * K);
+        uint32_t jc[PM::KP1][D];
+        PM::gather(jc, a.coords, nb, a.n0 + m);
+        PM::template assemble<KEEP_R>(L, R, jc, a.scale, tab);
+        PM::chol(L);
+    }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Flat kernels.
+// ---------------------------------------------------------------------------------------------
+
+// Conditional-mean weights and std of points [m_begin, m_end) (refine_meanvec_std_kernel!,
+// src/kernels.jl:61-78): mv is (M, K) point-major, sd is (M).
+template <typename T, int K, int D>
+__global__ void __launch_bounds__(kFlatThreads)
+k_factor(PointArgs<T> a, int64_t m_begin, int64_t m_end, T* __restrict__ mv, T* __restrict__ sd) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    SmemTable<T> tab;
+    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
+    __syncthreads();
+    for (int64_t m = m_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < m_end;
+         m += (int64_t)gridDim.x * blockDim.x) {
+        PointFactor<T, K, D, false> f;
+        f.compute(a, tab, m);
+        T x[K];
+        PointMath<T, K, D>::solve(x, f.L, a.tab.pivc);
+        store_row_t<T, K>(mv + m * K, x);
+        sd[m] = f.L[tri(K, K)];
+    }
+}
+
+// refine_inv_kernel! (src/kernels.jl:37-56).
+template <typename T, int K, int D>
+__global__ void __launch_bounds__(kFlatThreads)
+k_inv(PointArgs<T> a, const T* __restrict__ values, T* __restrict__ xi_out, int64_t M) {
+    using N = Num<T>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    SmemTable<T> tab;
+    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
+    __syncthreads();
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
+         m += (int64_t)gridDim.x * blockDim.x) {
+        PointFactor<T, K, D, false> f;
+        f.compute(a, tab, m);
+        T x[K];
+        PointMath<T, K, D>::solve(x, f.L, a.tab.pivc);
+        T mean = T(0);
+        sfor<0, K>([&](auto j_) {
+            GPB2_CI(j);
+            mean = N::add(mean, N::mul(x[j], values[f.nb[j]]));
+        });
+        xi_out[m] = N::div(N::sub(values[a.n0 + m], mean), f.L[tri(K, K)]);
+    }
+}
+
+// refine_logdet_kernel! (src/kernels.jl:25-35) + the sum, accumulated in double.
+template <typename T, int K, int D>
+__global__ void __launch_bounds__(kFlatThreads)
+k_logdet(PointArgs<T> a, T* __restrict__ terms, double* __restrict__ acc, int64_t M) {
+    using N = Num<T>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ double red[32];
+    SmemTable<T> tab;
+    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
+    __syncthreads();
+    double s = 0.0;
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
+         m += (int64_t)gridDim.x * blockDim.x) {
+        PointFactor<T, K, D, false> f;
+        f.compute(a, tab, m);
+        const T t = N::log(f.L[tri(K, K)]);
+        if (terms) terms[m] = t;
+        s += (double)t;
+    }
+    s = block_sum_double(s, red);
+    if (threadIdx.x == 0) atomicAdd(acc, s);
+}
+
+// Scatter a point's A-bar (lower triangle, in B) into the CTA histogram: the diagonal sum into
+// bin 0, each off-diagonal through the interpolation weights of its radius
+// (_scatter_Abar_hist!, src/kernels_adjoint.jl:50-74).
+template <typename T, int K, int D>
+__device__ __forceinline__ void scatter_hist(double* hist, const T (&B)[PointMath<T, K, D>::NT],
+                                             const T (&R)[PointMath<T, K, D>::NR],
+                                             const SmemTable<T>& tab) {
+    using N = Num<T>;
+    constexpr int KP1 = K + 1;
+    T dsum = T(0);
+    sfor<0, KP1>([&](auto a_) {
+        GPB2_CI(a);
+        dsum = N::add(dsum, B[tri(a, a)]);
+    });
+    atomicAdd(&hist[0], (double)dsum);
+    sfor<1, KP1>([&](auto a_) {
+        GPB2_CI(a);
+        sfor<0, a>([&](auto b_) {
+            GPB2_CI(b);
+            T wlo, whi;
+            const int lo = tab.weights(R[tri(a - 1, b)], wlo, whi);
+            const T g = B[tri(a, b)];
+            atomicAdd(&hist[lo], (double)N::mul(g, wlo));
+            atomicAdd(&hist[lo + 1], (double)N::mul(g, whi));
+        });
+    });
+}
+
+__device__ __forceinline__ void flush_hist(double* __restrict__ gacc, const double* hist, int nb) {
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+        const double h = hist[i];
+        if (h != 0.0) atomicAdd(&gacc[i], h);
+    }
+}
+
+// refine_logdet_and_grad_hist_kernel! (src/kernels_adjoint.jl:117-152), seed 1.
+template <typename T, int K, int D>
+__global__ void __launch_bounds__(kFlatThreads)
+k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld_acc,
+              T* __restrict__ terms, int64_t M) {
+    using N = Num<T>;
+    using PM = PointMath<T, K, D>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ double red[32];
+    SmemTable<T> tab;
+    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
+    double* hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
+    for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
+    __syncthreads();
+    double s = 0.0;
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
+         m += (int64_t)gridDim.x * blockDim.x) {
+        PointFactor<T, K, D, true> f;
+        f.compute(a, tab, m);
+        const T lkk = f.L[tri(K, K)];
+        const T t = N::log(lkk);
+        if (terms) terms[m] = t;
+        s += (double)t;
+        T B[PM::NT];
+        sfor<0, PM::NT>([&](auto i_) {
+            GPB2_CI(i);
+            B[i] = T(0);
+        });
+        B[tri(K, K)] = N::div(T(1), lkk);  // chol_logdet_pullback! seed (src/linalg.jl:220-229)
+        PM::pullback(B, f.L);
+        scatter_hist<T, K, D>(hist, B, f.R, tab);
+    }
+    s = block_sum_double(s, red);
+    if (threadIdx.x == 0 && ld_acc) atomicAdd(ld_acc, s);
+    __syncthreads();
+    flush_hist(gacc, hist, a.tab.nb);
+}
+
+// Per-point vals-gradient of generate (generate_grad_vals_rev_kernel!,
+// src/kernels_adjoint.jl:484-553), run over ALL points after the reverse sweep has finalised
+// vb: every point's cotangent seed (vb[p]*xi[p], vb[p]*v[nbr]) is then known, and the point's
+// pullback needs nothing else, so the batches need not be visited in order.
+template <typename T, int K, int D>
+__global__ void __launch_bounds__(kFlatThreads)
+k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
+            const T* __restrict__ vb, double* __restrict__ gacc, int64_t M) {
+    using N = Num<T>;
+    using PM = PointMath<T, K, D>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    SmemTable<T> tab;
+    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
+    double* hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
+    for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
+    __syncthreads();
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
+         m += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t p = a.n0 + m;
+        const T vbp = vb[p];
+        PointFactor<T, K, D, true> f;
+        f.compute(a, tab, m);
+        T x[K];
+        PM::solve(x, f.L, a.tab.pivc);
+        const T pivfloor = N::mul(a.tab.pivc, f.L[0]);
+        T B[PM::NT];
+        sfor<0, PM::NT>([&](auto i_) {
+            GPB2_CI(i);
+            B[i] = T(0);
+        });
+        B[tri(K, K)] = N::mul(vbp, xih[p]);
+        T z[K];
+        sfor<0, K>([&](auto j_) {
+            GPB2_CI(j);
+            z[j] = N::mul(vbp, v[f.nb[j]]);
+        });
+        PM::template forward_subst<true>(z, f.L, pivfloor);
+        PM::seed_from_solve(B, z, x);
+        PM::pullback(B, f.L);
+        scatter_hist<T, K, D>(hist, B, f.R, tab);
+    }
+    __syncthreads();
+    flush_hist(gacc, hist, a.tab.nb);
+}
+
+// refine_inv_loss_grad_hist_kernel! (src/kernels_adjoint.jl:155-221): loss 0.5*sum(xi^2) and its
+// vals-gradient; the z-bar solve has no pivot guard, as in the reference.
+template <typename T, int K, int D>
+__global__ void __launch_bounds__(kFlatThreads)
+k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict__ gacc,
+                double* __restrict__ loss_acc, T* __restrict__ xi_out, int64_t M) {
+    using N = Num<T>;
+    using PM = PointMath<T, K, D>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ double red[32];
+    SmemTable<T> tab;
+    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
+    double* hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
+    for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
+    __syncthreads();
+    double ls = 0.0;
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
+         m += (int64_t)gridDim.x * blockDim.x) {
+        PointFactor<T, K, D, true> f;
+        f.compute(a, tab, m);
+        T x[K];
+        PM::solve(x, f.L, a.tab.pivc);
+        const T sd = f.L[tri(K, K)];
+        T vn[K];
+        T mean = T(0);
+        sfor<0, K>([&](auto j_) {
+            GPB2_CI(j);
+            vn[j] = values[f.nb[j]];
+            mean = N::add(mean, N::mul(x[j], vn[j]));
+        });
+        const T xim = N::div(N::sub(values[a.n0 + m], mean), sd);
+        if (xi_out) xi_out[m] = xim;
+        ls += (double)N::div(N::mul(xim, xim), T(2));
+        T B[PM::NT];
+        sfor<0, PM::NT>([&](auto i_) {
+            GPB2_CI(i);
+            B[i] = T(0);
+        });
+        B[tri(K, K)] = N::div(N::mul(-xim, xim), sd);
+        T z[K];
+        sfor<0, K>([&](auto j_) {
+            GPB2_CI(j);
+            z[j] = N::div(N::mul(-xim, vn[j]), sd);
+        });
+        PM::template forward_subst<false>(z, f.L, T(0));
+        PM::seed_from_solve(B, z, x);
+        PM::pullback(B, f.L);
+        scatter_hist<T, K, D>(hist, B, f.R, tab);
+    }
+    ls = block_sum_double(ls, red);
+    if (threadIdx.x == 0 && loss_acc) atomicAdd(loss_acc, ls);
+    __syncthreads();
+    flush_hist(gacc, hist, a.tab.nb);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Per-batch kernels.
+// ---------------------------------------------------------------------------------------------
+
+// Fused forward for tree positions [p_lo, p_hi) (refine_apply_fused_kernel!,
+// src/kernels.jl:101-119): values[p] = std*xi + sum_j mv[j]*values[nbr_j], in that order.
+template <typename T, int K, int D>
+__global__ void __launch_bounds__(kFlatThreads)
+k_fused_fwd(PointArgs<T> a, T* __restrict__ values, const T* __restrict__ xi_ref, int64_t p_lo,
+            int64_t p_hi) {
+    using N = Num<T>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    SmemTable<T> tab;
+    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
+    __syncthreads();
+    for (int64_t p = p_lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < p_hi;
+         p += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = p - a.n0;
+        PointFactor<T, K, D, false> f;
+        f.compute(a, tab, m);
+        T x[K];
+        PointMath<T, K, D>::solve(x, f.L, a.tab.pivc);
+        T acc = N::mul(f.L[tri(K, K)], xi_ref[m]);
+        sfor<0, K>([&](auto j_) {
+            GPB2_CI(j);
+            acc = N::add(acc, N::mul(x[j], values[f.nb[j]]));
+        });
+        values[p] = acc;
+    }
+}
+
+// Forward sweep step from materialised weights (refine_apply_kernel!, src/kernels.jl:83-94,
+// with the fused kernel's accumulation order: std*xi first).
+template <typename T, int K>
+__global__ void __launch_bounds__(kSweepThreads)
+k_sweep_fwd(T* __restrict__ values, const T* __restrict__ xi_ref, const T* __restrict__ mv,
+            const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0, int64_t p_lo,
+            int64_t p_hi) {
+    using N = Num<T>;
+    const int64_t p = p_lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= p_hi) return;
+    const int64_t m = p - n0;
+    int nb[K];
+    T w[K];
+    load_row_i32<K>(nb, nbrs + m * K);
+    load_row_t<T, K>(w, mv + m * K);
+    T acc = N::mul(__ldg(sd + m), __ldg(xi_ref + m));
+#pragma unroll
+    for (int j = 0; j < K; j++) acc = N::add(acc, N::mul(w[j], values[nb[j]]));
+    values[p] = acc;
+}
+
+// Reverse sweep step (refine_reverse_apply_kernel!, src/kernels_adjoint.jl:433-447):
+// xg[p] = std*vb[p]; vb[nbr_j] += mv[j]*vb[p] (atomic: batch-mates can share a neighbour).
+template <typename T, int K>
+__global__ void __launch_bounds__(kSweepThreads)
+k_sweep_rev(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv,
+            const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0, int64_t p_lo,
+            int64_t p_hi) {
+    using N = Num<T>;
+    const int64_t p = p_lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= p_hi) return;
+    const int64_t m = p - n0;
+    int nb[K];
+    T w[K];
+    load_row_i32<K>(nb, nbrs + m * K);
+    load_row_t<T, K>(w, mv + m * K);
+    const T vbp = vb[p];
+    if (xg) xg[p] = N::mul(__ldg(sd + m), vbp);
+#pragma unroll
+    for (int j = 0; j < K; j++) atomicAdd(vb + nb[j], N::mul(w[j], vbp));
+}
+
+// ---------------------------------------------------------------------------------------------
+// Launchers, bundled per (T, K, D) into an Ops table.
+// ---------------------------------------------------------------------------------------------
+template <typename T>
+struct Ops {
+    cudaError_t (*factor)(const PointArgs<T>&, int64_t, int64_t, T*, T*, cudaStream_t);
+    cudaError_t (*inv)(const PointArgs<T>&, const T*, T*, int64_t, cudaStream_t);
+    cudaError_t (*logdet)(const PointArgs<T>&, T*, double*, int64_t, cudaStream_t);
+    cudaError_t (*logdet_grad)(const PointArgs<T>&, double*, double*, T*, int64_t, cudaStream_t);
+    cudaError_t (*grad_vals)(const PointArgs<T>&, const T*, const T*, const T*, double*, int64_t,
+                             cudaStream_t);
+    cudaError_t (*inv_loss_grad)(const PointArgs<T>&, const T*, double*, double*, T*, int64_t,
+                                 cudaStream_t);
+    cudaError_t (*fused_fwd)(const PointArgs<T>&, T*, const T*, int64_t, int64_t, cudaStream_t);
+    cudaError_t (*sweep_fwd)(T*, const T*, const T*, const T*, const int*, int64_t, int64_t,
+                             int64_t, cudaStream_t);
+    cudaError_t (*sweep_rev)(T*, T*, const T*, const T*, const int*, int64_t, int64_t, int64_t,
+                             cudaStream_t);
+};
+
+template <typename T>
+inline size_t flat_smem(const PointArgs<T>& a, bool hist) {
+    return table_smem_bytes<T>(a.tab.nb, a.tab.nkeys) + (hist ? sizeof(double) * a.tab.nb : 0);
+}
+
+template <typename T, int K, int D>
+struct Launch {
+    template <class Kern, class... Args>
+    static cudaError_t flat(const char* name, Kern kern, size_t smem, int64_t work,
+                            cudaStream_t s, Args... args) {
+        if (work <= 0) return cudaSuccess;
+        cudaError_t e = prepare_kernel_smem((const void*)kern, smem);
+        if (e != cudaSuccess) return e;
+        const int grid = flat_grid((const void*)kern, kFlatThreads, smem, work);
+        return launch_prof(name, kern, dim3(grid), dim3(kFlatThreads), smem, s, args...);
+    }
+    static cudaError_t factor(const PointArgs<T>& a, int64_t mb, int64_t me, T* mv, T* sd,
+                              cudaStream_t s) {
+        return flat("factor", k_factor<T, K, D>, flat_smem(a, false), me - mb, s, a, mb, me, mv,
+                    sd);
+    }
+    static cudaError_t inv(const PointArgs<T>& a, const T* values, T* xi, int64_t M,
+                           cudaStream_t s) {
+        return flat("inv", k_inv<T, K, D>, flat_smem(a, false), M, s, a, values, xi, M);
+    }
+    static cudaError_t logdet(const PointArgs<T>& a, T* terms, double* acc, int64_t M,
+                              cudaStream_t s) {
+        return flat("logdet", k_logdet<T, K, D>, flat_smem(a, false), M, s, a, terms, acc, M);
+    }
+    static cudaError_t logdet_grad(const PointArgs<T>& a, double* gacc, double* ld, T* terms,
+                                   int64_t M, cudaStream_t s) {
+        return flat("logdet_grad", k_logdet_grad<T, K, D>, flat_smem(a, true), M, s, a, gacc, ld,
+                    terms, M);
+    }
+    static cudaError_t grad_vals(const PointArgs<T>& a, const T* v, const T* xih, const T* vb,
+                                 double* gacc, int64_t M, cudaStream_t s) {
+        return flat("grad_vals", k_grad_vals<T, K, D>, flat_smem(a, true), M, s, a, v, xih, vb,
+                    gacc, M);
+    }
+    static cudaError_t inv_loss_grad(const PointArgs<T>& a, const T* values, double* gacc,
+                                     double* loss, T* xi_out, int64_t M, cudaStream_t s) {
+        return flat("inv_loss_grad", k_inv_loss_grad<T, K, D>, flat_smem(a, true), M, s, a,
+                    values, gacc, loss, xi_out, M);
+    }
+    static cudaError_t fused_fwd(const PointArgs<T>& a, T* values, const T* xi_ref, int64_t lo,
+                                 int64_t hi, cudaStream_t s) {
+        return flat("fused_fwd", k_fused_fwd<T, K, D>, flat_smem(a, false), hi - lo, s, a,
+                    values, xi_ref, lo, hi);
+    }
+    static cudaError_t sweep_fwd(T* values, const T* xi_ref, const T* mv, const T* sd,
+                                 const int* nbrs, int64_t n0, int64_t lo, int64_t hi,
+                                 cudaStream_t s) {
+        if (hi <= lo) return cudaSuccess;
+        const int64_t grid = (hi - lo + kSweepThreads - 1) / kSweepThreads;
+        return launch_prof("sweep_fwd", k_sweep_fwd<T, K>, dim3((unsigned)grid),
+                           dim3(kSweepThreads), 0, s, values, xi_ref, mv, sd, nbrs, n0, lo, hi);
+    }
+    static cudaError_t sweep_rev(T* xg, T* vb, const T* mv, const T* sd, const int* nbrs,
+                                 int64_t n0, int64_t lo, int64_t hi, cudaStream_t s) {
+        if (hi <= lo) return cudaSuccess;
+        const int64_t grid = (hi - lo + kSweepThreads - 1) / kSweepThreads;
+        return launch_prof("sweep_rev", k_sweep_rev<T, K>, dim3((unsigned)grid),
+                           dim3(kSweepThreads), 0, s, xg, vb, mv, sd, nbrs, n0, lo, hi);
+    }
+    static const Ops<T>* ops() {
+        static const Ops<T> o = {factor,    inv,       logdet,    logdet_grad, grad_vals,
+                                 inv_loss_grad, fused_fwd, sweep_fwd, sweep_rev};
+        return &o;
+    }
+};
+
+// Registry: the (K, D) pairs with a compiled kernel set (gpb2_inst_*.cu).
+template <typename T>
+const Ops<T>* find_ops(int K, int D);
+
+}  // namespace gpb2

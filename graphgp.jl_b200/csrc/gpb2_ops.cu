@@ -1,0 +1,442 @@
+// gpb2_ops.cu -- the C-ABI operations: orchestration of the refine kernels, the dense layer and
+// the tree<->original permutation (src/orchestrate.jl, src/api.jl, src/grad.jl,
+// src/grad_generate_vals.jl).
+//
+// Forward and reverse depth sweeps.  The conditional-mean weights and std of every refined point
+// depend only on the graph and the table, not on the field, so they are produced by one flat
+// kernel over all M points (full-GPU occupancy regardless of batch sizes) and the depth batches
+// are then swept by a light kernel per batch (K gathers and K multiply-adds per point).  The
+// reference's fused per-batch kernel (refine_apply_fused_kernel!) recomputes the factor inside
+// the sweep; it is kept as the "fused" forward mode (GPB2_FWD=fused) and gives the identical
+// result bit for bit: both evaluate the same per-point arithmetic in the same order.
+//
+// generate_grad_vals.  Every point's contribution to d(vals) is linear in its final cotangent
+// vb[p]; once the reverse sweep has finalised vb for all points, the per-point pullbacks are
+// independent and run as one flat kernel instead of one launch per batch.
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "gpb2_problem.h"
+
+namespace gpb2 {
+
+namespace {
+
+template <typename T>
+__global__ void k_gather(const T* __restrict__ src, const int* __restrict__ idx,
+                         T* __restrict__ dst, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = src[idx[i]];
+}
+
+template <typename T>
+__global__ void k_scatter(const T* __restrict__ src, const int* __restrict__ idx,
+                          T* __restrict__ dst, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        dst[idx[i]] = src[i];
+}
+
+template <typename T>
+__global__ void k_hist_to_t(const double* __restrict__ acc, T* __restrict__ out, int64_t nb) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nb;
+         i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = (T)acc[i];
+}
+
+inline unsigned grid1d(int64_t n) {
+    int64_t g = (n + 255) / 256;
+    return (unsigned)(g < 1 ? 1 : (g > 148 * 16 ? 148 * 16 : g));
+}
+
+enum class FwdMode { Sweep = 0, Fused = 1 };
+
+// Process-wide forward mode: GPB2_FWD=fused at load time, or gpb2_set_forward_mode().
+std::atomic<int> g_fwd_mode{[] {
+    const char* e = std::getenv("GPB2_FWD");
+    return (e && std::strcmp(e, "fused") == 0) ? 1 : 0;
+}()};
+
+FwdMode fwd_mode() { return g_fwd_mode.load() == 1 ? FwdMode::Fused : FwdMode::Sweep; }
+
+}  // namespace
+
+template <typename T>
+struct Impl {
+    using P = gpb2_problem;
+
+    static int check_launch(cudaError_t e, const char* what) {
+        if (e != cudaSuccess)
+            return set_error(GPB2_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+        return GPB2_OK;
+    }
+
+    // original -> tree: dst[i] = src[indices[i]]
+    static int gather(P* p, const T* src, T* dst, cudaStream_t s) {
+        return check_launch(launch_prof("gather", k_gather<T>, dim3(grid1d(p->n)), dim3(256), 0,
+                                        s, src, (const int*)p->indices, dst, p->n),
+                            "gather");
+    }
+    // tree -> original: dst[indices[i]] = src[i]
+    static int scatter(P* p, const T* src, T* dst, cudaStream_t s) {
+        return check_launch(launch_prof("scatter", k_scatter<T>, dim3(grid1d(p->n)), dim3(256), 0,
+                                        s, src, (const int*)p->indices, dst, p->n),
+                            "scatter");
+    }
+
+    static int factor_all(P* p, cudaStream_t s) {
+        return check_launch(ops_of<T>(p)->factor(point_args<T>(p), 0, p->m, (T*)p->mv, (T*)p->sd,
+                                                 s),
+                            "factor");
+    }
+
+    // values[0:n0] preset; fills values[n0:N] batch by batch.
+    static int refine_sweep(P* p, T* values, const T* xi_ref, bool have_factor, cudaStream_t s) {
+        const Ops<T>* o = ops_of<T>(p);
+        if (fwd_mode() == FwdMode::Fused && !have_factor) {
+            const PointArgs<T> a = point_args<T>(p);
+            for (size_t b = 1; b < p->offsets.size(); b++)
+                GPB2_TRY(check_launch(
+                    o->fused_fwd(a, values, xi_ref, p->offsets[b - 1], p->offsets[b], s),
+                    "fused forward"));
+            return GPB2_OK;
+        }
+        if (!have_factor) GPB2_TRY(factor_all(p, s));
+        for (size_t b = 1; b < p->offsets.size(); b++)
+            GPB2_TRY(check_launch(o->sweep_fwd(values, xi_ref, (const T*)p->mv,
+                                               (const T*)p->sd, p->nbrs, p->n0,
+                                               p->offsets[b - 1], p->offsets[b], s),
+                                  "forward sweep"));
+        return GPB2_OK;
+    }
+
+    // Reverse sweep over the batches, latest first; xg may be NULL.
+    static int reverse_sweep(P* p, T* xg, T* vb, cudaStream_t s) {
+        const Ops<T>* o = ops_of<T>(p);
+        for (size_t b = p->offsets.size() - 1; b >= 1; b--)
+            GPB2_TRY(check_launch(o->sweep_rev(xg, vb, (const T*)p->mv, (const T*)p->sd, p->nbrs,
+                                               p->n0, p->offsets[b - 1], p->offsets[b], s),
+                                  "reverse sweep"));
+        return GPB2_OK;
+    }
+
+    static int finish_hist(P* p, T* dvals, cudaStream_t s) {
+        return check_launch(launch_prof("hist_to_t", k_hist_to_t<T>, dim3(grid1d(p->nb)),
+                                        dim3(256), 0, s, (const double*)p->dacc, dvals, p->nb),
+                            "histogram convert");
+    }
+
+    static int zero_acc(P* p, cudaStream_t s) {
+        GPB2_CUDA_TRY(cudaMemsetAsync(p->dacc, 0, sizeof(double) * (p->nb + 8), s));
+        return GPB2_OK;
+    }
+
+    static int read_scalars(P* p, double* h, cudaStream_t s) {
+        GPB2_CUDA_TRY(
+            cudaMemcpyAsync(h, p->dacc + p->nb, sizeof(double) * 4, cudaMemcpyDeviceToHost, s));
+        GPB2_CUDA_TRY(cudaStreamSynchronize(s));
+        return GPB2_OK;
+    }
+
+    // ---------------------------------------------------------------- refine layer (tree order)
+    static int refine(P* p, T* values, const T* xi_ref, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, true));
+        return refine_sweep(p, values, xi_ref, false, s);
+    }
+
+    static int refine_inv(P* p, const T* values, T* xi_ref, cudaStream_t s) {
+        return check_launch(ops_of<T>(p)->inv(point_args<T>(p), values, xi_ref, p->m, s),
+                            "refine_inv");
+    }
+
+    static int refine_logdet(P* p, T* terms, double* out, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        GPB2_TRY(zero_acc(p, s));
+        GPB2_TRY(check_launch(
+            ops_of<T>(p)->logdet(point_args<T>(p), terms, p->dacc + p->nb, p->m, s), "logdet"));
+        if (out) {
+            double h[4];
+            GPB2_TRY(read_scalars(p, h, s));
+            *out = h[0];
+        }
+        return GPB2_OK;
+    }
+
+    static int refine_logdet_grad_vals(P* p, T* dvals, double* ld, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        GPB2_TRY(zero_acc(p, s));
+        GPB2_TRY(check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p), p->dacc,
+                                                        p->dacc + p->nb, nullptr, p->m, s),
+                              "logdet grad"));
+        GPB2_TRY(finish_hist(p, dvals, s));
+        if (ld) {
+            double h[4];
+            GPB2_TRY(read_scalars(p, h, s));
+            *ld = h[0];
+        }
+        return GPB2_OK;
+    }
+
+    static int refine_inv_loss_grad_vals(P* p, const T* values, T* dvals, double* loss,
+                                         cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        GPB2_TRY(zero_acc(p, s));
+        GPB2_TRY(check_launch(ops_of<T>(p)->inv_loss_grad(point_args<T>(p), values, p->dacc,
+                                                          p->dacc + p->nb + 1, nullptr, p->m, s),
+                              "inverse-loss grad"));
+        GPB2_TRY(finish_hist(p, dvals, s));
+        if (loss) {
+            double h[4];
+            GPB2_TRY(read_scalars(p, h, s));
+            *loss = h[1];
+        }
+        return GPB2_OK;
+    }
+
+    // ---------------------------------------------------------------- orchestrated (original order)
+    static int generate(P* p, const T* xi, T* out, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, true));
+        const T* xt = xi;
+        if (p->indices) {
+            GPB2_TRY(gather(p, xi, (T*)p->buf_b, s));
+            xt = (const T*)p->buf_b;
+        }
+        T* values = p->indices ? (T*)p->buf_a : out;
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(Dense<T>::apply_L(p, xt, values, s));
+        GPB2_TRY(refine_sweep(p, values, xt + p->n0, false, s));
+        if (p->indices) GPB2_TRY(scatter(p, values, out, s));
+        return GPB2_OK;
+    }
+
+    static int generate_inv(P* p, const T* values, T* xi, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        const T* vt = values;
+        if (p->indices) {
+            GPB2_TRY(gather(p, values, (T*)p->buf_a, s));
+            vt = (const T*)p->buf_a;
+        }
+        T* xt = p->indices ? (T*)p->buf_b : xi;
+        GPB2_TRY(refine_inv(p, vt, xt + p->n0, s));
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(Dense<T>::solve_L(p, vt, xt, s));
+        if (p->indices) GPB2_TRY(scatter(p, xt, xi, s));
+        return GPB2_OK;
+    }
+
+    static int generate_logdet(P* p, double* out, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        GPB2_TRY(zero_acc(p, s));
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(Dense<T>::logdet(p, p->dacc + p->nb + 2, s));
+        GPB2_TRY(check_launch(
+            ops_of<T>(p)->logdet(point_args<T>(p), nullptr, p->dacc + p->nb, p->m, s), "logdet"));
+        double h[4];
+        GPB2_TRY(read_scalars(p, h, s));
+        *out = h[2] + h[0];
+        return GPB2_OK;
+    }
+
+    static int generate_grad_xi(P* p, const T* vbar, T* xbar, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, true));
+        T* vb = (T*)p->buf_c;
+        if (p->indices)
+            GPB2_TRY(gather(p, vbar, vb, s));
+        else
+            GPB2_CUDA_TRY(
+                cudaMemcpyAsync(vb, vbar, sizeof(T) * p->n, cudaMemcpyDeviceToDevice, s));
+        T* xg = p->indices ? (T*)p->buf_d : xbar;
+        GPB2_TRY(factor_all(p, s));
+        GPB2_TRY(reverse_sweep(p, xg, vb, s));
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(Dense<T>::apply_Lt(p, vb, xg, s));
+        if (p->indices) GPB2_TRY(scatter(p, xg, xbar, s));
+        return GPB2_OK;
+    }
+
+    static int generate_grad_vals(P* p, const T* xi, const T* vbar, T* dvals, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, true));
+        const T* xt = xi;
+        if (p->indices) {
+            GPB2_TRY(gather(p, xi, (T*)p->buf_b, s));
+            xt = (const T*)p->buf_b;
+        }
+        T* v = (T*)p->buf_a;
+        T* vb = (T*)p->buf_c;
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(Dense<T>::apply_L(p, xt, v, s));
+        GPB2_TRY(factor_all(p, s));
+        GPB2_TRY(refine_sweep(p, v, xt + p->n0, true, s));
+        if (p->indices)
+            GPB2_TRY(gather(p, vbar, vb, s));
+        else
+            GPB2_CUDA_TRY(
+                cudaMemcpyAsync(vb, vbar, sizeof(T) * p->n, cudaMemcpyDeviceToDevice, s));
+        GPB2_TRY(reverse_sweep(p, nullptr, vb, s));
+        GPB2_TRY(zero_acc(p, s));
+        GPB2_TRY(check_launch(
+            ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb, p->dacc, p->m, s), "grad_vals"));
+        GPB2_TRY(Dense<T>::grad_vals(p, vb, xt, p->dacc, s));
+        return finish_hist(p, dvals, s);
+    }
+
+    static int generate_logdet_grad_vals(P* p, T* dvals, double* ld, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        GPB2_TRY(zero_acc(p, s));
+        GPB2_TRY(check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p), p->dacc,
+                                                        p->dacc + p->nb, nullptr, p->m, s),
+                              "logdet grad"));
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(Dense<T>::logdet(p, p->dacc + p->nb + 2, s));
+        GPB2_TRY(Dense<T>::logdet_grad(p, p->dacc, s));
+        GPB2_TRY(finish_hist(p, dvals, s));
+        if (ld) {
+            double h[4];
+            GPB2_TRY(read_scalars(p, h, s));
+            *ld = h[2] + h[0];
+        }
+        return GPB2_OK;
+    }
+
+    static int generate_inv_loss_grad_vals(P* p, const T* data, T* dvals, double* loss,
+                                           cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        const T* yt = data;
+        if (p->indices) {
+            GPB2_TRY(gather(p, data, (T*)p->buf_a, s));
+            yt = (const T*)p->buf_a;
+        }
+        GPB2_TRY(zero_acc(p, s));
+        GPB2_TRY(check_launch(ops_of<T>(p)->inv_loss_grad(point_args<T>(p), yt, p->dacc,
+                                                          p->dacc + p->nb + 1, nullptr, p->m, s),
+                              "inverse-loss grad"));
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(Dense<T>::inv_loss_grad(p, yt, p->dacc, p->dacc + p->nb + 1, s));
+        GPB2_TRY(finish_hist(p, dvals, s));
+        if (loss) {
+            double h[4];
+            GPB2_TRY(read_scalars(p, h, s));
+            *loss = h[1];
+        }
+        return GPB2_OK;
+    }
+};
+
+}  // namespace gpb2
+
+using namespace gpb2;
+
+#define GPB2_DISPATCH(p, CALL32, CALL64)                                                       \
+    do {                                                                                       \
+        clear_error();                                                                         \
+        if (!(p)) return set_error(GPB2_ERR_INVALID_ARG, "%s: NULL problem", __func__);         \
+        DeviceGuard _dg((p)->device);                                                          \
+        if (!_dg.ok) return set_error(GPB2_ERR_NO_DEVICE, "cudaSetDevice(%d) failed", (p)->device); \
+        cudaStream_t s = (cudaStream_t)stream;                                                 \
+        (void)s;                                                                               \
+        return (p)->dtype == GPB2_F32 ? (CALL32) : (CALL64);                                   \
+    } while (0)
+
+#define F32(x) static_cast<float*>(const_cast<void*>(x))
+#define F64(x) static_cast<double*>(const_cast<void*>(x))
+#define CF32(x) static_cast<const float*>(x)
+#define CF64(x) static_cast<const double*>(x)
+
+static int need(const void* ptr, const char* name) {
+    return ptr ? GPB2_OK : set_error(GPB2_ERR_INVALID_ARG, "%s is NULL", name);
+}
+
+extern "C" {
+
+int gpb2_set_forward_mode(int mode) {
+    if (mode != 0 && mode != 1)
+        return set_error(GPB2_ERR_INVALID_ARG, "forward mode must be 0 (sweep) or 1 (fused)");
+    g_fwd_mode.store(mode);
+    return GPB2_OK;
+}
+
+int gpb2_refine(gpb2_problem* p, void* values, const void* xi_ref, void* stream) {
+    GPB2_TRY(need(values, "values") | need(xi_ref, "xi_ref"));
+    GPB2_DISPATCH(p, Impl<float>::refine(p, F32(values), CF32(xi_ref), s),
+                  Impl<double>::refine(p, F64(values), CF64(xi_ref), s));
+}
+
+int gpb2_refine_inv(gpb2_problem* p, const void* values, void* xi_ref, void* stream) {
+    GPB2_TRY(need(values, "values") | need(xi_ref, "xi_ref"));
+    GPB2_DISPATCH(p, Impl<float>::refine_inv(p, CF32(values), F32(xi_ref), s),
+                  Impl<double>::refine_inv(p, CF64(values), F64(xi_ref), s));
+}
+
+int gpb2_refine_logdet_terms(gpb2_problem* p, void* terms, void* stream) {
+    GPB2_TRY(need(terms, "terms"));
+    GPB2_DISPATCH(p, Impl<float>::refine_logdet(p, F32(terms), nullptr, s),
+                  Impl<double>::refine_logdet(p, F64(terms), nullptr, s));
+}
+
+int gpb2_refine_logdet(gpb2_problem* p, double* out, void* stream) {
+    GPB2_TRY(need(out, "logdet_host"));
+    GPB2_DISPATCH(p, Impl<float>::refine_logdet(p, nullptr, out, s),
+                  Impl<double>::refine_logdet(p, nullptr, out, s));
+}
+
+int gpb2_refine_logdet_grad_vals(gpb2_problem* p, void* dvals, double* ld, void* stream) {
+    GPB2_TRY(need(dvals, "dvals"));
+    GPB2_DISPATCH(p, Impl<float>::refine_logdet_grad_vals(p, F32(dvals), ld, s),
+                  Impl<double>::refine_logdet_grad_vals(p, F64(dvals), ld, s));
+}
+
+int gpb2_refine_inv_loss_grad_vals(gpb2_problem* p, const void* values, void* dvals,
+                                   double* loss, void* stream) {
+    GPB2_TRY(need(values, "values") | need(dvals, "dvals"));
+    GPB2_DISPATCH(p, Impl<float>::refine_inv_loss_grad_vals(p, CF32(values), F32(dvals), loss, s),
+                  Impl<double>::refine_inv_loss_grad_vals(p, CF64(values), F64(dvals), loss, s));
+}
+
+int gpb2_generate(gpb2_problem* p, const void* xi, void* out, void* stream) {
+    GPB2_TRY(need(xi, "xi") | need(out, "out"));
+    GPB2_DISPATCH(p, Impl<float>::generate(p, CF32(xi), F32(out), s),
+                  Impl<double>::generate(p, CF64(xi), F64(out), s));
+}
+
+int gpb2_generate_inv(gpb2_problem* p, const void* values, void* xi, void* stream) {
+    GPB2_TRY(need(values, "values") | need(xi, "xi"));
+    GPB2_DISPATCH(p, Impl<float>::generate_inv(p, CF32(values), F32(xi), s),
+                  Impl<double>::generate_inv(p, CF64(values), F64(xi), s));
+}
+
+int gpb2_generate_logdet(gpb2_problem* p, double* out, void* stream) {
+    GPB2_TRY(need(out, "logdet_host"));
+    GPB2_DISPATCH(p, Impl<float>::generate_logdet(p, out, s),
+                  Impl<double>::generate_logdet(p, out, s));
+}
+
+int gpb2_generate_grad_xi(gpb2_problem* p, const void* vbar, void* xbar, void* stream) {
+    GPB2_TRY(need(vbar, "vbar") | need(xbar, "xbar"));
+    GPB2_DISPATCH(p, Impl<float>::generate_grad_xi(p, CF32(vbar), F32(xbar), s),
+                  Impl<double>::generate_grad_xi(p, CF64(vbar), F64(xbar), s));
+}
+
+int gpb2_generate_grad_vals(gpb2_problem* p, const void* xi, const void* vbar, void* dvals,
+                            void* stream) {
+    GPB2_TRY(need(xi, "xi") | need(vbar, "vbar") | need(dvals, "dvals"));
+    GPB2_DISPATCH(p, Impl<float>::generate_grad_vals(p, CF32(xi), CF32(vbar), F32(dvals), s),
+                  Impl<double>::generate_grad_vals(p, CF64(xi), CF64(vbar), F64(dvals), s));
+}
+
+int gpb2_generate_logdet_grad_vals(gpb2_problem* p, void* dvals, double* ld, void* stream) {
+    GPB2_TRY(need(dvals, "dvals"));
+    GPB2_DISPATCH(p, Impl<float>::generate_logdet_grad_vals(p, F32(dvals), ld, s),
+                  Impl<double>::generate_logdet_grad_vals(p, F64(dvals), ld, s));
+}
+
+int gpb2_generate_inv_loss_grad_vals(gpb2_problem* p, const void* data, void* dvals,
+                                     double* loss, void* stream) {
+    GPB2_TRY(need(data, "data") | need(dvals, "dvals"));
+    GPB2_DISPATCH(p, Impl<float>::generate_inv_loss_grad_vals(p, CF32(data), F32(dvals), loss, s),
+                  Impl<double>::generate_inv_loss_grad_vals(p, CF64(data), F64(dvals), loss, s));
+}
+
+}  // extern "C"

@@ -1,0 +1,413 @@
+// gpb2_problem.cu -- problem handle: upload, layout conversion, graph validation, interpolation
+// table, scratch management, error plumbing.
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <string>
+#include <vector>
+
+#include "gpb2_problem.h"
+
+namespace gpb2 {
+
+static thread_local std::string g_last_error;
+
+int set_error(int status, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int ensure_alloc(void** ptr, size_t bytes) {
+    if (*ptr) return GPB2_OK;
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e != cudaSuccess) {
+        *ptr = nullptr;
+        cudaGetLastError();
+        return set_error(e == cudaErrorMemoryAllocation ? GPB2_ERR_OOM : GPB2_ERR_CUDA,
+                         "cudaMalloc(%zu bytes) failed: %s", bytes, cudaGetErrorString(e));
+    }
+    return GPB2_OK;
+}
+
+static size_t tsize(const gpb2_problem* p) { return p->dtype == GPB2_F32 ? 4 : 8; }
+
+int ensure_scratch(gpb2_problem* p, bool need_mv) {
+    const size_t ts = tsize(p);
+    GPB2_TRY(ensure_alloc(&p->buf_a, ts * p->n));
+    GPB2_TRY(ensure_alloc(&p->buf_b, ts * p->n));
+    GPB2_TRY(ensure_alloc(&p->buf_c, ts * p->n));
+    GPB2_TRY(ensure_alloc(&p->buf_d, ts * p->n));
+    GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&p->dacc), sizeof(double) * (p->nb + 8)));
+    if (need_mv) {
+        GPB2_TRY(ensure_alloc(&p->mv, ts * p->m * p->k));
+        GPB2_TRY(ensure_alloc(&p->sd, ts * p->m));
+    }
+    return GPB2_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Conversion / validation kernels.
+// ------------------------------------------------------------------------------------------
+__global__ void k_convert_coords(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst,
+                                 int64_t n, int D, int DS) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n * DS;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t pnt = i / DS;
+        const int d = (int)(i - pnt * DS);
+        dst[i] = d < D ? src[pnt * D + d] : 0u;
+    }
+}
+
+// Neighbour conversion to int32 0-based, checking the invariants the batch kernels rely on
+// (check_graph, src/graph_build.jl:20-57): every neighbour of a point at tree position p lies
+// strictly before the start of p's depth batch (hence before p).  Unset entries (index < 0
+// after rebasing) are rejected too: the forward path reads every neighbour.
+template <typename IT>
+__global__ void k_convert_nbrs(const IT* __restrict__ src, int base, int64_t M, int K,
+                               int64_t n0, const int64_t* __restrict__ offs, int64_t n_off,
+                               int* __restrict__ dst, unsigned long long* __restrict__ bad,
+                               unsigned long long* __restrict__ first_bad) {
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
+         m += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t p = n0 + m;
+        // Batch b with offs[b-1] <= p < offs[b]: the last index with offs[idx] <= p.
+        int64_t lo = 0, hi = n_off - 1;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi + 1) >> 1;
+            if (offs[mid] <= p) lo = mid; else hi = mid - 1;
+        }
+        const int64_t lstart = offs[lo];
+        for (int j = 0; j < K; j++) {
+            const long long v = (long long)src[m * K + j] - base;
+            const bool ok = v >= 0 && v < lstart;
+            dst[m * K + j] = ok ? (int)v : 0;
+            if (!ok) {
+                atomicAdd(bad, 1ull);
+                atomicMin(first_bad, (unsigned long long)(m * K + j));
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Interpolation table (see gpb2_device.cuh).
+// ------------------------------------------------------------------------------------------
+template <typename T> struct HostBits;
+template <> struct HostBits<float> {
+    using U = uint32_t;
+    static U bits(float x) { U u; std::memcpy(&u, &x, 4); return u; }
+    static float from(U u) { float x; std::memcpy(&x, &u, 4); return x; }
+};
+template <> struct HostBits<double> {
+    using U = uint64_t;
+    static U bits(double x) { U u; std::memcpy(&u, &x, 8); return u; }
+    static double from(U u) { double x; std::memcpy(&x, &u, 8); return x; }
+};
+
+constexpr int kMaxKeys = 4096;
+constexpr size_t kMaxSmem = 220 * 1024;
+
+template <typename T>
+static int build_table(gpb2_problem* p, const T* hb, const T* hv, cudaStream_t s) {
+    using HB = HostBits<T>;
+    using U = typename HB::U;
+    const int64_t nb = p->nb;
+    if (nb < 2)
+        return set_error(GPB2_ERR_UNSUPPORTED_TABLE, "covariance table needs >= 2 bins (got %lld)",
+                         (long long)nb);
+    if (nb - 2 > 65535)
+        return set_error(GPB2_ERR_UNSUPPORTED_TABLE, "at most 65537 bins are supported");
+    for (int64_t i = 0; i < nb; i++)
+        if (!std::isfinite((double)hb[i]) || !std::isfinite((double)hv[i]))
+            return set_error(GPB2_ERR_UNSUPPORTED_TABLE, "bins/vals[%lld] is not finite",
+                             (long long)i);
+    for (int64_t i = 1; i < nb; i++)
+        if (!(hb[i] > hb[i - 1]))
+            return set_error(GPB2_ERR_UNSUPPORTED_TABLE,
+                             "bins must be strictly increasing (bins[%lld] <= bins[%lld])",
+                             (long long)i, (long long)(i - 1));
+    if (!(hb[1] > T(0)))
+        return set_error(GPB2_ERR_UNSUPPORTED_TABLE, "bins[1] must be > 0");
+
+    // Segments {x0, x1, y0, slope}; slope is the quotient cov_lookup forms, in T.
+    std::vector<T> seg(4 * (nb - 1));
+    for (int64_t lo = 0; lo < nb - 1; lo++) {
+        const T x0 = hb[lo], x1 = hb[lo + 1], y0 = hv[lo], y1 = hv[lo + 1];
+        const T dy = y1 - y0;
+        const T dx = x1 - x0;
+        seg[4 * lo + 0] = x0;
+        seg[4 * lo + 1] = x1;
+        seg[4 * lo + 2] = y0;
+        seg[4 * lo + 3] = dy / dx;
+    }
+    // Bucket index on the IEEE bits of r (monotone for r > 0).
+    const U k1 = HB::bits(hb[1]), kN = HB::bits(hb[nb - 1]);
+    int shift = 0;
+    while (shift < (int)(8 * sizeof(U)) - 1 && (uint64_t)((kN >> shift) - (k1 >> shift)) + 1 >
+                                                   (uint64_t)kMaxKeys)
+        shift++;
+    const U base = k1 >> shift;
+    const int nkeys = (int)((kN >> shift) - base + 1);
+    std::vector<uint16_t> start(nkeys);
+    int64_t l = 0;
+    for (int i = 0; i < nkeys; i++) {
+        const T vmin = HB::from((U)(base + (U)i) << shift);
+        while (l + 1 <= nb - 2 && hb[l + 1] <= vmin) l++;
+        start[i] = (uint16_t)l;
+    }
+    const size_t smem = table_smem_bytes<T>((int)nb, nkeys) + sizeof(double) * nb;
+    if (smem > kMaxSmem)
+        return set_error(GPB2_ERR_UNSUPPORTED_TABLE,
+                         "covariance table of %lld bins needs %zu bytes of shared memory "
+                         "(limit %zu)", (long long)nb, smem, kMaxSmem);
+
+    GPB2_TRY(ensure_alloc(&p->seg, sizeof(T) * seg.size()));
+    GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&p->start), sizeof(uint16_t) * kMaxKeys));
+    GPB2_CUDA_TRY(cudaMemcpyAsync(p->seg, seg.data(), sizeof(T) * seg.size(),
+                                  cudaMemcpyHostToDevice, s));
+    GPB2_CUDA_TRY(cudaMemcpyAsync(p->start, start.data(), sizeof(uint16_t) * nkeys,
+                                  cudaMemcpyHostToDevice, s));
+    // The host vectors die at return: finish the copies first.
+    GPB2_CUDA_TRY(cudaStreamSynchronize(s));
+    p->nkeys = nkeys;
+    p->shift = shift;
+    p->key_base = (uint64_t)base;
+    p->b0 = (double)hb[0];
+    p->b1 = (double)hb[1];
+    p->bN = (double)hb[nb - 1];
+    p->v0 = (double)hv[0];
+    p->vN = (double)hv[nb - 1];
+    const T pivc = T(1.5) * std::sqrt(std::numeric_limits<T>::epsilon());
+    p->pivc = (double)pivc;
+    return GPB2_OK;
+}
+
+static int load_table(gpb2_problem* p, const void* vals_dev, cudaStream_t s) {
+    const size_t ts = tsize(p);
+    GPB2_CUDA_TRY(cudaMemcpyAsync(p->vals, vals_dev, ts * p->nb, cudaMemcpyDeviceToDevice, s));
+    std::vector<unsigned char> hb(ts * p->nb), hv(ts * p->nb);
+    GPB2_CUDA_TRY(cudaMemcpyAsync(hb.data(), p->bins, ts * p->nb, cudaMemcpyDeviceToHost, s));
+    GPB2_CUDA_TRY(cudaMemcpyAsync(hv.data(), p->vals, ts * p->nb, cudaMemcpyDeviceToHost, s));
+    GPB2_CUDA_TRY(cudaStreamSynchronize(s));
+    if (p->dtype == GPB2_F32)
+        return build_table<float>(p, reinterpret_cast<const float*>(hb.data()),
+                                  reinterpret_cast<const float*>(hv.data()), s);
+    return build_table<double>(p, reinterpret_cast<const double*>(hb.data()),
+                               reinterpret_cast<const double*>(hv.data()), s);
+}
+
+static void free_problem(gpb2_problem* p) {
+    void* bufs[] = {p->coords, p->nbrs, p->indices, p->bins, p->vals,  p->seg,
+                    p->start,  p->mv,   p->sd,      p->buf_a, p->buf_b, p->buf_c,
+                    p->buf_d,  p->dacc, p->Ld,      p->Wd,   p->Wd2,   p->dwork,
+                    p->dinfo};
+    for (void* b : bufs)
+        if (b) cudaFree(b);
+    if (p->solver) cusolverDnDestroy(p->solver);
+    if (p->blas) cublasDestroy(p->blas);
+    delete p;
+}
+
+}  // namespace gpb2
+
+using namespace gpb2;
+
+extern "C" {
+
+int gpb2_version(void) { return GPB2_VERSION; }
+
+const char* gpb2_last_error(void) { return g_last_error.c_str(); }
+
+int gpb2_problem_create(gpb2_problem** out, int dtype, int device, const uint32_t* coords_dev,
+                        int64_t d, int64_t n, const void* neighbors_dev, int neighbor_bytes,
+                        int neighbor_base, int64_t k, const int64_t* offsets_host,
+                        int64_t n_offsets, int64_t n0, double scale, const void* bins_dev,
+                        const void* vals_dev, int64_t nbins, const int64_t* indices_host,
+                        int indices_base, void* stream) {
+    clear_error();
+    if (!out) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_create: out is NULL");
+    *out = nullptr;
+    if (dtype != GPB2_F32 && dtype != GPB2_F64)
+        return set_error(GPB2_ERR_INVALID_ARG, "dtype must be GPB2_F32 or GPB2_F64");
+    if (!coords_dev || !neighbors_dev || !offsets_host || !bins_dev || !vals_dev)
+        return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_create: NULL array argument");
+    if (n <= 0 || n0 <= 0 || n0 > n || k <= 0 || nbins <= 0 || n > (int64_t)INT32_MAX)
+        return set_error(GPB2_ERR_INVALID_ARG,
+                         "invalid sizes n=%lld n0=%lld k=%lld nbins=%lld (need 0<n0<=n<2^31)",
+                         (long long)n, (long long)n0, (long long)k, (long long)nbins);
+    if (neighbor_bytes != 4 && neighbor_bytes != 8)
+        return set_error(GPB2_ERR_INVALID_ARG, "neighbor_bytes must be 4 or 8");
+    if (neighbor_base != 0 && neighbor_base != 1)
+        return set_error(GPB2_ERR_INVALID_ARG, "neighbor_base must be 0 or 1");
+    if (!(scale > 0.0) || !std::isfinite(scale))
+        return set_error(GPB2_ERR_INVALID_ARG, "scale must be finite and > 0");
+    if (n_offsets < 1 || offsets_host[0] != n0 || offsets_host[n_offsets - 1] != n)
+        return set_error(GPB2_ERR_GRAPH, "offsets must start at n0 (%lld) and end at N (%lld)",
+                         (long long)n0, (long long)n);
+    for (int64_t b = 1; b < n_offsets; b++)
+        if (offsets_host[b] < offsets_host[b - 1])
+            return set_error(GPB2_ERR_GRAPH, "offsets must be non-decreasing (offsets[%lld])",
+                             (long long)b);
+    if (d < 1 || d > 8) return set_error(GPB2_ERR_UNSUPPORTED_D, "unsupported D=%lld", (long long)d);
+
+    auto* p = new gpb2_problem();
+    p->dtype = dtype;
+    p->device = device;
+    p->n = n;
+    p->n0 = n0;
+    p->m = n - n0;
+    p->k = k;
+    p->d = d;
+    p->nb = nbins;
+    p->scale = scale;
+    p->offsets.assign(offsets_host, offsets_host + n_offsets);
+    if (dtype == GPB2_F32) {
+        p->ops32 = find_ops<float>((int)k, (int)d);
+        if (!p->ops32) {
+            delete p;
+            return set_error(GPB2_ERR_UNSUPPORTED_K, "no f32 kernels compiled for K=%lld, D=%lld",
+                             (long long)k, (long long)d);
+        }
+    } else {
+        p->ops64 = find_ops<double>((int)k, (int)d);
+        if (!p->ops64) {
+            delete p;
+            return set_error(GPB2_ERR_UNSUPPORTED_K, "no f64 kernels compiled for K=%lld, D=%lld",
+                             (long long)k, (long long)d);
+        }
+    }
+
+    DeviceGuard dg(device);
+    if (!dg.ok) {
+        delete p;
+        return set_error(GPB2_ERR_NO_DEVICE, "cudaSetDevice(%d) failed", device);
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    int st = GPB2_OK;
+    do {
+        const int DS = coord_stride((int)d);
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&p->coords), sizeof(uint32_t) * n * DS)))
+            break;
+        k_convert_coords<<<(unsigned)std::min<int64_t>((n * DS + 255) / 256, 65535), 256, 0, s>>>(
+            coords_dev, p->coords, n, (int)d, DS);
+        // Neighbours.
+        const int64_t M = p->m;
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&p->nbrs), sizeof(int) * M * k))) break;
+        int64_t* doffs = nullptr;
+        unsigned long long* dbad = nullptr;
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&doffs), sizeof(int64_t) * n_offsets)))
+            break;
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&dbad), 2 * sizeof(unsigned long long)))) {
+            cudaFree(doffs);
+            break;
+        }
+        unsigned long long hbad[2] = {0ull, ~0ull};
+        cudaMemcpyAsync(doffs, offsets_host, sizeof(int64_t) * n_offsets, cudaMemcpyHostToDevice,
+                        s);
+        cudaMemcpyAsync(dbad, hbad, sizeof(hbad), cudaMemcpyHostToDevice, s);
+        const unsigned g = (unsigned)std::min<int64_t>((M + 255) / 256, 65535);
+        if (M > 0) {
+            if (neighbor_bytes == 8)
+                k_convert_nbrs<long long><<<g, 256, 0, s>>>(
+                    (const long long*)neighbors_dev, neighbor_base, M, (int)k, n0, doffs,
+                    n_offsets, p->nbrs, dbad, dbad + 1);
+            else
+                k_convert_nbrs<int><<<g, 256, 0, s>>>((const int*)neighbors_dev, neighbor_base, M,
+                                                      (int)k, n0, doffs, n_offsets, p->nbrs, dbad,
+                                                      dbad + 1);
+        }
+        cudaMemcpyAsync(hbad, dbad, sizeof(hbad), cudaMemcpyDeviceToHost, s);
+        cudaError_t e = cudaStreamSynchronize(s);
+        cudaFree(doffs);
+        cudaFree(dbad);
+        if (e != cudaSuccess) {
+            st = set_error(GPB2_ERR_CUDA, "neighbour upload failed: %s", cudaGetErrorString(e));
+            break;
+        }
+        if (hbad[0] != 0) {
+            const long long fb = (long long)hbad[1];
+            st = set_error(GPB2_ERR_GRAPH,
+                           "%llu neighbour entries are unset or not in an earlier depth batch "
+                           "(first: refined point %lld, slot %lld)",
+                           hbad[0], fb / k, fb % k);
+            break;
+        }
+        // Permutation.
+        if (indices_host) {
+            std::vector<int> idx(n);
+            std::vector<unsigned char> seen(n, 0);
+            for (int64_t i = 0; i < n; i++) {
+                const int64_t v = indices_host[i] - indices_base;
+                if (v < 0 || v >= n || seen[v]) {
+                    st = set_error(GPB2_ERR_INVALID_ARG,
+                                   "indices is not a permutation of 0..N-1 (entry %lld)",
+                                   (long long)i);
+                    break;
+                }
+                seen[v] = 1;
+                idx[i] = (int)v;
+            }
+            if (st) break;
+            if ((st = ensure_alloc(reinterpret_cast<void**>(&p->indices), sizeof(int) * n))) break;
+            if (cudaMemcpyAsync(p->indices, idx.data(), sizeof(int) * n, cudaMemcpyHostToDevice,
+                                s) != cudaSuccess ||
+                cudaStreamSynchronize(s) != cudaSuccess) {
+                st = set_error(GPB2_ERR_CUDA, "indices upload failed");
+                break;
+            }
+        }
+        // Table.
+        const size_t ts = tsize(p);
+        if ((st = ensure_alloc(&p->bins, ts * nbins))) break;
+        if ((st = ensure_alloc(&p->vals, ts * nbins))) break;
+        if (cudaMemcpyAsync(p->bins, bins_dev, ts * nbins, cudaMemcpyDeviceToDevice, s) !=
+            cudaSuccess) {
+            st = set_error(GPB2_ERR_CUDA, "bins copy failed");
+            break;
+        }
+        if ((st = load_table(p, vals_dev, s))) break;
+    } while (0);
+    if (st != GPB2_OK) {
+        cudaGetLastError();
+        free_problem(p);
+        return st;
+    }
+    *out = p;
+    return GPB2_OK;
+}
+
+int gpb2_problem_set_vals(gpb2_problem* p, const void* vals_dev, void* stream) {
+    clear_error();
+    if (!p || !vals_dev) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_set_vals: NULL");
+    DeviceGuard dg(p->device);
+    return load_table(p, vals_dev, (cudaStream_t)stream);
+}
+
+int gpb2_problem_info(const gpb2_problem* p, int64_t* n, int64_t* m, int64_t* k, int64_t* d,
+                      int64_t* n_batches) {
+    if (!p) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_info: NULL problem");
+    if (n) *n = p->n;
+    if (m) *m = p->m;
+    if (k) *k = p->k;
+    if (d) *d = p->d;
+    if (n_batches) *n_batches = (int64_t)p->offsets.size() - 1;
+    return GPB2_OK;
+}
+
+int gpb2_problem_destroy(gpb2_problem* p) {
+    if (!p) return GPB2_OK;
+    DeviceGuard dg(p->device);
+    cudaDeviceSynchronize();
+    free_problem(p);
+    return GPB2_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,127 @@
+// gpb2_problem.h -- the problem handle behind gpb2_problem* (internal).
+#pragma once
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+#include <cusolverDn.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "gpb2_internal.h"
+#include "gpb2_kernels.cuh"
+
+struct gpb2_problem {
+    int dtype = GPB2_F32;
+    int device = 0;
+    int64_t n = 0, m = 0, k = 0, d = 0, n0 = 0, nb = 0;
+    double scale = 0.0;
+    std::vector<int64_t> offsets;  // host: offsets[0] == n0, offsets.back() == n
+
+    // Device copies owned by the handle.
+    uint32_t* coords = nullptr;  // (N, coord_stride(D))
+    int* nbrs = nullptr;         // (M, K) int32, 0-based
+    int* indices = nullptr;      // (N) tree -> original, 0-based; nullptr = identity
+    void* bins = nullptr;        // (nb) T
+    void* vals = nullptr;        // (nb) T
+    void* seg = nullptr;         // 4 * (nb - 1) T
+    uint16_t* start = nullptr;   // nkeys
+    int nkeys = 0, shift = 0;
+    uint64_t key_base = 0;
+    double b0 = 0, b1 = 0, bN = 0, v0 = 0, vN = 0, pivc = 0;  // exact T values, widened
+
+    // Scratch, allocated on first use and kept until destroy.
+    void* mv = nullptr;      // (M, K) T
+    void* sd = nullptr;      // (M) T
+    void* buf_a = nullptr;   // (N) T   tree-order field / values
+    void* buf_b = nullptr;   // (N) T   tree-order xi
+    void* buf_c = nullptr;   // (N) T   tree-order cotangent
+    void* buf_d = nullptr;   // (N) T   tree-order xbar
+    double* dacc = nullptr;  // nb histogram + 8 scalars (double accumulators)
+
+    // Dense n0 block.
+    void* Ld = nullptr;       // (n0, n0) column-major: Cholesky factor (lower)
+    void* Wd = nullptr;       // (n0, n0) work
+    void* Wd2 = nullptr;      // (n0, n0) work
+    void* dwork = nullptr;    // cuSOLVER workspace
+    int64_t dwork_bytes = 0;
+    int* dinfo = nullptr;     // cuSOLVER info
+    cusolverDnHandle_t solver = nullptr;
+    cublasHandle_t blas = nullptr;
+    double dense_jitter = 0.0;  // eps of the ladder that succeeded on the last factorisation
+
+    const gpb2::Ops<float>* ops32 = nullptr;
+    const gpb2::Ops<double>* ops64 = nullptr;
+};
+
+namespace gpb2 {
+
+// RAII: make the problem's device current for the duration of a call, restore afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <typename T>
+TableView<T> table_view(const gpb2_problem* p) {
+    TableView<T> tv;
+    tv.seg = static_cast<const T*>(p->seg);
+    tv.start = p->start;
+    tv.base = (typename Num<T>::U)p->key_base;
+    tv.nb = (int)p->nb;
+    tv.nkeys = p->nkeys;
+    tv.shift = p->shift;
+    tv.b0 = (T)p->b0;
+    tv.b1 = (T)p->b1;
+    tv.bN = (T)p->bN;
+    tv.v0 = (T)p->v0;
+    tv.vN = (T)p->vN;
+    tv.pivc = (T)p->pivc;
+    return tv;
+}
+
+template <typename T>
+PointArgs<T> point_args(const gpb2_problem* p) {
+    PointArgs<T> a;
+    a.tab = table_view<T>(p);
+    a.coords = p->coords;
+    a.nbrs = p->nbrs;
+    a.n0 = p->n0;
+    a.scale = (T)p->scale;
+    return a;
+}
+
+template <typename T>
+const Ops<T>* ops_of(const gpb2_problem* p);
+template <>
+inline const Ops<float>* ops_of<float>(const gpb2_problem* p) { return p->ops32; }
+template <>
+inline const Ops<double>* ops_of<double>(const gpb2_problem* p) { return p->ops64; }
+
+int ensure_alloc(void** ptr, size_t bytes);
+int ensure_scratch(gpb2_problem* p, bool need_mv);
+int ensure_dense(gpb2_problem* p);
+
+// Dense first layer (gpb2_dense.cu).  All on `s`; factor() synchronises once to read the
+// Cholesky status (the jitter ladder of src/dense.jl:46-67 branches on it).
+template <typename T>
+struct Dense {
+    static int factor(gpb2_problem* p, cudaStream_t s);
+    static int apply_L(gpb2_problem* p, const T* x, T* y, cudaStream_t s);   // y = L x
+    static int apply_Lt(gpb2_problem* p, const T* x, T* y, cudaStream_t s);  // y = L^T x
+    static int solve_L(gpb2_problem* p, const T* b, T* y, cudaStream_t s);   // y = L \ b
+    static int logdet(gpb2_problem* p, double* acc, cudaStream_t s);         // acc += sum log diag
+    static int grad_vals(gpb2_problem* p, const T* vb, const T* xi, double* hist, cudaStream_t s);
+    static int logdet_grad(gpb2_problem* p, double* hist, cudaStream_t s);
+    static int inv_loss_grad(gpb2_problem* p, const T* y, double* hist, double* loss,
+                             cudaStream_t s);
+};
+
+}  // namespace gpb2

@@ -1,0 +1,176 @@
+"""GraphGPProblem: the container the whole API dispatches on (src/types.jl:22-60).
+
+Memory layout is the reference's: ``coords`` holds a point's D lattice coordinates contiguously
+(Julia's (D, N) column-major UInt32 == numpy (N, D) row-major), ``neighbors`` holds a refined
+point's K neighbour indices contiguously (Julia's (K, M) column-major == numpy (M, K)).  The
+Python mirror uses 0-based neighbour and permutation indices (the convention of the Python
+``graphgp`` package and of the reference's .npz fixtures); the Julia binding passes its 1-based
+arrays to the same C entry points with ``neighbor_base = 1``.
+
+``offsets`` are the batch ends with ``offsets[0] == n0`` and ``offsets[-1] == N``; batch b covers
+tree positions ``[offsets[b-1], offsets[b])``.  ``indices[tree_pos] = original_pos`` (or None for
+the identity), as ``GraphGPProblem.indices``.
+
+The device-side state lives in a library handle (``gpb2_problem``) created on first use: it holds
+int32 neighbours, padded coordinates and the interpolation table, and validates the graph
+(check_graph's invariants) on the device.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import weakref
+
+import numpy as np
+import torch
+
+from . import _lib
+
+_DT = {np.dtype(np.float32): _lib.GPB2_F32, np.dtype(np.float64): _lib.GPB2_F64}
+_TORCH_DT = {np.dtype(np.float32): torch.float32, np.dtype(np.float64): torch.float64}
+
+
+def _np_dtype(x) -> np.dtype:
+    if isinstance(x, torch.Tensor):
+        return np.dtype(str(x.dtype).replace("torch.", ""))
+    return np.asarray(x).dtype
+
+
+def _host(x, dtype=None) -> np.ndarray:
+    if isinstance(x, torch.Tensor):
+        x = x.detach().cpu().numpy()
+    return np.ascontiguousarray(x, dtype=dtype)
+
+
+def _destroy(handle_value: int) -> None:
+    try:
+        _lib.lib().gpb2_problem_destroy(C.c_void_p(handle_value))
+    except Exception:  # interpreter shutdown: the library may already be gone
+        pass
+
+
+class GraphGPProblem:
+    """GraphGPProblem(coords, neighbors, offsets, n0, scale, bins, vals, indices=None)."""
+
+    def __init__(self, coords, neighbors, offsets, n0, scale, bins, vals, indices=None, *,
+                 dtype=None, device=None, neighbor_base: int = 0):
+        dt = np.dtype(dtype) if dtype is not None else _np_dtype(vals)
+        if dt not in _DT:
+            raise TypeError(f"vals must be float32 or float64 (got {dt})")
+        self.dtype = dt
+        self.coords = coords
+        self.neighbors = neighbors
+        self.offsets = _host(offsets, np.int64)
+        self.n0 = int(n0)
+        self.scale = float(scale)
+        self.bins = bins
+        self.vals = vals
+        self.indices = None if indices is None else _host(indices, np.int64)
+        self.neighbor_base = int(neighbor_base)
+        if device is None:
+            device = coords.device if isinstance(coords, torch.Tensor) and coords.is_cuda \
+                else torch.device("cuda", torch.cuda.current_device() if torch.cuda.is_available() else 0)
+        self.device = torch.device(device)
+        self.host_arrays = not isinstance(coords, torch.Tensor)
+        shape_c = tuple(coords.shape)
+        shape_n = tuple(neighbors.shape)
+        if len(shape_c) != 2 or len(shape_n) != 2:
+            raise ValueError("coords must be (N, D) and neighbors (M, K)")
+        self._N, self._D = shape_c
+        self._M, self._K = shape_n
+        if self._N - self._M != self.n0:
+            raise ValueError(f"n0 ({self.n0}) must equal npoints - nrefined ({self._N - self._M})")
+        self._handle = None
+        self._finalizer = None
+
+    # -- sizes (src/types.jl:372-376) ----------------------------------------------------------
+    def npoints(self) -> int:
+        return self._N
+
+    def ndims_space(self) -> int:
+        return self._D
+
+    def nneighbors(self) -> int:
+        return self._K
+
+    def nrefined(self) -> int:
+        return self._M
+
+    def nbins(self) -> int:
+        return int(len(self.bins))
+
+    @property
+    def torch_dtype(self):
+        return _TORCH_DT[self.dtype]
+
+    def n_batches(self) -> int:
+        return len(self.offsets) - 1
+
+    # -- device handle -------------------------------------------------------------------------
+    def _dev(self, x, dtype):
+        if isinstance(x, torch.Tensor):
+            return x.to(device=self.device, dtype=dtype).contiguous()
+        return torch.from_numpy(np.ascontiguousarray(x)).to(device=self.device, dtype=dtype)
+
+    @property
+    def handle(self) -> C.c_void_p:
+        if self._handle is None:
+            self._handle = self._create()
+            self._finalizer = weakref.finalize(self, _destroy, self._handle.value)
+        return self._handle
+
+    def _create(self) -> C.c_void_p:
+        L = _lib.lib()
+        with torch.cuda.device(self.device):
+            c = self.coords
+            if isinstance(c, torch.Tensor):
+                c = c.view(torch.int32) if c.dtype == torch.uint32 else c
+                coords = c.to(device=self.device, dtype=torch.int32).contiguous()
+            else:
+                coords = torch.from_numpy(
+                    np.ascontiguousarray(c, dtype=np.uint32).view(np.int32)).to(self.device)
+            nb = self.neighbors
+            nb_dt = torch.int32 if _np_dtype(nb) in (np.dtype(np.int32), np.dtype(np.uint32)) \
+                else torch.int64
+            nbd = self._dev(nb, nb_dt)
+            bins = self._dev(self.bins, self.torch_dtype)
+            vals = self._dev(self.vals, self.torch_dtype)
+            offs = np.ascontiguousarray(self.offsets, dtype=np.int64)
+            idx = None if self.indices is None else np.ascontiguousarray(self.indices, np.int64)
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            h = C.c_void_p()
+            st = L.gpb2_problem_create(
+                C.byref(h), _DT[self.dtype], self.device.index or 0,
+                C.c_void_p(coords.data_ptr()), self._D, self._N,
+                C.c_void_p(nbd.data_ptr()), 4 if nb_dt == torch.int32 else 8, self.neighbor_base,
+                self._K, offs.ctypes.data_as(_lib.PI64), len(offs), self.n0, self.scale,
+                C.c_void_p(bins.data_ptr()), C.c_void_p(vals.data_ptr()), self.nbins(),
+                None if idx is None else idx.ctypes.data_as(_lib.PI64), 0,
+                C.c_void_p(stream))
+            _lib.check(st, "GraphGPProblem upload")
+        return h
+
+    def release(self) -> None:
+        """Free the device handle now (it is otherwise freed with the object)."""
+        if self._finalizer is not None:
+            self._finalizer()
+        self._handle = None
+        self._finalizer = None
+
+    def __repr__(self) -> str:
+        return (f"GraphGPProblem(N={self._N}, D={self._D}, K={self._K}, n0={self.n0}, "
+                f"batches={self.n_batches()}, nbins={self.nbins()}, dtype={self.dtype.name}, "
+                f"indices={'yes' if self.indices is not None else 'no'})")
+
+
+def to_backend(prob: GraphGPProblem, device) -> GraphGPProblem:
+    """A copy of ``prob`` bound to ``device`` (src/types.jl:97-106)."""
+    return GraphGPProblem(prob.coords, prob.neighbors, prob.offsets, prob.n0, prob.scale,
+                          prob.bins, prob.vals, prob.indices, dtype=prob.dtype, device=device,
+                          neighbor_base=prob.neighbor_base)
+
+
+def set_vals(prob: GraphGPProblem, vals) -> GraphGPProblem:
+    """``_set_vals`` (src/chainrules.jl:18-21): the same problem with ``vals`` replaced."""
+    return GraphGPProblem(prob.coords, prob.neighbors, prob.offsets, prob.n0, prob.scale,
+                          prob.bins, vals, prob.indices, dtype=prob.dtype, device=prob.device,
+                          neighbor_base=prob.neighbor_base)

@@ -1,0 +1,184 @@
+/*
+ * graphgp_b200.h -- C ABI of libgraphgp_b200.so, the B200 (sm_100a) implementation of
+ * GraphGP.jl's per-point Vecchia refine path and its analytic adjoints.
+ *
+ * Drop-in boundary.  The reference reaches CUDA through KernelAbstractions launches selected by
+ * `_is_cpu(backend)` (src/cpu_native.jl:13) and through the opt-in ccall bridge
+ * ext/GraphGPCUDAExt.jl:39-64 over csrc/graphgp_capi.cu:70-119.  Every entry point below names
+ * the reference function (path:line inside the GraphGP.jl tree) whose device work it replaces.
+ *
+ * Conventions
+ *  - Every function returns a gpb2_status; nothing aborts or exits.  The message of the last
+ *    failure on the calling thread is available from gpb2_last_error().
+ *  - Arrays use the reference's memory layout: coords is Julia's (D, N) column-major uint32
+ *    (a point's D coordinates contiguous); neighbors is Julia's (K, M) column-major (a refined
+ *    point's K neighbour indices contiguous), int64 or int32, 1-based (Julia) or 0-based.
+ *    offsets is the reference's host Vector{Int}: offsets[0] == n0, offsets[last] == N, depth
+ *    batch b covers tree positions [offsets[b-1], offsets[b]).  indices (host, optional) is
+ *    the tree->original permutation: indices[tree_pos] = original_pos.
+ *  - Floating-point buffers are float (dtype GPB2_F32) or double (GPB2_F64), matching the
+ *    problem's dtype.  Buffers named *_dev are device pointers on the problem's device; the
+ *    *_host outputs are host scalars (those calls synchronise the stream).
+ *  - Calls are ordered on the caller's `stream` (a cudaStream_t; NULL = legacy default
+ *    stream).  One problem handle must not be used by two threads at once.
+ *  - In/out device buffers are caller-owned; the library owns only the problem handle's
+ *    internal copies and scratch, released by gpb2_problem_destroy.
+ */
+#ifndef GRAPHGP_B200_H
+#define GRAPHGP_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GPB2_VERSION 1
+
+typedef enum gpb2_status {
+    GPB2_OK = 0,
+    GPB2_ERR_INVALID_ARG = 1,
+    GPB2_ERR_UNSUPPORTED_K = 2,     /* same code as csrc/graphgp_capi.cu:53-68 ("unsupported k") */
+    GPB2_ERR_UNSUPPORTED_D = 3,     /* same code as csrc/graphgp_capi.cu:53-68 ("unsupported D") */
+    GPB2_ERR_OOM = 4,
+    GPB2_ERR_CUDA = 5,
+    GPB2_ERR_NCCL = 6,
+    GPB2_ERR_TIMEOUT = 7,
+    GPB2_ERR_GRAPH = 8,             /* check_graph invariant violated (src/graph_build.jl:20-57) */
+    GPB2_ERR_NOT_PD = 9,            /* dense block not PD at 1e-2 jitter (src/dense.jl:65-66) */
+    GPB2_ERR_UNSUPPORTED_TABLE = 10,/* bins not strictly increasing / too many bins */
+    GPB2_ERR_NO_DEVICE = 11
+} gpb2_status;
+
+typedef enum gpb2_dtype { GPB2_F32 = 0, GPB2_F64 = 1 } gpb2_dtype;
+
+typedef struct gpb2_problem gpb2_problem;
+typedef struct gpb2_graph gpb2_graph;
+
+/* Library version (GPB2_VERSION) and the last error message on this thread ("" if none). */
+int gpb2_version(void);
+const char* gpb2_last_error(void);
+
+/* ------------------------------------------------------------------------------------------
+ * Problem handle.  Replaces the per-call `_prep` conversion of ext/GraphGPCUDAExt.jl:27-35
+ * (float positions, 0-based Int64 neighbours) with a one-time upload: the library keeps a
+ * 0-based int32 copy of the neighbours, a padded copy of the coords, the level table and the
+ * interpolation table, and validates the graph invariants of check_graph
+ * (src/graph_build.jl:20-57) on the device.  Mirrors the GraphGPProblem constructor
+ * (src/types.jl:22-60) and `to_backend` (src/types.jl:97-106).
+ * ---------------------------------------------------------------------------------------- */
+int gpb2_problem_create(gpb2_problem** out, int dtype, int device,
+                        const uint32_t* coords_dev, int64_t d, int64_t n,
+                        const void* neighbors_dev, int neighbor_bytes, int neighbor_base,
+                        int64_t k, const int64_t* offsets_host, int64_t n_offsets, int64_t n0,
+                        double scale, const void* bins_dev, const void* vals_dev, int64_t nbins,
+                        const int64_t* indices_host, int indices_base, void* stream);
+
+/* Replace the covariance values (`_set_vals`, src/chainrules.jl:18-21). */
+int gpb2_problem_set_vals(gpb2_problem* prob, const void* vals_dev, void* stream);
+
+/* Sizes: N, M = N - n0, K, D, number of depth batches (n_offsets - 1). */
+int gpb2_problem_info(const gpb2_problem* prob, int64_t* n, int64_t* m, int64_t* k, int64_t* d,
+                      int64_t* n_batches);
+
+int gpb2_problem_destroy(gpb2_problem* prob);
+
+/* Launch profiler, process-wide (no reference counterpart; the reference times with
+ * CUDA.@elapsed around whole calls, bench/compare/run_gradmem.jl:19-36).  Every kernel the
+ * library launches is counted (gpb2_launch_count); with profiling enabled each launch is also
+ * bracketed by a CUDA event pair on its own stream.  gpb2_profile_report synchronises those
+ * events and writes one line per kernel kind, "name launches total_ms\n", into buf. */
+int gpb2_profile_enable(int on);
+int gpb2_profile_reset(void);
+int gpb2_profile_report(char* buf, int64_t cap);
+int64_t gpb2_launch_count(void);
+
+/* Forward-sweep strategy, process-wide: 0 = one flat factor kernel over all refined points, then a
+ * light kernel per depth batch (default); 1 = the reference's fused per-batch kernel
+ * (refine_apply_fused_kernel!, src/kernels.jl:101-119).  Both give bit-identical values. */
+int gpb2_set_forward_mode(int mode);
+
+/* ------------------------------------------------------------------------------------------
+ * Refine layer, tree order.
+ * ---------------------------------------------------------------------------------------- */
+
+/* refine!: values_dev[0:n0] preset, values_dev[n0:N] written; xi_ref_dev has M entries.
+ * Replaces the per-batch refine_apply_fused_kernel! launches of src/api.jl:364-392. */
+int gpb2_refine(gpb2_problem* prob, void* values_dev, const void* xi_ref_dev, void* stream);
+
+/* refine_inv!: xi_ref_dev[m] = (values[n0+m] - mean) / std.  Replaces src/api.jl:317-343
+ * (refine_inv_kernel!, src/kernels.jl:37-56) and gpcuda_refine_inv_f32 (csrc/graphgp_capi.cu:90-99). */
+int gpb2_refine_inv(gpb2_problem* prob, const void* values_dev, void* xi_ref_dev, void* stream);
+
+/* refine_logdet_terms: terms_dev[m] = log(std_m).  Replaces src/api.jl:281-308. */
+int gpb2_refine_logdet_terms(gpb2_problem* prob, void* terms_dev, void* stream);
+
+/* refine_logdet: sum of the terms, accumulated in double.  Replaces src/api.jl:275-278 and
+ * gpcuda_refine_logdet_f32 (csrc/graphgp_capi.cu:76-88).  Synchronous. */
+int gpb2_refine_logdet(gpb2_problem* prob, double* logdet_host, void* stream);
+
+/* refine_logdet_grad_vals: d(refine_logdet)/d(vals) into dvals_dev (nbins, problem dtype);
+ * logdet_host (optional) receives the fused logdet sum (refine_logdet_and_grad_hist_kernel!).
+ * Replaces src/grad.jl:96-119 and the fused src/grad.jl:680-715 device branch. */
+int gpb2_refine_logdet_grad_vals(gpb2_problem* prob, void* dvals_dev, double* logdet_host,
+                                 void* stream);
+
+/* refine_inv_loss_grad_vals: loss = 0.5*||refine_inv(values)||^2 and its vals-gradient.
+ * Replaces src/grad.jl:630-671 (refine_inv_loss_grad_hist_kernel!, src/kernels_adjoint.jl:155-221). */
+int gpb2_refine_inv_loss_grad_vals(gpb2_problem* prob, const void* values_dev, void* dvals_dev,
+                                   double* loss_host, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Orchestrated operations, ORIGINAL point order in and out (src/orchestrate.jl): the
+ * tree<->original permutation, the dense n0 block (on the device) and the refine layer.
+ * ---------------------------------------------------------------------------------------- */
+
+/* generate(prob, xi) -> out (src/orchestrate.jl:19-42). */
+int gpb2_generate(gpb2_problem* prob, const void* xi_dev, void* out_dev, void* stream);
+
+/* generate_inv(prob, values) -> xi (src/orchestrate.jl:53-81). */
+int gpb2_generate_inv(gpb2_problem* prob, const void* values_dev, void* xi_dev, void* stream);
+
+/* generate_logdet(prob) (src/orchestrate.jl:89-97).  Synchronous. */
+int gpb2_generate_logdet(gpb2_problem* prob, double* logdet_host, void* stream);
+
+/* generate_grad_xi(prob, vbar) -> xbar (src/grad.jl:392-506). */
+int gpb2_generate_grad_xi(gpb2_problem* prob, const void* vbar_dev, void* xbar_dev, void* stream);
+
+/* generate_grad_vals(prob, xi, vbar) -> dvals (nbins) (src/grad_generate_vals.jl:111-282). */
+int gpb2_generate_grad_vals(gpb2_problem* prob, const void* xi_dev, const void* vbar_dev,
+                            void* dvals_dev, void* stream);
+
+/* generate_logdet_grad_vals (src/grad.jl:149-154) and the fused
+ * generate_logdet_and_grad_vals (src/grad.jl:680-715; logdet_host may be NULL). */
+int gpb2_generate_logdet_grad_vals(gpb2_problem* prob, void* dvals_dev, double* logdet_host,
+                                   void* stream);
+
+/* generate_inv_loss_grad_vals (src/grad.jl:514-526): loss and vals-gradient of
+ * 0.5*||generate_inv(data)||^2; data in original order. */
+int gpb2_generate_inv_loss_grad_vals(gpb2_problem* prob, const void* data_dev, void* dvals_dev,
+                                     double* loss_host, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Graph build (host, the input producer of the path).  Restates build_graph
+ * (src/graph_build.jl:256-288: special-order tree, preceding k-NN, depths, stable order by
+ * depth, 21-bit quantisation, offsets); its output is byte-identical to the reference's.
+ * Replaces gpcuda_build_graph_f32 (csrc/graphgp_capi.cu:100-117) as the graph source.
+ * points: N x D float64, dim-major (Julia's (N, D) column-major) when points_dim_major != 0,
+ * else point-major.  Export: coords (N*D uint32, point-major), nbrs (M*K int64, 0-based, -1 =
+ * unset), indices (N int64, 0-based tree->original), offsets (gpb2_graph_n_offsets entries).
+ * ---------------------------------------------------------------------------------------- */
+int gpb2_build_graph(const double* points, int64_t n, int64_t d, int64_t points_dim_major,
+                     int64_t n0, int64_t k, int64_t lattice_bits, int64_t nthreads,
+                     gpb2_graph** out);
+int64_t gpb2_graph_n_offsets(const gpb2_graph* g);
+int64_t gpb2_graph_n0(const gpb2_graph* g);
+int gpb2_graph_export(const gpb2_graph* g, uint32_t* coords, int64_t* nbrs, int64_t* indices,
+                      int64_t* offsets, double* scale);
+void gpb2_graph_free(gpb2_graph* g);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GRAPHGP_B200_H */

@@ -1,0 +1,365 @@
+"""CPU oracle for the GraphGP.jl refine path -- TEST INFRASTRUCTURE ONLY.
+
+Thin numpy/ctypes layer over ``libgp_oracle.so`` (the C restatement in ``gp_oracle.c``).  Only
+``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline legs may import this
+module; the product path (``graphgp_b200``) never does.
+
+Problems are duck-typed: any object with the attributes
+``coords`` (N, D) uint32, ``nbrs`` (M, K) int64 0-based, ``offsets`` (int64, offsets[0] == n0),
+``n0``, ``scale``, ``bins``, ``vals``, ``indices`` (0-based tree->original or None) and ``dtype``
+(numpy float32 / float64).  This is the memory layout of the reference's ``GraphGPProblem``
+(``src/types.jl:22-60``): Julia's column-major (D, N) coords and (K, M) neighbours.
+
+Orchestration follows ``src/orchestrate.jl:19-97`` (gather xi original->tree, dense block,
+refine, scatter tree->original) and the gradient drivers of ``src/grad.jl`` and
+``src/grad_generate_vals.jl``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from types import SimpleNamespace
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libgp_oracle.so")
+_lib = None
+
+P = C.c_void_p
+I64 = C.c_int64
+I32 = C.c_int
+
+
+def build() -> str:
+    """Compile libgp_oracle.so with the committed Makefile (gcc, -ffp-contract=off)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH) or (
+            os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "gp_oracle.c"))
+        ):
+            build()
+        _lib = C.CDLL(_LIB_PATH)
+    return _lib
+
+
+def _sfx(dtype) -> str:
+    return "_f32" if np.dtype(dtype) == np.float32 else "_f64"
+
+
+def _ct(dtype):
+    return C.c_float if np.dtype(dtype) == np.float32 else C.c_double
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(P)
+
+
+def _fn(name, dtype):
+    return getattr(lib(), name + _sfx(dtype))
+
+
+def make_problem(coords, nbrs, offsets, n0, scale, bins, vals, indices=None, dtype=np.float64):
+    """Bundle arrays in the oracle's layout (see module docstring)."""
+    dt = np.dtype(dtype)
+    return SimpleNamespace(
+        coords=np.ascontiguousarray(coords, dtype=np.uint32),
+        nbrs=np.ascontiguousarray(nbrs, dtype=np.int64),
+        offsets=np.ascontiguousarray(offsets, dtype=np.int64),
+        n0=int(n0),
+        scale=dt.type(scale),
+        bins=np.ascontiguousarray(bins, dtype=dt),
+        vals=np.ascontiguousarray(vals, dtype=dt),
+        indices=None if indices is None else np.ascontiguousarray(indices, dtype=np.int64),
+        dtype=dt,
+    )
+
+
+def _dims(p):
+    N, D = p.coords.shape
+    M, K = p.nbrs.shape
+    return N, D, M, K
+
+
+def _common(p):
+    N, D, M, K = _dims(p)
+    return (I64(p.n0), I32(K), I32(D), _ct(p.dtype)(p.scale), _p(p.bins), _p(p.vals),
+            I64(len(p.bins)))
+
+
+# ---------------------------------------------------------------------------------------------
+# L0 scalar numerics
+# ---------------------------------------------------------------------------------------------
+
+def cov_lookup(r, bins, vals):
+    """src/interp.jl:10-34 on an array of radii."""
+    dt = np.asarray(bins).dtype
+    r = np.ascontiguousarray(np.atleast_1d(r), dtype=dt)
+    bins = np.ascontiguousarray(bins, dtype=dt)
+    vals = np.ascontiguousarray(vals, dtype=dt)
+    out = np.empty_like(r)
+    _fn("gpo_cov_lookup", dt)(_p(r), I64(r.size), _p(bins), _p(vals), I64(bins.size), _p(out))
+    return out
+
+
+def cov_lookup_weights(r, bins):
+    """src/interp.jl:62-83: (lo 0-based, w_lo, w_hi)."""
+    dt = np.asarray(bins).dtype
+    r = np.ascontiguousarray(np.atleast_1d(r), dtype=dt)
+    bins = np.ascontiguousarray(bins, dtype=dt)
+    lo = np.empty(r.size, np.int64)
+    wlo = np.empty_like(r)
+    whi = np.empty_like(r)
+    _fn("gpo_cov_lookup_weights", dt)(_p(r), I64(r.size), _p(bins), I64(bins.size), _p(lo),
+                                      _p(wlo), _p(whi))
+    return lo, wlo, whi
+
+
+def chol_solve(A, K):
+    """chol_lower! + mean_vec_solve! (src/linalg.jl:121-186) on one (K+1)x(K+1) matrix."""
+    A = np.ascontiguousarray(A).copy()
+    mv = np.empty(K, A.dtype)
+    _fn("gpo_chol_solve", A.dtype)(_p(A), I32(K + 1), _p(mv))
+    return np.tril(A), mv
+
+
+# ---------------------------------------------------------------------------------------------
+# Refine layer (tree order)
+# ---------------------------------------------------------------------------------------------
+
+def refine(p, initial_values, xi_ref, nthreads=0):
+    """refine(prob, initial_values, xi) (src/api.jl:427-433)."""
+    N, D, M, K = _dims(p)
+    values = np.zeros(N, p.dtype)
+    values[: p.n0] = initial_values
+    xi_ref = np.ascontiguousarray(xi_ref, dtype=p.dtype)
+    rc = _fn("gpo_refine", p.dtype)(_p(values), _p(xi_ref), _p(p.coords), _p(p.nbrs),
+                                    _p(p.offsets), I64(len(p.offsets)), *_common(p), I32(nthreads))
+    assert rc == 0
+    return values
+
+
+def meanvec_std(p, nthreads=0):
+    N, D, M, K = _dims(p)
+    mv = np.empty((M, K), p.dtype)
+    sd = np.empty(M, p.dtype)
+    rc = _fn("gpo_meanvec_std", p.dtype)(_p(mv), _p(sd), _p(p.coords), _p(p.nbrs), I64(M),
+                                         *_common(p), I32(nthreads))
+    assert rc == 0
+    return mv, sd
+
+
+def refine_inv(p, values, nthreads=0):
+    """refine_inv (src/api.jl:317-354)."""
+    N, D, M, K = _dims(p)
+    values = np.ascontiguousarray(values, dtype=p.dtype)
+    xi = np.empty(M, p.dtype)
+    rc = _fn("gpo_refine_inv", p.dtype)(_p(xi), _p(values), _p(p.coords), _p(p.nbrs), I64(M),
+                                        *_common(p), I32(nthreads))
+    assert rc == 0
+    return xi
+
+
+def refine_logdet_terms(p, nthreads=0):
+    N, D, M, K = _dims(p)
+    terms = np.empty(M, p.dtype)
+    rc = _fn("gpo_refine_logdet_terms", p.dtype)(_p(terms), _p(p.coords), _p(p.nbrs), I64(M),
+                                                 *_common(p), I32(nthreads))
+    assert rc == 0
+    return terms
+
+
+def refine_logdet(p, nthreads=0):
+    """refine_logdet (src/api.jl:275-278); the sum is taken in float64."""
+    return float(np.sum(refine_logdet_terms(p, nthreads).astype(np.float64)))
+
+
+def refine_logdet_grad_vals(p, nthreads=0, acc_t=False):
+    """refine_logdet_grad_vals (src/grad.jl:96-119) + the fused logdet sum.
+
+    Returns (logdet_refine, dvals float64).  acc_t=True accumulates in T like the reference."""
+    N, D, M, K = _dims(p)
+    dv = np.zeros(len(p.bins), np.float64)
+    ld = C.c_double(0.0)
+    rc = _fn("gpo_refine_logdet_grad_vals", p.dtype)(
+        _p(dv), C.byref(ld), _p(p.coords), _p(p.nbrs), I64(M), *_common(p), I32(nthreads),
+        I32(1 if acc_t else 0))
+    assert rc == 0
+    return ld.value, dv
+
+
+def refine_inv_loss_grad_vals(p, values, nthreads=0, acc_t=False):
+    """refine_inv_loss_grad_vals (src/grad.jl:630-671): (loss, dvals float64)."""
+    N, D, M, K = _dims(p)
+    values = np.ascontiguousarray(values, dtype=p.dtype)
+    dv = np.zeros(len(p.bins), np.float64)
+    loss = C.c_double(0.0)
+    rc = _fn("gpo_refine_inv_loss_grad_vals", p.dtype)(
+        _p(dv), C.byref(loss), _p(values), _p(p.coords), _p(p.nbrs), I64(M), *_common(p),
+        I32(nthreads), I32(1 if acc_t else 0))
+    assert rc == 0
+    return loss.value, dv
+
+
+# ---------------------------------------------------------------------------------------------
+# Dense first layer (src/dense.jl)
+# ---------------------------------------------------------------------------------------------
+
+def dense_cov(p, n=None):
+    n = p.n0 if n is None else n
+    N, D, M, K = _dims(p)
+    Km = np.empty((n, n), p.dtype)
+    _fn("gpo_dense_cov", p.dtype)(_p(Km), _p(p.coords), I64(n), I32(D),
+                                  _ct(p.dtype)(p.scale), _p(p.bins), _p(p.vals), I64(len(p.bins)))
+    return Km
+
+
+def dense_chol(p):
+    """_dense_chol_L (src/dense.jl:46-67) -> (L, jitter_used)."""
+    Km = dense_cov(p)
+    n = Km.shape[0]
+    L = np.empty_like(Km)
+    jit = _ct(p.dtype)(0)
+    rc = _fn("gpo_dense_chol", p.dtype)(_p(L), _p(Km), I64(n), C.byref(jit))
+    if rc != 0:
+        raise RuntimeError("dense first-layer covariance is not positive definite even with "
+                           "1e-2 relative jitter")
+    return L, float(jit.value)
+
+
+def _tri(fn, L, x):
+    x = np.ascontiguousarray(x, dtype=L.dtype)
+    out = np.empty_like(x)
+    _fn(fn, L.dtype)(_p(out), _p(L), _p(x), I64(L.shape[0]))
+    return out
+
+
+def generate_dense(L, xi):
+    return _tri("gpo_trmv_lower", L, xi)
+
+
+def generate_dense_inv(L, values):
+    return _tri("gpo_trsv_lower", L, values)
+
+
+def dense_adjoint(L, vb):
+    return _tri("gpo_trmv_lower_t", L, vb)
+
+
+def dense_logdet(L):
+    """sum(log, diag(L)) (src/dense.jl:142-147)."""
+    f = _fn("gpo_dense_logdet", L.dtype)
+    f.restype = C.c_double
+    return float(f(_p(L), I64(L.shape[0])))
+
+
+def chol_pullback_dense(L, Lbar):
+    """chol_pullback_dyn! (src/grad_generate_vals.jl:18-39); returns Abar (lower)."""
+    L = np.ascontiguousarray(L)
+    Lbar = np.ascontiguousarray(Lbar, dtype=L.dtype).copy()
+    Abar = np.zeros_like(L)
+    _fn("gpo_chol_pullback_dense", L.dtype)(_p(Abar), _p(Lbar), _p(L), I64(L.shape[0]))
+    return Abar
+
+
+# ---------------------------------------------------------------------------------------------
+# Orchestration (original order in / out)
+# ---------------------------------------------------------------------------------------------
+
+def _gather(p, x):
+    x = np.asarray(x, dtype=p.dtype)
+    return x if p.indices is None else x[p.indices]
+
+
+def _scatter(p, x):
+    if p.indices is None:
+        return x
+    out = np.empty_like(x)
+    out[p.indices] = x
+    return out
+
+
+def generate(p, xi, nthreads=0):
+    """generate (src/orchestrate.jl:19-42)."""
+    xo = _gather(p, xi)
+    L, _ = dense_chol(p)
+    v0 = generate_dense(L, xo[: p.n0])
+    values = refine(p, v0, xo[p.n0:], nthreads)
+    return _scatter(p, values)
+
+
+def generate_inv(p, values, nthreads=0):
+    """generate_inv (src/orchestrate.jl:53-81)."""
+    vo = _gather(p, values)
+    xi_ref = refine_inv(p, vo, nthreads)
+    L, _ = dense_chol(p)
+    xi_d = generate_dense_inv(L, vo[: p.n0])
+    return _scatter(p, np.concatenate([xi_d, xi_ref]).astype(p.dtype))
+
+
+def generate_logdet(p, nthreads=0):
+    """generate_logdet (src/orchestrate.jl:89-97)."""
+    L, _ = dense_chol(p)
+    return dense_logdet(L) + refine_logdet(p, nthreads)
+
+
+def generate_grad_xi(p, vbar, nthreads=0):
+    """generate_grad_xi, CPU branch (src/grad.jl:392-465)."""
+    N, D, M, K = _dims(p)
+    mv, sd = meanvec_std(p, nthreads)
+    vb = np.array(_gather(p, vbar), dtype=p.dtype)
+    xg = np.zeros(N, p.dtype)
+    _fn("gpo_reverse_sweep", p.dtype)(_p(xg), _p(vb), _p(mv), _p(sd), _p(p.nbrs), _p(p.offsets),
+                                      I64(len(p.offsets)), I64(p.n0), I32(K))
+    L, _ = dense_chol(p)
+    xg[: p.n0] = dense_adjoint(L, vb[: p.n0])
+    return _scatter(p, xg)
+
+
+def generate_grad_vals(p, xi, vbar, nthreads=0, acc_t=False):
+    """generate_grad_vals (src/grad_generate_vals.jl:111-213) -> float64 d_vals.
+
+    The forward field is recomputed with refine (the operation order of the device branch,
+    src/grad_generate_vals.jl:227-234)."""
+    N, D, M, K = _dims(p)
+    xih = _gather(p, xi).copy()
+    L, _ = dense_chol(p)
+    v0 = generate_dense(L, xih[: p.n0])
+    v = refine(p, v0, xih[p.n0:], nthreads)
+    vb = np.array(_gather(p, vbar), dtype=p.dtype)
+    mv, sd = meanvec_std(p, nthreads)
+    dv = np.zeros(len(p.bins), np.float64)
+    rc = _fn("gpo_generate_grad_vals_refine", p.dtype)(
+        _p(dv), _p(vb), _p(v), _p(xih), _p(mv), _p(p.coords), _p(p.nbrs), _p(p.offsets),
+        I64(len(p.offsets)), I64(p.n0), I32(K), I32(D), _ct(p.dtype)(p.scale), _p(p.bins),
+        _p(p.vals), I64(len(p.bins)), I32(1 if acc_t else 0))
+    assert rc == 0
+    vbd = np.ascontiguousarray(vb[: p.n0])
+    xid = np.ascontiguousarray(xih[: p.n0])
+    _fn("gpo_dense_grad_vals", p.dtype)(_p(dv), _p(L), _p(vbd), _p(xid), _p(p.coords),
+                                        I64(p.n0), I32(D), _ct(p.dtype)(p.scale), _p(p.bins),
+                                        I64(len(p.bins)), I32(1 if acc_t else 0))
+    return dv
+
+
+def dense_logdet_grad_vals(p, acc_t=False):
+    """_dense_logdet_grad_vals (src/dense.jl:153-183) -> float64."""
+    N, D, M, K = _dims(p)
+    L, _ = dense_chol(p)
+    dv = np.zeros(len(p.bins), np.float64)
+    _fn("gpo_dense_logdet_grad_vals", p.dtype)(_p(dv), _p(L), _p(p.coords), I64(p.n0), I32(D),
+                                               _ct(p.dtype)(p.scale), _p(p.bins),
+                                               I64(len(p.bins)), I32(1 if acc_t else 0))
+    return dv
+
+
+def generate_logdet_grad_vals(p, nthreads=0, acc_t=False):
+    """generate_logdet_grad_vals (src/grad.jl:149-154)."""
+    _, dv = refine_logdet_grad_vals(p, nthreads, acc_t)
+    return dv + dense_logdet_grad_vals(p, acc_t)

@@ -1,0 +1,302 @@
+"""Parity of the CUDA path (libgraphgp_b200.so through its C ABI) with the CPU oracle and with
+the reference's golden vectors.
+
+Bars: the forward refine and refine_inv kernels evaluate each point's arithmetic in the oracle's
+exact order with IEEE round-to-nearest operations and no contraction, so they are compared BIT
+FOR BIT.  Everything that sums in a different order (logdet sums, the dense block through
+cuBLAS/cuSOLVER, atomic reverse sweeps and histograms) is compared by norm-relative error:
+1e-12 in float64 and 1e-5 in float32, the tolerances of the drop-in target.
+"""
+import numpy as np
+import pytest
+import torch
+
+import graphgp_b200 as gp
+from conftest import relerr
+from graphgp_b200 import _lib
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = {np.float64: 1e-12, np.float32: 1e-5}
+FIXTURES = ["small", "medium", "generate_parity"]
+
+
+def _tag(dt):
+    return "64" if dt == np.float64 else "32"
+
+
+def _pair(d, dt, with_indices=False):
+    """(device problem, oracle problem) on the same arrays."""
+    tag = _tag(dt) if f"cov_bins{_tag(dt)}" in d else "64"
+    bins = d["cov_bins" + tag].astype(dt)
+    vals = d["cov_vals" + tag].astype(dt)
+    idx = d["indices"] if with_indices and "indices" in d else None
+    prob = gp.GraphGPProblem(d["coords"], d["neighbors"], d["offsets"], int(d["n0"]),
+                             dt(d["scale"]), bins, vals, idx, dtype=dt)
+    orc = O.make_problem(d["coords"], d["neighbors"], d["offsets"], d["n0"], dt(d["scale"]),
+                         bins, vals, idx, dt)
+    return prob, orc
+
+
+@pytest.fixture(autouse=True)
+def _sweep_mode():
+    _lib.lib().gpb2_set_forward_mode(0)
+    yield
+    _lib.lib().gpb2_set_forward_mode(0)
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+@pytest.mark.parametrize("name", FIXTURES)
+@pytest.mark.parametrize("mode", [0, 1])
+def test_refine_bit_exact(golden, cuda_device, name, dt, mode):
+    d = golden(name)
+    prob, orc = _pair(d, dt)
+    rng = np.random.default_rng(1)
+    iv = rng.standard_normal(prob.n0).astype(dt)
+    xr = rng.standard_normal(prob.nrefined()).astype(dt)
+    _lib.check(_lib.lib().gpb2_set_forward_mode(mode))
+    v = gp.refine(prob, iv, xr)
+    vo = O.refine(orc, iv, xr)
+    assert np.array_equal(v, vo), relerr(v, vo)
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+@pytest.mark.parametrize("name", FIXTURES)
+def test_refine_inv_bit_exact(golden, cuda_device, name, dt):
+    d = golden(name)
+    prob, orc = _pair(d, dt)
+    vals = np.random.default_rng(2).standard_normal(prob.npoints()).astype(dt)
+    assert np.array_equal(gp.refine_inv(prob, vals), O.refine_inv(orc, vals))
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+@pytest.mark.parametrize("name", ["small", "medium"])
+def test_refine_vs_golden(golden, cuda_device, name, dt):
+    # The reference's fixture values (test/test_refine.jl): f64 tight, f32 at its tolerance.
+    d = golden(name)
+    prob, _ = _pair(d, dt)
+    t = _tag(dt)
+    v = gp.refine(prob, d["initial_values" + t], d["xi_ref" + t])
+    xi = gp.refine_inv(prob, d["values" + t])
+    ld = gp.refine_logdet(prob)
+    if dt == np.float64:
+        assert relerr(v, d["refine_values64"]) < 1e-12
+        assert relerr(xi, d["xi64"]) < 1e-12
+        assert abs(ld - d["logdet64"]) < 1e-12 * abs(d["logdet64"])
+    else:
+        assert relerr(v, d["refine_values32"]) < 1e-4
+        assert relerr(xi, d["xi32"]) < 1e-3
+        assert abs(ld - d["logdet32"]) < 2e-3 * abs(d["logdet32"])
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+@pytest.mark.parametrize("name", FIXTURES)
+def test_logdet_terms(golden, cuda_device, name, dt):
+    d = golden(name)
+    prob, orc = _pair(d, dt)
+    terms = gp.refine_logdet_terms(prob)
+    assert relerr(terms, O.refine_logdet_terms(orc)) < (1e-15 if dt == np.float64 else 1e-7)
+    assert abs(gp.refine_logdet(prob) - O.refine_logdet(orc)) <= TOL[dt] * abs(O.refine_logdet(orc))
+
+
+def test_generate_parity_golden(golden, cuda_device):
+    # test/python_parity_generate.jl: generate / generate_inv in ORIGINAL order at 1e-12.
+    d = golden("generate_parity")
+    prob, orc = _pair(d, np.float64, with_indices=True)
+    f = gp.generate(prob, d["xi"])
+    assert relerr(f, d["generate_field"]) < 1e-12
+    assert relerr(gp.generate_inv(prob, d["values"]), d["generate_inv_xi"]) < 1e-12
+    assert relerr(gp.generate_inv(prob, f), d["xi"]) < 1e-10
+    assert relerr(f, O.generate(orc, d["xi"])) < 1e-12
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+@pytest.mark.parametrize("name", FIXTURES)
+def test_generate_ops_vs_oracle(golden, cuda_device, name, dt):
+    d = golden(name)
+    prob, orc = _pair(d, dt, with_indices=True)
+    N = prob.npoints()
+    rng = np.random.default_rng(3)
+    xi = rng.standard_normal(N).astype(dt)
+    vb = rng.standard_normal(N).astype(dt)
+    tol = TOL[dt]
+    f = gp.generate(prob, xi)
+    assert relerr(f, O.generate(orc, xi)) < tol
+    assert relerr(gp.generate_inv(prob, f), O.generate_inv(orc, f)) < tol
+    lo = O.generate_logdet(orc)
+    assert abs(gp.generate_logdet(prob) - lo) <= tol * abs(lo)
+    assert relerr(gp.generate_grad_xi(prob, vb), O.generate_grad_xi(orc, vb)) < tol
+    assert relerr(gp.generate_grad_vals(prob, xi, vb), O.generate_grad_vals(orc, xi, vb)) < tol
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+@pytest.mark.parametrize("name", ["small", "medium"])
+def test_vals_gradients(golden, cuda_device, name, dt):
+    d = golden(name)
+    prob, orc = _pair(d, dt)
+    tol = TOL[dt]
+    ld_o, g_o = O.refine_logdet_grad_vals(orc)
+    g = gp.refine_logdet_grad_vals(prob)
+    assert relerr(g, g_o) < tol
+    ld, gg = gp.generate_logdet_and_grad_vals(prob)
+    assert relerr(gg, O.generate_logdet_grad_vals(orc)) < tol
+    assert abs(ld - O.generate_logdet(orc)) <= tol * abs(ld)
+    t = _tag(dt)
+    loss, gi = gp.refine_inv_loss_grad_vals(prob, d["values" + t])
+    loss_o, gi_o = O.refine_inv_loss_grad_vals(orc, d["values" + t])
+    assert abs(loss - loss_o) <= tol * abs(loss_o)
+    assert relerr(gi, gi_o) < tol
+    if dt == np.float64:  # the reference's JAX gradients (test/test_gradients.jl)
+        nz = d["grad_logdet_vals64"] != 0
+        assert relerr(g[nz], d["grad_logdet_vals64"][nz]) < 1e-12
+        nz = d["grad_inv_loss_vals64"] != 0
+        assert relerr(gi[nz], d["grad_inv_loss_vals64"][nz]) < 1e-12
+        assert abs(loss - d["inv_loss64"]) < 1e-12 * d["inv_loss64"]
+
+
+def test_generate_inv_loss_dense_part(golden, cuda_device):
+    d = golden("small")
+    prob, orc = _pair(d, np.float64)
+    data = d["values64"]
+    loss, g = gp.generate_inv_loss_grad_vals(prob, data)
+    # dense part: 0.5*||L^-1 y||^2 and its gradient through K^-1 y (src/dense.jl:244-266).
+    L, _ = O.dense_chol(orc)
+    z = O.generate_dense_inv(L, data[: prob.n0])
+    loss_ref = 0.5 * float(z @ z) + O.refine_inv_loss_grad_vals(orc, data)[0]
+    assert abs(loss - loss_ref) <= 1e-12 * abs(loss_ref)
+    # FD of the loss w.r.t. a few vals entries (f64 problem).
+    for i in (0, 7, 60):
+        h = 1e-6
+        e = h * (np.arange(prob.nbins()) == i)
+        lp = gp.generate_inv_loss_grad_vals(gp.set_vals(prob, prob.vals + e), data)[0]
+        lm = gp.generate_inv_loss_grad_vals(gp.set_vals(prob, prob.vals - e), data)[0]
+        assert np.isclose(g[i], (lp - lm) / (2 * h), rtol=1e-5, atol=1e-3 * abs(g).max() * 1e-6)
+
+
+def _config_problem(N, D, n0, k, dt, seed, kernel="rbf"):
+    rng = np.random.default_rng(seed)
+    pts = rng.standard_normal((N, D))
+    if kernel == "rbf":
+        bins, vals = gp.rbf_kernel(1.0, 0.3, 1e-4, 10.0, 1000, jitter=1e-5)
+    else:
+        bins, vals = gp.matern_kernel(1, 1.0, 0.05, 1e-5, 2.0, 2000, jitter=1e-5)
+    g = gp.build_graph_arrays(pts, n0, k)
+    prob = gp.GraphGPProblem(g["coords"], g["neighbors"], g["offsets"], g["n0"],
+                             dt(g["scale"]), bins.astype(dt), vals.astype(dt), g["indices"],
+                             dtype=dt)
+    orc = O.make_problem(g["coords"], g["neighbors"], g["offsets"], g["n0"], dt(g["scale"]),
+                         bins.astype(dt), vals.astype(dt), g["indices"], dt)
+    return prob, orc
+
+
+def test_config1_f64(cuda_device):
+    # BASELINE config 1 shape: N=10000, D=2, n0=100, k=10, RBF(1, 0.3, 1e-4..10, 1000 bins,
+    # jitter 1e-5), f64; ops generate / generate_inv / generate_logdet.
+    prob, orc = _config_problem(10_000, 2, 100, 10, np.float64, 99)
+    xi = np.random.default_rng(7).standard_normal(prob.npoints())
+    f = gp.generate(prob, xi)
+    assert relerr(f, O.generate(orc, xi)) < 1e-12
+    assert relerr(gp.generate_inv(prob, f), xi) < 1e-8
+    lo = O.generate_logdet(orc)
+    assert abs(gp.generate_logdet(prob) - lo) < 1e-12 * abs(lo)
+
+
+@pytest.mark.parametrize("K,D,kernel", [(8, 2, "rbf"), (8, 3, "rbf"), (16, 3, "matern"),
+                                        (6, 3, "rbf"), (4, 2, "rbf"), (12, 2, "rbf")])
+def test_supported_shapes_f32(cuda_device, K, D, kernel):
+    prob, orc = _config_problem(6000, D, 200, K, np.float32, 11 + K + D, kernel)
+    rng = np.random.default_rng(4)
+    xi = rng.standard_normal(prob.npoints()).astype(np.float32)
+    vb = rng.standard_normal(prob.npoints()).astype(np.float32)
+    f = gp.generate(prob, xi)
+    assert relerr(f, O.generate(orc, xi)) < 1e-5
+    assert relerr(gp.generate_grad_xi(prob, vb), O.generate_grad_xi(orc, vb)) < 1e-5
+    assert relerr(gp.generate_grad_vals(prob, xi, vb), O.generate_grad_vals(orc, xi, vb)) < 1e-5
+    assert relerr(gp.refine_logdet_grad_vals(prob), O.refine_logdet_grad_vals(orc)[1]) < 1e-5
+
+
+def test_degenerate_duplicates(cuda_device):
+    # test/test_degenerate.jl: 30 exact duplicate points must give finite results everywhere.
+    rng = np.random.default_rng(0xDEAD)
+    n, D, n0, k = 5000, 3, 128, 10
+    p = rng.uniform(size=(n, D))
+    p[200:230] = p[:30]
+    bins = np.linspace(0, 2, 200)
+    vals = np.exp(-bins ** 1.5)
+    vals[0] *= 1.001
+    g = gp.build_graph_arrays(p, n0, k)
+    prob = gp.GraphGPProblem(g["coords"], g["neighbors"], g["offsets"], g["n0"], g["scale"],
+                             bins, vals, g["indices"])
+    orc = O.make_problem(g["coords"], g["neighbors"], g["offsets"], g["n0"], g["scale"], bins,
+                         vals, g["indices"], np.float64)
+    xi = rng.standard_normal(n)
+    f = gp.generate(prob, xi)
+    assert np.all(np.isfinite(f))
+    assert np.all(np.isfinite(gp.generate_inv(prob, f)))
+    assert np.all(np.isfinite(gp.generate_grad_xi(prob, rng.standard_normal(n))))
+    assert np.isfinite(gp.generate_logdet(prob))
+    assert relerr(f, O.generate(orc, xi)) < 1e-12
+
+
+def test_torch_tensors_in_and_out(golden, cuda_device):
+    d = golden("generate_parity")
+    prob, orc = _pair(d, np.float64, with_indices=True)
+    xi = torch.from_numpy(d["xi"]).to(cuda_device)
+    f = gp.generate(prob, xi)
+    assert isinstance(f, torch.Tensor) and f.is_cuda
+    assert relerr(f.cpu().numpy(), d["generate_field"]) < 1e-12
+
+
+def test_autodiff_generate_of_vals(golden, cuda_device):
+    d = golden("generate_parity")
+    prob, orc = _pair(d, np.float64, with_indices=True)
+    vals = torch.from_numpy(prob.vals.copy()).to(cuda_device).requires_grad_(True)
+    xi = torch.from_numpy(d["xi"]).to(cuda_device).requires_grad_(True)
+    w = torch.from_numpy(np.random.default_rng(5).standard_normal(len(d["xi"]))).to(cuda_device)
+    (w * gp.generate_of_vals(prob, vals, xi)).sum().backward()
+    wn = w.cpu().numpy()
+    assert relerr(vals.grad.cpu().numpy(), O.generate_grad_vals(orc, d["xi"], wn)) < 1e-12
+    assert relerr(xi.grad.cpu().numpy(), O.generate_grad_xi(orc, wn)) < 1e-12
+
+
+def test_invalid_graph_rejected(golden, cuda_device):
+    d = golden("small")
+    nb = d["neighbors"].copy()
+    nb[5, 0] = d["n0"] + 5  # a point that is its own neighbour (not in an earlier batch)
+    prob = gp.GraphGPProblem(d["coords"], nb, d["offsets"], int(d["n0"]), d["scale"],
+                             d["cov_bins64"], d["cov_vals64"])
+    with pytest.raises(gp.GraphInvariantError):
+        gp.check_graph(prob)
+
+
+def test_unsupported_k_rejected(cuda_device):
+    rng = np.random.default_rng(1)
+    g = gp.build_graph_arrays(rng.standard_normal((500, 2)), 40, 7)
+    bins, vals = gp.rbf_kernel(1.0, 0.3, 1e-4, 10.0, 100, jitter=1e-3)
+    prob = gp.GraphGPProblem(g["coords"], g["neighbors"], g["offsets"], g["n0"], g["scale"],
+                             bins, vals)
+    with pytest.raises(gp.UnsupportedError):
+        gp.generate_logdet(prob)
+
+
+def test_large_roundtrip_and_linearity_f32(cuda_device):
+    # Size-independent properties at a BASELINE config 2 scale (N = 10^6, D = 2, k = 8, f32):
+    # generate_inv(generate(xi)) ~ xi and the adjoint identity <vb, G xi> = <G^T vb, xi>.
+    rng = np.random.default_rng(1)
+    pts = rng.standard_normal((1_000_000, 2))
+    g = gp.build_graph_arrays(pts, 1000, 8)
+    bins, vals = gp.rbf_kernel(1.0, 0.3, 1e-4, 10.0, 1000, jitter=1e-5)
+    prob = gp.GraphGPProblem(g["coords"], g["neighbors"], g["offsets"], g["n0"],
+                             np.float32(g["scale"]), bins.astype(np.float32),
+                             vals.astype(np.float32), g["indices"])
+    xi = torch.from_numpy(rng.standard_normal(1_000_000).astype(np.float32)).to(cuda_device)
+    vb = torch.from_numpy(rng.standard_normal(1_000_000).astype(np.float32)).to(cuda_device)
+    f = gp.generate(prob, xi)
+    back = gp.generate_inv(prob, f)
+    assert relerr(back.cpu().numpy(), xi.cpu().numpy()) < 1e-3
+    lhs = float(torch.dot(vb.double(), f.double()))
+    rhs = float(torch.dot(gp.generate_grad_xi(prob, vb).double(), xi.double()))
+    assert abs(lhs - rhs) <= 1e-4 * abs(lhs)
+    dv = gp.generate_grad_vals(prob, xi, vb)
+    assert torch.isfinite(dv).all()
