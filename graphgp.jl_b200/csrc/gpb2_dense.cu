@@ -1,10 +1,10 @@
 // gpb2_dense.cu -- the dense first layer (the n0 root points) on the device.
 //
 // Follows src/dense.jl: the n0 x n0 covariance is assembled with the same integer-distance +
-// interpolation pipeline as the refine kernels (_assemble_dense_cov, :15-40), factorised with
-// LAPACK-style potrf (cuSOLVER) and, when that fails, refactorised with K + eps*mean(diag) for
-// eps = 1e-9, 1e-8, ..., 1e-2 evaluated in T (_dense_chol_L, :46-67).  generate_dense is L*xi,
-// generate_dense_inv is L\v, generate_dense_logdet is sum(log(diag(L))).
+// interpolation pipeline as the refine kernels (_assemble_dense_cov, :15-40) and factorised with
+// the jitter ladder of _dense_chol_L (:46-67) by the exact-order kernels of gpb2_dense_chol.cu.
+// generate_dense is L*xi, generate_dense_inv is L\v, generate_dense_logdet is
+// sum(log(diag(L))); the triangular products and solves use cuBLAS.
 //
 // Adjoints:
 //  * generate_grad_vals dense block (src/grad_generate_vals.jl:252-280): L-bar = tril(vb xi^T)
@@ -67,24 +67,11 @@ inline cublasStatus_t trsm(cublasHandle_t h, cublasSideMode_t side, cublasOperat
     return cublasDtrsm(h, side, CUBLAS_FILL_MODE_LOWER, op, CUBLAS_DIAG_NON_UNIT, n, n, &one, A,
                        n, B, n);
 }
-inline cusolverStatus_t potrf_ws(cusolverDnHandle_t h, int n, float* A, int* lw) {
-    return cusolverDnSpotrf_bufferSize(h, CUBLAS_FILL_MODE_LOWER, n, A, n, lw);
-}
-inline cusolverStatus_t potrf_ws(cusolverDnHandle_t h, int n, double* A, int* lw) {
-    return cusolverDnDpotrf_bufferSize(h, CUBLAS_FILL_MODE_LOWER, n, A, n, lw);
-}
 inline cusolverStatus_t potri_ws(cusolverDnHandle_t h, int n, float* A, int* lw) {
     return cusolverDnSpotri_bufferSize(h, CUBLAS_FILL_MODE_LOWER, n, A, n, lw);
 }
 inline cusolverStatus_t potri_ws(cusolverDnHandle_t h, int n, double* A, int* lw) {
     return cusolverDnDpotri_bufferSize(h, CUBLAS_FILL_MODE_LOWER, n, A, n, lw);
-}
-inline cusolverStatus_t potrf(cusolverDnHandle_t h, int n, float* A, float* w, int lw, int* info) {
-    return cusolverDnSpotrf(h, CUBLAS_FILL_MODE_LOWER, n, A, n, w, lw, info);
-}
-inline cusolverStatus_t potrf(cusolverDnHandle_t h, int n, double* A, double* w, int lw,
-                              int* info) {
-    return cusolverDnDpotrf(h, CUBLAS_FILL_MODE_LOWER, n, A, n, w, lw, info);
 }
 inline cusolverStatus_t potri(cusolverDnHandle_t h, int n, float* A, float* w, int lw, int* info) {
     return cusolverDnSpotri(h, CUBLAS_FILL_MODE_LOWER, n, A, n, w, lw, info);
@@ -121,29 +108,6 @@ __device__ __forceinline__ T pair_radius(const uint32_t* __restrict__ coords, in
         sq += di * di;
     }
     return Num<T>::mul(Num<T>::sqrt(Num<T>::from_i64(sq)), scale);
-}
-
-// _assemble_dense_cov (src/dense.jl:15-40), column-major, plus `jit` added to the diagonal
-// (K[i,i] + jit, the retry matrix of src/dense.jl:58-60; jit == 0 for the first attempt).
-template <typename T>
-__global__ void k_dense_assemble(TableView<T> tv, const uint32_t* __restrict__ coords, int D,
-                                 int DS, T scale, int64_t n, T jit, T* __restrict__ K) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    SmemTable<T> tab;
-    tab.stage(tv, smem, threadIdx.x, blockDim.x);
-    __syncthreads();
-    const T diag = tab.lookup(T(0));
-    for (int64_t j = blockIdx.x; j < n; j += gridDim.x) {
-        for (int64_t i = j + threadIdx.x; i < n; i += blockDim.x) {
-            if (i == j) {
-                K[j * n + j] = jit == T(0) ? diag : Num<T>::add(diag, jit);
-            } else {
-                const T v = tab.lookup(pair_radius<T>(coords, DS, D, i, j, scale));
-                K[j * n + i] = v;
-                K[i * n + j] = v;
-            }
-        }
-    }
 }
 
 template <typename T>
@@ -259,40 +223,24 @@ int scatter(gpb2_problem* p, int mode, const T* A, double* hist, cudaStream_t s)
     return GPB2_OK;
 }
 
-template <typename T>
-int assemble(gpb2_problem* p, T jit, T* K, cudaStream_t s) {
-    const size_t smem = table_smem_bytes<T>((int)p->nb, p->nkeys);
-    GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_dense_assemble<T>, smem));
-    const int grid = (int)std::min<int64_t>(p->n0, 4 * 148);
-    GPB2_CUDA_TRY(launch_prof("dense_assemble", k_dense_assemble<T>, dim3(grid),
-                              dim3(kDenseThreads), smem, s, table_view<T>(p),
-                              (const uint32_t*)p->coords, (int)p->d, coord_stride((int)p->d),
-                              (T)p->scale, p->n0, jit, K));
-    return GPB2_OK;
-}
-
 }  // namespace
 
 int ensure_dense(gpb2_problem* p) {
     const size_t ts = p->dtype == GPB2_F32 ? 4 : 8;
     const size_t nn = (size_t)p->n0 * (size_t)p->n0;
-    GPB2_TRY(ensure_alloc(&p->Ld, ts * nn));
     GPB2_TRY(ensure_alloc(&p->Wd, ts * nn));
     GPB2_TRY(ensure_alloc(&p->Wd2, ts * nn));
     GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&p->dinfo), sizeof(int) * 4));
     if (!p->solver) GPB2_SOLVER_TRY(cusolverDnCreate(&p->solver));
     if (!p->blas) GPB2_BLAS_TRY(cublasCreate(&p->blas));
     if (!p->dwork) {
-        int lw1 = 0, lw2 = 0;
+        int lw = 0;
         const int n = (int)p->n0;
-        if (p->dtype == GPB2_F32) {
-            GPB2_SOLVER_TRY(potrf_ws(p->solver, n, (float*)p->Ld, &lw1));
-            GPB2_SOLVER_TRY(potri_ws(p->solver, n, (float*)p->Ld, &lw2));
-        } else {
-            GPB2_SOLVER_TRY(potrf_ws(p->solver, n, (double*)p->Ld, &lw1));
-            GPB2_SOLVER_TRY(potri_ws(p->solver, n, (double*)p->Ld, &lw2));
-        }
-        p->dwork_bytes = (int64_t)ts * std::max(std::max(lw1, lw2), 1);
+        if (p->dtype == GPB2_F32)
+            GPB2_SOLVER_TRY(potri_ws(p->solver, n, (float*)p->Wd, &lw));
+        else
+            GPB2_SOLVER_TRY(potri_ws(p->solver, n, (double*)p->Wd, &lw));
+        p->dwork_bytes = (int64_t)ts * std::max(lw, 1);
         GPB2_TRY(ensure_alloc(&p->dwork, (size_t)p->dwork_bytes));
     }
     return GPB2_OK;
@@ -301,35 +249,7 @@ int ensure_dense(gpb2_problem* p) {
 template <typename T>
 int Dense<T>::factor(gpb2_problem* p, cudaStream_t s) {
     GPB2_TRY(ensure_dense(p));
-    GPB2_SOLVER_TRY(cusolverDnSetStream(p->solver, s));
-    const int n = (int)p->n0;
-    const int lw = (int)(p->dwork_bytes / sizeof(T));
-    T* L = static_cast<T*>(p->Ld);
-    GPB2_TRY(assemble<T>(p, T(0), L, s));
-    GPB2_SOLVER_TRY(potrf(p->solver, n, L, static_cast<T*>(p->dwork), lw, p->dinfo));
-    int info = 0;
-    GPB2_CUDA_TRY(cudaMemcpyAsync(&info, p->dinfo, sizeof(int), cudaMemcpyDeviceToHost, s));
-    GPB2_CUDA_TRY(cudaStreamSynchronize(s));
-    p->dense_jitter = 0.0;
-    if (info == 0) return GPB2_OK;
-    // Jitter ladder, evaluated in T exactly as src/dense.jl:50-64 writes it.
-    T dmean = T(0);
-    const T v0 = (T)p->v0;  // every diagonal entry is cov_lookup(0) == vals[0]
-    for (int i = 0; i < n; i++) dmean = dmean + v0;
-    dmean = dmean / (T)(n > 1 ? n : 1);
-    for (T eps = T(1e-9); eps <= T(1e-2); eps *= T(10)) {
-        GPB2_TRY(assemble<T>(p, eps * dmean, L, s));
-        GPB2_SOLVER_TRY(potrf(p->solver, n, L, static_cast<T*>(p->dwork), lw, p->dinfo));
-        GPB2_CUDA_TRY(cudaMemcpyAsync(&info, p->dinfo, sizeof(int), cudaMemcpyDeviceToHost, s));
-        GPB2_CUDA_TRY(cudaStreamSynchronize(s));
-        if (info == 0) {
-            p->dense_jitter = (double)eps;
-            return GPB2_OK;
-        }
-    }
-    return set_error(GPB2_ERR_NOT_PD,
-                     "dense first-layer covariance is not positive definite even with 1e-2 "
-                     "relative jitter; increase the kernel `jitter` or reduce n0");
+    return dense_cholesky_ladder<T>(p, s);  // gpb2_dense_chol.cu
 }
 
 template <typename T>

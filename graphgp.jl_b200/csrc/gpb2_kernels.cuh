@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include "gpb2_device.cuh"
+#include "gpb2_sync.cuh"
 
 namespace gpb2 {
 
@@ -405,6 +406,106 @@ k_sweep_rev(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv,
 }
 
 // ---------------------------------------------------------------------------------------------
+// Persistent sweeps: one cooperative launch per full sweep.  The grid walks the depth batches in
+// order with a grid barrier between consecutive batches; before each barrier every thread loads
+// the read-only inputs of its first point of the next batch (neighbour list, weights, std, xi),
+// so after the barrier only the dependent gathers remain.  Field values and cotangents cross
+// the barrier through L2 (ld/st .cg), never through an SM's L1.
+// ---------------------------------------------------------------------------------------------
+constexpr int kPersistThreads = 1024;
+
+template <typename T, int K>
+struct SweepPoint {
+    int nb[K];
+    T w[K];
+    T a;  // forward: std * xi (the first product of the sum); reverse: std
+    __device__ __forceinline__ void load_fwd(const T* __restrict__ mv, const T* __restrict__ sd,
+                                             const T* __restrict__ xi_ref,
+                                             const int* __restrict__ nbrs, int64_t m) {
+        load_row_i32<K>(nb, nbrs + m * K);
+        load_row_t<T, K>(w, mv + m * K);
+        a = Num<T>::mul(__ldg(sd + m), __ldg(xi_ref + m));
+    }
+    __device__ __forceinline__ void load_rev(const T* __restrict__ mv, const T* __restrict__ sd,
+                                             const int* __restrict__ nbrs, int64_t m) {
+        load_row_i32<K>(nb, nbrs + m * K);
+        load_row_t<T, K>(w, mv + m * K);
+        a = __ldg(sd + m);
+    }
+};
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kPersistThreads)
+k_sweep_fwd_all(T* __restrict__ values, const T* __restrict__ xi_ref, const T* __restrict__ mv,
+                const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
+                const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
+    using N = Num<T>;
+    const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
+    SweepPoint<T, K> sp;
+    int64_t p = offs[0] + gtid;
+    bool have = p < offs[1];
+    if (have) sp.load_fwd(mv, sd, xi_ref, nbrs, p - n0);
+    for (int b = 0; b < nbatch; b++) {
+        const int64_t hi = offs[b + 1];
+        while (have) {
+            T acc = sp.a;
+            sfor<0, K>([&](auto j_) {
+                GPB2_CI(j);
+                acc = N::add(acc, N::mul(sp.w[j], __ldcg(values + sp.nb[j])));
+            });
+            __stcg(values + p, acc);
+            p += gsz;
+            have = p < hi;
+            if (have) sp.load_fwd(mv, sd, xi_ref, nbrs, p - n0);
+        }
+        if (b + 1 < nbatch) {
+            p = offs[b + 1] + gtid;
+            have = p < offs[b + 2];
+            if (have) sp.load_fwd(mv, sd, xi_ref, nbrs, p - n0);
+            if (!grid_sync(gs)) return;
+        }
+    }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kPersistThreads)
+k_sweep_rev_all(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv,
+                const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
+                const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
+    using N = Num<T>;
+    const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
+    SweepPoint<T, K> sp;
+    int64_t p = offs[nbatch - 1] + gtid;
+    bool have = p < offs[nbatch];
+    if (have) sp.load_rev(mv, sd, nbrs, p - n0);
+    for (int b = nbatch - 1; b >= 0; b--) {
+        const int64_t hi = offs[b + 1];
+        while (have) {
+            const T vbp = __ldcg(vb + p);
+            if (xg) xg[p] = N::mul(sp.a, vbp);
+            sfor<0, K>([&](auto j_) {
+                GPB2_CI(j);
+                atomicAdd(vb + sp.nb[j], N::mul(sp.w[j], vbp));
+            });
+            p += gsz;
+            have = p < hi;
+            if (have) sp.load_rev(mv, sd, nbrs, p - n0);
+        }
+        if (b > 0) {
+            p = offs[b - 1] + gtid;
+            have = p < offs[b];
+            if (have) sp.load_rev(mv, sd, nbrs, p - n0);
+            if (!grid_sync(gs)) return;
+        }
+    }
+}
+
+// Co-resident grid of a cooperative kernel (occupancy x SM count).
+int coop_grid(const void* kernel, int threads, size_t smem);
+
+// ---------------------------------------------------------------------------------------------
 // Launchers, bundled per (T, K, D) into an Ops table.
 // ---------------------------------------------------------------------------------------------
 template <typename T>
@@ -422,6 +523,10 @@ struct Ops {
                              int64_t, cudaStream_t);
     cudaError_t (*sweep_rev)(T*, T*, const T*, const T*, const int*, int64_t, int64_t, int64_t,
                              cudaStream_t);
+    cudaError_t (*sweep_fwd_all)(T*, const T*, const T*, const T*, const int*, int64_t,
+                                 const int64_t*, int, GridSync, cudaStream_t);
+    cudaError_t (*sweep_rev_all)(T*, T*, const T*, const T*, const int*, int64_t, const int64_t*,
+                                 int, GridSync, cudaStream_t);
 };
 
 template <typename T>
@@ -488,9 +593,34 @@ struct Launch {
         return launch_prof("sweep_rev", k_sweep_rev<T, K>, dim3((unsigned)grid),
                            dim3(kSweepThreads), 0, s, xg, vb, mv, sd, nbrs, n0, lo, hi);
     }
+    template <class Kern, class... Args>
+    static cudaError_t coop(const char* name, Kern kern, cudaStream_t s, Args... args) {
+        const int grid = coop_grid((const void*)kern, kPersistThreads, 0);
+        void* argv[] = {(void*)&args...};
+        const ProfToken t = prof_begin(name, s);
+        const cudaError_t e =
+            cudaLaunchCooperativeKernel((const void*)kern, grid, kPersistThreads, argv, 0, s);
+        prof_end(t, s);
+        return e;
+    }
+    static cudaError_t sweep_fwd_all(T* values, const T* xi_ref, const T* mv, const T* sd,
+                                     const int* nbrs, int64_t n0, const int64_t* offs, int nbatch,
+                                     GridSync gs, cudaStream_t s) {
+        if (nbatch <= 0) return cudaSuccess;
+        return coop("sweep_fwd_all", k_sweep_fwd_all<T, K>, s, values, xi_ref, mv, sd, nbrs, n0,
+                    offs, nbatch, gs);
+    }
+    static cudaError_t sweep_rev_all(T* xg, T* vb, const T* mv, const T* sd, const int* nbrs,
+                                     int64_t n0, const int64_t* offs, int nbatch, GridSync gs,
+                                     cudaStream_t s) {
+        if (nbatch <= 0) return cudaSuccess;
+        return coop("sweep_rev_all", k_sweep_rev_all<T, K>, s, xg, vb, mv, sd, nbrs, n0, offs,
+                    nbatch, gs);
+    }
     static const Ops<T>* ops() {
-        static const Ops<T> o = {factor,    inv,       logdet,    logdet_grad, grad_vals,
-                                 inv_loss_grad, fused_fwd, sweep_fwd, sweep_rev};
+        static const Ops<T> o = {factor,        inv,       logdet,    logdet_grad,
+                                 grad_vals,     inv_loss_grad, fused_fwd, sweep_fwd,
+                                 sweep_rev,     sweep_fwd_all, sweep_rev_all};
         return &o;
     }
 };

@@ -52,15 +52,19 @@ inline unsigned grid1d(int64_t n) {
     return (unsigned)(g < 1 ? 1 : (g > 148 * 16 ? 148 * 16 : g));
 }
 
-enum class FwdMode { Sweep = 0, Fused = 1 };
+// Process-wide sweep strategy (GPB2_FWD=persistent|fused|batched at load time, or
+// gpb2_set_forward_mode()): 0 = one cooperative kernel per sweep, 1 = the reference's fused
+// per-batch forward kernel, 2 = one light kernel launch per batch.
+enum class FwdMode { Persistent = 0, Fused = 1, Batched = 2 };
 
-// Process-wide forward mode: GPB2_FWD=fused at load time, or gpb2_set_forward_mode().
 std::atomic<int> g_fwd_mode{[] {
     const char* e = std::getenv("GPB2_FWD");
-    return (e && std::strcmp(e, "fused") == 0) ? 1 : 0;
+    if (e && std::strcmp(e, "fused") == 0) return 1;
+    if (e && std::strcmp(e, "batched") == 0) return 2;
+    return 0;
 }()};
 
-FwdMode fwd_mode() { return g_fwd_mode.load() == 1 ? FwdMode::Fused : FwdMode::Sweep; }
+FwdMode fwd_mode() { return static_cast<FwdMode>(g_fwd_mode.load()); }
 
 }  // namespace
 
@@ -105,6 +109,14 @@ struct Impl {
             return GPB2_OK;
         }
         if (!have_factor) GPB2_TRY(factor_all(p, s));
+        if (fwd_mode() == FwdMode::Persistent) {
+            GPB2_TRY(arm_sync(p, s));
+            GPB2_TRY(check_launch(o->sweep_fwd_all(values, xi_ref, (const T*)p->mv,
+                                                   (const T*)p->sd, p->nbrs, p->n0, p->d_offsets,
+                                                   nbatch(p), grid_sync_of(p), s),
+                                  "forward sweep"));
+            return check_sync(p, s);
+        }
         for (size_t b = 1; b < p->offsets.size(); b++)
             GPB2_TRY(check_launch(o->sweep_fwd(values, xi_ref, (const T*)p->mv,
                                                (const T*)p->sd, p->nbrs, p->n0,
@@ -116,10 +128,39 @@ struct Impl {
     // Reverse sweep over the batches, latest first; xg may be NULL.
     static int reverse_sweep(P* p, T* xg, T* vb, cudaStream_t s) {
         const Ops<T>* o = ops_of<T>(p);
+        if (fwd_mode() == FwdMode::Persistent) {
+            GPB2_TRY(arm_sync(p, s));
+            GPB2_TRY(check_launch(o->sweep_rev_all(xg, vb, (const T*)p->mv, (const T*)p->sd,
+                                                   p->nbrs, p->n0, p->d_offsets, nbatch(p),
+                                                   grid_sync_of(p), s),
+                                  "reverse sweep"));
+            return check_sync(p, s);
+        }
         for (size_t b = p->offsets.size() - 1; b >= 1; b--)
             GPB2_TRY(check_launch(o->sweep_rev(xg, vb, (const T*)p->mv, (const T*)p->sd, p->nbrs,
                                                p->n0, p->offsets[b - 1], p->offsets[b], s),
                                   "reverse sweep"));
+        return GPB2_OK;
+    }
+
+    static int nbatch(P* p) { return (int)p->offsets.size() - 1; }
+    static GridSync grid_sync_of(P* p) {
+        return GridSync{p->dsync, reinterpret_cast<int*>(p->dsync + 2)};
+    }
+    // Zero the barrier words before a cooperative launch.
+    static int arm_sync(P* p, cudaStream_t s) {
+        GPB2_CUDA_TRY(cudaMemsetAsync(p->dsync, 0, 4 * sizeof(unsigned int), s));
+        return GPB2_OK;
+    }
+    // The cooperative kernels' barriers are bounded: read the error word they leave behind
+    // (one small copy on the stream) and report a timeout instead of returning garbage.
+    static int check_sync(P* p, cudaStream_t s) {
+        unsigned int h = 0;
+        GPB2_CUDA_TRY(cudaMemcpyAsync(&h, p->dsync + 2, sizeof(h), cudaMemcpyDeviceToHost, s));
+        GPB2_CUDA_TRY(cudaStreamSynchronize(s));
+        if (h != 0)
+            return set_error(GPB2_ERR_TIMEOUT,
+                             "a grid barrier of the persistent sweep timed out (error word %u)", h);
         return GPB2_OK;
     }
 
@@ -352,8 +393,9 @@ static int need(const void* ptr, const char* name) {
 extern "C" {
 
 int gpb2_set_forward_mode(int mode) {
-    if (mode != 0 && mode != 1)
-        return set_error(GPB2_ERR_INVALID_ARG, "forward mode must be 0 (sweep) or 1 (fused)");
+    if (mode < 0 || mode > 2)
+        return set_error(GPB2_ERR_INVALID_ARG,
+                         "forward mode must be 0 (persistent), 1 (fused) or 2 (batched)");
     g_fwd_mode.store(mode);
     return GPB2_OK;
 }

@@ -207,8 +207,8 @@ static int load_table(gpb2_problem* p, const void* vals_dev, cudaStream_t s) {
 static void free_problem(gpb2_problem* p) {
     void* bufs[] = {p->coords, p->nbrs, p->indices, p->bins, p->vals,  p->seg,
                     p->start,  p->mv,   p->sd,      p->buf_a, p->buf_b, p->buf_c,
-                    p->buf_d,  p->dacc, p->Ld,      p->Wd,   p->Wd2,   p->dwork,
-                    p->dinfo};
+                    p->buf_d,  p->dacc, p->Lcand,   p->lad,  p->Wd,    p->Wd2,
+                    p->dwork,  p->dinfo, p->d_offsets, p->dsync};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);
@@ -301,14 +301,15 @@ int gpb2_problem_create(gpb2_problem** out, int dtype, int device, const uint32_
         // Neighbours.
         const int64_t M = p->m;
         if ((st = ensure_alloc(reinterpret_cast<void**>(&p->nbrs), sizeof(int) * M * k))) break;
-        int64_t* doffs = nullptr;
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&p->d_offsets),
+                               sizeof(int64_t) * n_offsets)))
+            break;
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&p->dsync), 4 * sizeof(unsigned int))))
+            break;
+        int64_t* doffs = p->d_offsets;
         unsigned long long* dbad = nullptr;
-        if ((st = ensure_alloc(reinterpret_cast<void**>(&doffs), sizeof(int64_t) * n_offsets)))
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&dbad), 2 * sizeof(unsigned long long))))
             break;
-        if ((st = ensure_alloc(reinterpret_cast<void**>(&dbad), 2 * sizeof(unsigned long long)))) {
-            cudaFree(doffs);
-            break;
-        }
         unsigned long long hbad[2] = {0ull, ~0ull};
         cudaMemcpyAsync(doffs, offsets_host, sizeof(int64_t) * n_offsets, cudaMemcpyHostToDevice,
                         s);
@@ -326,7 +327,6 @@ int gpb2_problem_create(gpb2_problem** out, int dtype, int device, const uint32_
         }
         cudaMemcpyAsync(hbad, dbad, sizeof(hbad), cudaMemcpyDeviceToHost, s);
         cudaError_t e = cudaStreamSynchronize(s);
-        cudaFree(doffs);
         cudaFree(dbad);
         if (e != cudaSuccess) {
             st = set_error(GPB2_ERR_CUDA, "neighbour upload failed: %s", cudaGetErrorString(e));
@@ -399,6 +399,21 @@ int gpb2_problem_info(const gpb2_problem* p, int64_t* n, int64_t* m, int64_t* k,
     if (k) *k = p->k;
     if (d) *d = p->d;
     if (n_batches) *n_batches = (int64_t)p->offsets.size() - 1;
+    return GPB2_OK;
+}
+
+int gpb2_problem_dense_jitter(const gpb2_problem* p, double* eps) {
+    if (!p || !eps) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_dense_jitter: NULL");
+    *eps = p->dense_candidate < 0 ? -1.0 : p->dense_jitter;
+    return GPB2_OK;
+}
+
+int gpb2_problem_dense_factor(const gpb2_problem* p, void* out, void* stream) {
+    if (!p || !out) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_dense_factor: NULL");
+    if (!p->Ld) return set_error(GPB2_ERR_INVALID_ARG, "no dense factorisation yet");
+    DeviceGuard dg(p->device);
+    GPB2_CUDA_TRY(cudaMemcpyAsync(out, p->Ld, tsize(p) * p->n0 * p->n0, cudaMemcpyDeviceToDevice,
+                                  (cudaStream_t)stream));
     return GPB2_OK;
 }
 

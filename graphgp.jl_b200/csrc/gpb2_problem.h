@@ -16,6 +16,9 @@ struct gpb2_problem {
     int64_t n = 0, m = 0, k = 0, d = 0, n0 = 0, nb = 0;
     double scale = 0.0;
     std::vector<int64_t> offsets;  // host: offsets[0] == n0, offsets.back() == n
+    int64_t* d_offsets = nullptr;  // device copy of offsets
+    unsigned int* dsync = nullptr; // grid barrier of the persistent kernels: [0] arrivals,
+                                   // [1] generation, [2] error word
 
     // Device copies owned by the handle.
     uint32_t* coords = nullptr;  // (N, coord_stride(D))
@@ -39,7 +42,10 @@ struct gpb2_problem {
     double* dacc = nullptr;  // nb histogram + 8 scalars (double accumulators)
 
     // Dense n0 block.
-    void* Ld = nullptr;       // (n0, n0) column-major: Cholesky factor (lower)
+    void* Ld = nullptr;       // the selected ladder candidate inside Lcand (not owned)
+    void* Lcand = nullptr;    // ladder candidates, each (n0, n0) column-major lower
+    int* lad = nullptr;       // ladder flags: fail[16], select, jitters
+    int dense_candidate = -1;
     void* Wd = nullptr;       // (n0, n0) work
     void* Wd2 = nullptr;      // (n0, n0) work
     void* dwork = nullptr;    // cuSOLVER workspace
@@ -111,6 +117,9 @@ int ensure_dense(gpb2_problem* p);
 
 // Dense first layer (gpb2_dense.cu).  All on `s`; factor() synchronises once to read the
 // Cholesky status (the jitter ladder of src/dense.jl:46-67 branches on it).
+template <typename T>
+int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s);
+
 template <typename T>
 struct Dense {
     static int factor(gpb2_problem* p, cudaStream_t s);

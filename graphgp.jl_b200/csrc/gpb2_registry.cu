@@ -80,6 +80,10 @@ int flat_grid(const void* kernel, int threads, size_t smem, int64_t work) {
     return (int)(need < cap ? need : cap);
 }
 
+int coop_grid(const void* kernel, int threads, size_t smem) {
+    return flat_grid(kernel, threads, smem, INT64_MAX / 2);
+}
+
 // ------------------------------------------------------------------------------------------
 // Launch profiler.  Every kernel launch of the library goes through prof_begin/prof_end: the
 // launch counter is always on; with profiling enabled a CUDA event pair is recorded around the

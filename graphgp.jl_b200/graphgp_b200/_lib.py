@@ -81,6 +81,8 @@ _SIGNATURES = {
     "gpb2_problem_set_vals": (I32, [P, P, P]),
     "gpb2_problem_info": (I32, [P, PI64, PI64, PI64, PI64, PI64]),
     "gpb2_problem_destroy": (I32, [P]),
+    "gpb2_problem_dense_jitter": (I32, [P, PD]),
+    "gpb2_problem_dense_factor": (I32, [P, P, P]),
     "gpb2_profile_enable": (I32, [I32]),
     "gpb2_profile_reset": (I32, []),
     "gpb2_profile_report": (I32, [C.c_char_p, I64]),

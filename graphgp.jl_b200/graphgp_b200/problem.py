@@ -149,6 +149,23 @@ class GraphGPProblem:
             _lib.check(st, "GraphGPProblem upload")
         return h
 
+    def dense_jitter(self) -> float:
+        """Relative jitter of the dense block's last factorisation (0.0 = none needed, -1.0 =
+        not factorised yet), the ladder of src/dense.jl:46-67."""
+        out = C.c_double()
+        _lib.check(_lib.lib().gpb2_problem_dense_jitter(self.handle, C.byref(out)))
+        return out.value
+
+    def dense_factor(self) -> np.ndarray:
+        """The dense block's last Cholesky factor (n0 x n0 lower triangle) as a host array."""
+        n = self.n0
+        out = torch.empty((n, n), dtype=self.torch_dtype, device=self.device)
+        st = _lib.lib().gpb2_problem_dense_factor(
+            self.handle, C.c_void_p(out.data_ptr()),
+            C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        _lib.check(st, "dense_factor")
+        return np.tril(out.cpu().numpy().T)  # column-major on the device
+
     def release(self) -> None:
         """Free the device handle now (it is otherwise freed with the object)."""
         if self._finalizer is not None:

@@ -83,6 +83,16 @@ int gpb2_problem_info(const gpb2_problem* prob, int64_t* n, int64_t* m, int64_t*
 
 int gpb2_problem_destroy(gpb2_problem* prob);
 
+/* The relative jitter eps of the dense block's last factorisation: 0 when K itself factorised,
+ * else the first of 1e-9, 1e-8, ..., 1e-2 for which K + eps*mean(diag(K)) did
+ * (_dense_chol_L, src/dense.jl:46-67); -1 before any dense operation. */
+int gpb2_problem_dense_jitter(const gpb2_problem* prob, double* eps);
+
+/* Copy the dense block's last Cholesky factor (n0 x n0, column-major; lower triangle valid,
+ * upper triangle unspecified) into factor_dev.  No reference counterpart: the factor is internal
+ * to src/dense.jl; exposed for inspection and parity tests. */
+int gpb2_problem_dense_factor(const gpb2_problem* prob, void* factor_dev, void* stream);
+
 /* Launch profiler, process-wide (no reference counterpart; the reference times with
  * CUDA.@elapsed around whole calls, bench/compare/run_gradmem.jl:19-36).  Every kernel the
  * library launches is counted (gpb2_launch_count); with profiling enabled each launch is also
@@ -93,9 +103,13 @@ int gpb2_profile_reset(void);
 int gpb2_profile_report(char* buf, int64_t cap);
 int64_t gpb2_launch_count(void);
 
-/* Forward-sweep strategy, process-wide: 0 = one flat factor kernel over all refined points, then a
- * light kernel per depth batch (default); 1 = the reference's fused per-batch kernel
- * (refine_apply_fused_kernel!, src/kernels.jl:101-119).  Both give bit-identical values. */
+/* Depth-sweep strategy, process-wide.  The conditional-mean weights and std of all refined
+ * points come from one flat kernel; then 0 = one cooperative (persistent) kernel per sweep with a
+ * bounded grid barrier between depth batches (default); 2 = one light kernel launch per batch.
+ * 1 = the reference's fused per-batch forward kernel (refine_apply_fused_kernel!,
+ * src/kernels.jl:101-119), which recomputes the factor inside each batch.  All three give
+ * bit-identical forward values.  A barrier that times out makes the call return
+ * GPB2_ERR_TIMEOUT. */
 int gpb2_set_forward_mode(int mode);
 
 /* ------------------------------------------------------------------------------------------

@@ -48,7 +48,7 @@ def _sweep_mode():
 
 @pytest.mark.parametrize("dt", [np.float64, np.float32])
 @pytest.mark.parametrize("name", FIXTURES)
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 def test_refine_bit_exact(golden, cuda_device, name, dt, mode):
     d = golden(name)
     prob, orc = _pair(d, dt)
@@ -214,6 +214,34 @@ def test_supported_shapes_f32(cuda_device, K, D, kernel):
     assert relerr(gp.generate_grad_xi(prob, vb), O.generate_grad_xi(orc, vb)) < 1e-5
     assert relerr(gp.generate_grad_vals(prob, xi, vb), O.generate_grad_vals(orc, xi, vb)) < 1e-5
     assert relerr(gp.refine_logdet_grad_vals(prob), O.refine_logdet_grad_vals(orc)[1]) < 1e-5
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_dense_jitter_ladder(cuda_device, dt):
+    # The config-2 root block (n0 = 1000 spread tree medians, RBF scale 0.3, jitter 1e-5) is
+    # indefinite as a matrix of interpolated covariances, so the reference's ladder
+    # (src/dense.jl:46-67) must step up to eps = 1e-3.  The device factorisation must take the
+    # same step as the oracle and, being exact-order, produce the same field.
+    prob, orc = _config_problem(20_000, 2, 1000, 8, dt, 1)
+    xi = np.random.default_rng(2).standard_normal(prob.npoints()).astype(dt)
+    f = gp.generate(prob, xi)
+    _, jit_o = O.dense_chol(orc)
+    assert jit_o > 0
+    assert np.isclose(prob.dense_jitter(), jit_o, rtol=1e-6)
+    assert relerr(f, O.generate(orc, xi)) < TOL[dt]
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+@pytest.mark.parametrize("n0,N", [(1000, 20_000), (200, 3000), (37, 1000)])
+def test_dense_factor_bit_exact(cuda_device, dt, n0, N):
+    # The device's blocked, ladder-speculative Cholesky applies each entry's subtractions in the
+    # oracle's order: the factor (and the ladder step) must be identical bit for bit.
+    prob, orc = _config_problem(N, 2, n0, 8, dt, 5)
+    gp.generate_logdet(prob)
+    L_dev = prob.dense_factor()
+    L_ora, jit = O.dense_chol(orc)
+    assert np.isclose(prob.dense_jitter(), jit, rtol=1e-6)
+    assert np.array_equal(L_dev, np.tril(L_ora))
 
 
 def test_degenerate_duplicates(cuda_device):
