@@ -248,6 +248,9 @@ int ensure_dense(gpb2_problem* p) {
 
 template <typename T>
 int Dense<T>::factor(gpb2_problem* p, cudaStream_t s) {
+    // The factor depends only on the coordinates (fixed) and the covariance table: a checked
+    // factor of the current table is reused (the table setter clears the flag).
+    if (p->dense_valid) return GPB2_OK;
     GPB2_TRY(ensure_dense(p));
     return dense_cholesky_ladder<T>(p, s);  // gpb2_dense_chol.cu
 }

@@ -1,5 +1,5 @@
 // gpb2_dense_chol.cu -- the dense block's Cholesky factorisation with the reference's jitter
-// ladder (_dense_chol_L, src/dense.jl:46-67), as one cooperative kernel.
+// ladder (_dense_chol_L, src/dense.jl:46-67), one thread-block cluster per ladder candidate.
 //
 // Exact order.  The reference factorises with LAPACK; the oracle restates it as the unblocked
 // left-looking recurrence  L[i][j] = (A[i][j] - sum_{p<j} L[i][p]*L[j][p]) / L[j][j],  the sum
@@ -17,212 +17,326 @@
 // selected on the device; a larger block tries the candidates one after another.  A candidate
 // that fails stops at its failing panel.
 //
-// Schedule (one cooperative launch, bounded grid barriers between phases), per 32-wide panel:
-//   D  one warp per live candidate factors the 32 x 32 diagonal block, a row per lane;
-//   P  (candidate, 256-row chunk) tasks: each thread solves one row of the panel below the block;
-//   U  (candidate, 64 x 64 lower tile) tasks: the trailing update with the panel's 32 columns.
+// Schedule: one thread-block cluster per candidate, phases separated by the cluster barrier; per
+// 32-wide panel:
+//   D  one warp of the cluster factors the 32 x 32 diagonal block, a row per lane;
+//   P  256-row chunks over the cluster's CTAs: each thread solves one row below the block;
+//   U  64 x 64 lower tiles over the cluster's CTAs: the trailing update with the panel's columns.
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <vector>
 
+#include <cooperative_groups.h>
+
 #include "gpb2_problem.h"
+
+namespace cg = cooperative_groups;
 
 namespace gpb2 {
 
 namespace {
 
-constexpr int kB = 32;          // panel width (= warp size: one row per lane in phase D)
+constexpr int kB = 32;          // panel width (= warp size: a lane per row or column)
 constexpr int kSpecMax = 4096;  // concurrent ladder up to this n0
-constexpr int kCholThreads = 256;
-constexpr int kRowChunk = kCholThreads;
 
 template <typename T>
-__host__ __device__ constexpr int tile_of() { return sizeof(T) == 4 ? 64 : 32; }  // smem < 48 KB
+__host__ __device__ constexpr int chol_threads() { return 512; }
 
 template <typename T>
 struct CholArgs {
     T* base;          // nc candidates, each n x n column-major (lower triangle)
     int64_t n;
     int nc;
+    int first;        // ladder index of candidate 0 of this launch
     int* fail;        // fail[c] = failing column + 1, 0 while alive
-    int* sel;         // first live candidate, -1 if none
-    GridSync gs;
+    int* sel;         // sel[0]: ladder index of the first success (-1: none yet); sel[1]: its slot
+    int* done;        // done[c] = 1 once candidate c is fully factorised
+    unsigned long long* trace;  // diagnostics (GPB2_TRACE_DENSE): phase timestamps, or NULL
 };
 
-// Phase D: candidate c's diagonal block [p0, p0+bs)^2, lane i holding row i in registers.
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// x / d for d > 0, bit for bit as Num<T>::div.  A zero dividend gives a zero of its own sign;
+// the division sequence reaches that case only through its slow path (several times the
+// latency), and zeros are common here (padding rows, negligible covariances).
 template <typename T>
-__device__ void chol_diag_warp(const CholArgs<T>& a, int c, int p0) {
+__device__ __forceinline__ T div_pos(T x, T d) {
+    const T q = Num<T>::div(x == T(0) ? T(1) : x, d);
+    return x == T(0) ? x : q;
+}
+
+// Phase D (whole CTA): factor candidate c's diagonal block [p0, p0+bs)^2.  The CTA stages the
+// block in shared memory in one coalesced pass, warp 0 eliminates it in registers, and the CTA
+// writes it back.  Returns false (and records the column) if a pivot fails.
+template <typename T>
+__device__ __noinline__ bool chol_diag(const CholArgs<T>& a, int c, int64_t p0, T (*S)[kB + 1], int* s_bad,
+                          unsigned long long* st = nullptr) {
     using N = Num<T>;
-    const int lane = threadIdx.x & 31;
+    constexpr int NTH = chol_threads<T>();
     T* L = a.base + (int64_t)c * a.n * a.n;
     const int bs = a.n - p0 < kB ? (int)(a.n - p0) : kB;
-    T r[kB];
-    sfor<0, kB>([&](auto j_) {
-        GPB2_CI(j);
-        r[j] = (lane < bs && j <= lane) ? __ldcg(L + (p0 + lane) + (int64_t)(p0 + j) * a.n)
-                                        : T(0);
-    });
-    int bad = 0;
-    sfor<0, kB>([&](auto j_) {
-        GPB2_CI(j);
-        if (j < bs && !bad) {
-            const T s = __shfl_sync(0xffffffffu, r[j], j);
-            if (!(s > T(0))) {  // LAPACK potrf's failure test (also catches NaN)
-                bad = p0 + j + 1;
-            } else {
-                const T d = N::sqrt(s);
-                if (lane == j) r[j] = d;
-                else if (lane > j) r[j] = N::div(r[j], d);
-                sfor<j + 1, kB>([&](auto q_) {
-                    GPB2_CI(q);
-                    const T lqj = __shfl_sync(0xffffffffu, r[j], q);
-                    if (lane >= q) r[q] = N::sub(r[q], N::mul(r[j], lqj));
-                });
-            }
-        }
-    });
-    if (bad) {
-        if (lane == 0) a.fail[c] = bad;
-        return;
-    }
-    sfor<0, kB>([&](auto j_) {
-        GPB2_CI(j);
-        if (lane < bs && j <= lane) __stcg(L + (p0 + lane) + (int64_t)(p0 + j) * a.n, r[j]);
-    });
-}
-
-// Phase P: rows [r0, r0 + kRowChunk) below candidate c's diagonal block.
-template <typename T>
-__device__ void chol_panel_rows(const CholArgs<T>& a, int c, int p0, int64_t r0, T (*Dg)[kB + 1]) {
-    using N = Num<T>;
-    T* L = a.base + (int64_t)c * a.n * a.n;
-    for (int e = threadIdx.x; e < kB * kB; e += blockDim.x) {
-        const int i = e % kB, j = e / kB;
-        Dg[i][j] = (i >= j) ? __ldcg(L + (p0 + i) + (int64_t)(p0 + j) * a.n) : T(0);
+#pragma unroll
+    for (int e0 = 0; e0 < kB * kB; e0 += NTH) {
+        const int e = e0 + threadIdx.x, i = e % kB, j = e / kB;
+        if (i < bs && j <= i) S[i][j] = __ldcg(L + (p0 + i) + (p0 + j) * a.n);
     }
     __syncthreads();
-    const int64_t i = r0 + threadIdx.x;
-    if (i < a.n) {
+    if (st) st[0] = global_ns();
+    if (threadIdx.x < 32) {
+        // Row `lane` in registers, rotated: at step j, r[q] holds entry (lane, j + q), so the
+        // step body is the same code for every column (a compact loop: the block is factored
+        // once per panel and a fully unrolled body would be fetched from L2 every time).
+        // Column j's pivot and multipliers travel by shuffle; finished entries go to S.
+        const int lane = threadIdx.x;
+        T r[kB];
+        sfor<0, kB>([&](auto q_) {
+            GPB2_CI(q);
+            r[q] = (lane < bs && q <= lane) ? S[lane][q] : T(0);
+        });
+        int bad = 0;
+        for (int j = 0; j < bs; j++) {
+            const T sjj = __shfl_sync(0xffffffffu, r[0], j);
+            if (!(sjj > T(0))) {  // LAPACK potrf's failure test (also catches NaN)
+                bad = (int)p0 + j + 1;
+                break;
+            }
+            const T d = N::sqrt(sjj);
+            const T qv = div_pos(lane > j ? r[0] : T(1), d);  // branch-free
+            const T lj = lane == j ? d : qv;                   // L[lane][j] for lane >= j
+            if (lane >= j) S[lane][j] = lj;
+            sfor<1, kB>([&](auto q_) {
+                GPB2_CI(q);
+                const T lqj = __shfl_sync(0xffffffffu, lj, (j + q) & 31);
+                const T u = N::sub(r[q], N::mul(lj, lqj));
+                r[q - 1] = lane >= j + q ? u : r[q];  // update entry (lane, j + q) and rotate
+            });
+            r[kB - 1] = T(0);
+        }
+        if (lane == 0) {
+            *s_bad = bad;
+            if (bad) a.fail[c] = bad;
+        }
+    }
+    __syncthreads();
+    if (st) st[1] = global_ns();
+    const bool ok = *s_bad == 0;
+    if (ok) {
+#pragma unroll
+        for (int e0 = 0; e0 < kB * kB; e0 += NTH) {
+            const int e = e0 + threadIdx.x, i = e % kB, j = e / kB;
+            if (i < bs && j <= i) __stcg(L + (p0 + i) + (p0 + j) * a.n, S[i][j]);
+        }
+    }
+    __syncthreads();
+    return ok;
+}
+
+// Phase P (whole CTA): the rows below candidate c's diagonal block, X <- X * Dg^-T.  Rows go in
+// 32-row blocks, block b to cluster rank b % CL and warp (b / CL) % NW, a row per lane (loads
+// and stores along the contiguous dimension); each lane runs the forward substitution over its
+// row in registers, column by column -- the oracle's order for each entry.
+template <typename T>
+__device__ void chol_panel(const CholArgs<T>& a, int c, int64_t p0, int rank, int CL,
+                           T* Dg, unsigned long long* st = nullptr) {
+    using N = Num<T>;
+    constexpr int NTH = chol_threads<T>(), NW = NTH / 32;
+    T* L = a.base + (int64_t)c * a.n * a.n;
+    const int64_t r0 = p0 + kB;
+    const int64_t nrb = (a.n - r0 + kB - 1) / kB;
+    if (rank >= nrb) return;  // CTA-uniform
+#pragma unroll
+    for (int e0 = 0; e0 < kB * kB; e0 += NTH) {
+        const int e = e0 + threadIdx.x, i = e % kB, j = e / kB;
+        Dg[j * kB + i] = (i >= j) ? __ldcg(L + (p0 + i) + (p0 + j) * a.n) : T(0);
+    }
+    if (threadIdx.x < kB) Dg[kB * kB + threadIdx.x] = T(0);
+    __syncthreads();
+    if (st) st[0] = global_ns();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int64_t b = rank + (int64_t)CL * warp; b < nrb; b += (int64_t)CL * NW) {
+        const int64_t i = r0 + b * kB + lane;
+        const bool live = i < a.n;
+        T* Li = L + i + p0 * a.n;
+        // Fully unrolled (unlike the diagonal block: many warps run this code, and the unrolled
+        // form lets column j+1's division start while column j's updates are in flight).
         T x[kB];
-        sfor<0, kB>([&](auto j_) {
-            GPB2_CI(j);
-            x[j] = __ldcg(L + i + (int64_t)(p0 + j) * a.n);
+        sfor<0, kB>([&](auto q_) {
+            GPB2_CI(q);
+            x[q] = live ? __ldcg(Li + q * a.n) : T(0);
         });
         sfor<0, kB>([&](auto j_) {
             GPB2_CI(j);
-            x[j] = N::div(x[j], Dg[j][j]);
+            const T* dj = Dg + j * kB;  // dj[q] = L[p0 + q][p0 + j]
+            x[j] = div_pos(x[j], dj[j]);
             sfor<j + 1, kB>([&](auto q_) {
                 GPB2_CI(q);
-                x[q] = N::sub(x[q], N::mul(x[j], Dg[q][j]));
+                x[q] = N::sub(x[q], N::mul(x[j], dj[q]));
             });
         });
-        sfor<0, kB>([&](auto j_) {
-            GPB2_CI(j);
-            __stcg(L + i + (int64_t)(p0 + j) * a.n, x[j]);
-        });
+        if (live) {
+            sfor<0, kB>([&](auto q_) {
+                GPB2_CI(q);
+                __stcg(Li + q * a.n, x[q]);
+            });
+        }
     }
     __syncthreads();
+    if (st) st[1] = global_ns();
 }
 
-// Phase U: lower tile (bi, bj) of candidate c's trailing matrix [t0, n)^2.
-template <typename T>
-__device__ void chol_update_tile(const CholArgs<T>& a, int c, int p0, int bi, int bj,
+// Phase U: lower tile (bi, bj) of candidate c's trailing matrix [p0 + kB, n)^2, one subtraction
+// per panel column in order.  Thread (tx, ty) owns rows tx + 32*u (lanes along the contiguous
+// dimension) and columns ty + TY*v.
+template <typename T, int TL>
+__device__ void chol_update_tile(const CholArgs<T>& a, int c, int64_t p0, int bi, int bj,
                                  T (*Li)[kB + 1], T (*Lj)[kB + 1]) {
     using N = Num<T>;
-    constexpr int TL = tile_of<T>();
-    constexpr int R = TL / 16;
+    constexpr int NTH = chol_threads<T>();
+    constexpr int TY = NTH / 32;
+    constexpr int RU = TL / 32, RV = TL / TY;
+    static_assert(RU * 32 == TL && RV * TY == TL, "tile shape");
     T* L = a.base + (int64_t)c * a.n * a.n;
     const int64_t t0 = p0 + kB;
     const int64_t r0 = t0 + (int64_t)bi * TL, c0 = t0 + (int64_t)bj * TL;
-    for (int e = threadIdx.x; e < TL * kB; e += blockDim.x) {
-        const int rr = e % TL, p = e / TL;
+#pragma unroll
+    for (int e0 = 0; e0 < TL * kB; e0 += NTH) {
+        const int e = e0 + threadIdx.x, rr = e % TL, p = e / TL;
         const int64_t gi = r0 + rr, gj = c0 + rr;
-        Li[rr][p] = gi < a.n ? __ldcg(L + gi + (int64_t)(p0 + p) * a.n) : T(0);
-        Lj[rr][p] = gj < a.n ? __ldcg(L + gj + (int64_t)(p0 + p) * a.n) : T(0);
+        Li[rr][p] = gi < a.n ? __ldcg(L + gi + (p0 + p) * a.n) : T(0);
+        Lj[rr][p] = gj < a.n ? __ldcg(L + gj + (p0 + p) * a.n) : T(0);
     }
-    __syncthreads();
-    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-    T acc[R][R];
-    bool live[R][R];
+    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+    T acc[RU][RV];
 #pragma unroll
-    for (int u = 0; u < R; u++)
+    for (int u = 0; u < RU; u++)
 #pragma unroll
-        for (int v = 0; v < R; v++) {
-            const int64_t gi = r0 + ty + 16 * u, gj = c0 + tx + 16 * v;
-            live[u][v] = gi < a.n && gj < a.n && gi >= gj;
-            acc[u][v] = live[u][v] ? __ldcg(L + gi + gj * a.n) : T(0);
+        for (int v = 0; v < RV; v++) {
+            const int64_t gi = r0 + tx + 32 * u, gj = c0 + ty + TY * v;
+            acc[u][v] = (gi < a.n && gi >= gj) ? __ldcg(L + gi + gj * a.n) : T(0);
         }
+    __syncthreads();
 #pragma unroll 4
     for (int p = 0; p < kB; p++) {
-        T li[R], lj[R];
+        T li[RU], lj[RV];
 #pragma unroll
-        for (int u = 0; u < R; u++) li[u] = Li[ty + 16 * u][p];
+        for (int u = 0; u < RU; u++) li[u] = Li[tx + 32 * u][p];
 #pragma unroll
-        for (int v = 0; v < R; v++) lj[v] = Lj[tx + 16 * v][p];
+        for (int v = 0; v < RV; v++) lj[v] = Lj[ty + TY * v][p];
 #pragma unroll
-        for (int u = 0; u < R; u++)
+        for (int u = 0; u < RU; u++)
 #pragma unroll
-            for (int v = 0; v < R; v++) acc[u][v] = N::sub(acc[u][v], N::mul(li[u], lj[v]));
+            for (int v = 0; v < RV; v++) acc[u][v] = N::sub(acc[u][v], N::mul(li[u], lj[v]));
     }
 #pragma unroll
-    for (int u = 0; u < R; u++)
+    for (int u = 0; u < RU; u++)
 #pragma unroll
-        for (int v = 0; v < R; v++)
-            if (live[u][v]) __stcg(L + (r0 + ty + 16 * u) + (c0 + tx + 16 * v) * a.n, acc[u][v]);
+        for (int v = 0; v < RV; v++) {
+            const int64_t gi = r0 + tx + 32 * u, gj = c0 + ty + TY * v;
+            if (gi < a.n && gi >= gj) __stcg(L + gi + gj * a.n, acc[u][v]);
+        }
     __syncthreads();
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kCholThreads) k_chol_ladder(CholArgs<T> a) {
-    constexpr int TL = tile_of<T>();
-    __shared__ T S1[TL][kB + 1];
-    __shared__ T S2[TL][kB + 1];
-    __shared__ int s_live;
+// One cluster per ladder candidate; the cluster's CTAs split each phase and meet at the
+// hardware cluster barrier (release/acquire at cluster scope), so no grid-wide barrier is
+// needed and candidates proceed independently.  Look-ahead: the trailing tile that holds the
+// next diagonal block is updated first (by rank 0), which then factorises that block while the
+// other CTAs carry on with the trailing update, so phase D leaves the critical path.
+template <typename T, int TL>
+__global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> a) {
+    __shared__ T S[2 * TL][kB + 1];
+    // The panel's diagonal factor, transposed (row j = column j of the factor, zero above the
+    // diagonal), plus a zero row: row j read past its end runs into zeros.
+    __shared__ __align__(16) T Dg[(kB + 1) * kB];
+    __shared__ int s_bad;
+    __shared__ unsigned int s_ctr;      // rank 0: next trailing tile of the current panel
+    __shared__ unsigned int s_next[2];  // this CTA's next tile (double-buffered)
+    cg::cluster_group cl = cg::this_cluster();
+    const int CL = (int)cl.num_blocks();
+    const int rank = (int)cl.block_rank();
+    const int c = (int)(blockIdx.x / CL);
+    // A previous launch of the ladder already succeeded (sel is only written between launches).
+    if (__ldcg(a.sel) >= 0) return;
     const int npanels = (int)((a.n + kB - 1) / kB);
+    // Diagnostics: the last candidate's rank-0 thread 0 stamps the end of P, of its look-ahead
+    // (tile 0 + D) and of U per panel.
+    unsigned long long* tr =
+        (a.trace && c == a.nc - 1 && rank == 0 && threadIdx.x == 0) ? a.trace : nullptr;
+    if (rank == 0) chol_diag(a, c, 0, S, &s_bad);
+    cl.sync();
     for (int k = 0; k < npanels; k++) {
-        const int p0 = k * kB;
-        // D: warp 0 of CTA c handles candidate c.
-        if (blockIdx.x < (unsigned)a.nc && threadIdx.x < 32 && !__ldcg(a.fail + blockIdx.x))
-            chol_diag_warp(a, blockIdx.x, p0);
-        if (!grid_sync(a.gs)) return;
+        const int64_t p0 = (int64_t)k * kB;
+        unsigned long long* st = tr ? tr + 8 * k : nullptr;
+        if (st) st[0] = global_ns();
+        if (__ldcg(a.fail + c)) return;  // the whole cluster leaves after the same barrier
         const int64_t rows = a.n - p0 - kB;
         if (rows <= 0) break;
-        // P: (candidate, row chunk) tasks.
-        const int64_t chunks = (rows + kRowChunk - 1) / kRowChunk;
-        for (int64_t t = blockIdx.x; t < chunks * a.nc; t += gridDim.x) {
-            const int c = (int)(t / chunks);
-            if (threadIdx.x == 0) s_live = !__ldcg(a.fail + c);
-            __syncthreads();
-            if (s_live)
-                chol_panel_rows(a, c, p0, p0 + kB + (t % chunks) * kRowChunk, S1);
-            __syncthreads();
-        }
-        if (!grid_sync(a.gs)) return;
-        // U: (candidate, lower tile) tasks.
+        chol_panel<T>(a, c, p0, rank, CL, Dg, st ? st + 1 : nullptr);
+        if (rank == 0 && threadIdx.x == 0) s_ctr = 1u;  // tile 0 is rank 0's
+        if (st) st[3] = global_ns();
+        cl.sync();
         const int64_t nt = (rows + TL - 1) / TL;
-        const int64_t tiles = nt * (nt + 1) / 2;
-        for (int64_t t = blockIdx.x; t < tiles * a.nc; t += gridDim.x) {
-            const int c = (int)(t / tiles);
-            const int64_t tt = t % tiles;
-            int bi = (int)((sqrt(8.0 * (double)tt + 1.0) - 1.0) * 0.5);
-            while ((int64_t)(bi + 1) * (bi + 2) / 2 <= tt) bi++;
-            while ((int64_t)bi * (bi + 1) / 2 > tt) bi--;
-            const int bj = (int)(tt - (int64_t)bi * (bi + 1) / 2);
-            if (threadIdx.x == 0) s_live = !__ldcg(a.fail + c);
+        const unsigned int tiles = (unsigned int)(nt * (nt + 1) / 2);
+        // Tiles are handed out one at a time from rank 0's counter (tile 0, which holds the next
+        // diagonal block, is rank 0's); each CTA asks for its next tile while it computes.
+        unsigned int* ctr = cl.map_shared_rank(&s_ctr, 0);
+        unsigned int t = rank == 0 ? 0u : tiles;
+        if (rank != 0) {
+            if (threadIdx.x == 0) s_next[0] = atomicAdd(ctr, 1u);
             __syncthreads();
-            if (s_live) chol_update_tile(a, c, p0, bi, bj, S1, S2);
-            __syncthreads();
+            t = s_next[0];
         }
-        if (!grid_sync(a.gs)) return;
-    }
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        int s = -1;
-        for (int c = 0; c < a.nc; c++)
-            if (!__ldcg(a.fail + c)) {
-                s = c;
-                break;
+        for (int it = 1; t < tiles; it++) {
+            if (threadIdx.x == 0) s_next[it & 1] = atomicAdd(ctr, 1u);
+            int bi = (int)((sqrt(8.0 * (double)t + 1.0) - 1.0) * 0.5);
+            while ((int64_t)(bi + 1) * (bi + 2) / 2 <= (int64_t)t) bi++;
+            while ((int64_t)bi * (bi + 1) / 2 > (int64_t)t) bi--;
+            const int bj = (int)((int64_t)t - (int64_t)bi * (bi + 1) / 2);
+            chol_update_tile<T, TL>(a, c, p0, bi, bj, S, S + TL);  // ends with __syncthreads
+            if (t == 0) {  // the next diagonal block is final: factorise it now
+                if (st) st[4] = global_ns();
+                chol_diag(a, c, p0 + kB, S, &s_bad, st ? st + 5 : nullptr);
             }
-        a.sel[0] = s;
+            t = s_next[it & 1];
+        }
+        if (st) st[7] = global_ns();
+        cl.sync();
     }
+    if (rank == 0 && threadIdx.x == 0 && !__ldcg(a.fail + c)) a.done[c] = 1;
+}
+
+// After a launch: record the first candidate (in ladder order) that factorised, unless an
+// earlier launch already did.
+__global__ void k_ladder_mark(const int* __restrict__ done, int nc, int first,
+                              int* __restrict__ sel) {
+    if (sel[0] >= 0) return;
+    for (int c = 0; c < nc; c++)
+        if (done[c]) {
+            sel[0] = first + c;
+            sel[1] = c;
+            return;
+        }
+}
+
+// Copy the selected candidate into the fixed factor buffer (the triangular products and solves
+// downstream read it there); with no success the status word records it and the call fails.
+template <typename T>
+__global__ void k_ladder_pick(const T* __restrict__ base, const int* __restrict__ sel,
+                              int64_t nn, T* __restrict__ L, int* __restrict__ status) {
+    const int s = __ldcg(sel + 1);
+    if (__ldcg(sel) < 0) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) *status = 1;
+        return;
+    }
+    const T* src = base + (int64_t)s * nn;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nn;
+         i += (int64_t)gridDim.x * blockDim.x)
+        L[i] = src[i];
 }
 
 // Candidates 0..nc-1 of the ladder: K with jit[c] added to the diagonal (exact T sum).  Only the
@@ -257,6 +371,36 @@ __global__ void k_ladder_assemble(TableView<T> tv, const uint32_t* __restrict__ 
     }
 }
 
+// Largest cluster (16 with the non-portable opt-in, else 8, 4, ...) the factorisation kernel can
+// be resident with; decided once per precision.
+template <typename T, int TL>
+int cluster_size() {
+    static const int cs = [] {
+        cudaFuncSetAttribute((const void*)k_chol_cluster<T, TL>,
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        for (int c = 16; c >= 1; c /= 2) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)c);
+            cfg.blockDim = dim3(chol_threads<T>());
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = (unsigned)c;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int nclusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&nclusters, (const void*)k_chol_cluster<T, TL>, &cfg) ==
+                    cudaSuccess &&
+                nclusters > 0)
+                return c;
+            cudaGetLastError();
+        }
+        return 0;
+    }();
+    return cs;
+}
+
 }  // namespace
 
 template <typename T>
@@ -280,49 +424,107 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
     const int batch = spec ? ncand : 1;
     const size_t nn = (size_t)n * (size_t)n;
     GPB2_TRY(ensure_alloc(&p->Lcand, sizeof(T) * nn * batch));
-    // lad: fail[16] | sel[1] (+pad) | barrier words[4] | jitters (T x 16)
-    GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&p->lad), sizeof(int) * 32 + sizeof(T) * 16));
-    int* fail = p->lad;
-    int* sel = p->lad + 16;
-    unsigned int* bar = reinterpret_cast<unsigned int*>(p->lad + 20);
-    T* djit = reinterpret_cast<T*>(p->lad + 32);
+    GPB2_TRY(ensure_alloc(&p->Ld, sizeof(T) * nn));
+    GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&p->lad), sizeof(int) * kLadInts + sizeof(T) * 16));
+    int* fail = p->lad + kLadFail;
+    int* done = p->lad + kLadDone;
+    int* sel = p->lad + kLadSel;
+    T* djit = reinterpret_cast<T*>(p->lad + kLadInts);
     T* base = static_cast<T*>(p->Lcand);
     const size_t smem = table_smem_bytes<T>((int)p->nb, p->nkeys);
     GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_ladder_assemble<T>, smem));
-    const int grid = coop_grid((const void*)k_chol_ladder<T>, kCholThreads, 0);
+    // Trailing-update tile: the small one balances the cluster's CTAs better on small blocks.
+    constexpr int kTileS = sizeof(T) == 4 ? 64 : 32, kTileL = 2 * kTileS;
+    int tile = n <= 2048 ? kTileS : kTileL;
+    if (const char* e = std::getenv("GPB2_CHOL_TILE")) tile = std::atoi(e) == kTileL ? kTileL : kTileS;
+    void (*kern)(CholArgs<T>) =
+        tile == kTileS ? k_chol_cluster<T, kTileS> : k_chol_cluster<T, kTileL>;
+    const int csize = tile == kTileS ? cluster_size<T, kTileS>() : cluster_size<T, kTileL>();
+    if (csize <= 0) return set_error(GPB2_ERR_CUDA, "no thread-block cluster shape fits");
 
+    // Fresh status: no selection (-1), no failure or completion flags, no error.
+    GPB2_CUDA_TRY(cudaMemsetAsync(p->lad, 0, sizeof(int) * kLadInts, s));
+    GPB2_CUDA_TRY(cudaMemsetAsync(sel, 0xff, sizeof(int) * 2, s));
+    GPB2_CUDA_TRY(cudaMemcpyAsync(djit, jit.data(), sizeof(T) * ncand_used,
+                                  cudaMemcpyHostToDevice, s));
     for (int first = 0; first < ncand_used; first += batch) {
         const int nc = std::min(batch, ncand_used - first);
-        GPB2_CUDA_TRY(cudaMemcpyAsync(djit, jit.data() + first, sizeof(T) * nc,
-                                      cudaMemcpyHostToDevice, s));
-        GPB2_CUDA_TRY(cudaMemsetAsync(p->lad, 0, sizeof(int) * 32, s));
+        if (first > 0) {
+            GPB2_CUDA_TRY(cudaMemsetAsync(fail, 0, sizeof(int) * 16, s));
+            GPB2_CUDA_TRY(cudaMemsetAsync(done, 0, sizeof(int) * 16, s));
+        }
         GPB2_CUDA_TRY(launch_prof("dense_assemble", k_ladder_assemble<T>,
                                   dim3((unsigned)std::min<int64_t>(n, 4 * 148)), dim3(256), smem,
                                   s, table_view<T>(p), (const uint32_t*)p->coords, (int)p->d,
-                                  coord_stride((int)p->d), (T)p->scale, n, (const T*)djit, nc,
-                                  base));
-        CholArgs<T> args{base, n, nc, fail, sel, GridSync{bar, reinterpret_cast<int*>(bar + 2)}};
-        void* argv[] = {&args};
+                                  coord_stride((int)p->d), (T)p->scale, n,
+                                  (const T*)(djit + first), nc, base));
+        unsigned long long* trace = nullptr;
+        const int npan = (int)((n + kB - 1) / kB);
+        if (std::getenv("GPB2_TRACE_DENSE")) {
+            GPB2_TRY(ensure_alloc(&p->trace, sizeof(unsigned long long) * 8 * npan));
+            GPB2_CUDA_TRY(cudaMemsetAsync(p->trace, 0, sizeof(unsigned long long) * 8 * npan,
+                                          s));
+            trace = static_cast<unsigned long long*>(p->trace);
+        }
+        CholArgs<T> args{base, n, nc, first, fail, sel, done, trace};
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(nc * csize));
+        cfg.blockDim = dim3(chol_threads<T>());
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)csize;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
         const ProfToken t = prof_begin("dense_chol", s);
-        cudaError_t e = cudaLaunchCooperativeKernel((const void*)k_chol_ladder<T>, grid,
-                                                    kCholThreads, argv, 0, s);
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args);
         prof_end(t, s);
         GPB2_CUDA_TRY(e);
-        int h[8] = {-1, 0, 0, 0, 0, 0, 0, 0};
-        GPB2_CUDA_TRY(cudaMemcpyAsync(h, sel, sizeof(int) * 8, cudaMemcpyDeviceToHost, s));
-        GPB2_CUDA_TRY(cudaStreamSynchronize(s));
-        if (h[6] != 0)  // error word of the barrier (lad[22])
-            return set_error(GPB2_ERR_TIMEOUT, "dense factorisation barrier timed out");
-        if (h[0] >= 0) {
-            p->Ld = base + (size_t)h[0] * nn;
-            p->dense_jitter = (double)epsv[first + h[0]];
-            p->dense_candidate = first + h[0];
-            return GPB2_OK;
+        GPB2_CUDA_TRY(launch_prof("dense_mark", k_ladder_mark, dim3(1), dim3(1), 0, s,
+                                  (const int*)done, nc, first, sel));
+        if (trace) {  // diagnostics: per-phase totals of the last candidate of this launch
+            std::vector<unsigned long long> h(8 * (size_t)npan);
+            GPB2_CUDA_TRY(cudaMemcpyAsync(h.data(), trace, sizeof(unsigned long long) * h.size(),
+                                          cudaMemcpyDeviceToHost, s));
+            GPB2_CUDA_TRY(cudaStreamSynchronize(s));
+            // Per-panel intervals of rank 0: P load, P solve, P store, barrier + U tile 0, D load,
+            // D factor, D store + U rest, barrier.
+            double sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            int kk = 0;
+            for (; kk + 1 < npan && h[8 * (kk + 1)] != 0; kk++)
+                for (int q = 0; q < 8; q++) {
+                    const unsigned long long t1 = q < 7 ? h[8 * kk + q + 1] : h[8 * (kk + 1)];
+                    if (t1 && h[8 * kk + q]) sum[q] += (double)(t1 - h[8 * kk + q]);
+                }
+            std::fprintf(stderr,
+                         "gpb2 dense trace: n0=%lld cluster=%d tile=%d panels=%d/%d us: Pload %.1f "
+                         "Psolve %.1f Pstore %.1f bar+tile0 %.1f Dload %.1f Dfactor %.1f "
+                         "Dstore+Urest %.1f bar %.1f\n",
+                         (long long)n, csize, tile, kk, npan, sum[0] / 1e3, sum[1] / 1e3,
+                         sum[2] / 1e3, sum[3] / 1e3, sum[4] / 1e3, sum[5] / 1e3, sum[6] / 1e3,
+                         sum[7] / 1e3);
+            if (std::atoi(std::getenv("GPB2_TRACE_DENSE")) >= 2) {
+                for (int q = 0; q < 8; q++) {
+                    std::fprintf(stderr, "  interval %d:", q);
+                    for (int k2 = 0; k2 < kk; k2++) {
+                        const unsigned long long t1 =
+                            q < 7 ? h[8 * k2 + q + 1] : h[8 * (k2 + 1)];
+                        std::fprintf(stderr, " %.1f",
+                                     (t1 && h[8 * k2 + q]) ? (t1 - h[8 * k2 + q]) / 1e3 : -1.0);
+                    }
+                    std::fprintf(stderr, "\n");
+                }
+            }
         }
     }
-    return set_error(GPB2_ERR_NOT_PD,
-                     "dense first-layer covariance is not positive definite even with 1e-2 "
-                     "relative jitter; increase the kernel `jitter` or reduce n0");
+    GPB2_CUDA_TRY(launch_prof("dense_pick", k_ladder_pick<T>, dim3(4 * 148), dim3(256), 0, s,
+                              (const T*)base, (const int*)sel, (int64_t)nn,
+                              static_cast<T*>(p->Ld), p->lad + kLadNotPD));
+    p->ladder_eps.assign(epsv.begin(), epsv.begin() + ncand_used);
+    p->dense_pending = true;  // outcome checked by the call's finishing synchronisation
+    return GPB2_OK;
 }
 
 template int dense_cholesky_ladder<float>(gpb2_problem*, cudaStream_t);

@@ -440,7 +440,9 @@ k_sweep_fwd_all(T* __restrict__ values, const T* __restrict__ xi_ref, const T* _
                 const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
                 const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
     using N = Num<T>;
-    const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    // Consecutive points go to consecutive CTAs (one per SM), so a small batch is spread over
+    // every SM's load units instead of queueing on the first few.
+    const int64_t gtid = (int64_t)threadIdx.x * gridDim.x + blockIdx.x;
     const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
     SweepPoint<T, K> sp;
     int64_t p = offs[0] + gtid;
@@ -474,7 +476,9 @@ k_sweep_rev_all(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv
                 const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
                 const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
     using N = Num<T>;
-    const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    // Consecutive points go to consecutive CTAs (one per SM), so a small batch is spread over
+    // every SM's load units instead of queueing on the first few.
+    const int64_t gtid = (int64_t)threadIdx.x * gridDim.x + blockIdx.x;
     const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
     SweepPoint<T, K> sp;
     int64_t p = offs[nbatch - 1] + gtid;

@@ -115,7 +115,7 @@ struct Impl {
                                                    (const T*)p->sd, p->nbrs, p->n0, p->d_offsets,
                                                    nbatch(p), grid_sync_of(p), s),
                                   "forward sweep"));
-            return check_sync(p, s);
+            return GPB2_OK;  // the barrier's error word is read when the call finishes
         }
         for (size_t b = 1; b < p->offsets.size(); b++)
             GPB2_TRY(check_launch(o->sweep_fwd(values, xi_ref, (const T*)p->mv,
@@ -134,7 +134,7 @@ struct Impl {
                                                    p->nbrs, p->n0, p->d_offsets, nbatch(p),
                                                    grid_sync_of(p), s),
                                   "reverse sweep"));
-            return check_sync(p, s);
+            return GPB2_OK;
         }
         for (size_t b = p->offsets.size() - 1; b >= 1; b--)
             GPB2_TRY(check_launch(o->sweep_rev(xg, vb, (const T*)p->mv, (const T*)p->sd, p->nbrs,
@@ -147,20 +147,10 @@ struct Impl {
     static GridSync grid_sync_of(P* p) {
         return GridSync{p->dsync, reinterpret_cast<int*>(p->dsync + 2)};
     }
-    // Zero the barrier words before a cooperative launch.
+    // Zero the barrier words before a cooperative launch (the error word accumulates over the
+    // call and is cleared by finish_call).
     static int arm_sync(P* p, cudaStream_t s) {
-        GPB2_CUDA_TRY(cudaMemsetAsync(p->dsync, 0, 4 * sizeof(unsigned int), s));
-        return GPB2_OK;
-    }
-    // The cooperative kernels' barriers are bounded: read the error word they leave behind
-    // (one small copy on the stream) and report a timeout instead of returning garbage.
-    static int check_sync(P* p, cudaStream_t s) {
-        unsigned int h = 0;
-        GPB2_CUDA_TRY(cudaMemcpyAsync(&h, p->dsync + 2, sizeof(h), cudaMemcpyDeviceToHost, s));
-        GPB2_CUDA_TRY(cudaStreamSynchronize(s));
-        if (h != 0)
-            return set_error(GPB2_ERR_TIMEOUT,
-                             "a grid barrier of the persistent sweep timed out (error word %u)", h);
+        GPB2_CUDA_TRY(cudaMemsetAsync(p->dsync, 0, 2 * sizeof(unsigned int), s));
         return GPB2_OK;
     }
 
@@ -366,6 +356,36 @@ struct Impl {
     }
 };
 
+// Every call ends here: one synchronisation of the stream, after which the status words the
+// device left behind are read -- a grid barrier that timed out (persistent sweeps, dense
+// factorisation) or a dense block that no ladder step could factorise (src/dense.jl:65-66).
+// The reference's drivers also synchronise before returning (e.g. src/api.jl:139).
+static int finish_call(gpb2_problem* p, cudaStream_t s) {
+    int h[3] = {0, 0, 0};
+    GPB2_CUDA_TRY(cudaMemcpyAsync(&h[0], p->dsync + 2, sizeof(int), cudaMemcpyDeviceToHost, s));
+    const bool dense = p->dense_pending && p->lad;
+    if (dense) {
+        GPB2_CUDA_TRY(
+            cudaMemcpyAsync(&h[1], p->lad + kLadNotPD, sizeof(int), cudaMemcpyDeviceToHost, s));
+        GPB2_CUDA_TRY(
+            cudaMemcpyAsync(&h[2], p->lad + kLadBarErr, sizeof(int), cudaMemcpyDeviceToHost, s));
+    }
+    GPB2_CUDA_TRY(cudaStreamSynchronize(s));
+    p->dense_pending = false;
+    if (dense) p->dense_valid = h[0] == 0 && h[1] == 0 && h[2] == 0;
+    if (h[0] != 0) {
+        cudaMemsetAsync(p->dsync + 2, 0, sizeof(int), s);
+        return set_error(GPB2_ERR_TIMEOUT, "a grid barrier of a persistent sweep timed out");
+    }
+    if (dense && h[2] != 0)
+        return set_error(GPB2_ERR_TIMEOUT, "a grid barrier of the dense factorisation timed out");
+    if (dense && h[1] != 0)
+        return set_error(GPB2_ERR_NOT_PD,
+                         "dense first-layer covariance is not positive definite even with 1e-2 "
+                         "relative jitter; increase the kernel `jitter` or reduce n0");
+    return GPB2_OK;
+}
+
 }  // namespace gpb2
 
 using namespace gpb2;
@@ -377,8 +397,12 @@ using namespace gpb2;
         DeviceGuard _dg((p)->device);                                                          \
         if (!_dg.ok) return set_error(GPB2_ERR_NO_DEVICE, "cudaSetDevice(%d) failed", (p)->device); \
         cudaStream_t s = (cudaStream_t)stream;                                                 \
-        (void)s;                                                                               \
-        return (p)->dtype == GPB2_F32 ? (CALL32) : (CALL64);                                   \
+        const int _st = (p)->dtype == GPB2_F32 ? (CALL32) : (CALL64);                           \
+        if (_st != GPB2_OK) {                                                                  \
+            p->dense_pending = false;                                                          \
+            return _st;                                                                        \
+        }                                                                                      \
+        return finish_call(p, s);                                                              \
     } while (0)
 
 #define F32(x) static_cast<float*>(const_cast<void*>(x))

@@ -192,6 +192,7 @@ static int build_table(gpb2_problem* p, const T* hb, const T* hv, cudaStream_t s
 
 static int load_table(gpb2_problem* p, const void* vals_dev, cudaStream_t s) {
     const size_t ts = tsize(p);
+    p->dense_valid = false;  // the dense factor belongs to the previous table
     GPB2_CUDA_TRY(cudaMemcpyAsync(p->vals, vals_dev, ts * p->nb, cudaMemcpyDeviceToDevice, s));
     std::vector<unsigned char> hb(ts * p->nb), hv(ts * p->nb);
     GPB2_CUDA_TRY(cudaMemcpyAsync(hb.data(), p->bins, ts * p->nb, cudaMemcpyDeviceToHost, s));
@@ -208,7 +209,7 @@ static void free_problem(gpb2_problem* p) {
     void* bufs[] = {p->coords, p->nbrs, p->indices, p->bins, p->vals,  p->seg,
                     p->start,  p->mv,   p->sd,      p->buf_a, p->buf_b, p->buf_c,
                     p->buf_d,  p->dacc, p->Lcand,   p->lad,  p->Wd,    p->Wd2,
-                    p->dwork,  p->dinfo, p->d_offsets, p->dsync};
+                    p->dwork,  p->dinfo, p->d_offsets, p->dsync, p->Ld,    p->trace};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);
@@ -306,6 +307,7 @@ int gpb2_problem_create(gpb2_problem** out, int dtype, int device, const uint32_
             break;
         if ((st = ensure_alloc(reinterpret_cast<void**>(&p->dsync), 4 * sizeof(unsigned int))))
             break;
+        cudaMemsetAsync(p->dsync, 0, 4 * sizeof(unsigned int), s);
         int64_t* doffs = p->d_offsets;
         unsigned long long* dbad = nullptr;
         if ((st = ensure_alloc(reinterpret_cast<void**>(&dbad), 2 * sizeof(unsigned long long))))
@@ -404,7 +406,12 @@ int gpb2_problem_info(const gpb2_problem* p, int64_t* n, int64_t* m, int64_t* k,
 
 int gpb2_problem_dense_jitter(const gpb2_problem* p, double* eps) {
     if (!p || !eps) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_dense_jitter: NULL");
-    *eps = p->dense_candidate < 0 ? -1.0 : p->dense_jitter;
+    *eps = -1.0;
+    if (!p->lad || p->ladder_eps.empty()) return GPB2_OK;
+    DeviceGuard dg(p->device);
+    int sel = -1;
+    GPB2_CUDA_TRY(cudaMemcpy(&sel, p->lad + kLadSel, sizeof(int), cudaMemcpyDeviceToHost));
+    if (sel >= 0 && sel < (int)p->ladder_eps.size()) *eps = p->ladder_eps[sel];
     return GPB2_OK;
 }
 

@@ -42,9 +42,14 @@ struct gpb2_problem {
     double* dacc = nullptr;  // nb histogram + 8 scalars (double accumulators)
 
     // Dense n0 block.
-    void* Ld = nullptr;       // the selected ladder candidate inside Lcand (not owned)
+    void* Ld = nullptr;       // (n0, n0) column-major lower: the selected ladder candidate
     void* Lcand = nullptr;    // ladder candidates, each (n0, n0) column-major lower
-    int* lad = nullptr;       // ladder flags: fail[16], select, jitters
+    int* lad = nullptr;       // ladder status (layout: kLad* in gpb2::) + jitters
+    std::vector<double> ladder_eps;  // eps of each ladder index of the last factorisation
+    void* trace = nullptr;           // diagnostics buffer (GPB2_TRACE_DENSE)
+    bool dense_pending = false;      // a factorisation was launched and not yet checked
+    bool dense_valid = false;        // Ld holds the checked factor of the current table; reused
+                                     // by every call until the table changes
     int dense_candidate = -1;
     void* Wd = nullptr;       // (n0, n0) work
     void* Wd2 = nullptr;      // (n0, n0) work
@@ -60,6 +65,14 @@ struct gpb2_problem {
 };
 
 namespace gpb2 {
+
+// Layout of gpb2_problem::lad (ints), then 16 T of ladder jitters.
+constexpr int kLadFail = 0;     // [0, 16): per-candidate failing column + 1
+constexpr int kLadDone = 16;    // [16, 32): per-candidate completion flags
+constexpr int kLadSel = 32;     // ladder index of the first success (-1: none), then its slot
+constexpr int kLadNotPD = 34;   // set when no candidate succeeded
+constexpr int kLadBarErr = 36;  // error word of the factorisation (0: none)
+constexpr int kLadInts = 48;
 
 // RAII: make the problem's device current for the duration of a call, restore afterwards.
 struct DeviceGuard {

@@ -3,8 +3,13 @@
 // The kernels that use it are launched with cudaLaunchCooperativeKernel, so every CTA of the
 // grid is resident and a barrier cannot deadlock by construction.  The wait is still bounded:
 // after kSpinLimit polls a CTA records GPB2_SYNC_TIMEOUT in the shared error word and every CTA
-// leaves at its next barrier, so a fault elsewhere can never turn into a hung GPU.  The host reads
-// the error word after the launch and reports GPB2_ERR_TIMEOUT.
+// leaves at its next barrier, so a fault elsewhere can never turn into a hung GPU.  The host
+// reads the error word after the launch and reports GPB2_ERR_TIMEOUT.
+//
+// Arrival is one atomic per CTA on a single word: CTA 0 adds 2^31 - (nblocks - 1), every other
+// CTA adds 1, so the word's top bit flips exactly when the last CTA arrives and the low bits are
+// back where they started; a CTA waits for the top bit to differ from the value it saw on
+// arrival.  The word must be zero before the launch.
 #pragma once
 #include <cuda_runtime.h>
 
@@ -13,40 +18,44 @@ namespace gpb2 {
 constexpr int GPB2_SYNC_TIMEOUT = 1;
 
 struct GridSync {
-    unsigned int* bar;  // [0] arrivals, [1] generation (zeroed before the launch)
+    unsigned int* bar;  // arrival word (zeroed before the launch)
     int* err;           // error word (zeroed before the launch)
 };
 
-// ~2^22 polls x ~256 ns: a few seconds at most, far above any legitimate wait.
-constexpr unsigned int kSpinLimit = 1u << 22;
+// ~2^24 polls of an L2-resident word: well over a second, far above any legitimate wait.
+constexpr unsigned int kSpinLimit = 1u << 24;
+
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_relaxed_gpu(const int* p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 // All threads of all CTAs call this; returns false if the grid must stop (timeout anywhere).
 __device__ __forceinline__ bool grid_sync(const GridSync& gs) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-        int ok = 1;
-        volatile unsigned int* gen = gs.bar + 1;
-        const unsigned int g = *gen;
-        __threadfence();
         const unsigned int nb = gridDim.x * gridDim.y * gridDim.z;
-        if (atomicAdd(gs.bar, 1u) == nb - 1) {
-            atomicExch(gs.bar, 0u);
-            __threadfence();
-            atomicAdd(const_cast<unsigned int*>(gen), 1u);
-        } else {
-            unsigned int it = 0;
-            while (*gen == g) {
-                if (++it > kSpinLimit || *(volatile int*)gs.err) {
-                    atomicCAS(gs.err, 0, GPB2_SYNC_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(256);
+        const bool lead = (blockIdx.x | blockIdx.y | blockIdx.z) == 0;
+        const unsigned int add = lead ? (0x80000000u - (nb - 1u)) : 1u;
+        __threadfence();
+        const unsigned int old = atomicAdd(gs.bar, add);
+        int ok = 1;
+        unsigned int it = 0;
+        while (((old ^ ld_acquire_gpu(gs.bar)) & 0x80000000u) == 0u) {
+            if ((++it & 1023u) == 0u && (it > kSpinLimit || ld_relaxed_gpu(gs.err))) {
+                atomicCAS(gs.err, 0, GPB2_SYNC_TIMEOUT);
+                ok = 0;
+                break;
             }
         }
-        __threadfence();
-        if (*(volatile int*)gs.err) ok = 0;
+        if (ok && ld_relaxed_gpu(gs.err)) ok = 0;
         s_ok = ok;
     }
     __syncthreads();

@@ -149,6 +149,23 @@ class GraphGPProblem:
             _lib.check(st, "GraphGPProblem upload")
         return h
 
+    def update_vals(self, vals) -> "GraphGPProblem":
+        """Replace the covariance table in place (same bins; the handle and its device graph are
+        kept).  The dense block is refactorised by the next call that needs it; until then every
+        call reuses the factor of the current table."""
+        if self._handle is None:
+            self.vals = vals
+            return self
+        v = self._dev(vals, self.torch_dtype)
+        if v.numel() != self.nbins():
+            raise ValueError(f"vals has {v.numel()} entries, the table has {self.nbins()} bins")
+        st = _lib.lib().gpb2_problem_set_vals(
+            self.handle, C.c_void_p(v.data_ptr()),
+            C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        _lib.check(st, "update_vals")
+        self.vals = vals
+        return self
+
     def dense_jitter(self) -> float:
         """Relative jitter of the dense block's last factorisation (0.0 = none needed, -1.0 =
         not factorised yet), the ladder of src/dense.jl:46-67."""

@@ -244,6 +244,32 @@ def test_dense_factor_bit_exact(cuda_device, dt, n0, N):
     assert np.array_equal(L_dev, np.tril(L_ora))
 
 
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_update_vals_refactors(cuda_device, dt):
+    # The handle reuses the dense factor across calls until the table changes; a new table must
+    # give exactly what a fresh handle (and the oracle) gives for it, and switching back must
+    # reproduce the first result bit for bit.
+    prob, _ = _config_problem(3000, 2, 200, 8, dt, 21)
+    xi = np.random.default_rng(8).standard_normal(prob.npoints()).astype(dt)
+    f1 = gp.generate(prob, xi)
+    f1b = gp.generate(prob, xi)  # reuses the factor
+    assert np.array_equal(f1, f1b)
+    bins_b, vals_b = gp.rbf_kernel(1.3, 0.5, 1e-4, 10.0, 1000, jitter=1e-5)
+    assert np.allclose(bins_b.astype(dt), prob.bins)
+    prob.update_vals(vals_b.astype(dt))
+    f2 = gp.generate(prob, xi)
+    L2 = prob.dense_factor()
+    fresh = gp.set_vals(prob, vals_b.astype(dt))
+    assert np.array_equal(f2, gp.generate(fresh, xi))
+    orc_b = O.make_problem(prob.coords, prob.neighbors, prob.offsets, prob.n0, dt(prob.scale),
+                           prob.bins, vals_b.astype(dt), prob.indices, dt)
+    L_ora, _ = O.dense_chol(orc_b)
+    assert np.array_equal(L2, np.tril(L_ora))
+    assert relerr(f2, O.generate(orc_b, xi)) < TOL[dt]
+    prob.update_vals(gp.rbf_kernel(1.0, 0.3, 1e-4, 10.0, 1000, jitter=1e-5)[1].astype(dt))
+    assert np.array_equal(gp.generate(prob, xi), f1)
+
+
 def test_degenerate_duplicates(cuda_device):
     # test/test_degenerate.jl: 30 exact duplicate points must give finite results everywhere.
     rng = np.random.default_rng(0xDEAD)
