@@ -93,6 +93,7 @@ _SIGNATURES = {
     "gpb2_refine_logdet_terms": (I32, [P, P, P]),
     "gpb2_refine_logdet": (I32, [P, PD, P]),
     "gpb2_refine_logdet_grad_vals": (I32, [P, P, PD, P]),
+    "gpb2_refine_logdet_grad_vals_noalloc": (I32, [P, P, PD, P]),
     "gpb2_refine_inv_loss_grad_vals": (I32, [P, P, P, PD, P]),
     "gpb2_generate": (I32, [P, P, P, P]),
     "gpb2_generate_inv": (I32, [P, P, P, P]),

@@ -171,6 +171,21 @@ def refine_logdet_grad_vals(prob: GraphGPProblem):
     return _ret(out, prob.host_arrays)
 
 
+def refine_logdet_grad_vals_noalloc(prob: GraphGPProblem, out: torch.Tensor | None = None):
+    """refine_logdet_grad_vals computed without any device allocation inside the library call
+    (a fixed per-device accumulator; nbins <= 4096, overlapping calls on one device race).
+    ``out``: optional caller-owned device tensor of nbins entries in the problem's dtype."""
+    if out is None:
+        out = _empty(prob, prob.nbins())
+    elif (not isinstance(out, torch.Tensor) or out.device != prob.device
+          or out.dtype != prob.torch_dtype or out.numel() != prob.nbins()
+          or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous device tensor of nbins entries in the "
+                         "problem's dtype on the problem's device")
+    _call("gpb2_refine_logdet_grad_vals_noalloc", prob.handle, _ptr(out), None, _stream(prob))
+    return _ret(out, prob.host_arrays)
+
+
 def generate_logdet_grad_vals(prob: GraphGPProblem):
     """d(generate_logdet)/d(vals) (src/grad.jl:149-154)."""
     out = _empty(prob, prob.nbins())

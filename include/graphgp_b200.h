@@ -137,6 +137,18 @@ int gpb2_refine_logdet(gpb2_problem* prob, double* logdet_host, void* stream);
 int gpb2_refine_logdet_grad_vals(gpb2_problem* prob, void* dvals_dev, double* logdet_host,
                                  void* stream);
 
+/* refine_logdet_grad_vals_noalloc: the same result as gpb2_refine_logdet_grad_vals, computed
+ * without allocating any device memory during the call.  It has no counterpart in the
+ * reference; it serves callers whose framework allocator (CUDA.jl's pool, PyTorch's caching
+ * allocator) holds the free HBM, or who cannot afford the device synchronisation of a cudaMalloc,
+ * at the point of the call.  The histogram lives in a fixed __device__ array of 4096 + 8 doubles
+ * per device, cleared by the call on `stream`.  Limits: nbins <= 4096 (else
+ * GPB2_ERR_INVALID_ARG); calls that overlap in time on one device (other threads, streams or
+ * problems) race on the shared array; the first call on each device must be made outside stream
+ * capture (it resolves the array's address).  Synchronous, like the allocating form. */
+int gpb2_refine_logdet_grad_vals_noalloc(gpb2_problem* prob, void* dvals_dev,
+                                         double* logdet_host, void* stream);
+
 /* refine_inv_loss_grad_vals: loss = 0.5*||refine_inv(values)||^2 and its vals-gradient.
  * Replaces src/grad.jl:630-671 (refine_inv_loss_grad_hist_kernel!, src/kernels_adjoint.jl:155-221). */
 int gpb2_refine_inv_loss_grad_vals(gpb2_problem* prob, const void* values_dev, void* dvals_dev,
