@@ -171,9 +171,9 @@ __global__ void k_sum_sq_half(const T* __restrict__ z, int64_t n, double* __rest
 //   mode 0: S (full n x n):     g_ij = S_ij + S_ji (i > j), g_ii = S_ii
 //   mode 1: Kinv (lower valid): g_ij = Kinv_ij,             g_ii = Kinv_ii / 2
 //   mode 2: alpha (vector):     g_ij = -alpha_i * alpha_j,   g_ii = -alpha_i^2 / 2
-template <typename T>
+template <typename T, typename MT>
 __global__ void k_dense_scatter(TableView<T> tv, const uint32_t* __restrict__ coords, int D,
-                                int DS, T scale, int64_t n, int mode, const T* __restrict__ A,
+                                int DS, T scale, int64_t n, int mode, const MT* __restrict__ A,
                                 double* __restrict__ gacc) {
     using N = Num<T>;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -184,6 +184,20 @@ __global__ void k_dense_scatter(TableView<T> tv, const uint32_t* __restrict__ co
     __syncthreads();
     for (int64_t j = blockIdx.x; j < n; j += gridDim.x) {
         for (int64_t i = j + threadIdx.x; i < n; i += blockDim.x) {
+            if constexpr (!std::is_same<MT, T>::value) {  // double S from the triangular path
+                const double g = i == j ? (double)A[j * n + j]
+                                        : (double)A[j * n + i] + (double)A[i * n + j];
+                if (i == j) {
+                    atomicAdd(&hist[0], g);
+                } else {
+                    T wlo, whi;
+                    const int lo =
+                        tab.weights(pair_radius<T>(coords, DS, D, i, j, scale), wlo, whi);
+                    atomicAdd(&hist[lo], g * (double)wlo);
+                    atomicAdd(&hist[lo + 1], g * (double)whi);
+                }
+                continue;
+            } else {
             T g;
             if (mode == 0) g = i == j ? A[j * n + j] : N::add(A[j * n + i], A[i * n + j]);
             else if (mode == 1) g = i == j ? N::mul(T(0.5), A[j * n + j]) : A[j * n + i];
@@ -195,6 +209,7 @@ __global__ void k_dense_scatter(TableView<T> tv, const uint32_t* __restrict__ co
                 const int lo = tab.weights(pair_radius<T>(coords, DS, D, i, j, scale), wlo, whi);
                 atomicAdd(&hist[lo], (double)N::mul(g, wlo));
                 atomicAdd(&hist[lo + 1], (double)N::mul(g, whi));
+            }
             }
         }
     }
@@ -211,12 +226,12 @@ int grid_for(int64_t n) {
     return (int)(g < 1 ? 1 : (g > 4096 ? 4096 : g));
 }
 
-template <typename T>
-int scatter(gpb2_problem* p, int mode, const T* A, double* hist, cudaStream_t s) {
+template <typename T, typename MT = T>
+int scatter(gpb2_problem* p, int mode, const MT* A, double* hist, cudaStream_t s) {
     const size_t smem = table_smem_bytes<T>((int)p->nb, p->nkeys) + sizeof(double) * p->nb;
-    GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_dense_scatter<T>, smem));
+    GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_dense_scatter<T, MT>, smem));
     const int grid = (int)std::min<int64_t>(p->n0, 2 * 148);
-    GPB2_CUDA_TRY(launch_prof("dense_scatter", k_dense_scatter<T>, dim3(grid),
+    GPB2_CUDA_TRY(launch_prof("dense_scatter", k_dense_scatter<T, MT>, dim3(grid),
                               dim3(kDenseThreads), smem, s, table_view<T>(p),
                               (const uint32_t*)p->coords, (int)p->d, coord_stride((int)p->d),
                               (T)p->scale, p->n0, mode, A, hist));
@@ -252,11 +267,25 @@ int Dense<T>::factor(gpb2_problem* p, cudaStream_t s) {
     // factor of the current table is reused (the table setter clears the flag).
     if (p->dense_valid) return GPB2_OK;
     GPB2_TRY(ensure_dense(p));
-    return dense_cholesky_ladder<T>(p, s);  // gpb2_dense_chol.cu
+    p->tri_ready = false;
+    GPB2_TRY(dense_cholesky_ladder<T>(p, s));  // gpb2_dense_chol.cu
+    if (dense_tri_supported<T>(p)) {
+        GPB2_TRY(dense_tri_prepare<T>(p, s));   // gpb2_dense_tri.cu
+        p->tri_ready = true;
+    }
+    return GPB2_OK;
 }
 
 template <typename T>
 int Dense<T>::apply_L(gpb2_problem* p, const T* x, T* y, cudaStream_t s) {
+    if (p->tri_ready) {
+        if (x == y) {
+            GPB2_CUDA_TRY(cudaMemcpyAsync(p->Wd2, x, sizeof(T) * p->n0, cudaMemcpyDeviceToDevice,
+                                          s));
+            x = static_cast<const T*>(p->Wd2);
+        }
+        return dense_trmv<T>(p, false, x, y, s);
+    }
     if (x != y)
         GPB2_CUDA_TRY(cudaMemcpyAsync(y, x, sizeof(T) * p->n0, cudaMemcpyDeviceToDevice, s));
     GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
@@ -266,6 +295,14 @@ int Dense<T>::apply_L(gpb2_problem* p, const T* x, T* y, cudaStream_t s) {
 
 template <typename T>
 int Dense<T>::apply_Lt(gpb2_problem* p, const T* x, T* y, cudaStream_t s) {
+    if (p->tri_ready) {
+        if (x == y) {
+            GPB2_CUDA_TRY(cudaMemcpyAsync(p->Wd2, x, sizeof(T) * p->n0, cudaMemcpyDeviceToDevice,
+                                          s));
+            x = static_cast<const T*>(p->Wd2);
+        }
+        return dense_trmv<T>(p, true, x, y, s);
+    }
     if (x != y)
         GPB2_CUDA_TRY(cudaMemcpyAsync(y, x, sizeof(T) * p->n0, cudaMemcpyDeviceToDevice, s));
     GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
@@ -296,6 +333,11 @@ int Dense<T>::grad_vals(gpb2_problem* p, const T* vb, const T* xi, double* hist,
     T* W = static_cast<T*>(p->Wd);
     T* X = static_cast<T*>(p->Wd2);
     const T* L = static_cast<const T*>(p->Ld);
+    if (p->tri_ready) {  // S = L^-T Phi(tril((L^T vb) xi^T)) L^-1 by the triangular kernels
+        const T* S = nullptr;
+        GPB2_TRY(dense_chol_pullback_outer<T>(p, vb, xi, &S, s));
+        return scatter<T>(p, 0, S, hist, s);
+    }
     GPB2_CUDA_TRY(launch_prof("dense_outer", k_outer_tril<T>, dim3(grid_for<T>(nn)),
                               dim3(kDenseThreads), 0, s, vb, xi, (int64_t)n, W));
     GPB2_BLAS_TRY(cublasSetStream(p->blas, s));

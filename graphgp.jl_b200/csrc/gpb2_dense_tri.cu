@@ -1,0 +1,389 @@
+// gpb2_dense_tri.cu -- triangular kernels of the dense first layer: L*x, L^T*x and the Cholesky
+// pullback of generate_grad_vals (src/grad_generate_vals.jl:252-280).
+//
+// L*x and L^T*x (generate_dense, the dense adjoint of generate_grad_xi) accumulate each output
+// from 0 in ascending index with rounded multiplies and adds, the oracle's order, so the dense
+// layer's contribution to generate and generate_grad_xi is bit-identical to it.  Each CTA owns 32
+// outputs; its other warps stream the factor through shared memory while warp 0 runs the 32
+// sequential sums.
+//
+// The pullback of f = L*xi with cotangent vb is  S = L^-T Phi(L^T Lbar) L^-1  with
+// Lbar = tril(vb xi^T) (Phi: lower triangle, halved diagonal).  Because L^T is upper triangular,
+// (L^T Lbar)_ij = xi_j * sum_{k >= max(i,j)} L_ki vb_k, which for i >= j is xi_j * u_i with
+// u = L^T vb.  So Phi(L^T Lbar) = Phi(tril(u xi^T)) needs one matrix-vector product instead of a
+// triangular matrix product, and it is generated on the fly from u and xi.
+//
+// S is then two triangular solves with n right-hand sides:  X = L^-T P  and  S^T = L^-T X^T.
+// k_trsm_lt solves L^T X = B for a chunk of NB right-hand-side columns per CTA, by 32-row blocks
+// from the bottom: the rows already solved stay in shared memory; the block's right-hand side is
+// reduced against them with the factor streamed through a cp.async pipeline of 64-row tiles
+// (lanes along the block's 32 columns, warps along the tile's rows), and the block is finished by
+// a product with the transposed inverse of its 32x32 diagonal block (computed once per
+// factorisation by k_diag_inv, in parallel over blocks), so no step carries a chain of
+// divisions.  The output is written transposed, which is the right-hand side of the second solve.
+// The pullback is not an exact-order computation (neither is the reference's BLAS); it uses
+// fused multiply-adds.
+#include <algorithm>
+
+#include <cuda_pipeline_primitives.h>
+
+#include "gpb2_problem.h"
+
+namespace gpb2 {
+
+namespace {
+
+constexpr int kTB = 32;        // diagonal block size
+constexpr int kTriThreads = 256;
+constexpr int kTriWarps = kTriThreads / 32;
+constexpr int kDiagWarps = 4;  // k_diag_inv: blocks per CTA (its staging fits 48 KB in f64)
+constexpr int kTileRows = 64;  // rows of the factor per pipeline stage in k_trsm_lt
+
+template <typename T>
+__host__ __device__ constexpr int tri_stages() { return sizeof(T) == 4 ? 6 : 4; }
+
+// Pitch of the row-major copy: rows start on 128-byte boundaries (cp.async needs 16).
+inline int64_t tri_pitch(int64_t n) { return (n + 31) / 32 * 32; }
+
+// Row-major copy: R[i*ld + j] = L[i][j] = L_colmajor[i + j*n] (lower part; upper zero).
+template <typename T>
+__global__ void k_transpose_lower(const T* __restrict__ L, T* __restrict__ R, int64_t n,
+                                  int64_t ld) {
+    __shared__ T tile[32][33];
+    const int64_t nb = (n + 31) / 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (int64_t t = blockIdx.x; t < nb * nb; t += gridDim.x) {
+        const int64_t bi = t / nb, bj = t - bi * nb;  // output tile: rows bi*32.., cols bj*32..
+        for (int yy = ty; yy < 32; yy += blockDim.x / 32) {
+            const int64_t row = bi * 32 + tx, col = bj * 32 + yy;  // tile[yy][tx] = L[row][col]
+            tile[yy][tx] = (row < n && col < n) ? L[row + col * n] : T(0);
+        }
+        __syncthreads();
+        for (int yy = ty; yy < 32; yy += blockDim.x / 32) {
+            const int64_t i = bi * 32 + yy, j = bj * 32 + tx;  // R[i][j] = L[i][j]
+            if (i < n && j < ld) R[i * ld + j] = (j <= i && j < n) ? tile[tx][yy] : T(0);
+        }
+        __syncthreads();
+    }
+}
+
+// Exact-order L*x (TRANS = false) and L^T*x (TRANS = true), outputs [i0, i0 + 32) per CTA.
+//   L x:   y_i = sum_{j=0..i} L[i][j] x_j   (column-major factor: M(i, j) = L[i + j*n])
+//   L^T x: y_i = sum_{k=i..n-1} L[k][i] x_k (row-major copy:     M(i, k) = R[k*ld + i])
+// Warps 1.. load stage c+1 while warp 0 (lane = output) adds up stage c.
+template <typename T, bool TRANS>
+__global__ void __launch_bounds__(kTriThreads)
+k_trmv_exact(const T* __restrict__ M, int64_t ld, const T* __restrict__ x, T* __restrict__ y,
+             int64_t n) {
+    using N = Num<T>;
+    constexpr int kTrmvChunk = 512 / (int)sizeof(T);  // rows per stage: 2 x 16 KB of tiles
+    __shared__ T tile[2][kTrmvChunk][32];
+    __shared__ T xs[2][kTrmvChunk];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t i0 = (int64_t)blockIdx.x * 32, i = i0 + lane;
+    const int64_t lo = TRANS ? i0 : 0;  // summation index range
+    const int64_t hi = TRANS ? n : (i0 + 32 < n ? i0 + 32 : n);
+    const int64_t nch = (hi - lo + kTrmvChunk - 1) / kTrmvChunk;
+    auto load = [&](int64_t c, int buf, int t0, int nt) {
+        for (int e = t0; e < kTrmvChunk * 32; e += nt) {
+            const int kk = e >> 5, ii = e & 31;
+            const int64_t k = lo + c * kTrmvChunk + kk, r = i0 + ii;
+            T v = T(0);
+            if (k < hi && r < n) v = TRANS ? M[k * ld + r] : M[r + k * n];
+            tile[buf][kk][ii] = v;
+        }
+        for (int kk = t0; kk < kTrmvChunk; kk += nt) {
+            const int64_t k = lo + c * kTrmvChunk + kk;
+            xs[buf][kk] = k < hi ? x[k] : T(0);
+        }
+    };
+    load(0, 0, threadIdx.x, kTriThreads);
+    __syncthreads();
+    T acc = T(0);
+    for (int64_t c = 0; c < nch; c++) {
+        const int buf = (int)(c & 1);
+        if (w != 0) {
+            if (c + 1 < nch) load(c + 1, buf ^ 1, threadIdx.x - 32, kTriThreads - 32);
+        } else {
+            const int64_t k0 = lo + c * kTrmvChunk;
+            for (int kk = 0; kk < kTrmvChunk; kk++) {
+                const int64_t k = k0 + kk;
+                if (k >= hi) break;
+                if (TRANS ? (k >= i) : (k <= i))
+                    acc = N::add(acc, N::mul(tile[buf][kk][lane], xs[buf][kk]));
+            }
+        }
+        __syncthreads();
+    }
+    if (w == 0 && i < n) y[i] = acc;
+}
+
+// Transposed inverses of the 32x32 diagonal blocks of L: DinvT[b][j][i] = (L_bb^-1)[i][j].
+// One warp per block; lane j solves L_bb d = e_j by forward substitution.
+template <typename T>
+__global__ void k_diag_inv(const T* __restrict__ Lr, int64_t n, int64_t ld,
+                           T* __restrict__ DinvT) {
+    __shared__ T S[kDiagWarps][kTB][kTB + 1];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t nbk = (n + kTB - 1) / kTB;
+    const int64_t b = (int64_t)blockIdx.x * kDiagWarps + w;
+    if (b >= nbk) return;  // warp-uniform; no block-wide barrier below
+    const int64_t r0 = b * kTB;
+    const int bs = (int)(n - r0 < kTB ? n - r0 : kTB);
+    for (int i = 0; i < kTB; i++)
+        S[w][i][lane] = (i < bs && lane <= i) ? Lr[(r0 + i) * ld + r0 + lane] : T(0);
+    __syncwarp();
+    T d[kTB] = {};
+    sfor<0, kTB>([&](auto i_) {
+        GPB2_CI(i);
+        T s = (i == lane) ? T(1) : T(0);
+        sfor<0, i>([&](auto k_) {
+            GPB2_CI(k);
+            s = fma(-S[w][i][k], d[k], s);
+        });
+        d[i] = (i < bs && i >= lane) ? s / S[w][i][i] : T(0);
+    });
+    T* out = DinvT + b * kTB * kTB + lane * kTB;  // row `lane` of the transposed inverse
+    sfor<0, kTB>([&](auto i_) {
+        GPB2_CI(i);
+        out[i] = d[i];
+    });
+}
+
+// Solve L^T X = B for the right-hand-side columns [c0, c0 + NB), c0 = blockIdx.x * NB.
+//   GEN:  B = Phi(tril(u xi^T)) (generated);  else B = Bin, column-major n x n.
+//   Output: Xout[i*n + c] = X[i][c] (X row-major, i.e. X^T column-major).
+// Shared memory: Lt[stages][64][32] (factor tiles), Xs[npad][NB] (solved rows),
+// Red[warps][NB][32], Rb[32][NB+1], Dt[32][33].
+template <typename T, int NB, bool GEN>
+__global__ void __launch_bounds__(kTriThreads)
+k_trsm_lt(const T* __restrict__ Lr, int64_t ld, const T* __restrict__ DinvT,
+          const T* __restrict__ u, const T* __restrict__ xi, const T* __restrict__ Bin,
+          T* __restrict__ Xout, int64_t n) {
+    constexpr int NS = tri_stages<T>();
+    constexpr int kPieces = kTB * (int)sizeof(T) / 16;  // 16-byte pieces per tile row
+    constexpr int kPer = 16 / (int)sizeof(T);           // elements per piece
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int64_t nbk = (n + kTB - 1) / kTB, npad = nbk * kTB;
+    T* Lt = reinterpret_cast<T*>(smem_raw);  // [NS][64][32]
+    T* Xs = Lt + (size_t)NS * kTileRows * kTB;  // [npad][NB]
+    T* Red = Xs + npad * NB;                    // [warps][NB][32]
+    T (*Rb)[NB + 1] = reinterpret_cast<T (*)[NB + 1]>(Red + kTriWarps * kTB * NB);  // [32][NB+1]
+    T (*Dt)[kTB + 1] = reinterpret_cast<T (*)[kTB + 1]>(&Rb[kTB][0]);               // [32][33]
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t c0 = (int64_t)blockIdx.x * NB;
+
+    // Tile stream: blocks I = nbk-2 .. 0, each over rows [32(I+1), n) in 64-row tiles.
+    int64_t pI = nbk - 2, pk = (nbk - 1) * kTB;  // producer cursor (next tile to fetch)
+    int ptile = 0;                                 // tiles issued (committed groups)
+    auto issue = [&]() {
+        if (pI >= 0) {
+            T* dst = Lt + (size_t)(ptile % NS) * kTileRows * kTB;
+            const int64_t r0 = pI * kTB;
+            for (int e = threadIdx.x; e < kTileRows * kPieces; e += kTriThreads) {
+                const int kk = e / kPieces, q = e % kPieces;
+                const int64_t k = pk + kk;
+                if (k < n)
+                    __pipeline_memcpy_async(dst + kk * kTB + q * kPer,
+                                            Lr + k * ld + r0 + q * kPer, 16);
+            }
+            pk += kTileRows;
+            if (pk >= n) {
+                pI -= 1;
+                pk = (pI + 1) * kTB;
+            }
+        }
+        __pipeline_commit();
+        ptile++;
+    };
+    for (int st = 0; st < NS - 1; st++) issue();
+    int ctile = 0;  // tiles consumed
+
+    for (int64_t I = nbk - 1; I >= 0; I--) {
+        const int64_t r0 = I * kTB, r1 = r0 + kTB < n ? r0 + kTB : n;
+        // Operands of the block's finish, fetched now so their latency hides behind the tiles.
+        constexpr int kDin = kTB * kTB / kTriThreads;
+        T dreg[kDin];
+#pragma unroll
+        for (int q = 0; q < kDin; q++) dreg[q] = DinvT[I * kTB * kTB + threadIdx.x + q * kTriThreads];
+        constexpr int kRhs = (kTB * NB + kTriThreads - 1) / kTriThreads;
+        T breg[kRhs];
+#pragma unroll
+        for (int q = 0; q < kRhs; q++) {
+            const int e = threadIdx.x + q * kTriThreads;
+            const int i = e % kTB, c = e / kTB;
+            const int64_t gi = r0 + i, gc = c0 + c;
+            T b = T(0);
+            if (e < kTB * NB && gi < n && gc < n) {
+                if (GEN) {
+                    const T pr = u[gi] * xi[gc];
+                    b = gi > gc ? pr : (gi == gc ? T(0.5) * pr : T(0));
+                } else {
+                    b = Bin[gi + gc * n];
+                }
+            }
+            breg[q] = b;
+        }
+        // (1) partial sums of L[k][r0 + lane] * X[k][c] over the solved rows k >= r1
+        T acc[NB];
+#pragma unroll
+        for (int c = 0; c < NB; c++) acc[c] = T(0);
+        for (int64_t k0 = r1; k0 < n; k0 += kTileRows) {
+            __pipeline_wait_prior(NS - 2);  // this thread's copies of tile `ctile` have landed
+            __syncthreads();                // everyone's; the stage of tile ctile-1 is free
+            issue();
+            const T* tl = Lt + (size_t)(ctile % NS) * kTileRows * kTB;
+            const int rows = (int)(n - k0 < kTileRows ? n - k0 : kTileRows);
+            for (int kk = w; kk < rows; kk += kTriWarps) {
+                const T l = tl[kk * kTB + lane];
+                const T* xr = Xs + (k0 + kk) * NB;
+#pragma unroll
+                for (int c = 0; c < NB; c++) acc[c] = fma(l, xr[c], acc[c]);
+            }
+            ctile++;
+        }
+#pragma unroll
+        for (int c = 0; c < NB; c++) Red[(w * NB + c) * kTB + lane] = acc[c];
+#pragma unroll
+        for (int q = 0; q < kDin; q++) {
+            const int e = threadIdx.x + q * kTriThreads;
+            Dt[e / kTB][e % kTB] = dreg[q];
+        }
+        __syncthreads();
+        // (2) reduced right-hand side of the block
+#pragma unroll
+        for (int q = 0; q < kRhs; q++) {
+            const int e = threadIdx.x + q * kTriThreads;
+            if (e < kTB * NB) {
+                const int i = e % kTB, c = e / kTB;
+                T sum = T(0);
+#pragma unroll
+                for (int ww = 0; ww < kTriWarps; ww++) sum += Red[(ww * NB + c) * kTB + i];
+                Rb[i][c] = breg[q] - sum;
+            }
+        }
+        __syncthreads();
+        // (3) X_I = (L_II^-1)^T * Rb
+        for (int e = threadIdx.x; e < kTB * NB; e += kTriThreads) {
+            const int i = e % kTB, c = e / kTB;
+            T x = T(0);
+#pragma unroll 8
+            for (int ip = 0; ip < kTB; ip++) x = fma(Dt[i][ip], Rb[ip][c], x);
+            Xs[(r0 + i) * NB + c] = x;
+            const int64_t gi = r0 + i, gc = c0 + c;
+            if (gi < n && gc < n) Xout[gi * n + gc] = x;
+        }
+        __syncthreads();
+    }
+    __pipeline_wait_prior(0);
+}
+
+template <typename T, int NB>
+size_t trsm_smem(int64_t n) {
+    const int64_t npad = (n + kTB - 1) / kTB * kTB;
+    return sizeof(T) * ((size_t)tri_stages<T>() * kTileRows * kTB + (size_t)npad * NB +
+                        (size_t)kTriWarps * kTB * NB + kTB * (NB + 1) + kTB * (kTB + 1));
+}
+
+constexpr size_t kTriSmemMax = 220 * 1024;
+
+template <typename T, int NB>
+int launch_trsm(gpb2_problem* p, bool gen, const T* u, const T* xi, const T* Bin, T* Xout,
+                cudaStream_t s) {
+    const int64_t n = p->n0;
+    const size_t smem = trsm_smem<T, NB>(n);
+    const unsigned grid = (unsigned)((n + NB - 1) / NB);
+    const T* Lr = static_cast<const T*>(p->Ldr);
+    const T* Di = static_cast<const T*>(p->Dinv);
+    const int64_t ld = tri_pitch(n);
+    if (gen) {
+        GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_trsm_lt<T, NB, true>, smem));
+        GPB2_CUDA_TRY(launch_prof("dense_trsm", k_trsm_lt<T, NB, true>, dim3(grid),
+                                  dim3(kTriThreads), smem, s, Lr, ld, Di, u, xi,
+                                  (const T*)nullptr, Xout, n));
+    } else {
+        GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_trsm_lt<T, NB, false>, smem));
+        GPB2_CUDA_TRY(launch_prof("dense_trsm", k_trsm_lt<T, NB, false>, dim3(grid),
+                                  dim3(kTriThreads), smem, s, Lr, ld, Di, (const T*)nullptr,
+                                  (const T*)nullptr, Bin, Xout, n));
+    }
+    return GPB2_OK;
+}
+
+// Right-hand-side columns per CTA: about one CTA per SM, within the shared memory.
+template <typename T>
+int trsm_lt(gpb2_problem* p, bool gen, const T* u, const T* xi, const T* Bin, T* Xout,
+            cudaStream_t s) {
+    const int64_t n = p->n0;
+    if (n > 8 * 148 && trsm_smem<T, 16>(n) <= kTriSmemMax)
+        return launch_trsm<T, 16>(p, gen, u, xi, Bin, Xout, s);
+    if (n > 4 * 148 && trsm_smem<T, 8>(n) <= kTriSmemMax)
+        return launch_trsm<T, 8>(p, gen, u, xi, Bin, Xout, s);
+    return launch_trsm<T, 4>(p, gen, u, xi, Bin, Xout, s);
+}
+
+}  // namespace
+
+template <typename T>
+bool dense_tri_supported(const gpb2_problem* p) {
+    return trsm_smem<T, 4>(p->n0) <= kTriSmemMax;
+}
+
+template <typename T>
+int dense_tri_prepare(gpb2_problem* p, cudaStream_t s) {
+    const int64_t n = p->n0, ld = tri_pitch(n);
+    const int64_t nbk = (n + kTB - 1) / kTB;
+    const size_t nn = (size_t)n * (size_t)n;
+    GPB2_TRY(ensure_alloc(&p->Ldr, sizeof(T) * (size_t)n * (size_t)ld));
+    GPB2_TRY(ensure_alloc(&p->Dinv, sizeof(T) * (size_t)nbk * kTB * kTB));
+    GPB2_TRY(ensure_alloc(&p->Wtri, sizeof(T) * (2 * nn + (size_t)n)));
+    GPB2_CUDA_TRY(launch_prof("dense_transpose", k_transpose_lower<T>,
+                              dim3((unsigned)std::min<int64_t>(nbk * nbk, 4 * 148)),
+                              dim3(kTriThreads), 0, s, (const T*)p->Ld, (T*)p->Ldr, n, ld));
+    GPB2_CUDA_TRY(launch_prof("dense_diag_inv", k_diag_inv<T>,
+                              dim3((unsigned)((nbk + kDiagWarps - 1) / kDiagWarps)),
+                              dim3(32 * kDiagWarps), 0, s, (const T*)p->Ldr, n, ld,
+                              (T*)p->Dinv));
+    return GPB2_OK;
+}
+
+template <typename T>
+int dense_trmv(gpb2_problem* p, bool trans, const T* x, T* y, cudaStream_t s) {
+    const int64_t n = p->n0;
+    const dim3 grid((unsigned)((n + 31) / 32));
+    if (trans)
+        GPB2_CUDA_TRY(launch_prof("dense_trmv", k_trmv_exact<T, true>, grid, dim3(kTriThreads),
+                                  0, s, (const T*)p->Ldr, tri_pitch(n), x, y, n));
+    else
+        GPB2_CUDA_TRY(launch_prof("dense_trmv", k_trmv_exact<T, false>, grid, dim3(kTriThreads),
+                                  0, s, (const T*)p->Ld, n, x, y, n));
+    return GPB2_OK;
+}
+
+template <typename T>
+int dense_chol_pullback_outer(gpb2_problem* p, const T* vb, const T* xi, const T** S_out,
+                              cudaStream_t s) {
+    const int64_t n = p->n0;
+    const size_t nn = (size_t)n * (size_t)n;
+    T* X = static_cast<T*>(p->Wtri);
+    T* S = X + nn;
+    T* u = S + nn;
+    GPB2_TRY(dense_trmv<T>(p, true, vb, u, s));                 // u = L^T vb
+    GPB2_TRY(trsm_lt<T>(p, true, u, xi, nullptr, X, s));        // X = L^-T Phi(...), as X^T
+    GPB2_TRY(trsm_lt<T>(p, false, nullptr, nullptr, X, S, s));  // S^T = L^-T X^T, as S
+    *S_out = S;  // column-major S
+    return GPB2_OK;
+}
+
+template bool dense_tri_supported<float>(const gpb2_problem*);
+template bool dense_tri_supported<double>(const gpb2_problem*);
+template int dense_tri_prepare<float>(gpb2_problem*, cudaStream_t);
+template int dense_tri_prepare<double>(gpb2_problem*, cudaStream_t);
+template int dense_trmv<float>(gpb2_problem*, bool, const float*, float*, cudaStream_t);
+template int dense_trmv<double>(gpb2_problem*, bool, const double*, double*, cudaStream_t);
+template int dense_chol_pullback_outer<float>(gpb2_problem*, const float*, const float*,
+                                              const float**, cudaStream_t);
+template int dense_chol_pullback_outer<double>(gpb2_problem*, const double*, const double*,
+                                               const double**, cudaStream_t);
+
+}  // namespace gpb2

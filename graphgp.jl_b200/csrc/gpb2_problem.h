@@ -51,6 +51,10 @@ struct gpb2_problem {
     bool dense_valid = false;        // Ld holds the checked factor of the current table; reused
                                      // by every call until the table changes
     int dense_candidate = -1;
+    void* Ldr = nullptr;      // row-major copy of Ld, rows padded to 32 (triangular kernels)
+    void* Dinv = nullptr;     // transposed inverses of Ld's 32x32 diagonal blocks
+    void* Wtri = nullptr;     // 2 n0^2 + n0 T: the triangular kernels' work
+    bool tri_ready = false;   // Ldr / Dinv belong to the current Ld
     void* Wd = nullptr;       // (n0, n0) work
     void* Wd2 = nullptr;      // (n0, n0) work
     void* dwork = nullptr;    // cuSOLVER workspace
@@ -132,6 +136,17 @@ int ensure_dense(gpb2_problem* p);
 // Cholesky status (the jitter ladder of src/dense.jl:46-67 branches on it).
 template <typename T>
 int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s);
+
+// Triangular kernels of the dense layer (gpb2_dense_tri.cu).
+template <typename T>
+bool dense_tri_supported(const gpb2_problem* p);
+template <typename T>
+int dense_tri_prepare(gpb2_problem* p, cudaStream_t s);  // Ldr + Dinv from Ld
+template <typename T>
+int dense_trmv(gpb2_problem* p, bool trans, const T* x, T* y, cudaStream_t s);
+template <typename T>
+int dense_chol_pullback_outer(gpb2_problem* p, const T* vb, const T* xi, const T** S,
+                              cudaStream_t s);
 
 template <typename T>
 struct Dense {
