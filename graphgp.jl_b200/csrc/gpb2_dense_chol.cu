@@ -109,11 +109,12 @@ __device__ __noinline__ bool chol_diag(const CholArgs<T>& a, int c, int64_t p0, 
             const T qv = div_pos(lane > j ? r[0] : T(1), d);  // branch-free
             const T lj = lane == j ? d : qv;                   // L[lane][j] for lane >= j
             if (lane >= j) S[lane][j] = lj;
+            // Update entry (lane, j + q) and rotate.  Entries above the diagonal (lane < j + q)
+            // take meaningless values: they are never a pivot, a multiplier or stored.
             sfor<1, kB>([&](auto q_) {
                 GPB2_CI(q);
                 const T lqj = __shfl_sync(0xffffffffu, lj, (j + q) & 31);
-                const T u = N::sub(r[q], N::mul(lj, lqj));
-                r[q - 1] = lane >= j + q ? u : r[q];  // update entry (lane, j + q) and rotate
+                r[q - 1] = N::sub(r[q], N::mul(lj, lqj));
             });
             r[kB - 1] = T(0);
         }

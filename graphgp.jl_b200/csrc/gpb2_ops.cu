@@ -91,10 +91,15 @@ struct Impl {
                             "scatter");
     }
 
+    // mean_vec / std of every refined point.  They depend only on the graph and the table, so
+    // they are computed once per table and reused by every call until the table changes.
     static int factor_all(P* p, cudaStream_t s) {
-        return check_launch(ops_of<T>(p)->factor(point_args<T>(p), 0, p->m, (T*)p->mv, (T*)p->sd,
-                                                 s),
-                            "factor");
+        if (p->factor_valid) return GPB2_OK;
+        GPB2_TRY(check_launch(ops_of<T>(p)->factor(point_args<T>(p), 0, p->m, (T*)p->mv,
+                                                   (T*)p->sd, s),
+                              "factor"));
+        p->factor_valid = true;
+        return GPB2_OK;
     }
 
     // values[0:n0] preset; fills values[n0:N] batch by batch.

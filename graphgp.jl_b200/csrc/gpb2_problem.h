@@ -40,6 +40,7 @@ struct gpb2_problem {
     void* buf_c = nullptr;   // (N) T   tree-order cotangent
     void* buf_d = nullptr;   // (N) T   tree-order xbar
     double* dacc = nullptr;  // nb histogram + 8 scalars (double accumulators)
+    bool factor_valid = false;  // mv / sd hold the current table's per-point factors
 
     // Dense n0 block.
     void* Ld = nullptr;       // (n0, n0) column-major lower: the selected ladder candidate
