@@ -65,6 +65,22 @@ template <> struct Num<double> {
     static __host__ __device__ constexpr double eps() { return DBL_EPSILON; }
 };
 
+// Storage of a point's pair radii (kept by the adjoint kernels for their histogram scatter):
+// registers (compile-time indices), or the thread's column of a shared-memory block, which
+// frees registers for occupancy.
+template <typename T, int NR>
+struct RegArr {
+    T v[NR];
+    __device__ __forceinline__ T& operator[](int i) { return v[i]; }
+    __device__ __forceinline__ const T& operator[](int i) const { return v[i]; }
+};
+template <typename T>
+struct SmemCol {
+    T* p = nullptr;
+    int stride = 0;
+    __device__ __forceinline__ T& operator[](int i) const { return p[i * stride]; }
+};
+
 // ------------------------------------------------------------------------------------------
 // Interpolation table (built on the host by the problem handle, see gpb2_problem.cu).
 // ------------------------------------------------------------------------------------------
@@ -290,8 +306,8 @@ struct PointMath {
 
     // assemble_cov! (src/linalg.jl:98-112).  With KEEP_R the radius of pair (a, b), b < a, is
     // kept in R[tri(a-1, b)] for the adjoint's scatter.
-    template <bool KEEP_R>
-    static __device__ __forceinline__ void assemble(T (&L)[NT], T (&R)[NR],
+    template <bool KEEP_R, typename RT>
+    static __device__ __forceinline__ void assemble(T (&L)[NT], RT& R,
                                                     const uint32_t (&jc)[KP1][D], T scale,
                                                     const SmemTable<T>& tab) {
         const T diag = tab.lookup(T(0));

@@ -68,15 +68,37 @@ __device__ __forceinline__ double block_sum_double(double v, double* red /*>= 32
     return s;  // valid on thread 0
 }
 
+// Where the adjoint kernels keep a point's pair radii between the assembly and the histogram
+// scatter: the thread's column of a shared-memory block after the histogram when it fits (the
+// radii would otherwise occupy NR registers through the whole pullback), else registers.
+template <typename T, int K, int D>
+struct RadiusStore {
+    static constexpr int NR = PointMath<T, K, D>::NR;
+    static constexpr bool kSmem = (size_t)NR * kFlatThreads * sizeof(T) <= 36 * 1024;
+    using type = typename std::conditional<kSmem, SmemCol<T>, RegArr<T, NR>>::type;
+    static constexpr size_t bytes = kSmem ? (size_t)NR * kFlatThreads * sizeof(T) : 0;
+    static __device__ __forceinline__ type make(unsigned char* base) {
+        if constexpr (kSmem) {
+            SmemCol<T> c;
+            c.p = reinterpret_cast<T*>(base) + threadIdx.x;
+            c.stride = kFlatThreads;
+            return c;
+        } else {
+            return type{};
+        }
+    }
+};
+
 // ---------------------------------------------------------------------------------------------
 // Shared per-point preamble: neighbour list, joint coords, covariance, factor.
 // ---------------------------------------------------------------------------------------------
-template <typename T, int K, int D, bool KEEP_R>
+template <typename T, int K, int D, bool KEEP_R,
+          typename RT = RegArr<T, PointMath<T, K, D>::NR>>
 struct PointFactor {
     using PM = PointMath<T, K, D>;
     int nb[K];
     T L[PM::NT];
-    T R[PM::NR];
+    RT R;
 
     __device__ __forceinline__ void compute(const PointArgs<T>& a, const SmemTable<T>& tab,
                                             int64_t m) {
@@ -162,10 +184,9 @@ k_logdet(PointArgs<T> a, T* __restrict__ terms, double* __restrict__ acc, int64_
 // Scatter a point's A-bar (lower triangle, in B) into the CTA histogram: the diagonal sum into
 // bin 0, each off-diagonal through the interpolation weights of its radius
 // (_scatter_Abar_hist!, src/kernels_adjoint.jl:50-74).
-template <typename T, int K, int D>
+template <typename T, int K, int D, typename RT>
 __device__ __forceinline__ void scatter_hist(double* hist, const T (&B)[PointMath<T, K, D>::NT],
-                                             const T (&R)[PointMath<T, K, D>::NR],
-                                             const SmemTable<T>& tab) {
+                                             const RT& R, const SmemTable<T>& tab) {
     using N = Num<T>;
     constexpr int KP1 = K + 1;
     T dsum = T(0);
@@ -206,12 +227,15 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
     SmemTable<T> tab;
     tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
     double* hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
+    unsigned char* rbase = smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys) +
+                           sizeof(double) * a.tab.nb;
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
     double s = 0.0;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
          m += (int64_t)gridDim.x * blockDim.x) {
-        PointFactor<T, K, D, true> f;
+        PointFactor<T, K, D, true, typename RadiusStore<T, K, D>::type> f;
+        f.R = RadiusStore<T, K, D>::make(rbase);
         f.compute(a, tab, m);
         const T lkk = f.L[tri(K, K)];
         const T t = N::log(lkk);
@@ -239,23 +263,25 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
 template <typename T, int K, int D>
 __global__ void __launch_bounds__(kFlatThreads)
 k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
-            const T* __restrict__ vb, double* __restrict__ gacc, int64_t M) {
+            const T* __restrict__ vb, const T* __restrict__ mv, double* __restrict__ gacc,
+            int64_t M) {
     using N = Num<T>;
     using PM = PointMath<T, K, D>;
     extern __shared__ __align__(16) unsigned char smem[];
     SmemTable<T> tab;
     tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
     double* hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
+    unsigned char* rbase = smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys) +
+                           sizeof(double) * a.tab.nb;
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
          m += (int64_t)gridDim.x * blockDim.x) {
         const int64_t p = a.n0 + m;
         const T vbp = vb[p];
-        PointFactor<T, K, D, true> f;
+        PointFactor<T, K, D, true, typename RadiusStore<T, K, D>::type> f;
+        f.R = RadiusStore<T, K, D>::make(rbase);
         f.compute(a, tab, m);
-        T x[K];
-        PM::solve(x, f.L, a.tab.pivc);
         const T pivfloor = N::mul(a.tab.pivc, f.L[0]);
         T B[PM::NT];
         sfor<0, PM::NT>([&](auto i_) {
@@ -269,6 +295,11 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
             z[j] = N::mul(vbp, v[f.nb[j]]);
         });
         PM::template forward_subst<true>(z, f.L, pivfloor);
+        T x[K];  // mean_vec of the point: k_factor's output, the same solve bit for bit
+        sfor<0, K>([&](auto j_) {
+            GPB2_CI(j);
+            x[j] = mv[m * K + j];
+        });
         PM::seed_from_solve(B, z, x);
         PM::pullback(B, f.L);
         scatter_hist<T, K, D>(hist, B, f.R, tab);
@@ -290,12 +321,15 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
     SmemTable<T> tab;
     tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
     double* hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
+    unsigned char* rbase = smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys) +
+                           sizeof(double) * a.tab.nb;
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
     double ls = 0.0;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
          m += (int64_t)gridDim.x * blockDim.x) {
-        PointFactor<T, K, D, true> f;
+        PointFactor<T, K, D, true, typename RadiusStore<T, K, D>::type> f;
+        f.R = RadiusStore<T, K, D>::make(rbase);
         f.compute(a, tab, m);
         T x[K];
         PM::solve(x, f.L, a.tab.pivc);
@@ -518,8 +552,8 @@ struct Ops {
     cudaError_t (*inv)(const PointArgs<T>&, const T*, T*, int64_t, cudaStream_t);
     cudaError_t (*logdet)(const PointArgs<T>&, T*, double*, int64_t, cudaStream_t);
     cudaError_t (*logdet_grad)(const PointArgs<T>&, double*, double*, T*, int64_t, cudaStream_t);
-    cudaError_t (*grad_vals)(const PointArgs<T>&, const T*, const T*, const T*, double*, int64_t,
-                             cudaStream_t);
+    cudaError_t (*grad_vals)(const PointArgs<T>&, const T*, const T*, const T*, const T*, double*,
+                             int64_t, cudaStream_t);
     cudaError_t (*inv_loss_grad)(const PointArgs<T>&, const T*, double*, double*, T*, int64_t,
                                  cudaStream_t);
     cudaError_t (*fused_fwd)(const PointArgs<T>&, T*, const T*, int64_t, int64_t, cudaStream_t);
@@ -564,17 +598,17 @@ struct Launch {
     }
     static cudaError_t logdet_grad(const PointArgs<T>& a, double* gacc, double* ld, T* terms,
                                    int64_t M, cudaStream_t s) {
-        return flat("logdet_grad", k_logdet_grad<T, K, D>, flat_smem(a, true), M, s, a, gacc, ld,
+        return flat("logdet_grad", k_logdet_grad<T, K, D>, flat_smem(a, true) + RadiusStore<T, K, D>::bytes, M, s, a, gacc, ld,
                     terms, M);
     }
     static cudaError_t grad_vals(const PointArgs<T>& a, const T* v, const T* xih, const T* vb,
-                                 double* gacc, int64_t M, cudaStream_t s) {
-        return flat("grad_vals", k_grad_vals<T, K, D>, flat_smem(a, true), M, s, a, v, xih, vb,
-                    gacc, M);
+                                 const T* mv, double* gacc, int64_t M, cudaStream_t s) {
+        return flat("grad_vals", k_grad_vals<T, K, D>, flat_smem(a, true) + RadiusStore<T, K, D>::bytes, M, s, a, v, xih, vb,
+                    mv, gacc, M);
     }
     static cudaError_t inv_loss_grad(const PointArgs<T>& a, const T* values, double* gacc,
                                      double* loss, T* xi_out, int64_t M, cudaStream_t s) {
-        return flat("inv_loss_grad", k_inv_loss_grad<T, K, D>, flat_smem(a, true), M, s, a,
+        return flat("inv_loss_grad", k_inv_loss_grad<T, K, D>, flat_smem(a, true) + RadiusStore<T, K, D>::bytes, M, s, a,
                     values, gacc, loss, xi_out, M);
     }
     static cudaError_t fused_fwd(const PointArgs<T>& a, T* values, const T* xi_ref, int64_t lo,

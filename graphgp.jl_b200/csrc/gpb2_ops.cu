@@ -13,6 +13,7 @@
 // generate_grad_vals.  Every point's contribution to d(vals) is linear in its final cotangent
 // vb[p]; once the reverse sweep has finalised vb for all points, the per-point pullbacks are
 // independent and run as one flat kernel instead of one launch per batch.
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
@@ -232,6 +233,31 @@ struct Impl {
         return GPB2_OK;
     }
 
+    // ---------------------------------------------------------------- ranges of one depth batch
+    // (the building blocks of a level-sharded sweep: each rank runs its slice of a batch, the
+    // caller exchanges the batch's values between ranks; asynchronous on `s`)
+    static int refine_range(P* p, T* values, const T* xi_ref, int64_t lo, int64_t hi,
+                            cudaStream_t s) {
+        return check_launch(
+            ops_of<T>(p)->fused_fwd(point_args<T>(p), values, xi_ref, lo, hi, s), "refine range");
+    }
+
+    static int reverse_range(P* p, T* xg, T* vb, int64_t lo, int64_t hi, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, true));
+        if (!p->factor_valid)
+            GPB2_TRY(check_launch(ops_of<T>(p)->factor(point_args<T>(p), lo - p->n0, hi - p->n0,
+                                                       (T*)p->mv, (T*)p->sd, s),
+                                  "factor range"));
+        return check_launch(ops_of<T>(p)->sweep_rev(xg, vb, (const T*)p->mv, (const T*)p->sd,
+                                                    p->nbrs, p->n0, lo, hi, s),
+                            "reverse range");
+    }
+
+    static int dense_apply(P* p, int trans, const T* x, T* y, cudaStream_t s) {
+        GPB2_TRY(Dense<T>::factor(p, s));
+        return trans ? Dense<T>::apply_Lt(p, x, y, s) : Dense<T>::apply_L(p, x, y, s);
+    }
+
     // ---------------------------------------------------------------- orchestrated (original order)
     static int generate(P* p, const T* xi, T* out, cudaStream_t s) {
         GPB2_TRY(ensure_scratch(p, true));
@@ -314,7 +340,8 @@ struct Impl {
         GPB2_TRY(reverse_sweep(p, nullptr, vb, s));
         GPB2_TRY(zero_acc(p, s));
         GPB2_TRY(check_launch(
-            ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb, p->dacc, p->m, s), "grad_vals"));
+            ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb, (const T*)p->mv, p->dacc, p->m, s),
+            "grad_vals"));
         GPB2_TRY(Dense<T>::grad_vals(p, vb, xt, p->dacc, s));
         return finish_hist(p, dvals, s);
     }
@@ -433,6 +460,54 @@ int gpb2_refine(gpb2_problem* p, void* values, const void* xi_ref, void* stream)
     GPB2_TRY(need(values, "values") | need(xi_ref, "xi_ref"));
     GPB2_DISPATCH(p, Impl<float>::refine(p, F32(values), CF32(xi_ref), s),
                   Impl<double>::refine(p, F64(values), CF64(xi_ref), s));
+}
+
+// [lo, hi) must lie inside one depth batch (the ranges of a level-sharded sweep).
+static int check_range(const gpb2_problem* p, int64_t lo, int64_t hi, const char* what) {
+    if (!p) return set_error(GPB2_ERR_INVALID_ARG, "%s: NULL problem", what);
+    if (lo < p->n0 || hi > p->n || lo > hi)
+        return set_error(GPB2_ERR_INVALID_ARG, "%s: range [%lld, %lld) outside [n0, N) = [%lld, %lld)",
+                         what, (long long)lo, (long long)hi, (long long)p->n0, (long long)p->n);
+    if (lo == hi) return GPB2_OK;
+    const auto it = std::upper_bound(p->offsets.begin(), p->offsets.end(), lo);
+    if (it == p->offsets.end() || hi > *it)
+        return set_error(GPB2_ERR_INVALID_ARG, "%s: range [%lld, %lld) spans depth batches", what,
+                         (long long)lo, (long long)hi);
+    return GPB2_OK;
+}
+
+#define GPB2_ASYNC(p, CALL32, CALL64)                                                          \
+    do {                                                                                       \
+        DeviceGuard _dg((p)->device);                                                          \
+        if (!_dg.ok) return set_error(GPB2_ERR_NO_DEVICE, "cudaSetDevice(%d) failed", (p)->device); \
+        cudaStream_t s = (cudaStream_t)stream;                                                 \
+        return (p)->dtype == GPB2_F32 ? (CALL32) : (CALL64);                                    \
+    } while (0)
+
+int gpb2_refine_range(gpb2_problem* p, void* values, const void* xi_ref, int64_t lo, int64_t hi,
+                      void* stream) {
+    clear_error();
+    GPB2_TRY(check_range(p, lo, hi, "gpb2_refine_range"));
+    GPB2_TRY(need(values, "values") | need(xi_ref, "xi_ref"));
+    if (lo == hi) return GPB2_OK;
+    GPB2_ASYNC(p, Impl<float>::refine_range(p, F32(values), CF32(xi_ref), lo, hi, s),
+               Impl<double>::refine_range(p, F64(values), CF64(xi_ref), lo, hi, s));
+}
+
+int gpb2_refine_reverse_range(gpb2_problem* p, void* xg, void* vb, int64_t lo, int64_t hi,
+                              void* stream) {
+    clear_error();
+    GPB2_TRY(check_range(p, lo, hi, "gpb2_refine_reverse_range"));
+    GPB2_TRY(need(vb, "vb"));
+    if (lo == hi) return GPB2_OK;
+    GPB2_ASYNC(p, Impl<float>::reverse_range(p, F32(xg), F32(vb), lo, hi, s),
+               Impl<double>::reverse_range(p, F64(xg), F64(vb), lo, hi, s));
+}
+
+int gpb2_dense_apply(gpb2_problem* p, int trans, const void* x, void* y, void* stream) {
+    GPB2_TRY(need(x, "x") | need(y, "y"));
+    GPB2_DISPATCH(p, Impl<float>::dense_apply(p, trans, CF32(x), F32(y), s),
+                  Impl<double>::dense_apply(p, trans, CF64(x), F64(y), s));
 }
 
 int gpb2_refine_inv(gpb2_problem* p, const void* values, void* xi_ref, void* stream) {

@@ -90,6 +90,9 @@ _SIGNATURES = {
     "gpb2_set_forward_mode": (I32, [I32]),
     "gpb2_refine": (I32, [P, P, P, P]),
     "gpb2_refine_inv": (I32, [P, P, P, P]),
+    "gpb2_refine_range": (I32, [P, P, P, I64, I64, P]),
+    "gpb2_refine_reverse_range": (I32, [P, P, P, I64, I64, P]),
+    "gpb2_dense_apply": (I32, [P, I32, P, P, P]),
     "gpb2_refine_logdet_terms": (I32, [P, P, P]),
     "gpb2_refine_logdet": (I32, [P, PD, P]),
     "gpb2_refine_logdet_grad_vals": (I32, [P, P, PD, P]),

@@ -120,6 +120,25 @@ int gpb2_set_forward_mode(int mode);
  * Replaces the per-batch refine_apply_fused_kernel! launches of src/api.jl:364-392. */
 int gpb2_refine(gpb2_problem* prob, void* values_dev, const void* xi_ref_dev, void* stream);
 
+/* Ranges of one depth batch, the building blocks of a level-sharded sweep over several GPUs
+ * (each rank runs its slice of a batch, the caller exchanges the batch between ranks; the
+ * exchange replaces the reference's MPI/serial level loop, src/distributed.jl:293-322 and
+ * src/api.jl:364-392).  [lo, hi) are tree-order point indices inside one batch (n0 <= lo).
+ * Asynchronous on `stream` (no synchronisation; launch errors are returned).
+ *   refine_range:          values[p] = std_p*xi_ref[p-n0] + sum_j mv_pj*values[nbr_pj]
+ *                          (refine_apply_fused_kernel!, src/kernels.jl:101-119)
+ *   refine_reverse_range:  xg[p] = std_p*vb[p] (xg may be NULL); vb[nbr_pj] += mv_pj*vb[p]
+ *                          (refine_reverse_apply_fused_kernel!, src/kernels_adjoint.jl:453-474) */
+int gpb2_refine_range(gpb2_problem* prob, void* values_dev, const void* xi_ref_dev, int64_t lo,
+                      int64_t hi, void* stream);
+int gpb2_refine_reverse_range(gpb2_problem* prob, void* xg_dev, void* vb_dev, int64_t lo,
+                              int64_t hi, void* stream);
+
+/* Dense first layer: y[0:n0] = L x[0:n0] (trans = 0, generate_dense, src/dense.jl:112-119) or
+ * L^T x[0:n0] (trans = 1, the dense adjoint of generate_grad_xi, src/grad.jl:448-453); the
+ * block is factorised (with the jitter ladder) if the table changed.  Synchronous. */
+int gpb2_dense_apply(gpb2_problem* prob, int trans, const void* x_dev, void* y_dev, void* stream);
+
 /* refine_inv!: xi_ref_dev[m] = (values[n0+m] - mean) / std.  Replaces src/api.jl:317-343
  * (refine_inv_kernel!, src/kernels.jl:37-56) and gpcuda_refine_inv_f32 (csrc/graphgp_capi.cu:90-99). */
 int gpb2_refine_inv(gpb2_problem* prob, const void* values_dev, void* xi_ref_dev, void* stream);
