@@ -504,6 +504,64 @@ k_sweep_fwd_all(T* __restrict__ values, const T* __restrict__ xi_ref, const T* _
     }
 }
 
+// Dataflow forward sweep: one cooperative launch and no barrier.  values[n0:N] are set to the
+// pending pattern before the launch; each point waits only for its own K neighbour values, so
+// the sweep's critical path is the graph's dependency chain rather than one grid barrier per
+// batch.  Points are dealt in rounds (round k: p = n0 + gtid + k*gsz); every point depends only
+// on earlier batches, i.e. on smaller tree positions, so with the whole grid resident the
+// earliest unfinished point can always proceed.  Inside a warp the lanes poll together: each
+// pass, every lane whose neighbours are all published computes and publishes its point, and the
+// warp moves to the next round when all lanes are done -- so a lane never blocks while another
+// lane of its own warp still has to publish the value it needs.  Bit-identical to the other
+// sweeps (same arithmetic, same order).
+template <typename T, int K>
+__global__ void __launch_bounds__(kPersistThreads)
+k_sweep_fwd_flow(T* __restrict__ values, const T* __restrict__ xi_ref, const T* __restrict__ mv,
+                 const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0, int64_t n,
+                 int* __restrict__ err) {
+    using N = Num<T>;
+    using U = typename Pending<T>::U;
+    const int64_t gtid = (int64_t)threadIdx.x * gridDim.x + blockIdx.x;
+    const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
+    const int64_t rounds = (n - n0 + gsz - 1) / gsz;
+    SweepPoint<T, K> sp;
+    for (int64_t k = 0; k < rounds; k++) {
+        const int64_t p = n0 + gtid + k * gsz;
+        bool done = p >= n;
+        if (!done) sp.load_fwd(mv, sd, xi_ref, nbrs, p - n0);
+        unsigned int it = 0;
+        while (true) {
+            if (!done) {
+                T v[K];
+                bool ready = true;
+                sfor<0, K>([&](auto j_) {
+                    GPB2_CI(j);
+                    const U u = ld_relaxed_bits(values + sp.nb[j]);
+                    ready = ready && u != Pending<T>::kBits;
+                    v[j] = bits_to(u, T());
+                });
+                if (ready) {
+                    T acc = sp.a;
+                    sfor<0, K>([&](auto j_) {
+                        GPB2_CI(j);
+                        acc = N::add(acc, N::mul(sp.w[j], v[j]));
+                    });
+                    publish_value(values + p, acc);
+                    done = true;
+                }
+            }
+            if (__all_sync(0xffffffffu, done)) break;
+            if ((++it & 255u) == 0u) {  // `it` is warp-uniform, so is this test
+                const bool stop = it > kSpinLimit || ld_relaxed_gpu(err) != 0;
+                if (__any_sync(0xffffffffu, stop)) {
+                    if ((threadIdx.x & 31) == 0) atomicCAS(err, 0, GPB2_SYNC_TIMEOUT);
+                    return;
+                }
+            }
+        }
+    }
+}
+
 template <typename T, int K>
 __global__ void __launch_bounds__(kPersistThreads)
 k_sweep_rev_all(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv,
@@ -557,6 +615,8 @@ struct Ops {
     cudaError_t (*inv_loss_grad)(const PointArgs<T>&, const T*, double*, double*, T*, int64_t,
                                  cudaStream_t);
     cudaError_t (*fused_fwd)(const PointArgs<T>&, T*, const T*, int64_t, int64_t, cudaStream_t);
+    cudaError_t (*sweep_fwd_flow)(T*, const T*, const T*, const T*, const int*, int64_t, int64_t,
+                                  int*, cudaStream_t);
     cudaError_t (*sweep_fwd)(T*, const T*, const T*, const T*, const int*, int64_t, int64_t,
                              int64_t, cudaStream_t);
     cudaError_t (*sweep_rev)(T*, T*, const T*, const T*, const int*, int64_t, int64_t, int64_t,
@@ -648,6 +708,13 @@ struct Launch {
         return coop("sweep_fwd_all", k_sweep_fwd_all<T, K>, s, values, xi_ref, mv, sd, nbrs, n0,
                     offs, nbatch, gs);
     }
+    static cudaError_t sweep_fwd_flow(T* values, const T* xi_ref, const T* mv, const T* sd,
+                                      const int* nbrs, int64_t n0, int64_t n, int* err,
+                                      cudaStream_t s) {
+        if (n <= n0) return cudaSuccess;
+        return coop("sweep_fwd_flow", k_sweep_fwd_flow<T, K>, s, values, xi_ref, mv, sd, nbrs,
+                    n0, n, err);
+    }
     static cudaError_t sweep_rev_all(T* xg, T* vb, const T* mv, const T* sd, const int* nbrs,
                                      int64_t n0, const int64_t* offs, int nbatch, GridSync gs,
                                      cudaStream_t s) {
@@ -656,9 +723,9 @@ struct Launch {
                     nbatch, gs);
     }
     static const Ops<T>* ops() {
-        static const Ops<T> o = {factor,        inv,       logdet,    logdet_grad,
-                                 grad_vals,     inv_loss_grad, fused_fwd, sweep_fwd,
-                                 sweep_rev,     sweep_fwd_all, sweep_rev_all};
+        static const Ops<T> o = {factor,        inv,           logdet,    logdet_grad,
+                                 grad_vals,     inv_loss_grad, fused_fwd, sweep_fwd_flow,
+                                 sweep_fwd,     sweep_rev,     sweep_fwd_all, sweep_rev_all};
         return &o;
     }
 };

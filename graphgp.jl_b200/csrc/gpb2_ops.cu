@@ -56,12 +56,13 @@ inline unsigned grid1d(int64_t n) {
 // Process-wide sweep strategy (GPB2_FWD=persistent|fused|batched at load time, or
 // gpb2_set_forward_mode()): 0 = one cooperative kernel per sweep, 1 = the reference's fused
 // per-batch forward kernel, 2 = one light kernel launch per batch.
-enum class FwdMode { Persistent = 0, Fused = 1, Batched = 2 };
+enum class FwdMode { Persistent = 0, Fused = 1, Batched = 2, Flow = 3 };
 
 std::atomic<int> g_fwd_mode{[] {
     const char* e = std::getenv("GPB2_FWD");
     if (e && std::strcmp(e, "fused") == 0) return 1;
     if (e && std::strcmp(e, "batched") == 0) return 2;
+    if (e && std::strcmp(e, "flow") == 0) return 3;
     return 0;
 }()};
 
@@ -115,6 +116,14 @@ struct Impl {
             return GPB2_OK;
         }
         if (!have_factor) GPB2_TRY(factor_all(p, s));
+        if (fwd_mode() == FwdMode::Flow) {
+            GPB2_CUDA_TRY(cudaMemsetAsync(values + p->n0, 0xff, sizeof(T) * (p->n - p->n0), s));
+            GPB2_TRY(check_launch(o->sweep_fwd_flow(values, xi_ref, (const T*)p->mv,
+                                                    (const T*)p->sd, p->nbrs, p->n0, p->n,
+                                                    reinterpret_cast<int*>(p->dsync + 2), s),
+                                  "forward sweep"));
+            return GPB2_OK;  // the wait error word is read when the call finishes
+        }
         if (fwd_mode() == FwdMode::Persistent) {
             GPB2_TRY(arm_sync(p, s));
             GPB2_TRY(check_launch(o->sweep_fwd_all(values, xi_ref, (const T*)p->mv,
@@ -134,7 +143,7 @@ struct Impl {
     // Reverse sweep over the batches, latest first; xg may be NULL.
     static int reverse_sweep(P* p, T* xg, T* vb, cudaStream_t s) {
         const Ops<T>* o = ops_of<T>(p);
-        if (fwd_mode() == FwdMode::Persistent) {
+        if (fwd_mode() == FwdMode::Persistent || fwd_mode() == FwdMode::Flow) {
             GPB2_TRY(arm_sync(p, s));
             GPB2_TRY(check_launch(o->sweep_rev_all(xg, vb, (const T*)p->mv, (const T*)p->sd,
                                                    p->nbrs, p->n0, p->d_offsets, nbatch(p),
@@ -449,9 +458,9 @@ static int need(const void* ptr, const char* name) {
 extern "C" {
 
 int gpb2_set_forward_mode(int mode) {
-    if (mode < 0 || mode > 2)
+    if (mode < 0 || mode > 3)
         return set_error(GPB2_ERR_INVALID_ARG,
-                         "forward mode must be 0 (persistent), 1 (fused) or 2 (batched)");
+                         "forward mode must be 0 (persistent), 1 (fused), 2 (batched) or 3 (flow)");
     g_fwd_mode.store(mode);
     return GPB2_OK;
 }

@@ -107,9 +107,10 @@ int64_t gpb2_launch_count(void);
  * points come from one flat kernel; then 0 = one cooperative (persistent) kernel per sweep with a
  * bounded grid barrier between depth batches (default); 2 = one light kernel launch per batch.
  * 1 = the reference's fused per-batch forward kernel (refine_apply_fused_kernel!,
- * src/kernels.jl:101-119), which recomputes the factor inside each batch.  All three give
- * bit-identical forward values.  A barrier that times out makes the call return
- * GPB2_ERR_TIMEOUT. */
+ * src/kernels.jl:101-119), which recomputes the factor inside each batch.  3 = dataflow: one
+ * cooperative kernel with no barrier, each point waiting (bounded) for its own neighbours' values
+ * (the reverse sweep then runs as in mode 0).  All four give bit-identical forward values.  A
+ * barrier or wait that times out makes the call return GPB2_ERR_TIMEOUT. */
 int gpb2_set_forward_mode(int mode);
 
 /* ------------------------------------------------------------------------------------------

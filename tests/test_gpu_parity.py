@@ -48,7 +48,7 @@ def _sweep_mode():
 
 @pytest.mark.parametrize("dt", [np.float64, np.float32])
 @pytest.mark.parametrize("name", FIXTURES)
-@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
 def test_refine_bit_exact(golden, cuda_device, name, dt, mode):
     d = golden(name)
     prob, orc = _pair(d, dt)
