@@ -52,8 +52,29 @@ struct CholArgs {
     int* fail;        // fail[c] = failing column + 1, 0 while alive
     int* sel;         // sel[0]: ladder index of the first success (-1: none yet); sel[1]: its slot
     int* done;        // done[c] = 1 once candidate c is fully factorised
+    int* dflag;       // dflag[c]: last panel whose diagonal block candidate c has published
+    int* err;         // error word: a bounded wait gave up
     unsigned long long* trace;  // diagnostics (GPB2_TRACE_DENSE): phase timestamps, or NULL
 };
+
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+    asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait until *flag >= v (one thread); on timeout the error word is set and the wait
+// ends, so a failure elsewhere never hangs the cluster.
+__device__ __forceinline__ void wait_flag_gpu(const int* flag, int v, int* err) {
+    for (unsigned int it = 0; ld_acquire_gpu_s32(flag) < v; it++) {
+        if ((it & 1023u) == 1023u && (it > (1u << 24) || ld_acquire_gpu_s32(err) != 0)) {
+            atomicCAS(err, 0, 1);
+            return;
+        }
+    }
+}
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -88,36 +109,37 @@ __device__ __noinline__ bool chol_diag(const CholArgs<T>& a, int c, int64_t p0, 
     __syncthreads();
     if (st) st[0] = global_ns();
     if (threadIdx.x < 32) {
-        // Row `lane` in registers, rotated: at step j, r[q] holds entry (lane, j + q), so the
-        // step body is the same code for every column (a compact loop: the block is factored
-        // once per panel and a fully unrolled body would be fetched from L2 every time).
-        // Column j's pivot and multipliers travel by shuffle; finished entries go to S.
+        // Row `lane` in registers; column j's pivot and multipliers travel by shuffle; finished
+        // entries go to S.  Fully unrolled: about 500 update steps that follow the triangle, so
+        // the serial chain (pivot -> sqrt -> divisions -> next pivot) has the issue slots to
+        // itself.  Entries above the diagonal (lane < q) take meaningless values: they are never
+        // a pivot, a multiplier or stored.
         const int lane = threadIdx.x;
+        int bad = 0;
         T r[kB];
         sfor<0, kB>([&](auto q_) {
             GPB2_CI(q);
             r[q] = (lane < bs && q <= lane) ? S[lane][q] : T(0);
         });
-        int bad = 0;
-        for (int j = 0; j < bs; j++) {
-            const T sjj = __shfl_sync(0xffffffffu, r[0], j);
-            if (!(sjj > T(0))) {  // LAPACK potrf's failure test (also catches NaN)
-                bad = (int)p0 + j + 1;
-                break;
+        sfor<0, kB>([&](auto j_) {
+            GPB2_CI(j);
+            if (j < bs && !bad) {
+                const T sjj = __shfl_sync(0xffffffffu, r[j], j);
+                if (!(sjj > T(0))) {  // LAPACK potrf's failure test (also catches NaN)
+                    bad = (int)p0 + j + 1;
+                } else {
+                    const T d = N::sqrt(sjj);
+                    const T qv = div_pos(lane > j ? r[j] : T(1), d);  // branch-free
+                    r[j] = lane == j ? d : qv;                         // L[lane][j], lane >= j
+                    if (lane >= j) S[lane][j] = r[j];
+                    sfor<j + 1, kB>([&](auto q_) {
+                        GPB2_CI(q);
+                        const T lqj = __shfl_sync(0xffffffffu, r[j], q);
+                        r[q] = N::sub(r[q], N::mul(r[j], lqj));
+                    });
+                }
             }
-            const T d = N::sqrt(sjj);
-            const T qv = div_pos(lane > j ? r[0] : T(1), d);  // branch-free
-            const T lj = lane == j ? d : qv;                   // L[lane][j] for lane >= j
-            if (lane >= j) S[lane][j] = lj;
-            // Update entry (lane, j + q) and rotate.  Entries above the diagonal (lane < j + q)
-            // take meaningless values: they are never a pivot, a multiplier or stored.
-            sfor<1, kB>([&](auto q_) {
-                GPB2_CI(q);
-                const T lqj = __shfl_sync(0xffffffffu, lj, (j + q) & 31);
-                r[q - 1] = N::sub(r[q], N::mul(lj, lqj));
-            });
-            r[kB - 1] = T(0);
-        }
+        });
         if (lane == 0) {
             *s_bad = bad;
             if (bad) a.fail[c] = bad;
@@ -190,73 +212,162 @@ __device__ void chol_panel(const CholArgs<T>& a, int c, int64_t p0, int rank, in
     if (st) st[1] = global_ns();
 }
 
+// The panel's diagonal factor, transposed, into Dg (whole CTA; row j = column j of the factor,
+// zero above the diagonal, plus a zero row).
+template <typename T>
+__device__ __forceinline__ void load_diag_t(const CholArgs<T>& a, int c, int64_t p0, T* Dg) {
+    constexpr int NTH = chol_threads<T>();
+    const T* L = a.base + (int64_t)c * a.n * a.n;
+#pragma unroll
+    for (int e0 = 0; e0 < kB * kB; e0 += NTH) {
+        const int e = e0 + threadIdx.x, i = e % kB, j = e / kB;
+        Dg[j * kB + i] = (i >= j && p0 + i < a.n) ? __ldcg(L + (p0 + i) + (p0 + j) * a.n) : T(0);
+    }
+    if (threadIdx.x < kB) Dg[kB * kB + threadIdx.x] = T(0);
+}
+
+// Panel rows [r_lo, r_hi) (at most one tile: warp w takes rows r_lo + 32w + lane) solved against
+// the transposed diagonal factor Dg, as in chol_panel.
+template <typename T>
+__device__ void chol_rows(const CholArgs<T>& a, int c, int64_t p0, int64_t r_lo, int64_t r_hi,
+                          const T* Dg) {
+    using N = Num<T>;
+    T* L = a.base + (int64_t)c * a.n * a.n;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if ((int64_t)warp * 32 >= r_hi - r_lo) return;  // warp-uniform
+    const int64_t i = r_lo + warp * 32 + lane;
+    const bool live = i < r_hi;
+    T* Li = L + i + p0 * a.n;
+    T x[kB];
+    sfor<0, kB>([&](auto q_) {
+        GPB2_CI(q);
+        x[q] = live ? __ldcg(Li + q * a.n) : T(0);
+    });
+    sfor<0, kB>([&](auto j_) {
+        GPB2_CI(j);
+        const T* dj = Dg + j * kB;
+        x[j] = div_pos(x[j], dj[j]);
+        sfor<j + 1, kB>([&](auto q_) {
+            GPB2_CI(q);
+            x[q] = N::sub(x[q], N::mul(x[j], dj[q]));
+        });
+    });
+    if (live) {
+        sfor<0, kB>([&](auto q_) {
+            GPB2_CI(q);
+            __stcg(Li + q * a.n, x[q]);
+        });
+    }
+}
+
 // Phase U: lower tile (bi, bj) of candidate c's trailing matrix [p0 + kB, n)^2, one subtraction
 // per panel column in order.  Thread (tx, ty) owns rows tx + 32*u (lanes along the contiguous
-// dimension) and columns ty + TY*v.
+// dimension) and columns ty + TY*v.  A tile's operands are fetched into registers (fetch) while
+// the previous tile computes, then staged in shared memory (stage) and consumed (compute).
 template <typename T, int TL>
-__device__ void chol_update_tile(const CholArgs<T>& a, int c, int64_t p0, int bi, int bj,
-                                 T (*Li)[kB + 1], T (*Lj)[kB + 1]) {
-    using N = Num<T>;
-    constexpr int NTH = chol_threads<T>();
-    constexpr int TY = NTH / 32;
-    constexpr int RU = TL / 32, RV = TL / TY;
-    static_assert(RU * 32 == TL && RV * TY == TL, "tile shape");
-    T* L = a.base + (int64_t)c * a.n * a.n;
-    const int64_t t0 = p0 + kB;
-    const int64_t r0 = t0 + (int64_t)bi * TL, c0 = t0 + (int64_t)bj * TL;
-#pragma unroll
-    for (int e0 = 0; e0 < TL * kB; e0 += NTH) {
-        const int e = e0 + threadIdx.x, rr = e % TL, p = e / TL;
-        const int64_t gi = r0 + rr, gj = c0 + rr;
-        Li[rr][p] = gi < a.n ? __ldcg(L + gi + (p0 + p) * a.n) : T(0);
-        Lj[rr][p] = gj < a.n ? __ldcg(L + gj + (p0 + p) * a.n) : T(0);
-    }
-    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+struct TileWork {
+    static constexpr int NTH = chol_threads<T>();
+    static constexpr int TY = NTH / 32;
+    static constexpr int RU = TL / 32, RV = TL / TY;
+    static constexpr int NP = TL * kB / NTH;  // panel entries per thread per side
+    static_assert(RU * 32 == TL && RV * TY == TL && NP * NTH == TL * kB, "tile shape");
+    T li[NP], lj[NP];
     T acc[RU][RV];
+    int64_t r0, c0;
+
+    __device__ __forceinline__ void fetch(const CholArgs<T>& a, int c, int64_t p0, int bi,
+                                          int bj) {
+        const T* L = a.base + (int64_t)c * a.n * a.n;
+        const int64_t t0 = p0 + kB;
+        r0 = t0 + (int64_t)bi * TL;
+        c0 = t0 + (int64_t)bj * TL;
 #pragma unroll
-    for (int u = 0; u < RU; u++)
-#pragma unroll
-        for (int v = 0; v < RV; v++) {
-            const int64_t gi = r0 + tx + 32 * u, gj = c0 + ty + TY * v;
-            acc[u][v] = (gi < a.n && gi >= gj) ? __ldcg(L + gi + gj * a.n) : T(0);
+        for (int q = 0; q < NP; q++) {
+            const int e = q * NTH + threadIdx.x, rr = e % TL, pp = e / TL;
+            const int64_t gi = r0 + rr, gj = c0 + rr;
+            li[q] = gi < a.n ? __ldcg(L + gi + (p0 + pp) * a.n) : T(0);
+            lj[q] = gj < a.n ? __ldcg(L + gj + (p0 + pp) * a.n) : T(0);
         }
-    __syncthreads();
-#pragma unroll 4
-    for (int p = 0; p < kB; p++) {
-        T li[RU], lj[RV];
-#pragma unroll
-        for (int u = 0; u < RU; u++) li[u] = Li[tx + 32 * u][p];
-#pragma unroll
-        for (int v = 0; v < RV; v++) lj[v] = Lj[ty + TY * v][p];
+        const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
 #pragma unroll
         for (int u = 0; u < RU; u++)
 #pragma unroll
-            for (int v = 0; v < RV; v++) acc[u][v] = N::sub(acc[u][v], N::mul(li[u], lj[v]));
+            for (int v = 0; v < RV; v++) {
+                const int64_t gi = r0 + tx + 32 * u, gj = c0 + ty + TY * v;
+                acc[u][v] = (gi < a.n && gi >= gj) ? __ldcg(L + gi + gj * a.n) : T(0);
+            }
     }
+    __device__ __forceinline__ void stage(T (*Li)[kB + 1], T (*Lj)[kB + 1]) const {
 #pragma unroll
-    for (int u = 0; u < RU; u++)
-#pragma unroll
-        for (int v = 0; v < RV; v++) {
-            const int64_t gi = r0 + tx + 32 * u, gj = c0 + ty + TY * v;
-            if (gi < a.n && gi >= gj) __stcg(L + gi + gj * a.n, acc[u][v]);
+        for (int q = 0; q < NP; q++) {
+            const int e = q * NTH + threadIdx.x, rr = e % TL, pp = e / TL;
+            Li[rr][pp] = li[q];
+            Lj[rr][pp] = lj[q];
         }
-    __syncthreads();
+    }
+    // After stage() and a barrier: subtract the panel's products and store the tile.
+    __device__ __forceinline__ void compute(const CholArgs<T>& a, int c, T (*Li)[kB + 1],
+                                            T (*Lj)[kB + 1]) {
+        using N = Num<T>;
+        T* L = a.base + (int64_t)c * a.n * a.n;
+        const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+#pragma unroll 4
+        for (int p = 0; p < kB; p++) {
+            T xi[RU], xj[RV];
+#pragma unroll
+            for (int u = 0; u < RU; u++) xi[u] = Li[tx + 32 * u][p];
+#pragma unroll
+            for (int v = 0; v < RV; v++) xj[v] = Lj[ty + TY * v][p];
+#pragma unroll
+            for (int u = 0; u < RU; u++)
+#pragma unroll
+                for (int v = 0; v < RV; v++) acc[u][v] = N::sub(acc[u][v], N::mul(xi[u], xj[v]));
+        }
+#pragma unroll
+        for (int u = 0; u < RU; u++)
+#pragma unroll
+            for (int v = 0; v < RV; v++) {
+                const int64_t gi = r0 + tx + 32 * u, gj = c0 + ty + TY * v;
+                if (gi < a.n && gi >= gj) __stcg(L + gi + gj * a.n, acc[u][v]);
+            }
+    }
+};
+
+// Tile index t of panel k's trailing matrix (nt x nt tiles, lower triangle) -> (bi, bj): tile
+// 0 is (0, 0); then the inner triangle (bj >= 1); the first tile column last.
+__device__ __forceinline__ void tile_of_index(unsigned int t, int64_t nt, int& bi, int& bj) {
+    const unsigned int inner = (unsigned int)((nt - 1) * nt / 2);
+    if (t == 0) {
+        bi = bj = 0;
+    } else if (t - 1 < inner) {
+        const int64_t u = t - 1;
+        int q = (int)((sqrt(8.0 * (double)u + 1.0) - 1.0) * 0.5);
+        while ((int64_t)(q + 1) * (q + 2) / 2 <= u) q++;
+        while ((int64_t)q * (q + 1) / 2 > u) q--;
+        bi = q + 1;
+        bj = (int)(u - (int64_t)q * (q + 1) / 2) + 1;
+    } else {
+        bi = (int)(t - inner);
+        bj = 0;
+    }
 }
 
 // One cluster per ladder candidate; the cluster's CTAs split each phase and meet at the
 // hardware cluster barrier (release/acquire at cluster scope), so no grid-wide barrier is
-// needed and candidates proceed independently.  Look-ahead: the trailing tile that holds the
-// next diagonal block is updated first (by rank 0), which then factorises that block while the
-// other CTAs carry on with the trailing update, so phase D leaves the critical path.
+// needed and candidates proceed independently.  One barrier per panel: rank 0 updates tile
+// (0, 0) -- which holds the next diagonal block -- factors that block, publishes it and solves
+// the tile's rows below it; the other CTAs take the remaining trailing tiles from an atomic
+// counter in rank 0's shared memory, the tiles of the first tile column (which hold the next
+// panel's rows) last, and whoever updates one of those then solves its rows against the
+// published block.  At the barrier the next panel is final.
 template <typename T, int TL>
 __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> a) {
     __shared__ T S[2 * TL][kB + 1];
-    // The panel's diagonal factor, transposed (row j = column j of the factor, zero above the
-    // diagonal), plus a zero row: row j read past its end runs into zeros.
     __shared__ __align__(16) T Dg[(kB + 1) * kB];
     __shared__ int s_bad;
-    __shared__ unsigned int s_ctr;      // rank 0: next trailing tile of the current panel
+    __shared__ unsigned int s_ctr[2];   // rank 0: next trailing tile (by panel parity)
     __shared__ unsigned int s_next[2];  // this CTA's next tile (double-buffered)
+    __shared__ int s_dg;                // panel whose diagonal factor Dg holds (-1: none)
     cg::cluster_group cl = cg::this_cluster();
     const int CL = (int)cl.num_blocks();
     const int rank = (int)cl.block_rank();
@@ -264,11 +375,19 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
     // A previous launch of the ladder already succeeded (sel is only written between launches).
     if (__ldcg(a.sel) >= 0) return;
     const int npanels = (int)((a.n + kB - 1) / kB);
-    // Diagnostics: the last candidate's rank-0 thread 0 stamps the end of P, of its look-ahead
-    // (tile 0 + D) and of U per panel.
+    int* dflag = a.dflag + c;  // last panel whose diagonal block is published
     unsigned long long* tr =
         (a.trace && c == a.nc - 1 && rank == 0 && threadIdx.x == 0) ? a.trace : nullptr;
+    if (threadIdx.x == 0) {
+        s_ctr[0] = 1u;  // tile 0 of every panel is rank 0's
+        s_ctr[1] = 1u;
+        s_dg = -1;
+    }
+    // Panel 0: its diagonal block, then its rows.
     if (rank == 0) chol_diag(a, c, 0, S, &s_bad);
+    cl.sync();
+    if (__ldcg(a.fail + c)) return;
+    chol_panel<T>(a, c, 0, rank, CL, Dg, nullptr);
     cl.sync();
     for (int k = 0; k < npanels; k++) {
         const int64_t p0 = (int64_t)k * kB;
@@ -277,34 +396,77 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
         if (__ldcg(a.fail + c)) return;  // the whole cluster leaves after the same barrier
         const int64_t rows = a.n - p0 - kB;
         if (rows <= 0) break;
-        chol_panel<T>(a, c, p0, rank, CL, Dg, st ? st + 1 : nullptr);
-        if (rank == 0 && threadIdx.x == 0) s_ctr = 1u;  // tile 0 is rank 0's
-        if (st) st[3] = global_ns();
-        cl.sync();
+        const int64_t t0 = p0 + kB;        // trailing matrix [t0, n)^2
         const int64_t nt = (rows + TL - 1) / TL;
         const unsigned int tiles = (unsigned int)(nt * (nt + 1) / 2);
-        // Tiles are handed out one at a time from rank 0's counter (tile 0, which holds the next
-        // diagonal block, is rank 0's); each CTA asks for its next tile while it computes.
-        unsigned int* ctr = cl.map_shared_rank(&s_ctr, 0);
-        unsigned int t = rank == 0 ? 0u : tiles;
+        const unsigned int inner = (unsigned int)((nt - 1) * nt / 2);  // tiles with bj >= 1
+        unsigned int* ctr = cl.map_shared_rank(&s_ctr[k & 1], 0);
+        unsigned int t = 0u;
         if (rank != 0) {
             if (threadIdx.x == 0) s_next[0] = atomicAdd(ctr, 1u);
             __syncthreads();
             t = s_next[0];
         }
-        for (int it = 1; t < tiles; it++) {
-            if (threadIdx.x == 0) s_next[it & 1] = atomicAdd(ctr, 1u);
-            int bi = (int)((sqrt(8.0 * (double)t + 1.0) - 1.0) * 0.5);
-            while ((int64_t)(bi + 1) * (bi + 2) / 2 <= (int64_t)t) bi++;
-            while ((int64_t)bi * (bi + 1) / 2 > (int64_t)t) bi--;
-            const int bj = (int)((int64_t)t - (int64_t)bi * (bi + 1) / 2);
-            chol_update_tile<T, TL>(a, c, p0, bi, bj, S, S + TL);  // ends with __syncthreads
-            if (t == 0) {  // the next diagonal block is final: factorise it now
-                if (st) st[4] = global_ns();
-                chol_diag(a, c, p0 + kB, S, &s_bad, st ? st + 5 : nullptr);
-            }
-            t = s_next[it & 1];
+        TileWork<T, TL> cur;
+        int bi = 0, bj = 0;
+        if (t < tiles) {
+            tile_of_index(t, nt, bi, bj);
+            cur.fetch(a, c, p0, bi, bj);
         }
+        // Rank 0 takes only tile 0 (then the diagonal block and its rows: the critical path);
+        // the other CTAs share every other tile.  Each tile's successor is fetched into
+        // registers while the tile computes.
+        for (int it = 1; t < tiles; it++) {
+            if (threadIdx.x == 0) s_next[it & 1] = rank == 0 ? tiles : atomicAdd(ctr, 1u);
+            cur.stage(S, S + TL);
+            __syncthreads();
+            const unsigned int tn = s_next[it & 1];
+            int bin = 0, bjn = 0;
+            TileWork<T, TL> nxt;
+            if (tn < tiles) {
+                tile_of_index(tn, nt, bin, bjn);
+                nxt.fetch(a, c, p0, bin, bjn);
+            }
+            cur.compute(a, c, S, S + TL);
+            __syncthreads();
+            if (t == 0) {  // the next diagonal block is final: factorise it and publish it
+                if (st) st[4] = global_ns();
+                chol_diag(a, c, t0, S, &s_bad, st ? st + 5 : nullptr);  // ends with a barrier
+                if (threadIdx.x == 0) {
+                    __threadfence();
+                    st_release_gpu(dflag, k + 1);  // published even on failure: waiters go on
+                }
+                // This CTA's copy of the block, transposed, straight from shared memory.
+                for (int e = threadIdx.x; e < kB * kB; e += chol_threads<T>()) {
+                    const int i = e % kB, j = e / kB;
+                    Dg[j * kB + i] = (i >= j && t0 + i < a.n) ? S[i][j] : T(0);
+                }
+                if (threadIdx.x < kB) Dg[kB * kB + threadIdx.x] = T(0);
+                __syncthreads();
+                if (threadIdx.x == 0) s_dg = k + 1;
+                __syncthreads();
+            }
+            if (bj == 0) {  // rows of the next panel in this tile: solve them
+                const int64_t r_lo = t0 + (int64_t)bi * TL > t0 + kB ? t0 + (int64_t)bi * TL : t0 + kB;
+                const int64_t r_hi = t0 + (int64_t)(bi + 1) * TL < a.n ? t0 + (int64_t)(bi + 1) * TL : a.n;
+                if (r_lo < r_hi) {
+                    if (s_dg != k + 1) {
+                        if (threadIdx.x == 0) wait_flag_gpu(dflag, k + 1, a.err);
+                        __syncthreads();
+                        load_diag_t(a, c, t0, Dg);
+                        __syncthreads();
+                        if (threadIdx.x == 0) s_dg = k + 1;
+                    }
+                    chol_rows(a, c, t0, r_lo, r_hi, Dg);
+                    __syncthreads();
+                }
+            }
+            cur = nxt;
+            t = tn;
+            bi = bin;
+            bj = bjn;
+        }
+        if (rank == 0 && threadIdx.x == 0) s_ctr[(k + 1) & 1] = 1u;  // the next panel's counter
         if (st) st[7] = global_ns();
         cl.sync();
     }
@@ -453,6 +615,7 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
         if (first > 0) {
             GPB2_CUDA_TRY(cudaMemsetAsync(fail, 0, sizeof(int) * 16, s));
             GPB2_CUDA_TRY(cudaMemsetAsync(done, 0, sizeof(int) * 16, s));
+            GPB2_CUDA_TRY(cudaMemsetAsync(p->lad + kLadDflag, 0, sizeof(int) * 16, s));
         }
         GPB2_CUDA_TRY(launch_prof("dense_assemble", k_ladder_assemble<T>,
                                   dim3((unsigned)std::min<int64_t>(n, 4 * 148)), dim3(256), smem,
@@ -467,7 +630,8 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
                                           s));
             trace = static_cast<unsigned long long*>(p->trace);
         }
-        CholArgs<T> args{base, n, nc, first, fail, sel, done, trace};
+        CholArgs<T> args{base, n,    nc,   first, fail, sel, done, p->lad + kLadDflag,
+                         p->lad + kLadBarErr, trace};
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)(nc * csize));
         cfg.blockDim = dim3(chol_threads<T>());

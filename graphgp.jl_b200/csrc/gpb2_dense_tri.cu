@@ -13,6 +13,15 @@
 // u = L^T vb.  So Phi(L^T Lbar) = Phi(tril(u xi^T)) needs one matrix-vector product instead of a
 // triangular matrix product, and it is generated on the fly from u and xi.
 //
+// With A = L^-1 (computed once per factorisation, below) and P = D_u T' D_xi, where T' is the
+// lower all-ones matrix with 1/2 on its diagonal,  S = A^T P A = F^T H  with F = D_u A and
+// H = T' D_xi A (a running sum down each column of D_xi A, the current term halved): one GEMM
+// per call.  A itself is built by recursive doubling from the inverses of the 32x32 diagonal
+// blocks: for consecutive diagonal blocks of size s, A21 = -A22 (L21 A11), two strided-batched
+// GEMMs per level.  (k_trsm_lt below solves the same problem column-chunk by column-chunk, as
+// two triangular solves X = L^-T P, S^T = L^-T X^T; it serves blocks too large for the inverse
+// workspace.)
+//
 // S is then two triangular solves with n right-hand sides:  X = L^-T P  and  S^T = L^-T X^T.
 // k_trsm_lt solves L^T X = B for a chunk of NB right-hand-side columns per CTA, by 32-row blocks
 // from the bottom: the rows already solved stay in shared memory; the block's right-hand side is
@@ -70,48 +79,67 @@ __global__ void k_transpose_lower(const T* __restrict__ L, T* __restrict__ R, in
 // Exact-order L*x (TRANS = false) and L^T*x (TRANS = true), outputs [i0, i0 + 32) per CTA.
 //   L x:   y_i = sum_{j=0..i} L[i][j] x_j   (column-major factor: M(i, j) = L[i + j*n])
 //   L^T x: y_i = sum_{k=i..n-1} L[k][i] x_k (row-major copy:     M(i, k) = R[k*ld + i])
-// Warps 1.. load stage c+1 while warp 0 (lane = output) adds up stage c.
+// Warps 1.. form the rounded products of chunk c+1 (terms outside the sum are +0, which leaves
+// the running sum unchanged: it starts at +0 and can never become -0) while warp 0 (lane =
+// output) adds up chunk c in order.
 template <typename T, bool TRANS>
 __global__ void __launch_bounds__(kTriThreads)
 k_trmv_exact(const T* __restrict__ M, int64_t ld, const T* __restrict__ x, T* __restrict__ y,
              int64_t n) {
     using N = Num<T>;
-    constexpr int kTrmvChunk = 512 / (int)sizeof(T);  // rows per stage: 2 x 16 KB of tiles
-    __shared__ T tile[2][kTrmvChunk][32];
-    __shared__ T xs[2][kTrmvChunk];
+    constexpr int kCh = 512 / (int)sizeof(T);  // terms per stage: 2 x 16 KB of products
+    __shared__ T prod[2][kCh][32];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t i0 = (int64_t)blockIdx.x * 32, i = i0 + lane;
     const int64_t lo = TRANS ? i0 : 0;  // summation index range
     const int64_t hi = TRANS ? n : (i0 + 32 < n ? i0 + 32 : n);
-    const int64_t nch = (hi - lo + kTrmvChunk - 1) / kTrmvChunk;
-    auto load = [&](int64_t c, int buf, int t0, int nt) {
-        for (int e = t0; e < kTrmvChunk * 32; e += nt) {
+    const int64_t nch = (hi - lo + kCh - 1) / kCh;
+    // Each filling thread issues all its loads before any product is formed (one memory
+    // latency per stage instead of one per element).
+    auto fill = [&](int64_t c, int buf, int t0, int nt) {
+        constexpr int kPer = (kCh * 32 + 223) / 224;  // elements per thread when 224 fill
+        T mv[kPer], xv[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; u++) {
+            const int e = t0 + u * nt;
             const int kk = e >> 5, ii = e & 31;
-            const int64_t k = lo + c * kTrmvChunk + kk, r = i0 + ii;
-            T v = T(0);
-            if (k < hi && r < n) v = TRANS ? M[k * ld + r] : M[r + k * n];
-            tile[buf][kk][ii] = v;
+            const int64_t k = lo + c * kCh + kk, r = i0 + ii;
+            const bool in = e < kCh * 32 && k < hi && r < n && (TRANS ? k >= r : k <= r);
+            mv[u] = in ? (TRANS ? M[k * ld + r] : M[r + k * n]) : T(0);
+            xv[u] = in ? x[k] : T(0);
         }
-        for (int kk = t0; kk < kTrmvChunk; kk += nt) {
-            const int64_t k = lo + c * kTrmvChunk + kk;
-            xs[buf][kk] = k < hi ? x[k] : T(0);
+#pragma unroll
+        for (int u = 0; u < kPer; u++) {
+            const int e = t0 + u * nt;
+            if (e < kCh * 32) prod[buf][e >> 5][e & 31] = N::mul(mv[u], xv[u]);
+        }
+        for (int e = t0 + kPer * nt; e < kCh * 32; e += nt) {  // only when more threads idle
+            const int kk = e >> 5, ii = e & 31;
+            const int64_t k = lo + c * kCh + kk, r = i0 + ii;
+            T v = T(0);
+            if (k < hi && r < n && (TRANS ? k >= r : k <= r))
+                v = N::mul(TRANS ? M[k * ld + r] : M[r + k * n], x[k]);
+            prod[buf][kk][ii] = v;
         }
     };
-    load(0, 0, threadIdx.x, kTriThreads);
+    fill(0, 0, threadIdx.x, kTriThreads);
     __syncthreads();
     T acc = T(0);
     for (int64_t c = 0; c < nch; c++) {
         const int buf = (int)(c & 1);
         if (w != 0) {
-            if (c + 1 < nch) load(c + 1, buf ^ 1, threadIdx.x - 32, kTriThreads - 32);
+            if (c + 1 < nch) fill(c + 1, buf ^ 1, threadIdx.x - 32, kTriThreads - 32);
         } else {
-            const int64_t k0 = lo + c * kTrmvChunk;
-            for (int kk = 0; kk < kTrmvChunk; kk++) {
-                const int64_t k = k0 + kk;
-                if (k >= hi) break;
-                if (TRANS ? (k >= i) : (k <= i))
-                    acc = N::add(acc, N::mul(tile[buf][kk][lane], xs[buf][kk]));
+            const int cnt = (int)(hi - (lo + c * kCh) < kCh ? hi - (lo + c * kCh) : kCh);
+            int kk = 0;
+            for (; kk + 8 <= cnt; kk += 8) {
+                T q[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) q[u] = prod[buf][kk + u][lane];
+#pragma unroll
+                for (int u = 0; u < 8; u++) acc = N::add(acc, q[u]);
             }
+            for (; kk < cnt; kk++) acc = N::add(acc, prod[buf][kk][lane]);
         }
         __syncthreads();
     }
@@ -199,15 +227,15 @@ k_trsm_lt(const T* __restrict__ Lr, int64_t ld, const T* __restrict__ DinvT,
     for (int st = 0; st < NS - 1; st++) issue();
     int ctile = 0;  // tiles consumed
 
-    for (int64_t I = nbk - 1; I >= 0; I--) {
-        const int64_t r0 = I * kTB, r1 = r0 + kTB < n ? r0 + kTB : n;
-        // Operands of the block's finish, fetched now so their latency hides behind the tiles.
-        constexpr int kDin = kTB * kTB / kTriThreads;
-        T dreg[kDin];
+    // Operands of a block's finish (its diagonal inverse and right-hand side), fetched one block
+    // ahead so their latency hides behind the previous block's tiles.
+    constexpr int kDin = kTB * kTB / kTriThreads;
+    constexpr int kRhs = (kTB * NB + kTriThreads - 1) / kTriThreads;
+    auto fetch = [&](int64_t I, T (&dreg)[kDin], T (&breg)[kRhs]) {
+        const int64_t r0 = I * kTB;
 #pragma unroll
-        for (int q = 0; q < kDin; q++) dreg[q] = DinvT[I * kTB * kTB + threadIdx.x + q * kTriThreads];
-        constexpr int kRhs = (kTB * NB + kTriThreads - 1) / kTriThreads;
-        T breg[kRhs];
+        for (int q = 0; q < kDin; q++)
+            dreg[q] = DinvT[I * kTB * kTB + threadIdx.x + q * kTriThreads];
 #pragma unroll
         for (int q = 0; q < kRhs; q++) {
             const int e = threadIdx.x + q * kTriThreads;
@@ -224,6 +252,14 @@ k_trsm_lt(const T* __restrict__ Lr, int64_t ld, const T* __restrict__ DinvT,
             }
             breg[q] = b;
         }
+    };
+    T dreg[kDin], breg[kRhs];
+    fetch(nbk - 1, dreg, breg);
+
+    for (int64_t I = nbk - 1; I >= 0; I--) {
+        const int64_t r0 = I * kTB, r1 = r0 + kTB < n ? r0 + kTB : n;
+        T dnext[kDin], bnext[kRhs];
+        if (I > 0) fetch(I - 1, dnext, bnext);
         // (1) partial sums of L[k][r0 + lane] * X[k][c] over the solved rows k >= r1
         T acc[NB];
 #pragma unroll
@@ -232,13 +268,25 @@ k_trsm_lt(const T* __restrict__ Lr, int64_t ld, const T* __restrict__ DinvT,
             __pipeline_wait_prior(NS - 2);  // this thread's copies of tile `ctile` have landed
             __syncthreads();                // everyone's; the stage of tile ctile-1 is free
             issue();
-            const T* tl = Lt + (size_t)(ctile % NS) * kTileRows * kTB;
-            const int rows = (int)(n - k0 < kTileRows ? n - k0 : kTileRows);
-            for (int kk = w; kk < rows; kk += kTriWarps) {
-                const T l = tl[kk * kTB + lane];
-                const T* xr = Xs + (k0 + kk) * NB;
+            const T* tl = Lt + (ctile % NS) * (kTileRows * kTB) + lane;
+            const T* xt = Xs + (int)k0 * NB;
+            if (n - k0 >= kTileRows) {
 #pragma unroll
-                for (int c = 0; c < NB; c++) acc[c] = fma(l, xr[c], acc[c]);
+                for (int q = 0; q < kTileRows / kTriWarps; q++) {
+                    const int kk = w + q * kTriWarps;
+                    const T l = tl[kk * kTB];
+                    const T* xr = xt + kk * NB;
+#pragma unroll
+                    for (int c = 0; c < NB; c++) acc[c] = fma(l, xr[c], acc[c]);
+                }
+            } else {
+                const int rows = (int)(n - k0);
+                for (int kk = w; kk < rows; kk += kTriWarps) {
+                    const T l = tl[kk * kTB];
+                    const T* xr = xt + kk * NB;
+#pragma unroll
+                    for (int c = 0; c < NB; c++) acc[c] = fma(l, xr[c], acc[c]);
+                }
             }
             ctile++;
         }
@@ -274,8 +322,65 @@ k_trsm_lt(const T* __restrict__ Lr, int64_t ld, const T* __restrict__ DinvT,
             if (gi < n && gc < n) Xout[gi * n + gc] = x;
         }
         __syncthreads();
+        if (I > 0) {
+#pragma unroll
+            for (int q = 0; q < kDin; q++) dreg[q] = dnext[q];
+#pragma unroll
+            for (int q = 0; q < kRhs; q++) breg[q] = bnext[q];
+        }
     }
     __pipeline_wait_prior(0);
+}
+
+// A = L^-1 before the doubling: the inverses of the 32x32 diagonal blocks in place, zero
+// elsewhere (column-major n x n).
+template <typename T>
+__global__ void k_ainv_init(const T* __restrict__ DinvT, int64_t n, T* __restrict__ A) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n * n;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t col = e / n, row = e - col * n;
+        T v = T(0);
+        if (row / kTB == col / kTB && row >= col) {
+            const int64_t b = row / kTB;
+            const int i = (int)(row - b * kTB), j = (int)(col - b * kTB);
+            v = DinvT[b * kTB * kTB + j * kTB + i];  // DinvT[b][j][i] = (L_bb^-1)[i][j]
+        }
+        A[e] = v;
+    }
+}
+
+// F = D_u A and H = T' D_xi A (column-major n x n): one warp per column b, a warp scan down the
+// rows: H[c][b] = sum_{b <= k < c} xi_k A[k][b] + xi_c A[c][b] / 2 (zero above the diagonal).
+template <typename T>
+__global__ void k_pullback_fh(const T* __restrict__ A, const T* __restrict__ u,
+                              const T* __restrict__ xi, int64_t n, T* __restrict__ F,
+                              T* __restrict__ H) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n;
+         b += warps) {
+        const T* a = A + b * n;
+        T* f = F + b * n;
+        T* h = H + b * n;
+        T carry = T(0);
+        for (int64_t c0 = 0; c0 < n; c0 += 32) {
+            const int64_t c = c0 + lane;
+            const bool in = c < n;
+            const T av = (in && c >= b) ? a[c] : T(0);
+            const T g = in ? xi[c] * av : T(0);
+            T incl = g;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const T t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            if (in) {
+                f[c] = u[c] * av;
+                h[c] = carry + incl - T(0.5) * g;
+            }
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+    }
 }
 
 template <typename T, int NB>
@@ -322,6 +427,67 @@ int trsm_lt(gpb2_problem* p, bool gen, const T* u, const T* xi, const T* Bin, T*
     return launch_trsm<T, 4>(p, gen, u, xi, Bin, Xout, s);
 }
 
+inline cublasStatus_t gemm_sb(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb,
+                              int m, int nn, int k, float alpha, const float* A, int lda,
+                              long long sA, const float* B, int ldb, long long sB, float beta,
+                              float* C, int ldc, long long sC, int batch) {
+    return cublasSgemmStridedBatched(h, ta, tb, m, nn, k, &alpha, A, lda, sA, B, ldb, sB, &beta,
+                                     C, ldc, sC, batch);
+}
+inline cublasStatus_t gemm_sb(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb,
+                              int m, int nn, int k, double alpha, const double* A, int lda,
+                              long long sA, const double* B, int ldb, long long sB, double beta,
+                              double* C, int ldc, long long sC, int batch) {
+    return cublasDgemmStridedBatched(h, ta, tb, m, nn, k, &alpha, A, lda, sA, B, ldb, sB, &beta,
+                                     C, ldc, sC, batch);
+}
+
+#define GPB2_TRI_BLAS(expr)                                                                      \
+    do {                                                                                         \
+        cublasStatus_t _b = (expr);                                                              \
+        if (_b != CUBLAS_STATUS_SUCCESS)                                                         \
+            return set_error(GPB2_ERR_CUDA, "%s:%d: cuBLAS status %d", __FILE__, __LINE__,       \
+                             (int)_b);                                                           \
+    } while (0)
+
+// A = L^-1 by recursive doubling (see the top of the file).  W: n*n/2 + n entries of work.
+template <typename T>
+int build_inverse(gpb2_problem* p, T* A, T* W, cudaStream_t s) {
+    const int64_t n = p->n0;
+    const T* L = static_cast<const T*>(p->Ld);
+    GPB2_CUDA_TRY(launch_prof("dense_ainv_init", k_ainv_init<T>,
+                              dim3((unsigned)std::min<int64_t>((n * n + 255) / 256, 8 * 148)),
+                              dim3(256), 0, s, (const T*)p->Dinv, n, A));
+    GPB2_TRI_BLAS(cublasSetStream(p->blas, s));
+    const int ni = (int)n;
+    for (int64_t sz = kTB; sz < n; sz *= 2) {
+        const int64_t full = n / (2 * sz);  // complete pairs (A11, A22 both of size sz)
+        const long long diag = 2 * sz * (n + 1);  // stride between pairs along the diagonal
+        const int si = (int)sz;
+        if (full > 0) {
+            // W_b = L21 A11, then A21 = -A22 W_b
+            GPB2_TRI_BLAS(gemm_sb(p->blas, CUBLAS_OP_N, CUBLAS_OP_N, si, si, si, T(1), L + sz, ni,
+                                  diag, A, ni, diag, T(0), W, si, (long long)sz * sz,
+                                  (int)full));
+            GPB2_TRI_BLAS(gemm_sb(p->blas, CUBLAS_OP_N, CUBLAS_OP_N, si, si, si, T(-1),
+                                  A + sz * (n + 1), ni, diag, W, si, (long long)sz * sz, T(0),
+                                  A + sz, ni, diag, (int)full));
+        }
+        const int64_t j = full * 2 * sz;  // a trailing A11 of size sz with a shorter A22
+        const int64_t r = n - j - sz;
+        if (r > 0) {
+            const int ri = (int)r;
+            GPB2_TRI_BLAS(gemm_sb(p->blas, CUBLAS_OP_N, CUBLAS_OP_N, ri, si, si, T(1),
+                                  L + (j + sz) + j * n, ni, 0, A + j + j * n, ni, 0, T(0), W, ri,
+                                  0, 1));
+            GPB2_TRI_BLAS(gemm_sb(p->blas, CUBLAS_OP_N, CUBLAS_OP_N, ri, si, ri, T(-1),
+                                  A + (j + sz) + (j + sz) * n, ni, 0, W, ri, 0, T(0),
+                                  A + (j + sz) + j * n, ni, 0, 1));
+        }
+    }
+    return GPB2_OK;
+}
+
 }  // namespace
 
 template <typename T>
@@ -337,6 +503,7 @@ int dense_tri_prepare(gpb2_problem* p, cudaStream_t s) {
     GPB2_TRY(ensure_alloc(&p->Ldr, sizeof(T) * (size_t)n * (size_t)ld));
     GPB2_TRY(ensure_alloc(&p->Dinv, sizeof(T) * (size_t)nbk * kTB * kTB));
     GPB2_TRY(ensure_alloc(&p->Wtri, sizeof(T) * (2 * nn + (size_t)n)));
+    GPB2_TRY(ensure_alloc(&p->Ainv, sizeof(T) * nn));
     GPB2_CUDA_TRY(launch_prof("dense_transpose", k_transpose_lower<T>,
                               dim3((unsigned)std::min<int64_t>(nbk * nbk, 4 * 148)),
                               dim3(kTriThreads), 0, s, (const T*)p->Ld, (T*)p->Ldr, n, ld));
@@ -344,7 +511,10 @@ int dense_tri_prepare(gpb2_problem* p, cudaStream_t s) {
                               dim3((unsigned)((nbk + kDiagWarps - 1) / kDiagWarps)),
                               dim3(32 * kDiagWarps), 0, s, (const T*)p->Ldr, n, ld,
                               (T*)p->Dinv));
-    return GPB2_OK;
+    const ProfToken t = prof_begin("dense_inverse", s);
+    const int st = build_inverse<T>(p, static_cast<T*>(p->Ainv), static_cast<T*>(p->Wtri), s);
+    prof_end(t, s);
+    return st;
 }
 
 template <typename T>
@@ -365,12 +535,21 @@ int dense_chol_pullback_outer(gpb2_problem* p, const T* vb, const T* xi, const T
                               cudaStream_t s) {
     const int64_t n = p->n0;
     const size_t nn = (size_t)n * (size_t)n;
-    T* X = static_cast<T*>(p->Wtri);
-    T* S = X + nn;
-    T* u = S + nn;
-    GPB2_TRY(dense_trmv<T>(p, true, vb, u, s));                 // u = L^T vb
-    GPB2_TRY(trsm_lt<T>(p, true, u, xi, nullptr, X, s));        // X = L^-T Phi(...), as X^T
-    GPB2_TRY(trsm_lt<T>(p, false, nullptr, nullptr, X, S, s));  // S^T = L^-T X^T, as S
+    T* F = static_cast<T*>(p->Wtri);
+    T* H = F + nn;
+    T* u = H + nn;
+    T* S = static_cast<T*>(p->Wd2);
+    GPB2_TRY(dense_trmv<T>(p, true, vb, u, s));  // u = L^T vb
+    GPB2_CUDA_TRY(launch_prof("dense_pullback_fh", k_pullback_fh<T>,
+                              dim3((unsigned)std::min<int64_t>((n + 7) / 8, 8 * 148)),
+                              dim3(256), 0, s, (const T*)p->Ainv, (const T*)u, xi, n, F, H));
+    GPB2_TRI_BLAS(cublasSetStream(p->blas, s));
+    const int ni = (int)n;
+    const ProfToken t = prof_begin("dense_gemm", s);
+    const cublasStatus_t st = gemm_sb(p->blas, CUBLAS_OP_T, CUBLAS_OP_N, ni, ni, ni, T(1), F, ni,
+                                      0, H, ni, 0, T(0), S, ni, 0, 1);  // S = F^T H
+    prof_end(t, s);
+    GPB2_TRI_BLAS(st);
     *S_out = S;  // column-major S
     return GPB2_OK;
 }

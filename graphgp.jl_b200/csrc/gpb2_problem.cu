@@ -211,7 +211,7 @@ static void free_problem(gpb2_problem* p) {
                     p->start,  p->mv,   p->sd,      p->buf_a, p->buf_b, p->buf_c,
                     p->buf_d,  p->dacc, p->Lcand,   p->lad,  p->Wd,    p->Wd2,
                     p->dwork,  p->dinfo, p->d_offsets, p->dsync, p->Ld,    p->trace,
-                    p->Ldr,    p->Dinv,  p->Wtri};
+                    p->Ldr,    p->Dinv,  p->Wtri, p->Ainv};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);

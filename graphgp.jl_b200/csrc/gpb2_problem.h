@@ -55,6 +55,7 @@ struct gpb2_problem {
     void* Ldr = nullptr;      // row-major copy of Ld, rows padded to 32 (triangular kernels)
     void* Dinv = nullptr;     // transposed inverses of Ld's 32x32 diagonal blocks
     void* Wtri = nullptr;     // 2 n0^2 + n0 T: the triangular kernels' work
+    void* Ainv = nullptr;     // (n0, n0) column-major L^-1 of the current factor
     bool tri_ready = false;   // Ldr / Dinv belong to the current Ld
     void* Wd = nullptr;       // (n0, n0) work
     void* Wd2 = nullptr;      // (n0, n0) work
@@ -77,7 +78,8 @@ constexpr int kLadDone = 16;    // [16, 32): per-candidate completion flags
 constexpr int kLadSel = 32;     // ladder index of the first success (-1: none), then its slot
 constexpr int kLadNotPD = 34;   // set when no candidate succeeded
 constexpr int kLadBarErr = 36;  // error word of the factorisation (0: none)
-constexpr int kLadInts = 48;
+constexpr int kLadDflag = 48;   // [48, 64): per-candidate last published diagonal panel
+constexpr int kLadInts = 64;
 
 // RAII: make the problem's device current for the duration of a call, restore afterwards.
 struct DeviceGuard {
