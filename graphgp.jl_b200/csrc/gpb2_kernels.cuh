@@ -598,6 +598,63 @@ k_sweep_rev_all(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv
     }
 }
 
+// generate_grad_vals needs both the forward field v (from xi) and the reverse cotangent vb (from
+// vbar); neither sweep reads the other's output, so one persistent kernel runs them together:
+// step i sweeps forward batch i and reverse batch nbatch-1-i, one grid barrier per step instead
+// of one per batch of each sweep.  Per point, the same arithmetic and order as
+// k_sweep_fwd_all / k_sweep_rev_all (the reverse accumulation order is atomic either way).
+template <typename T, int K>
+__global__ void __launch_bounds__(kPersistThreads)
+k_sweep_fwdrev_all(T* __restrict__ values, const T* __restrict__ xi_ref, T* __restrict__ vb,
+                   const T* __restrict__ mv, const T* __restrict__ sd,
+                   const int* __restrict__ nbrs, int64_t n0, const int64_t* __restrict__ offs,
+                   int nbatch, GridSync gs) {
+    using N = Num<T>;
+    const int64_t gtid = (int64_t)threadIdx.x * gridDim.x + blockIdx.x;
+    const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
+    SweepPoint<T, K> fp, rp;
+    int64_t pf = offs[0] + gtid, pr = offs[nbatch - 1] + gtid;
+    bool hf = pf < offs[1], hr = pr < offs[nbatch];
+    if (hf) fp.load_fwd(mv, sd, xi_ref, nbrs, pf - n0);
+    if (hr) rp.load_rev(mv, sd, nbrs, pr - n0);
+    for (int i = 0; i < nbatch; i++) {
+        const int br = nbatch - 1 - i;
+        const int64_t hif = offs[i + 1], hir = offs[br + 1];
+        while (hf || hr) {
+            if (hf) {
+                T acc = fp.a;
+                sfor<0, K>([&](auto j_) {
+                    GPB2_CI(j);
+                    acc = N::add(acc, N::mul(fp.w[j], __ldcg(values + fp.nb[j])));
+                });
+                __stcg(values + pf, acc);
+                pf += gsz;
+                hf = pf < hif;
+                if (hf) fp.load_fwd(mv, sd, xi_ref, nbrs, pf - n0);
+            }
+            if (hr) {
+                const T vbp = __ldcg(vb + pr);
+                sfor<0, K>([&](auto j_) {
+                    GPB2_CI(j);
+                    atomicAdd(vb + rp.nb[j], N::mul(rp.w[j], vbp));
+                });
+                pr += gsz;
+                hr = pr < hir;
+                if (hr) rp.load_rev(mv, sd, nbrs, pr - n0);
+            }
+        }
+        if (i + 1 < nbatch) {
+            pf = offs[i + 1] + gtid;
+            hf = pf < offs[i + 2];
+            if (hf) fp.load_fwd(mv, sd, xi_ref, nbrs, pf - n0);
+            pr = offs[br - 1] + gtid;
+            hr = pr < offs[br];
+            if (hr) rp.load_rev(mv, sd, nbrs, pr - n0);
+            if (!grid_sync(gs)) return;
+        }
+    }
+}
+
 // Co-resident grid of a cooperative kernel (occupancy x SM count).
 int coop_grid(const void* kernel, int threads, size_t smem);
 
@@ -615,6 +672,8 @@ struct Ops {
     cudaError_t (*inv_loss_grad)(const PointArgs<T>&, const T*, double*, double*, T*, int64_t,
                                  cudaStream_t);
     cudaError_t (*fused_fwd)(const PointArgs<T>&, T*, const T*, int64_t, int64_t, cudaStream_t);
+    cudaError_t (*sweep_fwdrev_all)(T*, const T*, T*, const T*, const T*, const int*, int64_t,
+                                    const int64_t*, int, GridSync, cudaStream_t);
     cudaError_t (*sweep_fwd_flow)(T*, const T*, const T*, const T*, const int*, int64_t, int64_t,
                                   int*, cudaStream_t);
     cudaError_t (*sweep_fwd)(T*, const T*, const T*, const T*, const int*, int64_t, int64_t,
@@ -715,6 +774,14 @@ struct Launch {
         return coop("sweep_fwd_flow", k_sweep_fwd_flow<T, K>, s, values, xi_ref, mv, sd, nbrs,
                     n0, n, err);
     }
+    static cudaError_t sweep_fwdrev_all(T* values, const T* xi_ref, T* vb, const T* mv,
+                                        const T* sd, const int* nbrs, int64_t n0,
+                                        const int64_t* offs, int nbatch, GridSync gs,
+                                        cudaStream_t s) {
+        if (nbatch <= 0) return cudaSuccess;
+        return coop("sweep_fwdrev_all", k_sweep_fwdrev_all<T, K>, s, values, xi_ref, vb, mv, sd,
+                    nbrs, n0, offs, nbatch, gs);
+    }
     static cudaError_t sweep_rev_all(T* xg, T* vb, const T* mv, const T* sd, const int* nbrs,
                                      int64_t n0, const int64_t* offs, int nbatch, GridSync gs,
                                      cudaStream_t s) {
@@ -723,9 +790,11 @@ struct Launch {
                     nbatch, gs);
     }
     static const Ops<T>* ops() {
-        static const Ops<T> o = {factor,        inv,           logdet,    logdet_grad,
-                                 grad_vals,     inv_loss_grad, fused_fwd, sweep_fwd_flow,
-                                 sweep_fwd,     sweep_rev,     sweep_fwd_all, sweep_rev_all};
+        static const Ops<T> o = {factor,        inv,           logdet,
+                                 logdet_grad,   grad_vals,     inv_loss_grad,
+                                 fused_fwd,     sweep_fwdrev_all, sweep_fwd_flow,
+                                 sweep_fwd,     sweep_rev,     sweep_fwd_all,
+                                 sweep_rev_all};
         return &o;
     }
 };

@@ -340,13 +340,21 @@ struct Impl {
         GPB2_TRY(Dense<T>::factor(p, s));
         GPB2_TRY(Dense<T>::apply_L(p, xt, v, s));
         GPB2_TRY(factor_all(p, s));
-        GPB2_TRY(refine_sweep(p, v, xt + p->n0, true, s));
         if (p->indices)
             GPB2_TRY(gather(p, vbar, vb, s));
         else
             GPB2_CUDA_TRY(
                 cudaMemcpyAsync(vb, vbar, sizeof(T) * p->n, cudaMemcpyDeviceToDevice, s));
-        GPB2_TRY(reverse_sweep(p, nullptr, vb, s));
+        if (fwd_mode() == FwdMode::Persistent) {  // both sweeps in one persistent kernel
+            GPB2_TRY(arm_sync(p, s));
+            GPB2_TRY(check_launch(ops_of<T>(p)->sweep_fwdrev_all(
+                                      v, xt + p->n0, vb, (const T*)p->mv, (const T*)p->sd,
+                                      p->nbrs, p->n0, p->d_offsets, nbatch(p), grid_sync_of(p), s),
+                                  "forward+reverse sweep"));
+        } else {
+            GPB2_TRY(refine_sweep(p, v, xt + p->n0, true, s));
+            GPB2_TRY(reverse_sweep(p, nullptr, vb, s));
+        }
         GPB2_TRY(zero_acc(p, s));
         GPB2_TRY(check_launch(
             ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb, (const T*)p->mv, p->dacc, p->m, s),
