@@ -44,6 +44,9 @@ template <> struct Num<float> {
     static __device__ __forceinline__ float sub(float a, float b) { return __fsub_rn(a, b); }
     static __device__ __forceinline__ float div(float a, float b) { return __fdiv_rn(a, b); }
     static __device__ __forceinline__ float sqrt(float a) { return __fsqrt_rn(a); }
+    // c - a*b with one rounding (adjoint arithmetic only: not part of any exact-order path)
+    static __device__ __forceinline__ float fms(float a, float b, float c) { return fmaf(-a, b, c); }
+    static __device__ __forceinline__ float div_fast(float a, float b) { return __fdividef(a, b); }
     static __device__ __forceinline__ float log(float a) { return logf(a); }
     static __device__ __forceinline__ float from_i64(long long x) { return __ll2float_rn(x); }
     static __device__ __forceinline__ U bits(float x) { return __float_as_uint(x); }
@@ -57,6 +60,10 @@ template <> struct Num<double> {
     static __device__ __forceinline__ double sub(double a, double b) { return __dsub_rn(a, b); }
     static __device__ __forceinline__ double div(double a, double b) { return __ddiv_rn(a, b); }
     static __device__ __forceinline__ double sqrt(double a) { return __dsqrt_rn(a); }
+    static __device__ __forceinline__ double fms(double a, double b, double c) {
+        return fma(-a, b, c);
+    }
+    static __device__ __forceinline__ double div_fast(double a, double b) { return a / b; }
     static __device__ __forceinline__ double log(double a) { return ::log(a); }
     static __device__ __forceinline__ double from_i64(long long x) { return __ll2double_rn(x); }
     static __device__ __forceinline__ U bits(double x) {
@@ -161,6 +168,18 @@ struct SmemTable {
         const T x0 = seg[4 * lo + 0];
         const T x1 = seg[4 * lo + 1];
         const T t = N::div(N::sub(r, x0), N::sub(x1, x0));
+        wlo = N::sub(T(1), t);
+        whi = t;
+        return lo;
+    }
+    // The same with a fast (not correctly rounded) division: the gradient histograms' weights.
+    __device__ __forceinline__ int weights_fast(T r, T& wlo, T& whi) const {
+        if (r <= b0) { wlo = T(1); whi = T(0); return 0; }
+        if (r >= bN) { wlo = T(0); whi = T(1); return nb - 2; }
+        const int lo = locate(r);
+        const T x0 = seg[4 * lo + 0];
+        const T x1 = seg[4 * lo + 1];
+        const T t = N::div_fast(N::sub(r, x0), N::sub(x1, x0));
         wlo = N::sub(T(1), t);
         whi = t;
         return lo;
@@ -365,21 +384,33 @@ struct PointMath {
         });
     }
 
+    // Reciprocals of the factor's pivots (the adjoint arithmetic below multiplies by them).
+    static __device__ __forceinline__ void pivot_recips(T (&rp)[KP1], const T (&L)[NT]) {
+        sfor<0, KP1>([&](auto j_) {
+            GPB2_CI(j);
+            rp[j] = N::div(T(1), L[tri(j, j)]);
+        });
+    }
+
     // Adjoint of mean_vec_solve!: forward substitution L[0:K,0:K] z = z_in, optionally with
     // the pivot guard (src/kernels_adjoint.jl:520-530) or without it (src/grad.jl:574-580).
+    // Adjoint arithmetic (here and in seed_from_solve / pullback): fused multiply-adds and
+    // multiplication by the pivot reciprocals, not the forward's exact order -- these feed
+    // gradients, which are compared within tolerance.
     template <bool GUARD>
-    static __device__ __forceinline__ void forward_subst(T (&z)[K], const T (&L)[NT], T pivfloor) {
+    static __device__ __forceinline__ void forward_subst(T (&z)[K], const T (&L)[NT],
+                                                         const T (&rp)[KP1], T pivfloor) {
         sfor<0, K>([&](auto i_) {
             GPB2_CI(i);
             T s = z[i];
             sfor<0, i>([&](auto q_) {
                 GPB2_CI(q);
-                s = N::sub(s, N::mul(L[tri(i, q)], z[q]));
+                s = N::fms(L[tri(i, q)], z[q], s);
             });
             if constexpr (GUARD)
-                z[i] = L[tri(i, i)] > pivfloor ? N::div(s, L[tri(i, i)]) : T(0);
+                z[i] = L[tri(i, i)] > pivfloor ? N::mul(s, rp[i]) : T(0);
             else
-                z[i] = N::div(s, L[tri(i, i)]);
+                z[i] = N::mul(s, rp[i]);
         });
     }
 
@@ -392,7 +423,7 @@ struct PointMath {
             B[tri(K, j)] = N::add(B[tri(K, j)], z[j]);
             sfor<0, j + 1>([&](auto i_) {
                 GPB2_CI(i);
-                B[tri(j, i)] = N::sub(B[tri(j, i)], N::mul(z[i], x[j]));
+                B[tri(j, i)] = N::fms(z[i], x[j], B[tri(j, i)]);
             });
         });
     }
@@ -400,27 +431,28 @@ struct PointMath {
     // chol_pullback! (src/linalg.jl:195-217), in place: on entry B holds L-bar (lower), on
     // exit B holds A-bar.  Each L-bar[i][j] is last read exactly where A-bar[i][j] is written,
     // so one array serves both.
-    static __device__ __forceinline__ void pullback(T (&B)[NT], const T (&L)[NT]) {
+    static __device__ __forceinline__ void pullback(T (&B)[NT], const T (&L)[NT],
+                                                    const T (&rp)[KP1]) {
         sfor_down<0, KP1>([&](auto j_) {
             GPB2_CI(j);
-            const T ljj = L[tri(j, j)];
+            const T rj = rp[j];
             sfor_down<j + 1, KP1>([&](auto i_) {
                 GPB2_CI(i);
-                const T lbij = B[tri(i, j)];
-                const T tbar = N::div(lbij, ljj);
-                B[tri(j, j)] = N::sub(B[tri(j, j)], N::div(N::mul(lbij, L[tri(i, j)]), ljj));
+                const T tbar = N::mul(B[tri(i, j)], rj);  // L-bar[i][j] / L[j][j]
+                B[tri(j, j)] = N::fms(tbar, L[tri(i, j)], B[tri(j, j)]);
                 B[tri(i, j)] = tbar;
                 sfor<0, j>([&](auto p_) {
                     GPB2_CI(p);
-                    B[tri(i, p)] = N::sub(B[tri(i, p)], N::mul(tbar, L[tri(j, p)]));
-                    B[tri(j, p)] = N::sub(B[tri(j, p)], N::mul(tbar, L[tri(i, p)]));
+                    B[tri(i, p)] = N::fms(tbar, L[tri(j, p)], B[tri(i, p)]);
+                    B[tri(j, p)] = N::fms(tbar, L[tri(i, p)], B[tri(j, p)]);
                 });
             });
-            const T sbar = N::div(B[tri(j, j)], N::mul(T(2), ljj));
+            const T sbar = N::mul(B[tri(j, j)], N::mul(T(0.5), rj));
             B[tri(j, j)] = sbar;
+            const T s2 = N::mul(T(2), sbar);
             sfor<0, j>([&](auto p_) {
                 GPB2_CI(p);
-                B[tri(j, p)] = N::sub(B[tri(j, p)], N::mul(N::mul(T(2), sbar), L[tri(j, p)]));
+                B[tri(j, p)] = N::fms(s2, L[tri(j, p)], B[tri(j, p)]);
             });
         });
     }

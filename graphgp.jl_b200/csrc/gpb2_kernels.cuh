@@ -200,7 +200,7 @@ __device__ __forceinline__ void scatter_hist(double* hist, const T (&B)[PointMat
         sfor<0, a>([&](auto b_) {
             GPB2_CI(b);
             T wlo, whi;
-            const int lo = tab.weights(R[tri(a - 1, b)], wlo, whi);
+            const int lo = tab.weights_fast(R[tri(a - 1, b)], wlo, whi);
             const T g = B[tri(a, b)];
             atomicAdd(&hist[lo], (double)N::mul(g, wlo));
             atomicAdd(&hist[lo + 1], (double)N::mul(g, whi));
@@ -246,8 +246,10 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
             GPB2_CI(i);
             B[i] = T(0);
         });
-        B[tri(K, K)] = N::div(T(1), lkk);  // chol_logdet_pullback! seed (src/linalg.jl:220-229)
-        PM::pullback(B, f.L);
+        T rp[PM::KP1];
+        PM::pivot_recips(rp, f.L);
+        B[tri(K, K)] = rp[K];  // chol_logdet_pullback! seed 1/L[K][K] (src/linalg.jl:220-229)
+        PM::pullback(B, f.L, rp);
         scatter_hist<T, K, D>(hist, B, f.R, tab);
     }
     s = block_sum_double(s, red);
@@ -294,14 +296,16 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
             GPB2_CI(j);
             z[j] = N::mul(vbp, v[f.nb[j]]);
         });
-        PM::template forward_subst<true>(z, f.L, pivfloor);
+        T rp[PM::KP1];
+        PM::pivot_recips(rp, f.L);
+        PM::template forward_subst<true>(z, f.L, rp, pivfloor);
         T x[K];  // mean_vec of the point: k_factor's output, the same solve bit for bit
         sfor<0, K>([&](auto j_) {
             GPB2_CI(j);
             x[j] = mv[m * K + j];
         });
         PM::seed_from_solve(B, z, x);
-        PM::pullback(B, f.L);
+        PM::pullback(B, f.L, rp);
         scatter_hist<T, K, D>(hist, B, f.R, tab);
     }
     __syncthreads();
@@ -355,9 +359,11 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
             GPB2_CI(j);
             z[j] = N::div(N::mul(-xim, vn[j]), sd);
         });
-        PM::template forward_subst<false>(z, f.L, T(0));
+        T rp[PM::KP1];
+        PM::pivot_recips(rp, f.L);
+        PM::template forward_subst<false>(z, f.L, rp, T(0));
         PM::seed_from_solve(B, z, x);
-        PM::pullback(B, f.L);
+        PM::pullback(B, f.L, rp);
         scatter_hist<T, K, D>(hist, B, f.R, tab);
     }
     ls = block_sum_double(ls, red);
