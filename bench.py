@@ -347,13 +347,38 @@ def run_b200(args):
         out_d = torch.empty(prob.nbins(), dtype=torch.float32).pin_memory()
         vals_p = torch.from_numpy(vals).pin_memory()
 
+        # Inputs land and results leave on a copy stream, overlapped with the compute stream:
+        # vbar uploads during generate, each result downloads during the next call.
+        copy_s = torch.cuda.Stream(dev)
+        x_d = torch.empty(N, dtype=torch.float32, device=dev)
+        v_d = torch.empty(N, dtype=torch.float32, device=dev)
+        vals_d = torch.empty(prob.nbins(), dtype=torch.float32, device=dev)
+
         def e2e_step():
-            x = xi_p.to(dev, non_blocking=True)
-            v = vb_p.to(dev, non_blocking=True)
-            prob.update_vals(vals_p.to(dev, non_blocking=True))
-            out_f.copy_(gp.generate(prob, x), non_blocking=True)
-            out_x.copy_(gp.generate_grad_xi(prob, v), non_blocking=True)
-            out_d.copy_(gp.generate_grad_vals(prob, x, v), non_blocking=True)
+            comp = torch.cuda.current_stream(dev)
+            copy_s.wait_stream(comp)  # the previous step is done with the input buffers
+            with torch.cuda.stream(copy_s):
+                vals_d.copy_(vals_p, non_blocking=True)
+                x_d.copy_(xi_p, non_blocking=True)
+                ev_x = copy_s.record_event()
+                v_d.copy_(vb_p, non_blocking=True)
+                ev_v = copy_s.record_event()
+            comp.wait_event(ev_x)
+            prob.update_vals(vals_d)
+            outs = []
+            for name, fn in (("f", lambda: gp.generate(prob, x_d)),
+                             ("x", lambda: gp.generate_grad_xi(prob, v_d)),
+                             ("d", lambda: gp.generate_grad_vals(prob, x_d, v_d))):
+                if name == "x":
+                    comp.wait_event(ev_v)
+                r = fn()
+                ev = comp.record_event()
+                with torch.cuda.stream(copy_s):
+                    copy_s.wait_event(ev)
+                    {"f": out_f, "x": out_x, "d": out_d}[name].copy_(r, non_blocking=True)
+                    r.record_stream(copy_s)
+                outs.append(r)
+            comp.wait_stream(copy_s)  # the step ends when its last result has landed
 
         for _ in range(2):
             e2e_step()
