@@ -270,6 +270,26 @@ def test_update_vals_refactors(cuda_device, dt):
     assert np.array_equal(gp.generate(prob, xi), f1)
 
 
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_grad_vals_repeated_and_after_refactor(cuda_device, dt):
+    # Repeated vals-gradients on one handle, before and after the table is re-set (which
+    # refactors the dense block and the per-point factors), must agree with each other and with
+    # the oracle.
+    prob, orc = _config_problem(5000, 2, 200, 8, dt, 33)
+    rng = np.random.default_rng(9)
+    xi = rng.standard_normal(prob.npoints()).astype(dt)
+    vb = rng.standard_normal(prob.npoints()).astype(dt)
+    g1 = gp.generate_grad_vals(prob, xi, vb)
+    prob.update_vals(prob.vals)                        # same table: everything refactorised
+    g2 = gp.generate_grad_vals(prob, xi, vb)
+    g3 = gp.generate_grad_vals(prob, xi, vb)          # reuses the factors
+    g_o = O.generate_grad_vals(orc, xi, vb)
+    # (the reverse sweep's float atomics make repeated f32 gradients differ at ~1e-6)
+    assert relerr(g2, g1) < TOL[dt]
+    assert relerr(g3, g2) < TOL[dt]
+    assert relerr(g2, g_o) < TOL[dt]
+
+
 def test_degenerate_duplicates(cuda_device):
     # test/test_degenerate.jl: 30 exact duplicate points must give finite results everywhere.
     rng = np.random.default_rng(0xDEAD)
