@@ -205,6 +205,16 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+# DRAM bytes (read + write) per launch of the refine kernels at config 2, from one ncu capture
+# each (`ncu --set full ... python bench.py --ncu-case`; summaries in profiles/).  Measured, not
+# computed here: the bench itself never runs under a profiler.
+NCU_TRAFFIC = {
+    "grad_vals": (83.98e6 + 3.73e6, "profiles/k_grad_vals_config2.md"),
+    "factor": (40.06e6 + 2.19e6, "profiles/k_factor_config2.md"),
+    "sweep_fwdrev_all": (78.64e6 + 4.30e6, "profiles/k_sweep_fwdrev_all_config2.md"),
+}
+
+
 def algorithmic_bytes(kind: str, K: int, D: int, T: int = 4, I: int = 4) -> float:
     """Compulsory bytes per refined point of one kernel launch (no cache-reuse credit)."""
     coords = 4 * D * (K + 1)
@@ -218,6 +228,12 @@ def algorithmic_bytes(kind: str, K: int, D: int, T: int = 4, I: int = 4) -> floa
         return I * K + T * K + 2 * T + T + 2 * T * K
     if kind == "fused_fwd":   # the reference's fused forward: B_f = I*k + 4D(k+1) + T(k+2)
         return I * K + coords + T * (K + 2)
+    if kind == "sweep_fwd_all":     # persistent forward sweep over all batches
+        return algorithmic_bytes("sweep_fwd", K, D, T, I)
+    if kind == "sweep_rev_all":     # persistent reverse sweep
+        return algorithmic_bytes("sweep_rev", K, D, T, I)
+    if kind == "sweep_fwdrev_all":  # both sweeps of generate_grad_vals in one kernel
+        return algorithmic_bytes("sweep_fwd", K, D, T, I) + algorithmic_bytes("sweep_rev", K, D, T, I)
     return float("nan")
 
 
@@ -323,7 +339,9 @@ def run_b200(args):
     achieved = gbs(kind, cnt, tot_ms)
     all_ms = sum(v[1] for v in prof.values())
     roofline = {"bound": "hbm", "kernel": kind, "achieved": achieved, "peak": peak,
-                "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                "unit": "GB/s", "frac": achieved / peak,
+                "traffic": NCU_TRAFFIC[kind][0] if kind in NCU_TRAFFIC else None,
+                "traffic_source": NCU_TRAFFIC[kind][1] if kind in NCU_TRAFFIC else None,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks
                 else "fallback 6650 GB/s (of fallback)",
                 "bytes_per_point": algorithmic_bytes(kind, K, D),
