@@ -507,7 +507,9 @@ __global__ void k_ladder_pick(const T* __restrict__ base, const int* __restrict_
 template <typename T>
 __global__ void k_ladder_assemble(TableView<T> tv, const uint32_t* __restrict__ coords, int D,
                                   int DS, T scale, int64_t n, const T* __restrict__ jit, int nc,
-                                  T* __restrict__ base) {
+                                  T* __restrict__ base, const int* __restrict__ sel) {
+    // A later launch of the ladder must not overwrite the slots once a candidate is selected.
+    if (__ldcg(sel) >= 0) return;
     extern __shared__ __align__(16) unsigned char smem[];
     SmemTable<T> tab;
     tab.stage(tv, smem, threadIdx.x, blockDim.x);
@@ -621,7 +623,7 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
                                   dim3((unsigned)std::min<int64_t>(n, 4 * 148)), dim3(256), smem,
                                   s, table_view<T>(p), (const uint32_t*)p->coords, (int)p->d,
                                   coord_stride((int)p->d), (T)p->scale, n,
-                                  (const T*)(djit + first), nc, base));
+                                  (const T*)(djit + first), nc, base, (const int*)sel));
         unsigned long long* trace = nullptr;
         const int npan = (int)((n + kB - 1) / kB);
         if (std::getenv("GPB2_TRACE_DENSE")) {
