@@ -585,7 +585,9 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
             jit[ncand_used++] = eps * dmean;
         }
     }
-    const bool spec = n <= kSpecMax;
+    int64_t spec_max = kSpecMax;  // GPB2_DENSE_SPEC_MAX overrides it (tests: force sequential)
+    if (const char* e = std::getenv("GPB2_DENSE_SPEC_MAX")) spec_max = std::atoll(e);
+    const bool spec = n <= spec_max;
     const int batch = spec ? ncand : 1;
     const size_t nn = (size_t)n * (size_t)n;
     GPB2_TRY(ensure_alloc(&p->Lcand, sizeof(T) * nn * batch));

@@ -290,6 +290,20 @@ def test_grad_vals_repeated_and_after_refactor(cuda_device, dt):
     assert relerr(g2, g_o) < TOL[dt]
 
 
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_dense_ladder_sequential_launches(cuda_device, dt, monkeypatch):
+    # Above the speculation limit the ladder runs one candidate per launch, reusing one slot; the
+    # step it settles on and the factor must be the same as the oracle's (the config-2 root block
+    # needs eight launches: eps = 0, 1e-9, ..., 1e-3).
+    monkeypatch.setenv("GPB2_DENSE_SPEC_MAX", "0")
+    prob, orc = _config_problem(20_000, 2, 1000, 8, dt, 1)
+    gp.generate_logdet(prob)
+    L_ora, jit = O.dense_chol(orc)
+    assert jit > 0
+    assert np.isclose(prob.dense_jitter(), jit, rtol=1e-6)
+    assert np.array_equal(prob.dense_factor(), np.tril(L_ora))
+
+
 def test_degenerate_duplicates(cuda_device):
     # test/test_degenerate.jl: 30 exact duplicate points must give finite results everywhere.
     rng = np.random.default_rng(0xDEAD)
