@@ -22,6 +22,7 @@
 //   D  one warp of the cluster factors the 32 x 32 diagonal block, a row per lane;
 //   P  256-row chunks over the cluster's CTAs: each thread solves one row below the block;
 //   U  64 x 64 lower tiles over the cluster's CTAs: the trailing update with the panel's columns.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -49,11 +50,12 @@ struct CholArgs {
     int64_t n;
     int nc;
     int first;        // ladder index of candidate 0 of this launch
-    int* fail;        // fail[c] = failing column + 1, 0 while alive
+    int* fail;        // fail[c] = failing column + 1 (or stop column + 1), 0 while alive
     int* sel;         // sel[0]: ladder index of the first success (-1: none yet); sel[1]: its slot
     int* done;        // done[c] = 1 once candidate c is fully factorised
     int* dflag;       // dflag[c]: last panel whose diagonal block candidate c has published
     int* err;         // error word: a bounded wait gave up
+    const int* order; // order[c]: ladder index of candidate slot c
     unsigned long long* trace;  // diagnostics (GPB2_TRACE_DENSE): phase timestamps, or NULL
 };
 
@@ -352,6 +354,16 @@ __device__ __forceinline__ void tile_of_index(unsigned int t, int64_t nt, int& b
     }
 }
 
+// Whether candidate c stops before the panel whose trailing block starts at column `lim`.  Rank 0
+// records a stop (a failed pivot, or a supersede) as that column + 1 while other CTAs may still
+// be reading the word for the previous panel; filtering by column makes every thread of the
+// cluster take the same decision after the same barrier, so they all leave together.
+template <class T>
+__device__ __forceinline__ bool chol_stopped(const CholArgs<T>& a, int c, int64_t lim) {
+    const int f = __ldcg(a.fail + c);
+    return f != 0 && (int64_t)f - 1 < lim;
+}
+
 // One cluster per ladder candidate; the cluster's CTAs split each phase and meet at the
 // hardware cluster barrier (release/acquire at cluster scope), so no grid-wide barrier is
 // needed and candidates proceed independently.  One barrier per panel: rank 0 updates tile
@@ -378,6 +390,16 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
     int* dflag = a.dflag + c;  // last panel whose diagonal block is published
     unsigned long long* tr =
         (a.trace && c == a.nc - 1 && rank == 0 && threadIdx.x == 0) ? a.trace : nullptr;
+    // Diagnostics: each candidate's start and end times and how it ended, after the panel trace.
+    unsigned long long* life =
+        (a.trace && rank == 0 && threadIdx.x == 0) ? a.trace + 8 * npanels + 3 * c : nullptr;
+    if (life) life[0] = global_ns();
+    auto leave = [&](unsigned long long how) {
+        if (life) {
+            life[1] = global_ns();
+            life[2] = how;
+        }
+    };
     if (threadIdx.x == 0) {
         s_ctr[0] = 1u;  // tile 0 of every panel is rank 0's
         s_ctr[1] = 1u;
@@ -386,14 +408,14 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
     // Panel 0: its diagonal block, then its rows.
     if (rank == 0) chol_diag(a, c, 0, S, &s_bad);
     cl.sync();
-    if (__ldcg(a.fail + c)) return;
+    if (chol_stopped(a, c, kB)) return leave(1);
     chol_panel<T>(a, c, 0, rank, CL, Dg, nullptr);
     cl.sync();
     for (int k = 0; k < npanels; k++) {
         const int64_t p0 = (int64_t)k * kB;
         unsigned long long* st = tr ? tr + 8 * k : nullptr;
         if (st) st[0] = global_ns();
-        if (__ldcg(a.fail + c)) return;  // the whole cluster leaves after the same barrier
+        if (chol_stopped(a, c, p0 + kB)) return leave(2 + k);  // the whole cluster leaves together
         const int64_t rows = a.n - p0 - kB;
         if (rows <= 0) break;
         const int64_t t0 = p0 + kB;        // trailing matrix [t0, n)^2
@@ -466,24 +488,35 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
             bi = bin;
             bj = bjn;
         }
-        if (rank == 0 && threadIdx.x == 0) s_ctr[(k + 1) & 1] = 1u;  // the next panel's counter
+        if (rank == 0 && threadIdx.x == 0) {
+            s_ctr[(k + 1) & 1] = 1u;  // the next panel's counter
+            // Superseded: a smaller ladder step has already factorised, so this candidate can no
+            // longer be selected -- stop (after the barrier, with the whole cluster) and free its
+            // SMs for candidates still waiting for a slot.
+            bool sup = false;
+            for (int c2 = 0; c2 < a.nc; c2++)
+                sup = sup || (a.order[c2] < a.order[c] && __ldcg(a.done + c2));
+            if (sup && !__ldcg(a.fail + c)) a.fail[c] = (int)(p0 + kB) + 1;
+        }
         if (st) st[7] = global_ns();
         cl.sync();
     }
     if (rank == 0 && threadIdx.x == 0 && !__ldcg(a.fail + c)) a.done[c] = 1;
+    leave(1000);
 }
 
 // After a launch: record the first candidate (in ladder order) that factorised, unless an
 // earlier launch already did.
-__global__ void k_ladder_mark(const int* __restrict__ done, int nc, int first,
+__global__ void k_ladder_mark(const int* __restrict__ done, const int* __restrict__ order, int nc,
                               int* __restrict__ sel) {
     if (sel[0] >= 0) return;
-    for (int c = 0; c < nc; c++)
-        if (done[c]) {
-            sel[0] = first + c;
-            sel[1] = c;
-            return;
-        }
+    int best = -1;
+    for (int c = 0; c < nc; c++)  // the smallest ladder index that factorised
+        if (done[c] && (best < 0 || order[c] < order[best])) best = c;
+    if (best >= 0) {
+        sel[0] = order[best];
+        sel[1] = best;
+    }
 }
 
 // Copy the selected candidate into the fixed factor buffer (the triangular products and solves
@@ -612,7 +645,23 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
     // Fresh status: no selection (-1), no failure or completion flags, no error.
     GPB2_CUDA_TRY(cudaMemsetAsync(p->lad, 0, sizeof(int) * kLadInts, s));
     GPB2_CUDA_TRY(cudaMemsetAsync(sel, 0xff, sizeof(int) * 2, s));
-    GPB2_CUDA_TRY(cudaMemcpyAsync(djit, jit.data(), sizeof(T) * ncand_used,
+    // Candidate slots in launch order.  Only some clusters are resident at once; the rest start
+    // as slots free up.  A speculative launch starts with the ladder step that succeeded last
+    // time (it runs to the end), then the smaller steps, which must all be seen to fail and fail
+    // sooner the smaller they are, and last the larger steps, needed only if the hint fails and
+    // otherwise superseded as soon as it completes.  Every slot is still examined, so the first
+    // success in ladder order is selected whatever the order.  Sequential launches keep ladder
+    // order.
+    std::vector<int> order;
+    order.reserve(ncand_used);
+    const int hint = spec && p->ladder_hint >= 0 && p->ladder_hint < ncand_used ? p->ladder_hint : 0;
+    for (int i = hint; i >= 0; i--) order.push_back(i);
+    for (int i = hint + 1; i < ncand_used; i++) order.push_back(i);
+    std::vector<T> jit_slot(ncand_used);
+    for (int i = 0; i < ncand_used; i++) jit_slot[i] = jit[order[i]];
+    GPB2_CUDA_TRY(cudaMemcpyAsync(djit, jit_slot.data(), sizeof(T) * ncand_used,
+                                  cudaMemcpyHostToDevice, s));
+    GPB2_CUDA_TRY(cudaMemcpyAsync(p->lad + kLadOrder, order.data(), sizeof(int) * ncand_used,
                                   cudaMemcpyHostToDevice, s));
     for (int first = 0; first < ncand_used; first += batch) {
         const int nc = std::min(batch, ncand_used - first);
@@ -629,13 +678,13 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
         unsigned long long* trace = nullptr;
         const int npan = (int)((n + kB - 1) / kB);
         if (std::getenv("GPB2_TRACE_DENSE")) {
-            GPB2_TRY(ensure_alloc(&p->trace, sizeof(unsigned long long) * 8 * npan));
-            GPB2_CUDA_TRY(cudaMemsetAsync(p->trace, 0, sizeof(unsigned long long) * 8 * npan,
-                                          s));
+            const size_t tn = 8 * (size_t)npan + 3 * 16;
+            GPB2_TRY(ensure_alloc(&p->trace, sizeof(unsigned long long) * tn));
+            GPB2_CUDA_TRY(cudaMemsetAsync(p->trace, 0, sizeof(unsigned long long) * tn, s));
             trace = static_cast<unsigned long long*>(p->trace);
         }
-        CholArgs<T> args{base, n,    nc,   first, fail, sel, done, p->lad + kLadDflag,
-                         p->lad + kLadBarErr, trace};
+        CholArgs<T> args{base,  n,    nc,   first, fail, sel, done, p->lad + kLadDflag,
+                         p->lad + kLadBarErr, p->lad + kLadOrder + first, trace};
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)(nc * csize));
         cfg.blockDim = dim3(chol_threads<T>());
@@ -652,9 +701,10 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
         prof_end(t, s);
         GPB2_CUDA_TRY(e);
         GPB2_CUDA_TRY(launch_prof("dense_mark", k_ladder_mark, dim3(1), dim3(1), 0, s,
-                                  (const int*)done, nc, first, sel));
+                                  (const int*)done, (const int*)(p->lad + kLadOrder + first), nc,
+                                  sel));
         if (trace) {  // diagnostics: per-phase totals of the last candidate of this launch
-            std::vector<unsigned long long> h(8 * (size_t)npan);
+            std::vector<unsigned long long> h(8 * (size_t)npan + 3 * 16);
             GPB2_CUDA_TRY(cudaMemcpyAsync(h.data(), trace, sizeof(unsigned long long) * h.size(),
                                           cudaMemcpyDeviceToHost, s));
             GPB2_CUDA_TRY(cudaStreamSynchronize(s));
@@ -675,6 +725,17 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
                          sum[2] / 1e3, sum[3] / 1e3, sum[4] / 1e3, sum[5] / 1e3, sum[6] / 1e3,
                          sum[7] / 1e3);
             if (std::atoi(std::getenv("GPB2_TRACE_DENSE")) >= 2) {
+                // Candidate lifetimes relative to the first start (us); end code 1000 = done,
+                // 1 = failed in panel 0's block, 2 + k = stopped at the top of panel k.
+                unsigned long long t00 = ~0ull;
+                for (int q = 0; q < nc; q++)
+                    if (h[8 * npan + 3 * q]) t00 = std::min(t00, h[8 * npan + 3 * q]);
+                for (int q = 0; q < nc; q++) {
+                    const unsigned long long* lf = h.data() + 8 * npan + 3 * q;
+                    std::fprintf(stderr, "  slot %d ladder %d: start %.1f end %.1f how %llu\n", q,
+                                 order[first + q], lf[0] ? (lf[0] - t00) / 1e3 : -1.0,
+                                 lf[1] ? (lf[1] - t00) / 1e3 : -1.0, lf[2]);
+                }
                 for (int q = 0; q < 8; q++) {
                     std::fprintf(stderr, "  interval %d:", q);
                     for (int k2 = 0; k2 < kk; k2++) {

@@ -68,6 +68,24 @@ std::atomic<int> g_fwd_mode{[] {
 
 FwdMode fwd_mode() { return static_cast<FwdMode>(g_fwd_mode.load()); }
 
+// Whether the dense first-layer factor runs beside the per-point factor (GPB2_OVERLAP=0 at load
+// time runs them one after the other on the call's stream).
+const bool g_overlap = [] {
+    const char* e = std::getenv("GPB2_OVERLAP");
+    return !(e && std::strcmp(e, "0") == 0);
+}();
+
+// The problem's high-priority stream and its two events, created on first use.
+static int ensure_dense_stream(gpb2_problem* p) {
+    if (p->dstream) return GPB2_OK;
+    int least = 0, greatest = 0;
+    GPB2_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+    GPB2_CUDA_TRY(cudaEventCreateWithFlags(&p->ev_fork, cudaEventDisableTiming));
+    GPB2_CUDA_TRY(cudaEventCreateWithFlags(&p->ev_join, cudaEventDisableTiming));
+    GPB2_CUDA_TRY(cudaStreamCreateWithPriority(&p->dstream, cudaStreamNonBlocking, greatest));
+    return GPB2_OK;
+}
+
 }  // namespace
 
 template <typename T>
@@ -101,6 +119,33 @@ struct Impl {
                                                    (T*)p->sd, s),
                               "factor"));
         p->factor_valid = true;
+        return GPB2_OK;
+    }
+
+    // Both factors of the current table: the dense first-layer Cholesky and the per-point
+    // mean_vec / std.  They are independent, and the dense ladder is a few thread-block clusters
+    // whose candidates mostly stop early, leaving most SMs idle for most of its run.  When both
+    // are stale the ladder runs on the problem's high-priority stream (its waiting clusters take
+    // SMs as they free up, ahead of the other kernel's blocks) while the per-point factor fills
+    // the remaining SMs on the call's stream; the call's stream then waits for the ladder.
+    // Neither kernel waits on the other, so any co-scheduling is correct.
+    static int factor_both(P* p, cudaStream_t s) {
+        if (!g_overlap || p->dense_valid || p->factor_valid) {
+            GPB2_TRY(Dense<T>::factor(p, s));
+            return factor_all(p, s);
+        }
+        GPB2_TRY(ensure_dense_stream(p));
+        GPB2_CUDA_TRY(cudaEventRecord(p->ev_fork, s));
+        GPB2_CUDA_TRY(cudaStreamWaitEvent(p->dstream, p->ev_fork, 0));
+        const int sd = Dense<T>::factor(p, p->dstream);
+        const int sf = sd == GPB2_OK ? factor_all(p, s) : GPB2_OK;
+        // The join is recorded whatever happened, so nothing of this call outlives the stream.
+        const cudaError_t e1 = cudaEventRecord(p->ev_join, p->dstream);
+        const cudaError_t e2 = cudaStreamWaitEvent(s, p->ev_join, 0);
+        GPB2_TRY(sd);
+        GPB2_TRY(sf);
+        GPB2_CUDA_TRY(e1);
+        GPB2_CUDA_TRY(e2);
         return GPB2_OK;
     }
 
@@ -276,7 +321,7 @@ struct Impl {
             xt = (const T*)p->buf_b;
         }
         T* values = p->indices ? (T*)p->buf_a : out;
-        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(fwd_mode() == FwdMode::Fused ? Dense<T>::factor(p, s) : factor_both(p, s));
         GPB2_TRY(Dense<T>::apply_L(p, xt, values, s));
         GPB2_TRY(refine_sweep(p, values, xt + p->n0, false, s));
         if (p->indices) GPB2_TRY(scatter(p, values, out, s));
@@ -320,9 +365,8 @@ struct Impl {
             GPB2_CUDA_TRY(
                 cudaMemcpyAsync(vb, vbar, sizeof(T) * p->n, cudaMemcpyDeviceToDevice, s));
         T* xg = p->indices ? (T*)p->buf_d : xbar;
-        GPB2_TRY(factor_all(p, s));
+        GPB2_TRY(factor_both(p, s));
         GPB2_TRY(reverse_sweep(p, xg, vb, s));
-        GPB2_TRY(Dense<T>::factor(p, s));
         GPB2_TRY(Dense<T>::apply_Lt(p, vb, xg, s));
         if (p->indices) GPB2_TRY(scatter(p, xg, xbar, s));
         return GPB2_OK;
@@ -337,9 +381,8 @@ struct Impl {
         }
         T* v = (T*)p->buf_a;
         T* vb = (T*)p->buf_c;
-        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(factor_both(p, s));
         GPB2_TRY(Dense<T>::apply_L(p, xt, v, s));
-        GPB2_TRY(factor_all(p, s));
         if (p->indices)
             GPB2_TRY(gather(p, vbar, vb, s));
         else
@@ -410,7 +453,7 @@ struct Impl {
 // factorisation) or a dense block that no ladder step could factorise (src/dense.jl:65-66).
 // The reference's drivers also synchronise before returning (e.g. src/api.jl:139).
 static int finish_call(gpb2_problem* p, cudaStream_t s) {
-    int h[3] = {0, 0, 0};
+    int h[4] = {0, 0, 0, -1};
     GPB2_CUDA_TRY(cudaMemcpyAsync(&h[0], p->dsync + 2, sizeof(int), cudaMemcpyDeviceToHost, s));
     const bool dense = p->dense_pending && p->lad;
     if (dense) {
@@ -418,10 +461,14 @@ static int finish_call(gpb2_problem* p, cudaStream_t s) {
             cudaMemcpyAsync(&h[1], p->lad + kLadNotPD, sizeof(int), cudaMemcpyDeviceToHost, s));
         GPB2_CUDA_TRY(
             cudaMemcpyAsync(&h[2], p->lad + kLadBarErr, sizeof(int), cudaMemcpyDeviceToHost, s));
+        GPB2_CUDA_TRY(
+            cudaMemcpyAsync(&h[3], p->lad + kLadSel, sizeof(int), cudaMemcpyDeviceToHost, s));
     }
     GPB2_CUDA_TRY(cudaStreamSynchronize(s));
     p->dense_pending = false;
     if (dense) p->dense_valid = h[0] == 0 && h[1] == 0 && h[2] == 0;
+    // The selected ladder step orders the next factorisation's speculative candidates.
+    if (dense && h[3] >= 0) p->ladder_hint = h[3];
     if (h[0] != 0) {
         cudaMemsetAsync(p->dsync + 2, 0, sizeof(int), s);
         return set_error(GPB2_ERR_TIMEOUT, "a grid barrier of a persistent sweep timed out");

@@ -64,7 +64,11 @@ struct gpb2_problem {
     int* dinfo = nullptr;     // cuSOLVER info
     cusolverDnHandle_t solver = nullptr;
     cublasHandle_t blas = nullptr;
+    cudaStream_t dstream = nullptr;   // high-priority stream of the overlapped dense factor
+    cudaEvent_t ev_fork = nullptr;    // call stream -> dstream
+    cudaEvent_t ev_join = nullptr;    // dstream -> call stream
     double dense_jitter = 0.0;  // eps of the ladder that succeeded on the last factorisation
+    int ladder_hint = -1;       // ladder index that succeeded last time (-1: none yet)
 
     const gpb2::Ops<float>* ops32 = nullptr;
     const gpb2::Ops<double>* ops64 = nullptr;
@@ -79,7 +83,8 @@ constexpr int kLadSel = 32;     // ladder index of the first success (-1: none),
 constexpr int kLadNotPD = 34;   // set when no candidate succeeded
 constexpr int kLadBarErr = 36;  // error word of the factorisation (0: none)
 constexpr int kLadDflag = 48;   // [48, 64): per-candidate last published diagonal panel
-constexpr int kLadInts = 64;
+constexpr int kLadOrder = 64;   // [64, 80): ladder index of each candidate slot of a launch
+constexpr int kLadInts = 80;
 
 // RAII: make the problem's device current for the duration of a call, restore afterwards.
 struct DeviceGuard {
