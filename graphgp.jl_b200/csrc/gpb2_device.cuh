@@ -87,6 +87,19 @@ struct SmemCol {
     int stride = 0;
     __device__ __forceinline__ T& operator[](int i) const { return p[i * stride]; }
 };
+// Per-thread columns of interpolation weights in shared memory: for entry i, the segment index
+// lo[i] and the fraction t[i] of the radius across it (w_lo = 1 - t, w_hi = t).  Kept by the
+// covariance assembly so the adjoint's histogram scatter needs no second table search.
+template <typename T>
+struct SmemWeights {
+    T* t = nullptr;
+    uint16_t* lo = nullptr;
+    int stride = 0;
+};
+template <typename RT>
+struct is_weight_store : std::false_type {};
+template <typename T>
+struct is_weight_store<SmemWeights<T>> : std::true_type {};
 
 // ------------------------------------------------------------------------------------------
 // Interpolation table (built on the host by the problem handle, see gpb2_problem.cu).
@@ -171,6 +184,20 @@ struct SmemTable {
         wlo = N::sub(T(1), t);
         whi = t;
         return lo;
+    }
+    // lookup() that also returns weights_fast()'s segment and fraction t (w_lo = 1 - t, w_hi = t),
+    // from the same segment search: the value and both weights bit for bit as the two calls.
+    __device__ __forceinline__ T lookup_w(T r, int& lo_out, T& t_out) const {
+        if (r <= b0) { lo_out = 0; t_out = T(0); return v0; }
+        if (r >= bN) { lo_out = nb - 2; t_out = T(1); return vN; }
+        const int lo = locate(r);
+        const T x0 = seg[4 * lo + 0];
+        const T x1 = seg[4 * lo + 1];
+        const T y0 = seg[4 * lo + 2];
+        const T slope = seg[4 * lo + 3];
+        lo_out = lo;
+        t_out = N::div_fast(N::sub(r, x0), N::sub(x1, x0));
+        return N::add(y0, N::mul(slope, N::sub(r, x0)));
     }
     // The same with a fast (not correctly rounded) division: the gradient histograms' weights.
     __device__ __forceinline__ int weights_fast(T r, T& wlo, T& whi) const {
@@ -324,7 +351,8 @@ struct PointMath {
     }
 
     // assemble_cov! (src/linalg.jl:98-112).  With KEEP_R the radius of pair (a, b), b < a, is
-    // kept in R[tri(a-1, b)] for the adjoint's scatter.
+    // kept in R[tri(a-1, b)] for the adjoint's scatter -- or, with a weight store, its
+    // interpolation segment and fraction.
     template <bool KEEP_R, typename RT>
     static __device__ __forceinline__ void assemble(T (&L)[NT], RT& R,
                                                     const uint32_t (&jc)[KP1][D], T scale,
@@ -336,8 +364,17 @@ struct PointMath {
             sfor<0, a>([&](auto b_) {
                 GPB2_CI(b);
                 const T r = radius(jc[a], jc[b], scale);
-                if constexpr (KEEP_R) R[tri(a - 1, b)] = r;
-                L[tri(a, b)] = tab.lookup(r);
+                if constexpr (KEEP_R && is_weight_store<RT>::value) {
+                    int lo;
+                    T t;
+                    L[tri(a, b)] = tab.lookup_w(r, lo, t);
+                    const int i = tri(a - 1, b) * R.stride;
+                    R.lo[i] = (uint16_t)lo;
+                    R.t[i] = t;
+                } else {
+                    if constexpr (KEEP_R) R[tri(a - 1, b)] = r;
+                    L[tri(a, b)] = tab.lookup(r);
+                }
             });
         });
     }

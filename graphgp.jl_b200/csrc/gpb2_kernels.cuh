@@ -74,11 +74,26 @@ __device__ __forceinline__ double block_sum_double(double v, double* red /*>= 32
 template <typename T, int K, int D>
 struct RadiusStore {
     static constexpr int NR = PointMath<T, K, D>::NR;
+    // Interpolation weights (segment + fraction) when they fit, else radii, in shared memory;
+    // else radii in registers.
+    static constexpr bool kWeights =
+        (size_t)NR * kFlatThreads * (sizeof(T) + sizeof(uint16_t)) <= 36 * 1024;
     static constexpr bool kSmem = (size_t)NR * kFlatThreads * sizeof(T) <= 36 * 1024;
-    using type = typename std::conditional<kSmem, SmemCol<T>, RegArr<T, NR>>::type;
-    static constexpr size_t bytes = kSmem ? (size_t)NR * kFlatThreads * sizeof(T) : 0;
+    using type = typename std::conditional<
+        kWeights, SmemWeights<T>,
+        typename std::conditional<kSmem, SmemCol<T>, RegArr<T, NR>>::type>::type;
+    static constexpr size_t bytes =
+        kWeights ? (size_t)NR * kFlatThreads * (sizeof(T) + sizeof(uint16_t))
+                 : (kSmem ? (size_t)NR * kFlatThreads * sizeof(T) : 0);
     static __device__ __forceinline__ type make(unsigned char* base) {
-        if constexpr (kSmem) {
+        if constexpr (kWeights) {
+            SmemWeights<T> w;
+            w.t = reinterpret_cast<T*>(base) + threadIdx.x;
+            w.lo = reinterpret_cast<uint16_t*>(base + (size_t)NR * kFlatThreads * sizeof(T)) +
+                   threadIdx.x;
+            w.stride = kFlatThreads;
+            return w;
+        } else if constexpr (kSmem) {
             SmemCol<T> c;
             c.p = reinterpret_cast<T*>(base) + threadIdx.x;
             c.stride = kFlatThreads;
@@ -183,10 +198,12 @@ k_logdet(PointArgs<T> a, T* __restrict__ terms, double* __restrict__ acc, int64_
 
 // Scatter a point's A-bar (lower triangle, in B) into the CTA histogram: the diagonal sum into
 // bin 0, each off-diagonal through the interpolation weights of its radius
-// (_scatter_Abar_hist!, src/kernels_adjoint.jl:50-74).
+// (_scatter_Abar_hist!, src/kernels_adjoint.jl:50-74).  The diagonal sum goes to the thread's
+// own accumulator `bin0` (added to bin 0 once per thread: every point hits that bin).
 template <typename T, int K, int D, typename RT>
-__device__ __forceinline__ void scatter_hist(double* hist, const T (&B)[PointMath<T, K, D>::NT],
-                                             const RT& R, const SmemTable<T>& tab) {
+__device__ __forceinline__ void scatter_hist(double* hist, double& bin0,
+                                             const T (&B)[PointMath<T, K, D>::NT], const RT& R,
+                                             const SmemTable<T>& tab) {
     using N = Num<T>;
     constexpr int KP1 = K + 1;
     T dsum = T(0);
@@ -194,13 +211,22 @@ __device__ __forceinline__ void scatter_hist(double* hist, const T (&B)[PointMat
         GPB2_CI(a);
         dsum = N::add(dsum, B[tri(a, a)]);
     });
-    atomicAdd(&hist[0], (double)dsum);
+    bin0 += (double)dsum;
     sfor<1, KP1>([&](auto a_) {
         GPB2_CI(a);
         sfor<0, a>([&](auto b_) {
             GPB2_CI(b);
             T wlo, whi;
-            const int lo = tab.weights_fast(R[tri(a - 1, b)], wlo, whi);
+            int lo;
+            if constexpr (is_weight_store<RT>::value) {
+                const int i = tri(a - 1, b) * R.stride;
+                const T t = R.t[i];
+                lo = R.lo[i];
+                wlo = N::sub(T(1), t);
+                whi = t;
+            } else {
+                lo = tab.weights_fast(R[tri(a - 1, b)], wlo, whi);
+            }
             const T g = B[tri(a, b)];
             atomicAdd(&hist[lo], (double)N::mul(g, wlo));
             atomicAdd(&hist[lo + 1], (double)N::mul(g, whi));
@@ -231,6 +257,7 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
                            sizeof(double) * a.tab.nb;
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
+    double bin0 = 0.0;  // this thread's share of histogram bin 0
     double s = 0.0;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
          m += (int64_t)gridDim.x * blockDim.x) {
@@ -250,10 +277,11 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
         PM::pivot_recips(rp, f.L);
         B[tri(K, K)] = rp[K];  // chol_logdet_pullback! seed 1/L[K][K] (src/linalg.jl:220-229)
         PM::pullback(B, f.L, rp);
-        scatter_hist<T, K, D>(hist, B, f.R, tab);
+        scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
     }
     s = block_sum_double(s, red);
     if (threadIdx.x == 0 && ld_acc) atomicAdd(ld_acc, s);
+    atomicAdd(&hist[0], bin0);
     __syncthreads();
     flush_hist(gacc, hist, a.tab.nb);
 }
@@ -277,6 +305,7 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
                            sizeof(double) * a.tab.nb;
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
+    double bin0 = 0.0;  // this thread's share of histogram bin 0
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
          m += (int64_t)gridDim.x * blockDim.x) {
         const int64_t p = a.n0 + m;
@@ -306,8 +335,9 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
         });
         PM::seed_from_solve(B, z, x);
         PM::pullback(B, f.L, rp);
-        scatter_hist<T, K, D>(hist, B, f.R, tab);
+        scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
     }
+    atomicAdd(&hist[0], bin0);
     __syncthreads();
     flush_hist(gacc, hist, a.tab.nb);
 }
@@ -329,6 +359,7 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
                            sizeof(double) * a.tab.nb;
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
+    double bin0 = 0.0;  // this thread's share of histogram bin 0
     double ls = 0.0;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
          m += (int64_t)gridDim.x * blockDim.x) {
@@ -364,10 +395,11 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
         PM::template forward_subst<false>(z, f.L, rp, T(0));
         PM::seed_from_solve(B, z, x);
         PM::pullback(B, f.L, rp);
-        scatter_hist<T, K, D>(hist, B, f.R, tab);
+        scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
     }
     ls = block_sum_double(ls, red);
     if (threadIdx.x == 0 && loss_acc) atomicAdd(loss_acc, ls);
+    atomicAdd(&hist[0], bin0);
     __syncthreads();
     flush_hist(gacc, hist, a.tab.nb);
 }
