@@ -94,19 +94,23 @@ __device__ __forceinline__ T div_pos(T x, T d) {
 }
 
 // Phase D (whole CTA): factor candidate c's diagonal block [p0, p0+bs)^2.  The CTA stages the
-// block in shared memory in one coalesced pass, warp 0 eliminates it in registers, and the CTA
-// writes it back.  Returns false (and records the column) if a pivot fails.
+// block in shared memory in one coalesced pass (unless `staged`: the caller left it in S), warp 0
+// eliminates it in registers, and the CTA writes it back.  Returns false (and records the
+// column) if a pivot fails.
 template <typename T>
-__device__ __noinline__ bool chol_diag(const CholArgs<T>& a, int c, int64_t p0, T (*S)[kB + 1], int* s_bad,
-                          unsigned long long* st = nullptr) {
+__device__ __noinline__ bool chol_diag(const CholArgs<T>& a, int c, int64_t p0, T (*S)[kB + 1],
+                                       int* s_bad, unsigned long long* st = nullptr,
+                                       bool staged = false) {
     using N = Num<T>;
     constexpr int NTH = chol_threads<T>();
     T* L = a.base + (int64_t)c * a.n * a.n;
     const int bs = a.n - p0 < kB ? (int)(a.n - p0) : kB;
+    if (!staged) {
 #pragma unroll
-    for (int e0 = 0; e0 < kB * kB; e0 += NTH) {
-        const int e = e0 + threadIdx.x, i = e % kB, j = e / kB;
-        if (i < bs && j <= i) S[i][j] = __ldcg(L + (p0 + i) + (p0 + j) * a.n);
+        for (int e0 = 0; e0 < kB * kB; e0 += NTH) {
+            const int e = e0 + threadIdx.x, i = e % kB, j = e / kB;
+            if (i < bs && j <= i) S[i][j] = __ldcg(L + (p0 + i) + (p0 + j) * a.n);
+        }
     }
     __syncthreads();
     if (st) st[0] = global_ns();
@@ -229,10 +233,11 @@ __device__ __forceinline__ void load_diag_t(const CholArgs<T>& a, int c, int64_t
 }
 
 // Panel rows [r_lo, r_hi) (at most one tile: warp w takes rows r_lo + 32w + lane) solved against
-// the transposed diagonal factor Dg, as in chol_panel.
+// the transposed diagonal factor Dg, as in chol_panel.  With Sr the rows come from shared memory
+// (row i at Sr[i - p0], as the tile holding them left them) instead of global memory.
 template <typename T>
 __device__ void chol_rows(const CholArgs<T>& a, int c, int64_t p0, int64_t r_lo, int64_t r_hi,
-                          const T* Dg) {
+                          const T* Dg, const T (*Sr)[kB + 1] = nullptr) {
     using N = Num<T>;
     T* L = a.base + (int64_t)c * a.n * a.n;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -241,10 +246,17 @@ __device__ void chol_rows(const CholArgs<T>& a, int c, int64_t p0, int64_t r_lo,
     const bool live = i < r_hi;
     T* Li = L + i + p0 * a.n;
     T x[kB];
-    sfor<0, kB>([&](auto q_) {
-        GPB2_CI(q);
-        x[q] = live ? __ldcg(Li + q * a.n) : T(0);
-    });
+    if (Sr) {
+        sfor<0, kB>([&](auto q_) {
+            GPB2_CI(q);
+            x[q] = live ? Sr[i - p0][q] : T(0);
+        });
+    } else {
+        sfor<0, kB>([&](auto q_) {
+            GPB2_CI(q);
+            x[q] = live ? __ldcg(Li + q * a.n) : T(0);
+        });
+    }
     sfor<0, kB>([&](auto j_) {
         GPB2_CI(j);
         const T* dj = Dg + j * kB;
@@ -262,20 +274,57 @@ __device__ void chol_rows(const CholArgs<T>& a, int c, int64_t p0, int64_t r_lo,
     }
 }
 
+// Packed single-precision pairs: mul.rn.f32x2 rounds each lane exactly as __fmul_rn does
+// (denormals included).  The subtraction stays scalar: a packed multiply whose only use is a
+// packed subtraction is contracted into a fused multiply-add by the code generator, which would
+// round once instead of twice.
+__device__ __forceinline__ unsigned long long pk2(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void upk2(unsigned long long v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long mul2_rn(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
 // Phase U: lower tile (bi, bj) of candidate c's trailing matrix [p0 + kB, n)^2, one subtraction
 // per panel column in order.  Thread (tx, ty) owns rows tx + 32*u (lanes along the contiguous
-// dimension) and columns ty + TY*v.  A tile's operands are fetched into registers (fetch) while
-// the previous tile computes, then staged in shared memory (stage) and consumed (compute).
+// dimension) and RV columns col(v): ty + TY*v, or in single precision adjacent pairs
+// 2*ty + 2*TY*w + {0, 1}, updated as packed pairs.  A tile's operands are fetched into
+// registers (fetch) while the previous tile computes, then staged in shared memory (stage) and
+// consumed (compute).
 template <typename T, int TL>
 struct TileWork {
     static constexpr int NTH = chol_threads<T>();
     static constexpr int TY = NTH / 32;
     static constexpr int RU = TL / 32, RV = TL / TY;
     static constexpr int NP = TL * kB / NTH;  // panel entries per thread per side
+    static constexpr bool kPair = sizeof(T) == 4;
     static_assert(RU * 32 == TL && RV * TY == TL && NP * NTH == TL * kB, "tile shape");
+    static_assert(!kPair || RV % 2 == 0, "column pairs");
     T li[NP], lj[NP];
     T acc[RU][RV];
     int64_t r0, c0;
+
+    // After compute() and a barrier: the tile's first kB columns into S[row][col] (the diagonal
+    // block and the rows below it of tile (0, 0), as chol_diag and chol_rows read them).
+    __device__ __forceinline__ void stash_first_cols(T (*S)[kB + 1]) const {
+        const int tx = threadIdx.x % 32;
+#pragma unroll
+        for (int u = 0; u < RU; u++)
+#pragma unroll
+            for (int v = 0; v < RV; v++)
+                if (col(v) < kB) S[tx + 32 * u][col(v)] = acc[u][v];
+    }
+    static __device__ __forceinline__ int col(int v) {
+        const int ty = threadIdx.x / 32;
+        return kPair ? 2 * ty + 2 * TY * (v / 2) + (v % 2) : ty + TY * v;
+    }
 
     __device__ __forceinline__ void fetch(const CholArgs<T>& a, int c, int64_t p0, int bi,
                                           int bj) {
@@ -290,21 +339,27 @@ struct TileWork {
             li[q] = gi < a.n ? __ldcg(L + gi + (p0 + pp) * a.n) : T(0);
             lj[q] = gj < a.n ? __ldcg(L + gj + (p0 + pp) * a.n) : T(0);
         }
-        const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+        const int tx = threadIdx.x % 32;
 #pragma unroll
         for (int u = 0; u < RU; u++)
 #pragma unroll
             for (int v = 0; v < RV; v++) {
-                const int64_t gi = r0 + tx + 32 * u, gj = c0 + ty + TY * v;
+                const int64_t gi = r0 + tx + 32 * u, gj = c0 + col(v);
                 acc[u][v] = (gi < a.n && gi >= gj) ? __ldcg(L + gi + gj * a.n) : T(0);
             }
     }
+    // Li[rr][pp] = L[r0 + rr][p0 + pp]; the column side likewise, or in single precision
+    // transposed (LjT[pp * TL + rr]) so that a column pair is one 8-byte load.
     __device__ __forceinline__ void stage(T (*Li)[kB + 1], T (*Lj)[kB + 1]) const {
+        T* LjT = &Lj[0][0];
 #pragma unroll
         for (int q = 0; q < NP; q++) {
             const int e = q * NTH + threadIdx.x, rr = e % TL, pp = e / TL;
             Li[rr][pp] = li[q];
-            Lj[rr][pp] = lj[q];
+            if constexpr (kPair)
+                LjT[pp * TL + rr] = lj[q];
+            else
+                Lj[rr][pp] = lj[q];
         }
     }
     // After stage() and a barrier: subtract the panel's products and store the tile.
@@ -313,23 +368,50 @@ struct TileWork {
         using N = Num<T>;
         T* L = a.base + (int64_t)c * a.n * a.n;
         const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+        if constexpr (kPair) {
+            const float* LjT = reinterpret_cast<const float*>(&Lj[0][0]);
 #pragma unroll 4
-        for (int p = 0; p < kB; p++) {
-            T xi[RU], xj[RV];
+            for (int p = 0; p < kB; p++) {
+                unsigned long long xb[RU], xj[RV / 2];
 #pragma unroll
-            for (int u = 0; u < RU; u++) xi[u] = Li[tx + 32 * u][p];
+                for (int u = 0; u < RU; u++) {
+                    const float x = Li[tx + 32 * u][p];
+                    xb[u] = pk2(x, x);
+                }
 #pragma unroll
-            for (int v = 0; v < RV; v++) xj[v] = Lj[ty + TY * v][p];
+                for (int w = 0; w < RV / 2; w++)
+                    xj[w] = *reinterpret_cast<const unsigned long long*>(LjT + p * TL + 2 * ty +
+                                                                         2 * TY * w);
 #pragma unroll
-            for (int u = 0; u < RU; u++)
+                for (int u = 0; u < RU; u++)
 #pragma unroll
-                for (int v = 0; v < RV; v++) acc[u][v] = N::sub(acc[u][v], N::mul(xi[u], xj[v]));
+                    for (int w = 0; w < RV / 2; w++) {
+                        float plo, phi;
+                        upk2(mul2_rn(xb[u], xj[w]), plo, phi);
+                        acc[u][2 * w] = N::sub(acc[u][2 * w], plo);
+                        acc[u][2 * w + 1] = N::sub(acc[u][2 * w + 1], phi);
+                    }
+            }
+        } else {
+#pragma unroll 4
+            for (int p = 0; p < kB; p++) {
+                T xi[RU], xj[RV];
+#pragma unroll
+                for (int u = 0; u < RU; u++) xi[u] = Li[tx + 32 * u][p];
+#pragma unroll
+                for (int v = 0; v < RV; v++) xj[v] = Lj[ty + TY * v][p];
+#pragma unroll
+                for (int u = 0; u < RU; u++)
+#pragma unroll
+                    for (int v = 0; v < RV; v++)
+                        acc[u][v] = N::sub(acc[u][v], N::mul(xi[u], xj[v]));
+            }
         }
 #pragma unroll
         for (int u = 0; u < RU; u++)
 #pragma unroll
             for (int v = 0; v < RV; v++) {
-                const int64_t gi = r0 + tx + 32 * u, gj = c0 + ty + TY * v;
+                const int64_t gi = r0 + tx + 32 * u, gj = c0 + col(v);
                 if (gi < a.n && gi >= gj) __stcg(L + gi + gj * a.n, acc[u][v]);
             }
     }
@@ -374,7 +456,7 @@ __device__ __forceinline__ bool chol_stopped(const CholArgs<T>& a, int c, int64_
 // published block.  At the barrier the next panel is final.
 template <typename T, int TL>
 __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> a) {
-    __shared__ T S[2 * TL][kB + 1];
+    __shared__ __align__(16) T S[2 * TL][kB + 1];
     __shared__ __align__(16) T Dg[(kB + 1) * kB];
     __shared__ int s_bad;
     __shared__ unsigned int s_ctr[2];   // rank 0: next trailing tile (by panel parity)
@@ -453,7 +535,8 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
             __syncthreads();
             if (t == 0) {  // the next diagonal block is final: factorise it and publish it
                 if (st) st[4] = global_ns();
-                chol_diag(a, c, t0, S, &s_bad, st ? st + 5 : nullptr);  // ends with a barrier
+                cur.stash_first_cols(S);  // block and rows straight from registers
+                chol_diag(a, c, t0, S, &s_bad, st ? st + 5 : nullptr, true);  // ends with a barrier
                 if (threadIdx.x == 0) {
                     __threadfence();
                     st_release_gpu(dflag, k + 1);  // published even on failure: waiters go on
@@ -479,7 +562,7 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
                         __syncthreads();
                         if (threadIdx.x == 0) s_dg = k + 1;
                     }
-                    chol_rows(a, c, t0, r_lo, r_hi, Dg);
+                    chol_rows(a, c, t0, r_lo, r_hi, Dg, t == 0 ? S : nullptr);
                     __syncthreads();
                 }
             }
