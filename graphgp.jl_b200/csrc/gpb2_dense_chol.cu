@@ -706,7 +706,7 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
     const bool spec = n <= spec_max;
     const int batch = spec ? ncand : 1;
     const size_t nn = (size_t)n * (size_t)n;
-    GPB2_TRY(ensure_alloc(&p->Lcand, sizeof(T) * nn * batch));
+    GPB2_TRY(ensure_capacity(&p->Lcand, &p->lcand_bytes, sizeof(T) * nn * batch));
     GPB2_TRY(ensure_alloc(&p->Ld, sizeof(T) * nn));
     GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&p->lad), sizeof(int) * kLadInts + sizeof(T) * 16));
     int* fail = p->lad + kLadFail;

@@ -37,6 +37,18 @@ int ensure_alloc(void** ptr, size_t bytes) {
     return GPB2_OK;
 }
 
+int ensure_capacity(void** ptr, size_t* cap, size_t bytes) {
+    if (*ptr && *cap >= bytes) return GPB2_OK;
+    if (*ptr) {
+        cudaFree(*ptr);  // waits for the device: work already queued on the old buffer finishes
+        *ptr = nullptr;
+    }
+    *cap = 0;
+    GPB2_TRY(ensure_alloc(ptr, bytes));
+    *cap = bytes;
+    return GPB2_OK;
+}
+
 static size_t tsize(const gpb2_problem* p) { return p->dtype == GPB2_F32 ? 4 : 8; }
 
 int ensure_scratch(gpb2_problem* p, bool need_mv) {

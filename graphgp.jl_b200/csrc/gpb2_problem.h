@@ -48,6 +48,7 @@ struct gpb2_problem {
     int* lad = nullptr;       // ladder status (layout: kLad* in gpb2::) + jitters
     std::vector<double> ladder_eps;  // eps of each ladder index of the last factorisation
     void* trace = nullptr;           // diagnostics buffer (GPB2_TRACE_DENSE)
+    size_t lcand_bytes = 0;          // capacity of Lcand (its candidate count can change per call)
     bool dense_pending = false;      // a factorisation was launched and not yet checked
     bool dense_valid = false;        // Ld holds the checked factor of the current table; reused
                                      // by every call until the table changes
@@ -137,6 +138,8 @@ template <>
 inline const Ops<double>* ops_of<double>(const gpb2_problem* p) { return p->ops64; }
 
 int ensure_alloc(void** ptr, size_t bytes);
+// Like ensure_alloc, but reallocates when the buffer (of *cap bytes) is smaller than `bytes`.
+int ensure_capacity(void** ptr, size_t* cap, size_t bytes);
 int ensure_scratch(gpb2_problem* p, bool need_mv);
 int ensure_dense(gpb2_problem* p);
 

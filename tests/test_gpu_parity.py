@@ -304,6 +304,22 @@ def test_dense_ladder_sequential_launches(cuda_device, dt, monkeypatch):
     assert np.array_equal(prob.dense_factor(), np.tril(L_ora))
 
 
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_dense_large_tile_and_ladder_switch(cuda_device, dt, monkeypatch):
+    # The large trailing tile (the default above n0 = 2048) gives the oracle's factor bit for bit
+    # at n0 = 1000 too; one handle switched between one-candidate-per-launch and speculative
+    # ladders (which need different candidate buffers) refactors correctly each time.
+    monkeypatch.setenv("GPB2_CHOL_TILE", "128" if dt == np.float32 else "64")
+    prob, orc = _config_problem(20_000, 2, 1000, 8, dt, 1)
+    L_ora, jit = O.dense_chol(orc)
+    for spec in ("0", "4096", "0"):
+        monkeypatch.setenv("GPB2_DENSE_SPEC_MAX", spec)
+        prob.update_vals(prob.vals)  # same table: the dense block is refactorised
+        gp.generate_logdet(prob)
+        assert np.isclose(prob.dense_jitter(), jit, rtol=1e-6)
+        assert np.array_equal(prob.dense_factor(), np.tril(L_ora))
+
+
 def test_degenerate_duplicates(cuda_device):
     # test/test_degenerate.jl: 30 exact duplicate points must give finite results everywhere.
     rng = np.random.default_rng(0xDEAD)
