@@ -76,73 +76,125 @@ __global__ void k_transpose_lower(const T* __restrict__ L, T* __restrict__ R, in
     }
 }
 
+// Asynchronous element copy global -> shared (cp.async, cached at L1+L2); `in` = false writes
+// zero and reads nothing.
+template <typename T>
+__device__ __forceinline__ void cp_async_elem(T* dst, const T* src, bool in) {
+    const unsigned int d = (unsigned int)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;" ::"r"(d), "l"(src),
+                 "n"((int)sizeof(T)), "r"(in ? (int)sizeof(T) : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Exact-order L*x (TRANS = false) and L^T*x (TRANS = true), outputs [i0, i0 + 32) per CTA.
 //   L x:   y_i = sum_{j=0..i} L[i][j] x_j   (column-major factor: M(i, j) = L[i + j*n])
 //   L^T x: y_i = sum_{k=i..n-1} L[k][i] x_k (row-major copy:     M(i, k) = R[k*ld + i])
-// Warps 1.. form the rounded products of chunk c+1 (terms outside the sum are +0, which leaves
-// the running sum unchanged: it starts at +0 and can never become -0) while warp 0 (lane =
-// output) adds up chunk c in order.
+// Either way term k of output row r is M[k * stride + r].  Each output is one chain of
+// additions in the oracle's order, so the kernel is built around warp 0 (lane = output) doing
+// nothing but those additions: warps 1.. stream the factor and x through a cp.async pipeline
+// of kCh-term chunks, form the rounded products and store them transposed (a row of terms per
+// output), from where warp 0 reads 16 bytes of terms per load.  Terms outside the triangle are
+// +0, which leaves the running sum unchanged (it starts at +0 and can never become -0).
+constexpr int kTrmvThreads = 512;  // warp 0 adds, 15 warps stream and form products
 template <typename T, bool TRANS>
-__global__ void __launch_bounds__(kTriThreads)
+__global__ void __launch_bounds__(kTrmvThreads)
 k_trmv_exact(const T* __restrict__ M, int64_t ld, const T* __restrict__ x, T* __restrict__ y,
              int64_t n) {
     using N = Num<T>;
-    constexpr int kCh = 512 / (int)sizeof(T);  // terms per stage: 2 x 16 KB of products
-    __shared__ T prod[2][kCh][32];
+    using V = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
+    constexpr int kV = 16 / (int)sizeof(T);       // terms per vector load
+    constexpr int kCh = 256 / (int)sizeof(T);     // terms per chunk (8 KB of the factor)
+    constexpr int kS = 3;                         // chunks of the factor in flight
+    constexpr int kP = kCh + kV;                  // row pitch of the product tile
+    constexpr int kProd = kTrmvThreads - 32;       // threads of warps 1..
+    __shared__ __align__(16) T raw[kS][kCh * 32];
+    __shared__ __align__(16) T xs[kS][kCh];
+    __shared__ __align__(16) T P[2][32 * kP];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t i0 = (int64_t)blockIdx.x * 32, i = i0 + lane;
     const int64_t lo = TRANS ? i0 : 0;  // summation index range
     const int64_t hi = TRANS ? n : (i0 + 32 < n ? i0 + 32 : n);
     const int64_t nch = (hi - lo + kCh - 1) / kCh;
-    // Each filling thread issues all its loads before any product is formed (one memory
-    // latency per stage instead of one per element).
-    auto fill = [&](int64_t c, int buf, int t0, int nt) {
-        constexpr int kPer = (kCh * 32 + 223) / 224;  // elements per thread when 224 fill
-        T mv[kPer], xv[kPer];
+    const int64_t stride = TRANS ? ld : n;
+    // Producer pt (warps 1..) always handles output row ii = pt % 32 and the chunk's terms
+    // kk = pt / 32 + kRows * m: kProd is a multiple of 32, so all index arithmetic below is a
+    // fixed per-thread offset plus 32-bit steps.
+    constexpr int kRows = kProd / 32;
+    const int pt = threadIdx.x - 32, ii = pt & 31, kk0 = pt >> 5;
+    const int r = (int)i0 + ii;
+    const bool r_in = r < n;
+    const int hi_i = (int)hi;
+    auto issue = [&](int64_t c) {  // producers: their share of chunk c, then one commit
+        if (c < nch) {
+            T* tb = raw[c % kS] + pt;
+            const int k0 = (int)(lo + c * kCh) + kk0;
+            const T* src = M + (int64_t)k0 * stride + r;
+            const int64_t step = (int64_t)kRows * stride;
 #pragma unroll
-        for (int u = 0; u < kPer; u++) {
-            const int e = t0 + u * nt;
-            const int kk = e >> 5, ii = e & 31;
-            const int64_t k = lo + c * kCh + kk, r = i0 + ii;
-            const bool in = e < kCh * 32 && k < hi && r < n && (TRANS ? k >= r : k <= r);
-            mv[u] = in ? (TRANS ? M[k * ld + r] : M[r + k * n]) : T(0);
-            xv[u] = in ? x[k] : T(0);
+            for (int m = 0; m * kRows + kk0 < kCh; m++) {
+                const bool in = r_in && k0 + m * kRows < hi_i;
+                cp_async_elem(tb + m * kProd, in ? src : M, in);
+                src += step;
+            }
+            if (pt < kCh) {
+                const int k = (int)(lo + c * kCh) + pt;
+                cp_async_elem(xs[c % kS] + pt, k < hi_i ? x + k : x, k < hi_i);
+            }
         }
+        cp_async_commit();
+    };
+    auto form = [&](int64_t c) {  // producers: rounded products of chunk c, transposed
+        cp_async_wait<kS - 2>();  // this thread's copies of chunk c have landed
+        asm volatile("bar.sync 1, %0;" ::"n"(kProd) : "memory");  // everyone's; chunk c-1 formed
+        issue(c + kS - 1);
+        const T* tb = raw[c % kS] + pt;
+        const T* xb = xs[c % kS] + kk0;
+        T* pb = P[c & 1] + ii * kP + kk0;
+        const int k0 = (int)(lo + c * kCh) + kk0;
 #pragma unroll
-        for (int u = 0; u < kPer; u++) {
-            const int e = t0 + u * nt;
-            if (e < kCh * 32) prod[buf][e >> 5][e & 31] = N::mul(mv[u], xv[u]);
-        }
-        for (int e = t0 + kPer * nt; e < kCh * 32; e += nt) {  // only when more threads idle
-            const int kk = e >> 5, ii = e & 31;
-            const int64_t k = lo + c * kCh + kk, r = i0 + ii;
-            T v = T(0);
-            if (k < hi && r < n && (TRANS ? k >= r : k <= r))
-                v = N::mul(TRANS ? M[k * ld + r] : M[r + k * n], x[k]);
-            prod[buf][kk][ii] = v;
+        for (int m = 0; m * kRows + kk0 < kCh; m++) {
+            const int k = k0 + m * kRows;
+            const bool valid = k < hi_i && (TRANS ? k >= r : k <= r);
+            const T pr = N::mul(tb[m * kProd], xb[m * kRows]);
+            pb[m * kRows] = valid ? pr : T(0);
         }
     };
-    fill(0, 0, threadIdx.x, kTriThreads);
+    if (w != 0) {
+#pragma unroll
+        for (int c = 0; c < kS - 1; c++) issue(c);
+        form(0);
+    }
     __syncthreads();
     T acc = T(0);
     for (int64_t c = 0; c < nch; c++) {
-        const int buf = (int)(c & 1);
-        if (w != 0) {
-            if (c + 1 < nch) fill(c + 1, buf ^ 1, threadIdx.x - 32, kTriThreads - 32);
-        } else {
-            const int cnt = (int)(hi - (lo + c * kCh) < kCh ? hi - (lo + c * kCh) : kCh);
-            int kk = 0;
-            for (; kk + 8 <= cnt; kk += 8) {
-                T q[8];
-#pragma unroll
-                for (int u = 0; u < 8; u++) q[u] = prod[buf][kk + u][lane];
-#pragma unroll
-                for (int u = 0; u < 8; u++) acc = N::add(acc, q[u]);
+        if (w == 0) {
+            const V* row = reinterpret_cast<const V*>(P[c & 1] + lane * kP);
+#pragma unroll 4
+            for (int q = 0; q < kCh / kV; q++) {
+                const V v = row[q];
+                if constexpr (sizeof(T) == 4) {
+                    acc = N::add(acc, v.x);
+                    acc = N::add(acc, v.y);
+                    acc = N::add(acc, v.z);
+                    acc = N::add(acc, v.w);
+                } else {
+                    acc = N::add(acc, v.x);
+                    acc = N::add(acc, v.y);
+                }
             }
-            for (; kk < cnt; kk++) acc = N::add(acc, prod[buf][kk][lane]);
+        } else if (c + 1 < nch) {
+            form(c + 1);
         }
-        __syncthreads();
+        __syncthreads();  // chunk c+1's products are ready; chunk c's are consumed
     }
+    if (w != 0) cp_async_wait<0>();
     if (w == 0 && i < n) y[i] = acc;
 }
 
@@ -522,10 +574,10 @@ int dense_trmv(gpb2_problem* p, bool trans, const T* x, T* y, cudaStream_t s) {
     const int64_t n = p->n0;
     const dim3 grid((unsigned)((n + 31) / 32));
     if (trans)
-        GPB2_CUDA_TRY(launch_prof("dense_trmv", k_trmv_exact<T, true>, grid, dim3(kTriThreads),
+        GPB2_CUDA_TRY(launch_prof("dense_trmv", k_trmv_exact<T, true>, grid, dim3(kTrmvThreads),
                                   0, s, (const T*)p->Ldr, tri_pitch(n), x, y, n));
     else
-        GPB2_CUDA_TRY(launch_prof("dense_trmv", k_trmv_exact<T, false>, grid, dim3(kTriThreads),
+        GPB2_CUDA_TRY(launch_prof("dense_trmv", k_trmv_exact<T, false>, grid, dim3(kTrmvThreads),
                                   0, s, (const T*)p->Ld, n, x, y, n));
     return GPB2_OK;
 }
