@@ -746,8 +746,21 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
                                   cudaMemcpyHostToDevice, s));
     GPB2_CUDA_TRY(cudaMemcpyAsync(p->lad + kLadOrder, order.data(), sizeof(int) * ncand_used,
                                   cudaMemcpyHostToDevice, s));
-    for (int first = 0; first < ncand_used; first += batch) {
-        const int nc = std::min(batch, ncand_used - first);
+    // Launches: one candidate each (sequential), or all at once (speculative) -- except that
+    // with a hint the steps above it get a second launch, which does nothing (every CTA returns
+    // at once) when the hint or a step below it succeeded: they would only have competed with
+    // the hinted candidate for the L2 and the cluster slots.
+    std::vector<std::pair<int, int>> launches;  // (first slot, candidates)
+    if (!spec) {
+        for (int f = 0; f < ncand_used; f++) launches.push_back({f, 1});
+    } else if (p->ladder_hint >= 0 && hint + 1 < ncand_used) {
+        launches.push_back({0, hint + 1});
+        launches.push_back({hint + 1, ncand_used - hint - 1});
+    } else {
+        launches.push_back({0, ncand_used});
+    }
+    for (const auto& ln : launches) {
+        const int first = ln.first, nc = ln.second;
         if (first > 0) {
             GPB2_CUDA_TRY(cudaMemsetAsync(fail, 0, sizeof(int) * 16, s));
             GPB2_CUDA_TRY(cudaMemsetAsync(done, 0, sizeof(int) * 16, s));

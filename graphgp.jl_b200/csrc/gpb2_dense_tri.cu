@@ -503,6 +503,99 @@ inline cublasStatus_t gemm_sb(cublasHandle_t h, cublasOperation_t ta, cublasOper
     } while (0)
 
 // A = L^-1 by recursive doubling (see the top of the file).  W: n*n/2 + n entries of work.
+// The first doubling levels of L^-1 for one 128 x 128 diagonal block per CTA, in shared memory:
+// from the inverted 32 x 32 diagonal blocks (Dinv), A21 = -A22 (L21 A11) for the 32- and then
+// the 64-wide pairs, so the library GEMMs start at 128 (eight small launches fewer).  Not an
+// exact-order computation: fused multiply-adds.
+constexpr int kIB = 128;             // block of k_inv_block
+constexpr int kIBP = kIB + 1;        // its row pitch in shared memory
+constexpr int kIW = 64, kIWP = 65;   // the W scratch of one pair
+template <typename T>
+size_t inv_block_smem() { return sizeof(T) * ((size_t)kIB * kIBP + (size_t)kIW * kIWP); }
+
+// out[r][c] = alpha * sum_k X[r][k] Y[k][c] for r < rows <= 64, c < cols <= 64 (row pitches
+// given); each of 256 threads owns a 4 x 4 patch.
+template <typename T>
+__device__ __forceinline__ void cta_gemm64(T* out, int ldo, const T* X, int ldx, const T* Y,
+                                           int ldy, int rows, int cols, int K, T alpha) {
+    const int tr = (threadIdx.x >> 4) * 4, tc = (threadIdx.x & 15) * 4;
+    if (tr >= rows || tc >= cols) return;
+    T acc[4][4] = {};
+    for (int k = 0; k < K; k++) {
+        T xv[4], yv[4];
+#pragma unroll
+        for (int a = 0; a < 4; a++) xv[a] = tr + a < rows ? X[(tr + a) * ldx + k] : T(0);
+#pragma unroll
+        for (int b = 0; b < 4; b++) yv[b] = tc + b < cols ? Y[k * ldy + tc + b] : T(0);
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) acc[a][b] = fma(xv[a], yv[b], acc[a][b]);
+    }
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++)
+            if (tr + a < rows && tc + b < cols) out[(tr + a) * ldo + tc + b] = alpha * acc[a][b];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_inv_block(const T* __restrict__ L,
+                                                   const T* __restrict__ DinvT, int64_t n,
+                                                   T* __restrict__ A) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T* M = reinterpret_cast<T*>(smem_raw);  // M[i * kIBP + j]: the block, row-major
+    T* W = M + kIB * kIBP;
+    const int64_t g0 = (int64_t)blockIdx.x * kIB;
+    const int m = (int)(n - g0 < kIB ? n - g0 : kIB);
+    // Staged in rounds of 16 elements per thread: all of a round's loads are issued before any
+    // is stored (one memory latency per round, not per element).
+    constexpr int kRound = 16;
+    for (int e0 = 0; e0 < kIB * kIB; e0 += 256 * kRound) {
+        T v[kRound];
+#pragma unroll
+        for (int u = 0; u < kRound; u++) {
+            const int e = e0 + u * 256 + (int)threadIdx.x;
+            const int i = e % kIB, j = e / kIB;  // coalesced along the column-major factor
+            v[u] = T(0);
+            if (i < m && j < m && i >= j) {
+                if (i / kTB == j / kTB) {
+                    const int64_t b = (g0 + i) / kTB;  // g0 is a multiple of kTB
+                    v[u] = DinvT[b * kTB * kTB + (j % kTB) * kTB + (i % kTB)];
+                } else {
+                    v[u] = L[(g0 + i) + (g0 + j) * n];
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kRound; u++) {
+            const int e = e0 + u * 256 + (int)threadIdx.x;
+            M[(e % kIB) * kIBP + e / kIB] = v[u];
+        }
+    }
+    __syncthreads();
+    for (int sz = kTB; sz < kIB; sz *= 2) {
+        // W_p = L21 A11 for every pair p at this level, then A21 = -A22 W_p.
+        for (int pass = 0; pass < 2; pass++) {
+            for (int a0 = 0; a0 + sz < m; a0 += 2 * sz) {
+                const int b0 = a0 + sz, s2 = m - b0 < sz ? m - b0 : sz;
+                T* Wp = W + (a0 / (2 * sz)) * (sz == kTB ? kTB * kIWP : 0);
+                if (pass == 0)
+                    cta_gemm64(Wp, kIWP, M + b0 * kIBP + a0, kIBP, M + a0 * kIBP + a0, kIBP, s2,
+                               sz, sz, T(1));
+                else
+                    cta_gemm64(M + b0 * kIBP + a0, kIBP, M + b0 * kIBP + b0, kIBP, Wp, kIWP, s2,
+                               sz, s2, T(-1));
+            }
+            __syncthreads();
+        }
+    }
+    for (int e = threadIdx.x; e < kIB * kIB; e += blockDim.x) {
+        const int i = e % kIB, j = e / kIB;
+        if (i < m && j < m && i >= j) A[(g0 + i) + (g0 + j) * n] = M[i * kIBP + j];
+    }
+}
+
 template <typename T>
 int build_inverse(gpb2_problem* p, T* A, T* W, cudaStream_t s) {
     const int64_t n = p->n0;
@@ -510,9 +603,15 @@ int build_inverse(gpb2_problem* p, T* A, T* W, cudaStream_t s) {
     GPB2_CUDA_TRY(launch_prof("dense_ainv_init", k_ainv_init<T>,
                               dim3((unsigned)std::min<int64_t>((n * n + 255) / 256, 8 * 148)),
                               dim3(256), 0, s, (const T*)p->Dinv, n, A));
+    // Levels 32 and 64 inside each 128-wide diagonal block, then library GEMMs from 128 up.
+    const size_t ism = inv_block_smem<T>();
+    GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_inv_block<T>, ism));
+    GPB2_CUDA_TRY(launch_prof("dense_inv_block", k_inv_block<T>,
+                              dim3((unsigned)((n + kIB - 1) / kIB)), dim3(256), ism, s, L,
+                              (const T*)p->Dinv, n, A));
     GPB2_TRI_BLAS(cublasSetStream(p->blas, s));
     const int ni = (int)n;
-    for (int64_t sz = kTB; sz < n; sz *= 2) {
+    for (int64_t sz = kIB; sz < n; sz *= 2) {
         const int64_t full = n / (2 * sz);  // complete pairs (A11, A22 both of size sz)
         const long long diag = 2 * sz * (n + 1);  // stride between pairs along the diagonal
         const int si = (int)sz;

@@ -338,16 +338,18 @@ struct PointMath {
         load_coords<D>(jc[K], coords, self);
     }
 
-    // r = sqrt(T(sq)) * scale with sq the exact Int64 squared lattice distance.
+    // r = sqrt(T(sq)) * scale with sq the exact Int64 squared lattice distance.  The squares are
+    // formed as |a - b|^2 from 32-bit differences by one widening multiply-add each; the sum
+    // wraps modulo 2^64 exactly as the Int64 sum of (a - b)^2 does, so sq has the same bits.
     static __device__ __forceinline__ T radius(const uint32_t (&a)[D], const uint32_t (&b)[D],
                                                T scale) {
-        long long sq = 0;
+        unsigned long long sq = 0;
         sfor<0, D>([&](auto d_) {
             GPB2_CI(d);
-            const long long di = (long long)a[d] - (long long)b[d];
-            sq += di * di;
+            const uint32_t di = a[d] > b[d] ? a[d] - b[d] : b[d] - a[d];
+            sq += (unsigned long long)di * di;
         });
-        return N::mul(N::sqrt(N::from_i64(sq)), scale);
+        return N::mul(N::sqrt(N::from_i64((long long)sq)), scale);
     }
 
     // assemble_cov! (src/linalg.jl:98-112).  With KEEP_R the radius of pair (a, b), b < a, is
