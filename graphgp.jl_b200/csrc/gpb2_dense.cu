@@ -265,7 +265,7 @@ template <typename T>
 int Dense<T>::factor(gpb2_problem* p, cudaStream_t s) {
     // The factor depends only on the coordinates (fixed) and the covariance table: a checked
     // factor of the current table is reused (the table setter clears the flag).
-    if (p->dense_valid) return GPB2_OK;
+    if (p->dense_valid || p->dense_launched) return GPB2_OK;  // (a prefactor launched it)
     GPB2_TRY(ensure_dense(p));
     p->tri_ready = false;
     GPB2_TRY(dense_cholesky_ladder<T>(p, s));  // gpb2_dense_chol.cu

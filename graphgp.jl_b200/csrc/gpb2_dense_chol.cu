@@ -850,6 +850,7 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
                               static_cast<T*>(p->Ld), p->lad + kLadNotPD));
     p->ladder_eps.assign(epsv.begin(), epsv.begin() + ncand_used);
     p->dense_pending = true;  // outcome checked by the call's finishing synchronisation
+    p->dense_launched = true;
     return GPB2_OK;
 }
 

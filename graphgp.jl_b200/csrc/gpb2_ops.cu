@@ -307,6 +307,12 @@ struct Impl {
                             "reverse range");
     }
 
+    // Both factorisations of the current table, queued on s without waiting for them.
+    static int prefactor(P* p, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, true));
+        return factor_both(p, s);
+    }
+
     static int dense_apply(P* p, int trans, const T* x, T* y, cudaStream_t s) {
         GPB2_TRY(Dense<T>::factor(p, s));
         return trans ? Dense<T>::apply_Lt(p, x, y, s) : Dense<T>::apply_L(p, x, y, s);
@@ -466,7 +472,10 @@ static int finish_call(gpb2_problem* p, cudaStream_t s) {
     }
     GPB2_CUDA_TRY(cudaStreamSynchronize(s));
     p->dense_pending = false;
-    if (dense) p->dense_valid = h[0] == 0 && h[1] == 0 && h[2] == 0;
+    if (dense) {
+        p->dense_valid = h[0] == 0 && h[1] == 0 && h[2] == 0;
+        if (!p->dense_valid) p->dense_launched = false;  // the next call factorises again
+    }
     // The selected ladder step orders the next factorisation's speculative candidates.
     if (dense && h[3] >= 0) p->ladder_hint = h[3];
     if (h[0] != 0) {
@@ -496,6 +505,7 @@ using namespace gpb2;
         const int _st = (p)->dtype == GPB2_F32 ? (CALL32) : (CALL64);                           \
         if (_st != GPB2_OK) {                                                                  \
             p->dense_pending = false;                                                          \
+            p->dense_launched = p->dense_valid;                                                \
             return _st;                                                                        \
         }                                                                                      \
         return finish_call(p, s);                                                              \
@@ -566,6 +576,12 @@ int gpb2_refine_reverse_range(gpb2_problem* p, void* xg, void* vb, int64_t lo, i
     if (lo == hi) return GPB2_OK;
     GPB2_ASYNC(p, Impl<float>::reverse_range(p, F32(xg), F32(vb), lo, hi, s),
                Impl<double>::reverse_range(p, F64(xg), F64(vb), lo, hi, s));
+}
+
+int gpb2_problem_prefactor(gpb2_problem* p, void* stream) {
+    clear_error();
+    if (!p) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_prefactor: NULL problem");
+    GPB2_ASYNC(p, Impl<float>::prefactor(p, s), Impl<double>::prefactor(p, s));
 }
 
 int gpb2_dense_apply(gpb2_problem* p, int trans, const void* x, void* y, void* stream) {

@@ -205,6 +205,7 @@ static int build_table(gpb2_problem* p, const T* hb, const T* hv, cudaStream_t s
 static int load_table(gpb2_problem* p, const void* vals_dev, cudaStream_t s) {
     const size_t ts = tsize(p);
     p->dense_valid = false;   // the dense factor belongs to the previous table
+    p->dense_launched = false;
     p->factor_valid = false;  // and so do the per-point mean_vec / std
     GPB2_CUDA_TRY(cudaMemcpyAsync(p->vals, vals_dev, ts * p->nb, cudaMemcpyDeviceToDevice, s));
     std::vector<unsigned char> hb(ts * p->nb), hv(ts * p->nb);

@@ -50,6 +50,8 @@ struct gpb2_problem {
     void* trace = nullptr;           // diagnostics buffer (GPB2_TRACE_DENSE)
     size_t lcand_bytes = 0;          // capacity of Lcand (its candidate count can change per call)
     bool dense_pending = false;      // a factorisation was launched and not yet checked
+    bool dense_launched = false;     // the current table's factorisation is launched (checked or
+                                     // not); cleared by a new table and by a failed check
     bool dense_valid = false;        // Ld holds the checked factor of the current table; reused
                                      // by every call until the table changes
     int dense_candidate = -1;

@@ -79,6 +79,7 @@ _SIGNATURES = {
     "gpb2_problem_create": (I32, [C.POINTER(P), I32, I32, P, I64, I64, P, I32, I32, I64, PI64,
                                   I64, I64, C.c_double, P, P, I64, PI64, I32, P]),
     "gpb2_problem_set_vals": (I32, [P, P, P]),
+    "gpb2_problem_prefactor": (I32, [P, P]),
     "gpb2_problem_info": (I32, [P, PI64, PI64, PI64, PI64, PI64]),
     "gpb2_problem_destroy": (I32, [P]),
     "gpb2_problem_dense_jitter": (I32, [P, PD]),

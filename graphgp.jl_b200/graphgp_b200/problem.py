@@ -166,6 +166,16 @@ class GraphGPProblem:
         self.vals = vals
         return self
 
+    def prefactor(self) -> "GraphGPProblem":
+        """Queue the current table's factorisations (dense block and per-point factors) on the
+        current stream without waiting, so they overlap whatever the caller does next (e.g.
+        copying the next inputs in).  Operations factor an unfactorised table themselves; a
+        dense block that no jitter step factorises is reported by the next operation."""
+        st = _lib.lib().gpb2_problem_prefactor(
+            self.handle, C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        _lib.check(st, "prefactor")
+        return self
+
     def dense_jitter(self) -> float:
         """Relative jitter of the dense block's last factorisation (0.0 = none needed, -1.0 =
         not factorised yet), the ladder of src/dense.jl:46-67."""

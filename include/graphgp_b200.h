@@ -77,6 +77,15 @@ int gpb2_problem_create(gpb2_problem** out, int dtype, int device,
 /* Replace the covariance values (`_set_vals`, src/chainrules.jl:18-21). */
 int gpb2_problem_set_vals(gpb2_problem* prob, const void* vals_dev, void* stream);
 
+/* Queue both factorisations of the current table (the dense first-layer Cholesky with its
+ * jitter ladder, and every refined point's mean_vec / std) on `stream` and return without
+ * waiting.  No separate counterpart in the reference: its generate factors the dense block
+ * at its start (src/api.jl:113-141); every operation here also factors a table that is not
+ * factorised yet, so this call only lets a caller start that work early, e.g. while the next
+ * inputs are still being copied to the device.  A numerical failure (no ladder step
+ * factorises the dense block) is reported by the next operation that uses the factor. */
+int gpb2_problem_prefactor(gpb2_problem* prob, void* stream);
+
 /* Sizes: N, M = N - n0, K, D, number of depth batches (n_offsets - 1). */
 int gpb2_problem_info(const gpb2_problem* prob, int64_t* n, int64_t* m, int64_t* k, int64_t* d,
                       int64_t* n_batches);

@@ -271,6 +271,32 @@ def test_update_vals_refactors(cuda_device, dt):
 
 
 @pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_prefactor(cuda_device, dt):
+    # prefactor() queues a new table's factorisations without waiting; the operations that
+    # follow use them (the same results as without it), and a dense block that no jitter step
+    # factorises is reported by the next operation -- again by the one after, on the same
+    # table -- while a good table afterwards works as before.
+    prob, orc = _config_problem(3000, 2, 200, 8, dt, 21)
+    rng = np.random.default_rng(8)
+    xi = rng.standard_normal(prob.npoints()).astype(dt)
+    vb = rng.standard_normal(prob.npoints()).astype(dt)
+    f0 = gp.generate(prob, xi)
+    g0 = gp.generate_grad_vals(prob, xi, vb)
+    good = np.array(prob.vals, copy=True)
+    prob.update_vals(good).prefactor()
+    assert np.array_equal(gp.generate(prob, xi), f0)
+    assert np.array_equal(prob.dense_factor(), np.tril(O.dense_chol(orc)[0]))
+    assert relerr(gp.generate_grad_vals(prob, xi, vb), g0) < TOL[dt]
+    prob.update_vals(-good).prefactor()  # negative variances: no jitter step helps
+    for _ in range(2):
+        with pytest.raises(_lib.GraphGPError) as e:
+            gp.generate(prob, xi)
+        assert e.value.status == _lib.GPB2_ERR_NOT_PD
+    prob.update_vals(good)
+    assert np.array_equal(gp.generate(prob, xi), f0)
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
 def test_grad_vals_repeated_and_after_refactor(cuda_device, dt):
     # Repeated vals-gradients on one handle, before and after the table is re-set (which
     # refactors the dense block and the per-point factors), must agree with each other and with
