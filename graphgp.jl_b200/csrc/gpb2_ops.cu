@@ -405,10 +405,30 @@ struct Impl {
             GPB2_TRY(reverse_sweep(p, nullptr, vb, s));
         }
         GPB2_TRY(zero_acc(p, s));
-        GPB2_TRY(check_launch(
-            ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb, (const T*)p->mv, p->dacc, p->m, s),
-            "grad_vals"));
-        GPB2_TRY(Dense<T>::grad_vals(p, vb, xt, p->dacc, s));
+        auto per_point = [&](cudaStream_t st) {
+            return check_launch(ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb,
+                                                        (const T*)p->mv, p->dacc, p->m, st),
+                                "grad_vals");
+        };
+        if (!g_overlap) {
+            GPB2_TRY(per_point(s));
+            GPB2_TRY(Dense<T>::grad_vals(p, vb, xt, p->dacc, s));
+            return finish_hist(p, dvals, s);
+        }
+        // The dense block's pullback (a short chain of small kernels) and the per-point kernel
+        // are independent and both add into the histogram: the chain goes first, on the
+        // high-priority stream, and runs beside the per-point kernel.
+        GPB2_TRY(ensure_dense_stream(p));
+        GPB2_CUDA_TRY(cudaEventRecord(p->ev_fork, s));
+        GPB2_CUDA_TRY(cudaStreamWaitEvent(p->dstream, p->ev_fork, 0));
+        const int sd = Dense<T>::grad_vals(p, vb, xt, p->dacc, p->dstream);
+        const int sp = sd == GPB2_OK ? per_point(s) : GPB2_OK;
+        const cudaError_t e1 = cudaEventRecord(p->ev_join, p->dstream);
+        const cudaError_t e2 = cudaStreamWaitEvent(s, p->ev_join, 0);
+        GPB2_TRY(sd);
+        GPB2_TRY(sp);
+        GPB2_CUDA_TRY(e1);
+        GPB2_CUDA_TRY(e2);
         return finish_hist(p, dvals, s);
     }
 
