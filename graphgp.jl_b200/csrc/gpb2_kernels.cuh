@@ -71,32 +71,32 @@ __device__ __forceinline__ double block_sum_double(double v, double* red /*>= 32
 // Where the adjoint kernels keep a point's pair radii between the assembly and the histogram
 // scatter: the thread's column of a shared-memory block after the histogram when it fits (the
 // radii would otherwise occupy NR registers through the whole pullback), else registers.
-template <typename T, int K, int D>
+template <typename T, int K, int D, int NTH = kFlatThreads, size_t CAP = 36 * 1024>
 struct RadiusStore {
     static constexpr int NR = PointMath<T, K, D>::NR;
     // Interpolation weights (segment + fraction) when they fit, else radii, in shared memory;
     // else radii in registers.
     static constexpr bool kWeights =
-        (size_t)NR * kFlatThreads * (sizeof(T) + sizeof(uint16_t)) <= 36 * 1024;
-    static constexpr bool kSmem = (size_t)NR * kFlatThreads * sizeof(T) <= 36 * 1024;
+        (size_t)NR * NTH * (sizeof(T) + sizeof(uint16_t)) <= CAP;
+    static constexpr bool kSmem = (size_t)NR * NTH * sizeof(T) <= CAP;
     using type = typename std::conditional<
         kWeights, SmemWeights<T>,
         typename std::conditional<kSmem, SmemCol<T>, RegArr<T, NR>>::type>::type;
     static constexpr size_t bytes =
-        kWeights ? (size_t)NR * kFlatThreads * (sizeof(T) + sizeof(uint16_t))
-                 : (kSmem ? (size_t)NR * kFlatThreads * sizeof(T) : 0);
+        kWeights ? (size_t)NR * NTH * (sizeof(T) + sizeof(uint16_t))
+                 : (kSmem ? (size_t)NR * NTH * sizeof(T) : 0);
     static __device__ __forceinline__ type make(unsigned char* base) {
         if constexpr (kWeights) {
             SmemWeights<T> w;
             w.t = reinterpret_cast<T*>(base) + threadIdx.x;
-            w.lo = reinterpret_cast<uint16_t*>(base + (size_t)NR * kFlatThreads * sizeof(T)) +
+            w.lo = reinterpret_cast<uint16_t*>(base + (size_t)NR * NTH * sizeof(T)) +
                    threadIdx.x;
-            w.stride = kFlatThreads;
+            w.stride = NTH;
             return w;
         } else if constexpr (kSmem) {
             SmemCol<T> c;
             c.p = reinterpret_cast<T*>(base) + threadIdx.x;
-            c.stride = kFlatThreads;
+            c.stride = NTH;
             return c;
         } else {
             return type{};
@@ -290,8 +290,21 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
 // src/kernels_adjoint.jl:484-553), run over ALL points after the reverse sweep has finalised
 // vb: every point's cotangent seed (vb[p]*xi[p], vb[p]*v[nbr]) is then known, and the point's
 // pullback needs nothing else, so the batches need not be visited in order.
+// Block shape of k_grad_vals: 320 threads, two blocks per SM (20 warps, within both the register
+// file at <= 102 registers and shared memory), when the interpolation weights of 320 threads fit
+// in 72 KB; else the flat kernels' 128 threads.
 template <typename T, int K, int D>
-__global__ void __launch_bounds__(kFlatThreads)
+struct GradShape {
+    static constexpr int kWide = 320;
+    static constexpr bool kUse =
+        (size_t)PointMath<T, K, D>::NR * kWide * (sizeof(T) + sizeof(uint16_t)) <= 72 * 1024;
+    static constexpr int kThreads = kUse ? kWide : kFlatThreads;
+    static constexpr int kMinBlocks = kUse ? 2 : 1;
+    using Store = RadiusStore<T, K, D, kThreads, kUse ? 72 * 1024 : 36 * 1024>;
+};
+
+template <typename T, int K, int D>
+__global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
             const T* __restrict__ vb, const T* __restrict__ mv, double* __restrict__ gacc,
             int64_t M) {
@@ -310,8 +323,8 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
          m += (int64_t)gridDim.x * blockDim.x) {
         const int64_t p = a.n0 + m;
         const T vbp = vb[p];
-        PointFactor<T, K, D, true, typename RadiusStore<T, K, D>::type> f;
-        f.R = RadiusStore<T, K, D>::make(rbase);
+        PointFactor<T, K, D, true, typename GradShape<T, K, D>::Store::type> f;
+        f.R = GradShape<T, K, D>::Store::make(rbase);
         f.compute(a, tab, m);
         const T pivfloor = N::mul(a.tab.pivc, f.L[0]);
         T B[PM::NT];
@@ -760,8 +773,13 @@ struct Launch {
     }
     static cudaError_t grad_vals(const PointArgs<T>& a, const T* v, const T* xih, const T* vb,
                                  const T* mv, double* gacc, int64_t M, cudaStream_t s) {
-        return flat("grad_vals", k_grad_vals<T, K, D>, flat_smem(a, true) + RadiusStore<T, K, D>::bytes, M, s, a, v, xih, vb,
-                    mv, gacc, M);
+        using G = GradShape<T, K, D>;
+        const size_t smem = flat_smem(a, true) + G::Store::bytes;
+        cudaError_t e = prepare_kernel_smem((const void*)k_grad_vals<T, K, D>, smem);
+        if (e != cudaSuccess) return e;
+        const int grid = flat_grid((const void*)k_grad_vals<T, K, D>, G::kThreads, smem, M);
+        return launch_prof("grad_vals", k_grad_vals<T, K, D>, dim3(grid), dim3(G::kThreads), smem,
+                           s, a, v, xih, vb, mv, gacc, M);
     }
     static cudaError_t inv_loss_grad(const PointArgs<T>& a, const T* values, double* gacc,
                                      double* loss, T* xi_out, int64_t M, cudaStream_t s) {
