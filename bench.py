@@ -210,7 +210,7 @@ class ClockSampler:
 # each (`ncu --set full ... python bench.py --ncu-case`; summaries in profiles/).  Measured, not
 # computed here: the bench itself never runs under a profiler.
 NCU_TRAFFIC = {
-    "grad_vals": (83.92e6 + 2.94e6, "profiles/k_grad_vals_config2.md"),
+    "grad_vals": (83.91e6 + 5.47e6, "profiles/k_grad_vals_config2.md"),
     "factor": (40.06e6 + 2.19e6, "profiles/k_factor_config2.md"),
     "sweep_fwdrev_all": (78.64e6 + 4.30e6, "profiles/k_sweep_fwdrev_all_config2.md"),
 }
