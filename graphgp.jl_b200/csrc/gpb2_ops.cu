@@ -225,10 +225,14 @@ struct Impl {
         return GPB2_OK;
     }
 
+    // The four scalar accumulators after the histogram, through pinned host memory.
     static int read_scalars(P* p, double* h, cudaStream_t s) {
-        GPB2_CUDA_TRY(
-            cudaMemcpyAsync(h, p->dacc + p->nb, sizeof(double) * 4, cudaMemcpyDeviceToHost, s));
+        if (!p->hscal)
+            GPB2_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&p->hscal), 4 * sizeof(double)));
+        GPB2_CUDA_TRY(cudaMemcpyAsync(p->hscal, p->dacc + p->nb, sizeof(double) * 4,
+                                      cudaMemcpyDeviceToHost, s));
         GPB2_CUDA_TRY(cudaStreamSynchronize(s));
+        for (int i = 0; i < 4; i++) h[i] = p->hscal[i];
         return GPB2_OK;
     }
 
@@ -479,7 +483,14 @@ struct Impl {
 // factorisation) or a dense block that no ladder step could factorise (src/dense.jl:65-66).
 // The reference's drivers also synchronise before returning (e.g. src/api.jl:139).
 static int finish_call(gpb2_problem* p, cudaStream_t s) {
-    int h[4] = {0, 0, 0, -1};
+    // Status words land in pinned host memory: the copies queue behind the call's kernels and
+    // one synchronisation waits for all of them (copies to pageable memory would each wait).
+    if (!p->hstat) GPB2_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&p->hstat), 4 * sizeof(int)));
+    int* h = p->hstat;
+    h[0] = 0;
+    h[1] = 0;
+    h[2] = 0;
+    h[3] = -1;
     GPB2_CUDA_TRY(cudaMemcpyAsync(&h[0], p->dsync + 2, sizeof(int), cudaMemcpyDeviceToHost, s));
     const bool dense = p->dense_pending && p->lad;
     if (dense) {

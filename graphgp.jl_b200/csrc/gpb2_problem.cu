@@ -229,6 +229,8 @@ static void free_problem(gpb2_problem* p) {
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);
     if (p->blas) cublasDestroy(p->blas);
+    if (p->hstat) cudaFreeHost(p->hstat);
+    if (p->hscal) cudaFreeHost(p->hscal);
     if (p->ev_fork) cudaEventDestroy(p->ev_fork);
     if (p->ev_join) cudaEventDestroy(p->ev_join);
     if (p->dstream) cudaStreamDestroy(p->dstream);

@@ -50,6 +50,8 @@ struct gpb2_problem {
     void* trace = nullptr;           // diagnostics buffer (GPB2_TRACE_DENSE)
     size_t lcand_bytes = 0;          // capacity of Lcand (its candidate count can change per call)
     bool dense_pending = false;      // a factorisation was launched and not yet checked
+    int* hstat = nullptr;            // pinned host copy of the status words (4 ints)
+    double* hscal = nullptr;         // pinned host copy of the scalar accumulators (4 doubles)
     bool dense_launched = false;     // the current table's factorisation is launched (checked or
                                      // not); cleared by a new table and by a failed check
     bool dense_valid = false;        // Ld holds the checked factor of the current table; reused
