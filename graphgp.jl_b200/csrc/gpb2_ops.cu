@@ -68,6 +68,14 @@ std::atomic<int> g_fwd_mode{[] {
 
 FwdMode fwd_mode() { return static_cast<FwdMode>(g_fwd_mode.load()); }
 
+// Process-wide call mode (GPB2_SYNC=0 at load time, or gpb2_set_synchronous()): 1 = every call
+// waits for its work and reports its status; 0 = calls return once their work is queued and
+// gpb2_problem_check() waits and reports (calls that return host values still wait for them).
+std::atomic<int> g_sync{[] {
+    const char* e = std::getenv("GPB2_SYNC");
+    return (e && std::strcmp(e, "0") == 0) ? 0 : 1;
+}()};
+
 // Whether the dense first-layer factor runs beside the per-point factor (GPB2_OVERLAP=0 at load
 // time runs them one after the other on the call's stream).
 const bool g_overlap = [] {
@@ -539,6 +547,7 @@ using namespace gpb2;
             p->dense_launched = p->dense_valid;                                                \
             return _st;                                                                        \
         }                                                                                      \
+        if (!g_sync.load()) return GPB2_OK;                                                    \
         return finish_call(p, s);                                                              \
     } while (0)
 
@@ -552,6 +561,19 @@ static int need(const void* ptr, const char* name) {
 }
 
 extern "C" {
+
+int gpb2_set_synchronous(int on) {
+    g_sync.store(on ? 1 : 0);
+    return GPB2_OK;
+}
+
+int gpb2_problem_check(gpb2_problem* p, void* stream) {
+    clear_error();
+    if (!p) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_check: NULL problem");
+    DeviceGuard dg(p->device);
+    if (!dg.ok) return set_error(GPB2_ERR_NO_DEVICE, "cudaSetDevice(%d) failed", p->device);
+    return finish_call(p, (cudaStream_t)stream);
+}
 
 int gpb2_set_forward_mode(int mode) {
     if (mode < 0 || mode > 3)

@@ -11,7 +11,7 @@ from .api import (check_graph, generate, generate_grad_vals, generate_grad_xi, g
                   generate_inv_loss_grad_vals, generate_logdet, generate_logdet_and_grad_vals,
                   generate_logdet_grad_vals, refine, refine_, refine_inv, refine_inv_,
                   refine_inv_loss_grad_vals, refine_logdet, refine_logdet_grad_vals,
-                  refine_logdet_grad_vals_noalloc, refine_logdet_terms)
+                  refine_logdet_grad_vals_noalloc, refine_logdet_terms, set_synchronous)
 from .autodiff import generate_of_vals, generate_t, inv_quadratic_loss_of_vals, logdet_of_vals
 from .extras import hyperparam_grad, make_cov_bins, matern_kernel, rbf_kernel
 from .graph import build_graph, build_graph_arrays, cached_graph
@@ -27,7 +27,7 @@ __all__ = [
     "generate_inv_loss_grad_vals", "logdet_of_vals", "inv_quadratic_loss_of_vals",
     "generate_of_vals", "generate_t", "make_cov_bins", "rbf_kernel", "matern_kernel",
     "hyperparam_grad", "GraphGPError", "GraphInvariantError", "UnsupportedError",
-    "NotPositiveDefiniteError",
+    "NotPositiveDefiniteError", "set_synchronous",
 ]
 
 

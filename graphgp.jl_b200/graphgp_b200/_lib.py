@@ -89,6 +89,8 @@ _SIGNATURES = {
     "gpb2_profile_report": (I32, [C.c_char_p, I64]),
     "gpb2_launch_count": (I64, []),
     "gpb2_set_forward_mode": (I32, [I32]),
+    "gpb2_set_synchronous": (I32, [I32]),
+    "gpb2_problem_check": (I32, [P, P]),
     "gpb2_refine": (I32, [P, P, P, P]),
     "gpb2_refine_inv": (I32, [P, P, P, P]),
     "gpb2_refine_range": (I32, [P, P, P, I64, I64, P]),

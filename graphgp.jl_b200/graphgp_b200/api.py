@@ -221,6 +221,14 @@ def generate_inv_loss_grad_vals(prob: GraphGPProblem, data):
     return loss.value, _ret(out, host)
 
 
+def set_synchronous(on: bool) -> None:
+    """Process-wide call mode.  True (the default): every operation waits for its work and
+    raises its numerical status (NotPositiveDefiniteError, barrier timeouts).  False: operations
+    on device tensors return once their work is queued, as CUDA launches do; `prob.check()`
+    waits and raises the status.  Operations that return host values still wait for them."""
+    _lib.check(_lib.lib().gpb2_set_synchronous(1 if on else 0), "set_synchronous")
+
+
 def check_graph(prob: GraphGPProblem) -> None:
     """Validate the graph invariants (src/graph_build.jl:20-57): offsets start at n0 and end at
     N, are non-decreasing, and every neighbour lies in an earlier depth batch.  The check runs

@@ -176,6 +176,14 @@ class GraphGPProblem:
         _lib.check(st, "prefactor")
         return self
 
+    def check(self) -> "GraphGPProblem":
+        """Wait for this handle's queued work on the current stream and raise its status (in
+        the asynchronous call mode, `set_synchronous(False)`, operations do not wait)."""
+        st = _lib.lib().gpb2_problem_check(
+            self.handle, C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        _lib.check(st, "check")
+        return self
+
     def dense_jitter(self) -> float:
         """Relative jitter of the dense block's last factorisation (0.0 = none needed, -1.0 =
         not factorised yet), the ladder of src/dense.jl:46-67."""

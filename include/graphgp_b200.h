@@ -122,6 +122,20 @@ int64_t gpb2_launch_count(void);
  * barrier or wait that times out makes the call return GPB2_ERR_TIMEOUT. */
 int gpb2_set_forward_mode(int mode);
 
+/* Call mode, process-wide (default 1; GPB2_SYNC=0 in the environment at load time sets 0).
+ * 1: every operation waits for its work and returns its status, including the numerical ones
+ *    (a dense block that no jitter step factorises, a grid barrier that timed out).
+ * 0: operations return once their work is queued on the stream, as CUDA launches do (the
+ *    reference's CUDA.jl path is asynchronous the same way: ext/GraphGPCUDAExt.jl:39-64);
+ *    launch errors are still returned, the numerical status is reported by the next
+ *    gpb2_problem_check on the handle.  Operations that return host values (logdets, losses)
+ *    still wait for them.  No counterpart in the reference's C API. */
+int gpb2_set_synchronous(int on);
+
+/* Wait for the handle's queued work on `stream` and return its status (see
+ * gpb2_set_synchronous).  No counterpart in the reference. */
+int gpb2_problem_check(gpb2_problem* prob, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Refine layer, tree order.
  * ---------------------------------------------------------------------------------------- */

@@ -296,6 +296,47 @@ def test_prefactor(cuda_device, dt):
     assert np.array_equal(gp.generate(prob, xi), f0)
 
 
+@pytest.fixture
+def _async_mode():
+    gp.set_synchronous(False)
+    yield
+    gp.set_synchronous(True)
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_asynchronous_calls(cuda_device, dt, _async_mode):
+    # With set_synchronous(False) the operations only queue their work; the results are the
+    # synchronous ones, and a dense block that no jitter step factorises is reported by
+    # check(), not by the operation.
+    prob, _ = _config_problem(3000, 2, 200, 8, dt, 21)
+    rng = np.random.default_rng(8)
+    xi_h = rng.standard_normal(prob.npoints()).astype(dt)
+    vb_h = rng.standard_normal(prob.npoints()).astype(dt)
+    xi = torch.from_numpy(xi_h).to(prob.device)
+    vb = torch.from_numpy(vb_h).to(prob.device)
+    good = np.array(prob.vals, copy=True)
+    prob.update_vals(good).prefactor()
+    f = gp.generate(prob, xi)
+    gx = gp.generate_grad_xi(prob, vb)
+    gv = gp.generate_grad_vals(prob, xi, vb)
+    prob.check()
+    gp.set_synchronous(True)
+    assert np.array_equal(f.cpu().numpy(), gp.generate(prob, xi_h))
+    assert np.array_equal(gx.cpu().numpy(), gp.generate_grad_xi(prob, vb_h)) or \
+        relerr(gx.cpu().numpy(), gp.generate_grad_xi(prob, vb_h)) < TOL[dt]
+    assert relerr(gv.cpu().numpy(), gp.generate_grad_vals(prob, xi_h, vb_h)) < TOL[dt]
+    gp.set_synchronous(False)
+    prob.update_vals(-good).prefactor()  # negative variances: no jitter step helps
+    gp.generate(prob, xi)                # queued; the status comes with check()
+    with pytest.raises(_lib.GraphGPError) as e:
+        prob.check()
+    assert e.value.status == _lib.GPB2_ERR_NOT_PD
+    prob.update_vals(good)
+    f2 = gp.generate(prob, xi)
+    prob.check()
+    assert np.array_equal(f2.cpu().numpy(), f.cpu().numpy())
+
+
 @pytest.mark.parametrize("dt", [np.float64, np.float32])
 def test_grad_vals_repeated_and_after_refactor(cuda_device, dt):
     # Repeated vals-gradients on one handle, before and after the table is re-set (which
