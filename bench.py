@@ -153,6 +153,70 @@ def run_reference(args):
 # ---------------------------------------------------------------------------------------------
 # GPU arm.
 # ---------------------------------------------------------------------------------------------
+class NvmlClockSampler:
+    """SM clock and clock-event (throttle) reasons read through NVML every 5 ms on a thread
+    during the timed region (a step takes a few ms, so nvidia-smi's 200 ms period would see
+    none); the NVML device is matched to the CUDA device by PCI bus id.  Read-only."""
+
+    def __init__(self, cuda_index: int):
+        import pynvml
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        import torch
+        pr = torch.cuda.get_device_properties(cuda_index)
+        try:
+            bus = "%08X:%02X:%02X.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+        self.samples = []
+        self.stop = None
+        self.thread = None
+
+    def _read(self):
+        nv = self.nv
+        sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+        rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        self.samples.append((sm, mx, rs))
+
+    def __enter__(self):
+        import threading
+        self.stop = threading.Event()
+        self._read()
+
+        def loop():
+            while not self.stop.wait(0.005):
+                self._read()
+        self.thread = threading.Thread(target=loop, daemon=True)
+        self.thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self.stop.set()
+        self.thread.join(timeout=5)
+        self._read()
+
+    def summary(self):
+        nv = self.nv
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        reasons = sorted({n for _, _, r in self.samples for n, b in bits.items() if r & b})
+        sm = [s for s, _, _ in self.samples]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(m for _, m, _ in self.samples) if self.samples else None,
+                "reasons": reasons, "samples": len(sm), "source": "nvml"}
+
+
+def clock_sampler(cuda_index: int):
+    try:
+        return NvmlClockSampler(cuda_index)
+    except Exception:
+        return ClockSampler(cuda_index)
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
 
@@ -301,7 +365,7 @@ def run_b200(args):
         step()
     barrier()
     launches0 = L.gpb2_launch_count()
-    with ClockSampler(local) as cs:
+    with clock_sampler(local) as cs:
         ms = timed(step, args.steps)
     barrier()
     launches = L.gpb2_launch_count() - launches0
