@@ -275,7 +275,9 @@ def test_prefactor(cuda_device, dt):
     # prefactor() queues a new table's factorisations without waiting; the operations that
     # follow use them (the same results as without it), and a dense block that no jitter step
     # factorises is reported by the next operation -- again by the one after, on the same
-    # table -- while a good table afterwards works as before.
+    # table -- while a good table afterwards works as before.  (Synchronous calls: the status
+    # of each call is what is checked.)
+    gp.set_synchronous(True)
     prob, orc = _config_problem(3000, 2, 200, 8, dt, 21)
     rng = np.random.default_rng(8)
     xi = rng.standard_normal(prob.npoints()).astype(dt)
