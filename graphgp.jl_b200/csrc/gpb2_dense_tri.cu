@@ -521,6 +521,7 @@ __device__ __forceinline__ void cta_gemm64(T* out, int ldo, const T* X, int ldx,
     const int tr = (threadIdx.x >> 4) * 4, tc = (threadIdx.x & 15) * 4;
     if (tr >= rows || tc >= cols) return;
     T acc[4][4] = {};
+#pragma unroll 8
     for (int k = 0; k < K; k++) {
         T xv[4], yv[4];
 #pragma unroll
