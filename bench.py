@@ -448,12 +448,15 @@ def run_b200(args):
             with torch.cuda.stream(copy_s):
                 vals_d.copy_(vals_p, non_blocking=True)
                 ev_t = copy_s.record_event()
+            comp.wait_event(ev_t)
+            prob.update_vals(vals_d).prefactor()
+            # The large uploads go after the table's and the ladder's small ones: copies in the
+            # same direction share the copy engine in issue order.
+            with torch.cuda.stream(copy_s):
                 x_d.copy_(xi_p, non_blocking=True)
                 ev_x = copy_s.record_event()
                 v_d.copy_(vb_p, non_blocking=True)
                 ev_v = copy_s.record_event()
-            comp.wait_event(ev_t)
-            prob.update_vals(vals_d).prefactor()
             comp.wait_event(ev_x)
             outs = []
             for name, fn in (("f", lambda: gp.generate(prob, x_d)),
