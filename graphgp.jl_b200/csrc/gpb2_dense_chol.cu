@@ -44,6 +44,17 @@ constexpr int kSpecMax = 4096;  // concurrent ladder up to this n0
 template <typename T>
 __host__ __device__ constexpr int chol_threads() { return 512; }
 
+// Per-slot data of one ladder launch, passed by value as kernel arguments (no host-to-device
+// copy per factorisation: such small copies would queue in the copy engine behind whatever
+// large transfers the caller has in flight).
+struct SlotOrder {
+    int v[16];  // ladder index of slot c
+};
+template <typename T>
+struct SlotJit {
+    T v[16];  // jitter added to slot c's diagonal
+};
+
 template <typename T>
 struct CholArgs {
     T* base;          // nc candidates, each n x n column-major (lower triangle)
@@ -55,7 +66,7 @@ struct CholArgs {
     int* done;        // done[c] = 1 once candidate c is fully factorised
     int* dflag;       // dflag[c]: last panel whose diagonal block candidate c has published
     int* err;         // error word: a bounded wait gave up
-    const int* order; // order[c]: ladder index of candidate slot c
+    int order[16];    // order[c]: ladder index of candidate slot c (a kernel argument)
     unsigned long long* trace;  // diagnostics (GPB2_TRACE_DENSE): phase timestamps, or NULL
 };
 
@@ -590,14 +601,14 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
 
 // After a launch: record the first candidate (in ladder order) that factorised, unless an
 // earlier launch already did.
-__global__ void k_ladder_mark(const int* __restrict__ done, const int* __restrict__ order, int nc,
+__global__ void k_ladder_mark(const int* __restrict__ done, SlotOrder order, int nc,
                               int* __restrict__ sel) {
     if (sel[0] >= 0) return;
     int best = -1;
     for (int c = 0; c < nc; c++)  // the smallest ladder index that factorised
-        if (done[c] && (best < 0 || order[c] < order[best])) best = c;
+        if (done[c] && (best < 0 || order.v[c] < order.v[best])) best = c;
     if (best >= 0) {
-        sel[0] = order[best];
+        sel[0] = order.v[best];
         sel[1] = best;
     }
 }
@@ -622,7 +633,7 @@ __global__ void k_ladder_pick(const T* __restrict__ base, const int* __restrict_
 // lower triangle is written: nothing downstream reads the upper one.
 template <typename T>
 __global__ void k_ladder_assemble(TableView<T> tv, const uint32_t* __restrict__ coords, int D,
-                                  int DS, T scale, int64_t n, const T* __restrict__ jit, int nc,
+                                  int DS, T scale, int64_t n, SlotJit<T> jit, int nc,
                                   T* __restrict__ base, const int* __restrict__ sel) {
     // A later launch of the ladder must not overwrite the slots once a candidate is selected.
     if (__ldcg(sel) >= 0) return;
@@ -636,7 +647,8 @@ __global__ void k_ladder_assemble(TableView<T> tv, const uint32_t* __restrict__ 
         for (int64_t i = j + threadIdx.x; i < n; i += blockDim.x) {
             if (i == j) {
                 for (int c = 0; c < nc; c++)
-                    base[c * nn + j * n + j] = jit[c] == T(0) ? diag : Num<T>::add(diag, jit[c]);
+                    base[c * nn + j * n + j] =
+                        jit.v[c] == T(0) ? diag : Num<T>::add(diag, jit.v[c]);
             } else {
                 long long sq = 0;
                 for (int d = 0; d < D; d++) {
@@ -712,7 +724,6 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
     int* fail = p->lad + kLadFail;
     int* done = p->lad + kLadDone;
     int* sel = p->lad + kLadSel;
-    T* djit = reinterpret_cast<T*>(p->lad + kLadInts);
     T* base = static_cast<T*>(p->Lcand);
     const size_t smem = table_smem_bytes<T>((int)p->nb, p->nkeys);
     GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_ladder_assemble<T>, smem));
@@ -742,10 +753,16 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
     for (int i = hint + 1; i < ncand_used; i++) order.push_back(i);
     std::vector<T> jit_slot(ncand_used);
     for (int i = 0; i < ncand_used; i++) jit_slot[i] = jit[order[i]];
-    GPB2_CUDA_TRY(cudaMemcpyAsync(djit, jit_slot.data(), sizeof(T) * ncand_used,
-                                  cudaMemcpyHostToDevice, s));
-    GPB2_CUDA_TRY(cudaMemcpyAsync(p->lad + kLadOrder, order.data(), sizeof(int) * ncand_used,
-                                  cudaMemcpyHostToDevice, s));
+    auto slot_jit = [&](int first, int nc) {
+        SlotJit<T> j{};
+        for (int c = 0; c < nc; c++) j.v[c] = jit_slot[first + c];
+        return j;
+    };
+    auto slot_order = [&](int first, int nc) {
+        SlotOrder o{};
+        for (int c = 0; c < nc; c++) o.v[c] = order[first + c];
+        return o;
+    };
     // Launches: one candidate each (sequential), or all at once (speculative) -- except that
     // with a hint the steps above it get a second launch, which does nothing (every CTA returns
     // at once) when the hint or a step below it succeeded: they would only have competed with
@@ -770,7 +787,7 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
                                   dim3((unsigned)std::min<int64_t>(n, 4 * 148)), dim3(256), smem,
                                   s, table_view<T>(p), (const uint32_t*)p->coords, (int)p->d,
                                   coord_stride((int)p->d), (T)p->scale, n,
-                                  (const T*)(djit + first), nc, base, (const int*)sel));
+                                  slot_jit(first, nc), nc, base, (const int*)sel));
         unsigned long long* trace = nullptr;
         const int npan = (int)((n + kB - 1) / kB);
         if (std::getenv("GPB2_TRACE_DENSE")) {
@@ -780,7 +797,9 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
             trace = static_cast<unsigned long long*>(p->trace);
         }
         CholArgs<T> args{base,  n,    nc,   first, fail, sel, done, p->lad + kLadDflag,
-                         p->lad + kLadBarErr, p->lad + kLadOrder + first, trace};
+                         p->lad + kLadBarErr, {}, trace};
+        const SlotOrder so = slot_order(first, nc);
+        for (int c = 0; c < 16; c++) args.order[c] = so.v[c];
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)(nc * csize));
         cfg.blockDim = dim3(chol_threads<T>());
@@ -797,7 +816,7 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
         prof_end(t, s);
         GPB2_CUDA_TRY(e);
         GPB2_CUDA_TRY(launch_prof("dense_mark", k_ladder_mark, dim3(1), dim3(1), 0, s,
-                                  (const int*)done, (const int*)(p->lad + kLadOrder + first), nc,
+                                  (const int*)done, so, nc,
                                   sel));
         if (trace) {  // diagnostics: per-phase totals of the last candidate of this launch
             std::vector<unsigned long long> h(8 * (size_t)npan + 3 * 16);
