@@ -12,7 +12,8 @@
 //    sequential; here it is the equivalent blocked form S = L^-T Phi(L^T L-bar) L^-1 (Phi =
 //    lower triangle with halved diagonal), whose lower-triangle gradient is S_ij + S_ji off
 //    the diagonal and S_ii on it -- the same quantity the recurrence computes.
-//  * _dense_logdet_grad_vals (src/dense.jl:153-183): K^-1 from the factor (potri); cotangent
+//  * _dense_logdet_grad_vals (src/dense.jl:153-183): K^-1 = L^-T L^-1 (one SYRK of the inverse
+//    kept with the factor; potri when that inverse is not kept); cotangent
 //    K^-1[a,b] off-diagonal, K^-1[a,a]/2 on the diagonal.
 //  * _dense_inv_loss_grad_vals (src/dense.jl:244-266): alpha = K^-1 y; cotangent -alpha_a*alpha_b,
 //    -alpha_a^2/2 on the diagonal.
@@ -67,6 +68,16 @@ inline cublasStatus_t trsm(cublasHandle_t h, cublasSideMode_t side, cublasOperat
     return cublasDtrsm(h, side, CUBLAS_FILL_MODE_LOWER, op, CUBLAS_DIAG_NON_UNIT, n, n, &one, A,
                        n, B, n);
 }
+// Lower triangle of C = A^T A (A n x n column-major).
+inline cublasStatus_t syrk_tn(cublasHandle_t h, int n, const float* A, float* C) {
+    const float one = 1.0f, zero = 0.0f;
+    return cublasSsyrk(h, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_T, n, n, &one, A, n, &zero, C, n);
+}
+inline cublasStatus_t syrk_tn(cublasHandle_t h, int n, const double* A, double* C) {
+    const double one = 1.0, zero = 0.0;
+    return cublasDsyrk(h, CUBLAS_FILL_MODE_LOWER, CUBLAS_OP_T, n, n, &one, A, n, &zero, C, n);
+}
+
 inline cusolverStatus_t potri_ws(cusolverDnHandle_t h, int n, float* A, int* lw) {
     return cusolverDnSpotri_bufferSize(h, CUBLAS_FILL_MODE_LOWER, n, A, n, lw);
 }
@@ -353,6 +364,13 @@ template <typename T>
 int Dense<T>::logdet_grad(gpb2_problem* p, double* hist, cudaStream_t s) {
     const int n = (int)p->n0;
     T* W = static_cast<T*>(p->Wd);
+    if (p->tri_ready) {
+        // K^-1 = L^-T L^-1 from the inverse kept with the factor: one symmetric rank-n update
+        // (potri recomputes L^-1 and then forms the same product).
+        GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
+        GPB2_BLAS_TRY(syrk_tn(p->blas, n, static_cast<const T*>(p->Ainv), W));
+        return scatter<T>(p, 1, W, hist, s);
+    }
     GPB2_CUDA_TRY(cudaMemcpyAsync(W, p->Ld, sizeof(T) * (size_t)n * n, cudaMemcpyDeviceToDevice,
                                   s));
     GPB2_SOLVER_TRY(cusolverDnSetStream(p->solver, s));
