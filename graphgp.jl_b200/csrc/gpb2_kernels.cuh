@@ -242,8 +242,21 @@ __device__ __forceinline__ void flush_hist(double* __restrict__ gacc, const doub
 }
 
 // refine_logdet_and_grad_hist_kernel! (src/kernels_adjoint.jl:117-152), seed 1.
+// Block shape of the histogram kernels (k_logdet_grad, k_grad_vals, k_inv_loss_grad): 320 threads, two blocks per SM (20 warps, within both the register
+// file at <= 102 registers and shared memory), when the interpolation weights of 320 threads fit
+// in 72 KB; else the flat kernels' 128 threads.
 template <typename T, int K, int D>
-__global__ void __launch_bounds__(kFlatThreads)
+struct GradShape {
+    static constexpr int kWide = 320;
+    static constexpr bool kUse =
+        (size_t)PointMath<T, K, D>::NR * kWide * (sizeof(T) + sizeof(uint16_t)) <= 72 * 1024;
+    static constexpr int kThreads = kUse ? kWide : kFlatThreads;
+    static constexpr int kMinBlocks = kUse ? 2 : 1;
+    using Store = RadiusStore<T, K, D, kThreads, kUse ? 72 * 1024 : 36 * 1024>;
+};
+
+template <typename T, int K, int D>
+__global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld_acc,
               T* __restrict__ terms, int64_t M) {
     using N = Num<T>;
@@ -261,8 +274,8 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
     double s = 0.0;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
          m += (int64_t)gridDim.x * blockDim.x) {
-        PointFactor<T, K, D, true, typename RadiusStore<T, K, D>::type> f;
-        f.R = RadiusStore<T, K, D>::make(rbase);
+        PointFactor<T, K, D, true, typename GradShape<T, K, D>::Store::type> f;
+        f.R = GradShape<T, K, D>::Store::make(rbase);
         f.compute(a, tab, m);
         const T lkk = f.L[tri(K, K)];
         const T t = N::log(lkk);
@@ -290,18 +303,6 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
 // src/kernels_adjoint.jl:484-553), run over ALL points after the reverse sweep has finalised
 // vb: every point's cotangent seed (vb[p]*xi[p], vb[p]*v[nbr]) is then known, and the point's
 // pullback needs nothing else, so the batches need not be visited in order.
-// Block shape of k_grad_vals: 320 threads, two blocks per SM (20 warps, within both the register
-// file at <= 102 registers and shared memory), when the interpolation weights of 320 threads fit
-// in 72 KB; else the flat kernels' 128 threads.
-template <typename T, int K, int D>
-struct GradShape {
-    static constexpr int kWide = 320;
-    static constexpr bool kUse =
-        (size_t)PointMath<T, K, D>::NR * kWide * (sizeof(T) + sizeof(uint16_t)) <= 72 * 1024;
-    static constexpr int kThreads = kUse ? kWide : kFlatThreads;
-    static constexpr int kMinBlocks = kUse ? 2 : 1;
-    using Store = RadiusStore<T, K, D, kThreads, kUse ? 72 * 1024 : 36 * 1024>;
-};
 
 template <typename T, int K, int D>
 __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
@@ -358,7 +359,7 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
 // refine_inv_loss_grad_hist_kernel! (src/kernels_adjoint.jl:155-221): loss 0.5*sum(xi^2) and its
 // vals-gradient; the z-bar solve has no pivot guard, as in the reference.
 template <typename T, int K, int D>
-__global__ void __launch_bounds__(kFlatThreads)
+__global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict__ gacc,
                 double* __restrict__ loss_acc, T* __restrict__ xi_out, int64_t M) {
     using N = Num<T>;
@@ -376,8 +377,8 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
     double ls = 0.0;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
          m += (int64_t)gridDim.x * blockDim.x) {
-        PointFactor<T, K, D, true, typename RadiusStore<T, K, D>::type> f;
-        f.R = RadiusStore<T, K, D>::make(rbase);
+        PointFactor<T, K, D, true, typename GradShape<T, K, D>::Store::type> f;
+        f.R = GradShape<T, K, D>::Store::make(rbase);
         f.compute(a, tab, m);
         T x[K];
         PM::solve(x, f.L, a.tab.pivc);
@@ -768,8 +769,13 @@ struct Launch {
     }
     static cudaError_t logdet_grad(const PointArgs<T>& a, double* gacc, double* ld, T* terms,
                                    int64_t M, cudaStream_t s) {
-        return flat("logdet_grad", k_logdet_grad<T, K, D>, flat_smem(a, true) + RadiusStore<T, K, D>::bytes, M, s, a, gacc, ld,
-                    terms, M);
+        using G = GradShape<T, K, D>;
+        const size_t smem = flat_smem(a, true) + G::Store::bytes;
+        cudaError_t e = prepare_kernel_smem((const void*)k_logdet_grad<T, K, D>, smem);
+        if (e != cudaSuccess) return e;
+        const int grid = flat_grid((const void*)k_logdet_grad<T, K, D>, G::kThreads, smem, M);
+        return launch_prof("logdet_grad", k_logdet_grad<T, K, D>, dim3(grid), dim3(G::kThreads),
+                           smem, s, a, gacc, ld, terms, M);
     }
     static cudaError_t grad_vals(const PointArgs<T>& a, const T* v, const T* xih, const T* vb,
                                  const T* mv, double* gacc, int64_t M, cudaStream_t s) {
@@ -783,8 +789,13 @@ struct Launch {
     }
     static cudaError_t inv_loss_grad(const PointArgs<T>& a, const T* values, double* gacc,
                                      double* loss, T* xi_out, int64_t M, cudaStream_t s) {
-        return flat("inv_loss_grad", k_inv_loss_grad<T, K, D>, flat_smem(a, true) + RadiusStore<T, K, D>::bytes, M, s, a,
-                    values, gacc, loss, xi_out, M);
+        using G = GradShape<T, K, D>;
+        const size_t smem = flat_smem(a, true) + G::Store::bytes;
+        cudaError_t e = prepare_kernel_smem((const void*)k_inv_loss_grad<T, K, D>, smem);
+        if (e != cudaSuccess) return e;
+        const int grid = flat_grid((const void*)k_inv_loss_grad<T, K, D>, G::kThreads, smem, M);
+        return launch_prof("inv_loss_grad", k_inv_loss_grad<T, K, D>, dim3(grid),
+                           dim3(G::kThreads), smem, s, a, values, gacc, loss, xi_out, M);
     }
     static cudaError_t fused_fwd(const PointArgs<T>& a, T* values, const T* xi_ref, int64_t lo,
                                  int64_t hi, cudaStream_t s) {
