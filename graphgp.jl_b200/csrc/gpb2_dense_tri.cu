@@ -384,23 +384,6 @@ k_trsm_lt(const T* __restrict__ Lr, int64_t ld, const T* __restrict__ DinvT,
     __pipeline_wait_prior(0);
 }
 
-// A = L^-1 before the doubling: the inverses of the 32x32 diagonal blocks in place, zero
-// elsewhere (column-major n x n).
-template <typename T>
-__global__ void k_ainv_init(const T* __restrict__ DinvT, int64_t n, T* __restrict__ A) {
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n * n;
-         e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t col = e / n, row = e - col * n;
-        T v = T(0);
-        if (row / kTB == col / kTB && row >= col) {
-            const int64_t b = row / kTB;
-            const int i = (int)(row - b * kTB), j = (int)(col - b * kTB);
-            v = DinvT[b * kTB * kTB + j * kTB + i];  // DinvT[b][j][i] = (L_bb^-1)[i][j]
-        }
-        A[e] = v;
-    }
-}
-
 // F = D_u A and H = T' D_xi A (column-major n x n): one warp per column b, a warp scan down the
 // rows: H[c][b] = sum_{b <= k < c} xi_k A[k][b] + xi_c A[c][b] / 2 (zero above the diagonal).
 template <typename T>
@@ -593,7 +576,7 @@ __global__ void __launch_bounds__(256) k_inv_block(const T* __restrict__ L,
     }
     for (int e = threadIdx.x; e < kIB * kIB; e += blockDim.x) {
         const int i = e % kIB, j = e / kIB;
-        if (i < m && j < m && i >= j) A[(g0 + i) + (g0 + j) * n] = M[i * kIBP + j];
+        if (i < m && j < m) A[(g0 + i) + (g0 + j) * n] = M[i * kIBP + j];  // zeros above
     }
 }
 
@@ -601,10 +584,10 @@ template <typename T>
 int build_inverse(gpb2_problem* p, T* A, T* W, cudaStream_t s) {
     const int64_t n = p->n0;
     const T* L = static_cast<const T*>(p->Ld);
-    GPB2_CUDA_TRY(launch_prof("dense_ainv_init", k_ainv_init<T>,
-                              dim3((unsigned)std::min<int64_t>((n * n + 255) / 256, 8 * 148)),
-                              dim3(256), 0, s, (const T*)p->Dinv, n, A));
-    // Levels 32 and 64 inside each 128-wide diagonal block, then library GEMMs from 128 up.
+    // A's upper triangle is zero from its allocation and nothing writes there: k_inv_block
+    // writes the whole 128-wide diagonal blocks (zeros above their diagonal included) and the
+    // GEMMs below write only blocks below the diagonal.  Levels 32 and 64 inside each
+    // 128-wide diagonal block, then library GEMMs from 128 up.
     const size_t ism = inv_block_smem<T>();
     GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_inv_block<T>, ism));
     GPB2_CUDA_TRY(launch_prof("dense_inv_block", k_inv_block<T>,
@@ -655,7 +638,10 @@ int dense_tri_prepare(gpb2_problem* p, cudaStream_t s) {
     GPB2_TRY(ensure_alloc(&p->Ldr, sizeof(T) * (size_t)n * (size_t)ld));
     GPB2_TRY(ensure_alloc(&p->Dinv, sizeof(T) * (size_t)nbk * kTB * kTB));
     GPB2_TRY(ensure_alloc(&p->Wtri, sizeof(T) * (2 * nn + (size_t)n)));
-    GPB2_TRY(ensure_alloc(&p->Ainv, sizeof(T) * nn));
+    if (!p->Ainv) {
+        GPB2_TRY(ensure_alloc(&p->Ainv, sizeof(T) * nn));
+        GPB2_CUDA_TRY(cudaMemsetAsync(p->Ainv, 0, sizeof(T) * nn, s));  // upper triangle: zero
+    }
     GPB2_CUDA_TRY(launch_prof("dense_transpose", k_transpose_lower<T>,
                               dim3((unsigned)std::min<int64_t>(nbk * nbk, 4 * 148)),
                               dim3(kTriThreads), 0, s, (const T*)p->Ld, (T*)p->Ldr, n, ld));
