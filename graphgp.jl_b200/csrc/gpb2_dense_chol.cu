@@ -748,9 +748,19 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
     // order.
     std::vector<int> order;
     order.reserve(ncand_used);
-    const int hint = spec && p->ladder_hint >= 0 && p->ladder_hint < ncand_used ? p->ladder_hint : 0;
-    for (int i = hint; i >= 0; i--) order.push_back(i);
-    for (int i = hint + 1; i < ncand_used; i++) order.push_back(i);
+    const bool hinted = spec && p->ladder_hint >= 0 && p->ladder_hint < ncand_used;
+    const int hint = hinted ? p->ladder_hint : 0;
+    if (spec && !hinted) {
+        // No hint yet: step 0 first (a well-conditioned block needs no jitter, and its success
+        // supersedes every other candidate), then the largest steps down, so that whichever
+        // step succeeds is among the resident clusters while the small ones, which fail early,
+        // wait for a slot.
+        order.push_back(0);
+        for (int i = ncand_used - 1; i >= 1; i--) order.push_back(i);
+    } else {
+        for (int i = hint; i >= 0; i--) order.push_back(i);
+        for (int i = hint + 1; i < ncand_used; i++) order.push_back(i);
+    }
     std::vector<T> jit_slot(ncand_used);
     for (int i = 0; i < ncand_used; i++) jit_slot[i] = jit[order[i]];
     auto slot_jit = [&](int first, int nc) {
@@ -770,7 +780,7 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
     std::vector<std::pair<int, int>> launches;  // (first slot, candidates)
     if (!spec) {
         for (int f = 0; f < ncand_used; f++) launches.push_back({f, 1});
-    } else if (p->ladder_hint >= 0 && hint + 1 < ncand_used) {
+    } else if (hinted && hint + 1 < ncand_used) {
         launches.push_back({0, hint + 1});
         launches.push_back({hint + 1, ncand_used - hint - 1});
     } else {
