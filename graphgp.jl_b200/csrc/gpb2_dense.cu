@@ -68,6 +68,18 @@ inline cublasStatus_t trsm(cublasHandle_t h, cublasSideMode_t side, cublasOperat
     return cublasDtrsm(h, side, CUBLAS_FILL_MODE_LOWER, op, CUBLAS_DIAG_NON_UNIT, n, n, &one, A,
                        n, B, n);
 }
+// y = op(A) x (A n x n column-major).
+inline cublasStatus_t gemv(cublasHandle_t h, cublasOperation_t op, int n, const float* A,
+                           const float* x, float* y) {
+    const float one = 1.0f, zero = 0.0f;
+    return cublasSgemv(h, op, n, n, &one, A, n, x, 1, &zero, y, 1);
+}
+inline cublasStatus_t gemv(cublasHandle_t h, cublasOperation_t op, int n, const double* A,
+                           const double* x, double* y) {
+    const double one = 1.0, zero = 0.0;
+    return cublasDgemv(h, op, n, n, &one, A, n, x, 1, &zero, y, 1);
+}
+
 // Lower triangle of C = A^T A (A n x n column-major).
 inline cublasStatus_t syrk_tn(cublasHandle_t h, int n, const float* A, float* C) {
     const float one = 1.0f, zero = 0.0f;
@@ -384,6 +396,17 @@ int Dense<T>::inv_loss_grad(gpb2_problem* p, const T* y, double* hist, double* l
                             cudaStream_t s) {
     const int n = (int)p->n0;
     T* z = static_cast<T*>(p->Wd);
+    if (p->tri_ready) {
+        // z = L^-1 y and alpha = L^-T z as two products with the inverse kept with the factor
+        // (two matrix-vector products instead of two triangular solves, each a dependent chain).
+        T* alpha = z + n;
+        GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
+        GPB2_BLAS_TRY(gemv(p->blas, CUBLAS_OP_N, n, static_cast<const T*>(p->Ainv), y, z));
+        GPB2_CUDA_TRY(launch_prof("dense_sumsq", k_sum_sq_half<T>, dim3(1), dim3(kDenseThreads),
+                                  0, s, (const T*)z, (int64_t)n, loss));
+        GPB2_BLAS_TRY(gemv(p->blas, CUBLAS_OP_T, n, static_cast<const T*>(p->Ainv), z, alpha));
+        return scatter<T>(p, 2, alpha, hist, s);
+    }
     GPB2_TRY(solve_L(p, y, z, s));  // z = L \ y  (generate_dense_inv)
     GPB2_CUDA_TRY(launch_prof("dense_sumsq", k_sum_sq_half<T>, dim3(1), dim3(kDenseThreads), 0, s,
                               (const T*)z, (int64_t)n, loss));
