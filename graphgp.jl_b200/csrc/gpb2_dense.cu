@@ -335,6 +335,11 @@ int Dense<T>::apply_Lt(gpb2_problem* p, const T* x, T* y, cudaStream_t s) {
 
 template <typename T>
 int Dense<T>::solve_L(gpb2_problem* p, const T* b, T* y, cudaStream_t s) {
+    if (p->tri_ready && b != y) {  // y = L^-1 b with the inverse kept with the factor
+        GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
+        GPB2_BLAS_TRY(gemv(p->blas, CUBLAS_OP_N, (int)p->n0, static_cast<const T*>(p->Ainv), b, y));
+        return GPB2_OK;
+    }
     if (b != y)
         GPB2_CUDA_TRY(cudaMemcpyAsync(y, b, sizeof(T) * p->n0, cudaMemcpyDeviceToDevice, s));
     GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
