@@ -285,19 +285,50 @@ int ensure_dense(gpb2_problem* p) {
 }
 
 template <typename T>
-int Dense<T>::factor(gpb2_problem* p, cudaStream_t s) {
+int Dense<T>::factor(gpb2_problem* p, cudaStream_t s, bool defer_tri) {
     // The factor depends only on the coordinates (fixed) and the covariance table: a checked
     // factor of the current table is reused (the table setter clears the flag).
     if (p->dense_valid || p->dense_launched) return GPB2_OK;  // (a prefactor launched it)
     GPB2_TRY(ensure_dense(p));
     p->tri_ready = false;
+    p->tri_pending = false;
+    p->tri_deferred = false;
     GPB2_TRY(dense_cholesky_ladder<T>(p, s));  // gpb2_dense_chol.cu
     if (dense_tri_supported<T>(p)) {
-        GPB2_TRY(dense_tri_prepare<T>(p, s));   // gpb2_dense_tri.cu
-        p->tri_ready = true;
+        p->tri_deferred = true;
+        if (!defer_tri) return finish_tri(p, s);
     }
     return GPB2_OK;
 }
+
+// The row-major copy, the diagonal-block inverses and L^-1 of a factor queued on s (the
+// ladder's stream).  When s is the dense stream the readers of these buffers order themselves
+// after ev_tri or ev_inv (wait_tri), so the preparation runs beside the caller's next kernels.
+template <typename T>
+int Dense<T>::finish_tri(gpb2_problem* p, cudaStream_t s) {
+    if (!p->tri_deferred) return GPB2_OK;
+    p->tri_deferred = false;
+    const bool queued = s == p->dstream && p->ev_tri;
+    GPB2_TRY(dense_tri_prepare<T>(p, s, queued ? p->ev_tri : nullptr));  // gpb2_dense_tri.cu
+    p->tri_ready = true;
+    if (queued) {
+        GPB2_CUDA_TRY(cudaEventRecord(p->ev_inv, s));
+        p->tri_pending = true;
+    }
+    return GPB2_OK;
+}
+
+namespace {
+
+// Orders s after the part of a triangular preparation still queued on the dense stream that
+// it reads: the row-major copy alone (inverse = false) or L^-1 as well.
+int wait_tri(gpb2_problem* p, cudaStream_t s, bool inverse) {
+    if (p->tri_pending && s != p->dstream)
+        GPB2_CUDA_TRY(cudaStreamWaitEvent(s, inverse ? p->ev_inv : p->ev_tri, 0));
+    return GPB2_OK;
+}
+
+}  // namespace
 
 template <typename T>
 int Dense<T>::apply_L(gpb2_problem* p, const T* x, T* y, cudaStream_t s) {
@@ -319,6 +350,7 @@ int Dense<T>::apply_L(gpb2_problem* p, const T* x, T* y, cudaStream_t s) {
 template <typename T>
 int Dense<T>::apply_Lt(gpb2_problem* p, const T* x, T* y, cudaStream_t s) {
     if (p->tri_ready) {
+        GPB2_TRY(wait_tri(p, s, false));  // reads the row-major copy
         if (x == y) {
             GPB2_CUDA_TRY(cudaMemcpyAsync(p->Wd2, x, sizeof(T) * p->n0, cudaMemcpyDeviceToDevice,
                                           s));
@@ -336,6 +368,7 @@ int Dense<T>::apply_Lt(gpb2_problem* p, const T* x, T* y, cudaStream_t s) {
 template <typename T>
 int Dense<T>::solve_L(gpb2_problem* p, const T* b, T* y, cudaStream_t s) {
     if (p->tri_ready && b != y) {  // y = L^-1 b with the inverse kept with the factor
+        GPB2_TRY(wait_tri(p, s, true));
         GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
         GPB2_BLAS_TRY(gemv(p->blas, CUBLAS_OP_N, (int)p->n0, static_cast<const T*>(p->Ainv), b, y));
         return GPB2_OK;
@@ -362,6 +395,7 @@ int Dense<T>::grad_vals(gpb2_problem* p, const T* vb, const T* xi, double* hist,
     T* X = static_cast<T*>(p->Wd2);
     const T* L = static_cast<const T*>(p->Ld);
     if (p->tri_ready) {  // S = L^-T Phi(tril((L^T vb) xi^T)) L^-1 by the triangular kernels
+        GPB2_TRY(wait_tri(p, s, true));
         const T* S = nullptr;
         GPB2_TRY(dense_chol_pullback_outer<T>(p, vb, xi, &S, s));
         return scatter<T>(p, 0, S, hist, s);
@@ -384,6 +418,7 @@ int Dense<T>::logdet_grad(gpb2_problem* p, double* hist, cudaStream_t s) {
     if (p->tri_ready) {
         // K^-1 = L^-T L^-1 from the inverse kept with the factor: one symmetric rank-n update
         // (potri recomputes L^-1 and then forms the same product).
+        GPB2_TRY(wait_tri(p, s, true));
         GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
         GPB2_BLAS_TRY(syrk_tn(p->blas, n, static_cast<const T*>(p->Ainv), W));
         return scatter<T>(p, 1, W, hist, s);
@@ -404,6 +439,7 @@ int Dense<T>::inv_loss_grad(gpb2_problem* p, const T* y, double* hist, double* l
     if (p->tri_ready) {
         // z = L^-1 y and alpha = L^-T z as two products with the inverse kept with the factor
         // (two matrix-vector products instead of two triangular solves, each a dependent chain).
+        GPB2_TRY(wait_tri(p, s, true));
         T* alpha = z + n;
         GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
         GPB2_BLAS_TRY(gemv(p->blas, CUBLAS_OP_N, n, static_cast<const T*>(p->Ainv), y, z));

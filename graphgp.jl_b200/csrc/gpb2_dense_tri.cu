@@ -631,7 +631,7 @@ bool dense_tri_supported(const gpb2_problem* p) {
 }
 
 template <typename T>
-int dense_tri_prepare(gpb2_problem* p, cudaStream_t s) {
+int dense_tri_prepare(gpb2_problem* p, cudaStream_t s, cudaEvent_t after_ldr) {
     const int64_t n = p->n0, ld = tri_pitch(n);
     const int64_t nbk = (n + kTB - 1) / kTB;
     const size_t nn = (size_t)n * (size_t)n;
@@ -645,6 +645,7 @@ int dense_tri_prepare(gpb2_problem* p, cudaStream_t s) {
     GPB2_CUDA_TRY(launch_prof("dense_transpose", k_transpose_lower<T>,
                               dim3((unsigned)std::min<int64_t>(nbk * nbk, 4 * 148)),
                               dim3(kTriThreads), 0, s, (const T*)p->Ld, (T*)p->Ldr, n, ld));
+    if (after_ldr) GPB2_CUDA_TRY(cudaEventRecord(after_ldr, s));
     GPB2_CUDA_TRY(launch_prof("dense_diag_inv", k_diag_inv<T>,
                               dim3((unsigned)((nbk + kDiagWarps - 1) / kDiagWarps)),
                               dim3(32 * kDiagWarps), 0, s, (const T*)p->Ldr, n, ld,
@@ -694,8 +695,8 @@ int dense_chol_pullback_outer(gpb2_problem* p, const T* vb, const T* xi, const T
 
 template bool dense_tri_supported<float>(const gpb2_problem*);
 template bool dense_tri_supported<double>(const gpb2_problem*);
-template int dense_tri_prepare<float>(gpb2_problem*, cudaStream_t);
-template int dense_tri_prepare<double>(gpb2_problem*, cudaStream_t);
+template int dense_tri_prepare<float>(gpb2_problem*, cudaStream_t, cudaEvent_t);
+template int dense_tri_prepare<double>(gpb2_problem*, cudaStream_t, cudaEvent_t);
 template int dense_trmv<float>(gpb2_problem*, bool, const float*, float*, cudaStream_t);
 template int dense_trmv<double>(gpb2_problem*, bool, const double*, double*, cudaStream_t);
 template int dense_chol_pullback_outer<float>(gpb2_problem*, const float*, const float*,

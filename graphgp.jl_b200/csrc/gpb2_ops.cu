@@ -90,6 +90,8 @@ static int ensure_dense_stream(gpb2_problem* p) {
     GPB2_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
     GPB2_CUDA_TRY(cudaEventCreateWithFlags(&p->ev_fork, cudaEventDisableTiming));
     GPB2_CUDA_TRY(cudaEventCreateWithFlags(&p->ev_join, cudaEventDisableTiming));
+    GPB2_CUDA_TRY(cudaEventCreateWithFlags(&p->ev_tri, cudaEventDisableTiming));
+    GPB2_CUDA_TRY(cudaEventCreateWithFlags(&p->ev_inv, cudaEventDisableTiming));
     GPB2_CUDA_TRY(cudaStreamCreateWithPriority(&p->dstream, cudaStreamNonBlocking, greatest));
     return GPB2_OK;
 }
@@ -145,16 +147,19 @@ struct Impl {
         GPB2_TRY(ensure_dense_stream(p));
         GPB2_CUDA_TRY(cudaEventRecord(p->ev_fork, s));
         GPB2_CUDA_TRY(cudaStreamWaitEvent(p->dstream, p->ev_fork, 0));
-        const int sd = Dense<T>::factor(p, p->dstream);
+        const int sd = Dense<T>::factor(p, p->dstream, true);
         const int sf = sd == GPB2_OK ? factor_all(p, s) : GPB2_OK;
-        // The join is recorded whatever happened, so nothing of this call outlives the stream.
+        // The join is recorded whatever happened, so no kernel of the ladder outlives the stream.
         const cudaError_t e1 = cudaEventRecord(p->ev_join, p->dstream);
         const cudaError_t e2 = cudaStreamWaitEvent(s, p->ev_join, 0);
         GPB2_TRY(sd);
         GPB2_TRY(sf);
         GPB2_CUDA_TRY(e1);
         GPB2_CUDA_TRY(e2);
-        return GPB2_OK;
+        // The triangular preparation needs only the factor and is queued after the join: it
+        // runs beside the caller's next kernels (a forward sweep needs only the factor), and its
+        // readers, and the call's final status read, wait for it.
+        return Dense<T>::finish_tri(p, p->dstream);
     }
 
     // values[0:n0] preset; fills values[n0:N] batch by batch.
@@ -494,6 +499,10 @@ static int finish_call(gpb2_problem* p, cudaStream_t s) {
     // Status words land in pinned host memory: the copies queue behind the call's kernels and
     // one synchronisation waits for all of them (copies to pageable memory would each wait).
     if (!p->hstat) GPB2_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&p->hstat), 4 * sizeof(int)));
+    // Nothing the call queued on the dense stream outlives it: the status reads below (and the
+    // synchronisation) come after the triangular preparation.
+    const bool tri = p->tri_pending;
+    if (tri) GPB2_CUDA_TRY(cudaStreamWaitEvent(s, p->ev_inv, 0));
     int* h = p->hstat;
     h[0] = 0;
     h[1] = 0;
@@ -510,6 +519,7 @@ static int finish_call(gpb2_problem* p, cudaStream_t s) {
             cudaMemcpyAsync(&h[3], p->lad + kLadSel, sizeof(int), cudaMemcpyDeviceToHost, s));
     }
     GPB2_CUDA_TRY(cudaStreamSynchronize(s));
+    if (tri) p->tri_pending = false;
     p->dense_pending = false;
     if (dense) {
         p->dense_valid = h[0] == 0 && h[1] == 0 && h[2] == 0;

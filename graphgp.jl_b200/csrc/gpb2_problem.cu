@@ -233,6 +233,8 @@ static void free_problem(gpb2_problem* p) {
     if (p->hscal) cudaFreeHost(p->hscal);
     if (p->ev_fork) cudaEventDestroy(p->ev_fork);
     if (p->ev_join) cudaEventDestroy(p->ev_join);
+    if (p->ev_tri) cudaEventDestroy(p->ev_tri);
+    if (p->ev_inv) cudaEventDestroy(p->ev_inv);
     if (p->dstream) cudaStreamDestroy(p->dstream);
     delete p;
 }

@@ -62,6 +62,8 @@ struct gpb2_problem {
     void* Wtri = nullptr;     // 2 n0^2 + n0 T: the triangular kernels' work
     void* Ainv = nullptr;     // (n0, n0) column-major L^-1 of the current factor
     bool tri_ready = false;   // Ldr / Dinv belong to the current Ld
+    bool tri_deferred = false;  // the ladder is queued and Ldr / Dinv / Ainv are not yet
+    bool tri_pending = false;   // Ldr / Dinv / Ainv are queued on dstream up to ev_tri
     void* Wd = nullptr;       // (n0, n0) work
     void* Wd2 = nullptr;      // (n0, n0) work
     void* dwork = nullptr;    // cuSOLVER workspace
@@ -72,6 +74,8 @@ struct gpb2_problem {
     cudaStream_t dstream = nullptr;   // high-priority stream of the overlapped dense factor
     cudaEvent_t ev_fork = nullptr;    // call stream -> dstream
     cudaEvent_t ev_join = nullptr;    // dstream -> call stream
+    cudaEvent_t ev_tri = nullptr;     // Ldr written (triangular preparation on dstream)
+    cudaEvent_t ev_inv = nullptr;     // Dinv and Ainv written (end of the preparation)
     double dense_jitter = 0.0;  // eps of the ladder that succeeded on the last factorisation
     int ladder_hint = -1;       // ladder index that succeeded last time (-1: none yet)
 
@@ -156,7 +160,8 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s);
 template <typename T>
 bool dense_tri_supported(const gpb2_problem* p);
 template <typename T>
-int dense_tri_prepare(gpb2_problem* p, cudaStream_t s);  // Ldr + Dinv from Ld
+// Ldr + Dinv + Ainv from Ld; after_ldr (if any) is recorded once Ldr is written.
+int dense_tri_prepare(gpb2_problem* p, cudaStream_t s, cudaEvent_t after_ldr = nullptr);
 template <typename T>
 int dense_trmv(gpb2_problem* p, bool trans, const T* x, T* y, cudaStream_t s);
 template <typename T>
@@ -165,7 +170,9 @@ int dense_chol_pullback_outer(gpb2_problem* p, const T* vb, const T* xi, const T
 
 template <typename T>
 struct Dense {
-    static int factor(gpb2_problem* p, cudaStream_t s);
+    // defer_tri: queue only the ladder; finish_tri() then queues Ldr / Dinv / Ainv.
+    static int factor(gpb2_problem* p, cudaStream_t s, bool defer_tri = false);
+    static int finish_tri(gpb2_problem* p, cudaStream_t s);
     static int apply_L(gpb2_problem* p, const T* x, T* y, cudaStream_t s);   // y = L x
     static int apply_Lt(gpb2_problem* p, const T* x, T* y, cudaStream_t s);  // y = L^T x
     static int solve_L(gpb2_problem* p, const T* b, T* y, cudaStream_t s);   // y = L \ b
