@@ -340,6 +340,37 @@ def test_asynchronous_calls(cuda_device, dt, _async_mode):
 
 
 @pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_inverse_readers_right_after_prefactor(cuda_device, dt, _async_mode):
+    # The triangular preparation (row-major copy of L, L^-1) is queued on the dense stream
+    # after the prefactor's join; every reader queued straight after it (L^T x, products with
+    # L^-1, K^-1) must order itself after it: the results equal those of synchronous calls on
+    # a handle whose preparation had long finished.
+    prob, _ = _config_problem(3000, 2, 200, 8, dt, 23)
+    rng = np.random.default_rng(9)
+    v_h = rng.standard_normal(prob.npoints()).astype(dt)
+    vb_h = rng.standard_normal(prob.npoints()).astype(dt)
+    v = torch.from_numpy(v_h).to(prob.device)
+    vb = torch.from_numpy(vb_h).to(prob.device)
+    good = np.array(prob.vals, copy=True)
+    got = {}
+    for name, call in (("inv", lambda: gp.generate_inv(prob, v)),
+                       ("gxi", lambda: gp.generate_grad_xi(prob, vb)),
+                       ("ldg", lambda: gp.generate_logdet_grad_vals(prob)),
+                       ("ilg", lambda: gp.generate_inv_loss_grad_vals(prob, v)[1])):
+        prob.update_vals(good).prefactor()
+        got[name] = call()
+        prob.check()
+    gp.set_synchronous(True)
+    want = {"inv": gp.generate_inv(prob, v_h), "gxi": gp.generate_grad_xi(prob, vb_h),
+            "ldg": gp.generate_logdet_grad_vals(prob),
+            "ilg": gp.generate_inv_loss_grad_vals(prob, v_h)[1]}
+    assert np.array_equal(got["inv"].cpu().numpy(), want["inv"])
+    for k in ("gxi", "ldg", "ilg"):
+        g = got[k].cpu().numpy() if hasattr(got[k], "cpu") else got[k]
+        assert relerr(g, want[k]) < TOL[dt], k
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
 def test_grad_vals_repeated_and_after_refactor(cuda_device, dt):
     # Repeated vals-gradients on one handle, before and after the table is re-set (which
     # refactors the dense block and the per-point factors), must agree with each other and with
