@@ -208,10 +208,22 @@ static int load_table(gpb2_problem* p, const void* vals_dev, cudaStream_t s) {
     p->dense_launched = false;
     p->factor_valid = false;  // and so do the per-point mean_vec / std
     GPB2_CUDA_TRY(cudaMemcpyAsync(p->vals, vals_dev, ts * p->nb, cudaMemcpyDeviceToDevice, s));
-    std::vector<unsigned char> hb(ts * p->nb), hv(ts * p->nb);
-    GPB2_CUDA_TRY(cudaMemcpyAsync(hb.data(), p->bins, ts * p->nb, cudaMemcpyDeviceToHost, s));
-    GPB2_CUDA_TRY(cudaMemcpyAsync(hv.data(), p->vals, ts * p->nb, cudaMemcpyDeviceToHost, s));
-    GPB2_CUDA_TRY(cudaStreamSynchronize(s));
+    // The bins do not change after creation: they are read back once, the values every time.
+    const bool first = p->hbins.size() != ts * p->nb;
+    if (first) p->hbins.assign(ts * p->nb, 0);
+    std::vector<unsigned char> hv(ts * p->nb);
+    const std::vector<unsigned char>& hb = p->hbins;
+    if (first && cudaMemcpyAsync(p->hbins.data(), p->bins, ts * p->nb, cudaMemcpyDeviceToHost,
+                                 s) != cudaSuccess) {
+        p->hbins.clear();
+        GPB2_CUDA_TRY(cudaGetLastError());
+        return set_error(GPB2_ERR_CUDA, "reading the bins back failed");
+    }
+    const cudaError_t e1 = cudaMemcpyAsync(hv.data(), p->vals, ts * p->nb, cudaMemcpyDeviceToHost, s);
+    const cudaError_t e2 = cudaStreamSynchronize(s);
+    if (first && (e1 != cudaSuccess || e2 != cudaSuccess)) p->hbins.clear();  // read again next time
+    GPB2_CUDA_TRY(e1);
+    GPB2_CUDA_TRY(e2);
     if (p->dtype == GPB2_F32)
         return build_table<float>(p, reinterpret_cast<const float*>(hb.data()),
                                   reinterpret_cast<const float*>(hv.data()), s);

@@ -46,6 +46,7 @@ struct gpb2_problem {
     void* Ld = nullptr;       // (n0, n0) column-major lower: the selected ladder candidate
     void* Lcand = nullptr;    // ladder candidates, each (n0, n0) column-major lower
     int* lad = nullptr;       // ladder status (layout: kLad* in gpb2::) + jitters
+    std::vector<unsigned char> hbins;  // host copy of the bins (fixed for the handle's life)
     std::vector<double> ladder_eps;  // eps of each ladder index of the last factorisation
     void* trace = nullptr;           // diagnostics buffer (GPB2_TRACE_DENSE)
     size_t lcand_bytes = 0;          // capacity of Lcand (its candidate count can change per call)
