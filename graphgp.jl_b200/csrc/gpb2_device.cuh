@@ -11,10 +11,10 @@
 // contracted into an FMA and each point's result is the same bit pattern the scalar restatement
 // produces.  Operation order follows:
 //   cov_lookup / cov_lookup_weights     src/interp.jl:10-34, 62-83
-//   assemble_cov!                       src/linalg.jl:98-112
-//   chol_lower!                         src/linalg.jl:121-156
-//   mean_vec_solve!                     src/linalg.jl:168-186
-//   chol_pullback!                      src/linalg.jl:195-217
+//   assemble_cov!                       src/linalg.jl:15-29
+//   chol_lower!                         src/linalg.jl:38-73
+//   mean_vec_solve!                     src/linalg.jl:85-103
+//   chol_pullback!                      src/linalg.jl:112-134
 //
 // Interpolation table.  The reference finds the bracketing bin with a binary search (about
 // log2(nbins) dependent loads per covariance entry).  Here the table is staged in shared memory
@@ -352,7 +352,7 @@ struct PointMath {
         return N::mul(N::sqrt(N::from_i64((long long)sq)), scale);
     }
 
-    // assemble_cov! (src/linalg.jl:98-112).  With KEEP_R the radius of pair (a, b), b < a, is
+    // assemble_cov! (src/linalg.jl:15-29).  With KEEP_R the radius of pair (a, b), b < a, is
     // kept in R[tri(a-1, b)] for the adjoint's scatter -- or, with a weight store, its
     // interpolation segment and fraction.
     template <bool KEEP_R, typename RT>
@@ -381,7 +381,7 @@ struct PointMath {
         });
     }
 
-    // chol_lower! (src/linalg.jl:121-156).  A degenerate column (s <= eps*A11, or NaN) gets
+    // chol_lower! (src/linalg.jl:38-73).  A degenerate column (s <= eps*A11, or NaN) gets
     // the diagonal sqrt(eps*A11) and a zeroed column; selects keep the thread branch-free.
     static __device__ __forceinline__ void chol(T (&L)[NT]) {
         const T pivmin = N::mul(N::eps(), L[0]);
@@ -407,7 +407,7 @@ struct PointMath {
         });
     }
 
-    // mean_vec_solve! (src/linalg.jl:168-186): L[0:K,0:K]^T x = L[K,0:K], weight zeroed where
+    // mean_vec_solve! (src/linalg.jl:85-103): L[0:K,0:K]^T x = L[K,0:K], weight zeroed where
     // the pivot sits at the clamp floor.
     static __device__ __forceinline__ void solve(T (&x)[K], const T (&L)[NT], T pivc) {
         const T pivfloor = N::mul(pivc, L[0]);
@@ -467,7 +467,7 @@ struct PointMath {
         });
     }
 
-    // chol_pullback! (src/linalg.jl:195-217), in place: on entry B holds L-bar (lower), on
+    // chol_pullback! (src/linalg.jl:112-134), in place: on entry B holds L-bar (lower), on
     // exit B holds A-bar.  Each L-bar[i][j] is last read exactly where A-bar[i][j] is written,
     // so one array serves both.
     static __device__ __forceinline__ void pullback(T (&B)[NT], const T (&L)[NT],

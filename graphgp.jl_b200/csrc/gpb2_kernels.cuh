@@ -288,7 +288,7 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
         });
         T rp[PM::KP1];
         PM::pivot_recips(rp, f.L);
-        B[tri(K, K)] = rp[K];  // chol_logdet_pullback! seed 1/L[K][K] (src/linalg.jl:220-229)
+        B[tri(K, K)] = rp[K];  // chol_logdet_pullback! seed 1/L[K][K] (src/linalg.jl:137-146)
         PM::pullback(B, f.L, rp);
         scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
     }

@@ -68,7 +68,7 @@ def _call(fn: str, *args) -> None:
 # ---------------------------------------------------------------------------------------------
 
 def refine_(values, prob: GraphGPProblem, xi):
-    """``refine!`` (src/api.jl:364-392): fills values[n0:] in place; values is a CUDA tensor."""
+    """``refine!`` (src/api.jl:113-141): fills values[n0:] in place; values is a CUDA tensor."""
     if not isinstance(values, torch.Tensor) or not values.is_cuda or \
             values.dtype != prob.torch_dtype or not values.is_contiguous():
         raise TypeError("refine_ needs a contiguous CUDA tensor of the problem's dtype; "
@@ -79,7 +79,7 @@ def refine_(values, prob: GraphGPProblem, xi):
 
 
 def refine(prob: GraphGPProblem, initial_values, xi):
-    """``refine(prob, initial_values, xi)`` (src/api.jl:427-433): values (N), tree order."""
+    """``refine(prob, initial_values, xi)`` (src/api.jl:176-182): values (N), tree order."""
     iv, host = _vec(prob, initial_values, prob.n0, "initial_values")
     values = torch.zeros(prob.npoints(), dtype=prob.torch_dtype, device=prob.device)
     values[: prob.n0] = iv
@@ -88,14 +88,14 @@ def refine(prob: GraphGPProblem, initial_values, xi):
 
 
 def refine_inv_(xi_out, prob: GraphGPProblem, values):
-    """``refine_inv!`` (src/api.jl:317-343)."""
+    """``refine_inv!`` (src/api.jl:66-97)."""
     v, _ = _vec(prob, values, prob.npoints(), "values")
     _call("gpb2_refine_inv", prob.handle, _ptr(v), _ptr(xi_out), _stream(prob))
     return xi_out
 
 
 def refine_inv(prob: GraphGPProblem, values):
-    """``refine_inv(prob, values)`` (src/api.jl:350-354): xi of the refined points (M)."""
+    """``refine_inv(prob, values)`` (src/api.jl:99-103): xi of the refined points (M)."""
     v, host = _vec(prob, values, prob.npoints(), "values")
     xi = _empty(prob, prob.nrefined())
     _call("gpb2_refine_inv", prob.handle, _ptr(v), _ptr(xi), _stream(prob))
@@ -103,14 +103,14 @@ def refine_inv(prob: GraphGPProblem, values):
 
 
 def refine_logdet_terms(prob: GraphGPProblem):
-    """Per-point log(std) (src/api.jl:281-308)."""
+    """Per-point log(std) (src/api.jl:30-57)."""
     terms = _empty(prob, prob.nrefined())
     _call("gpb2_refine_logdet_terms", prob.handle, _ptr(terms), _stream(prob))
     return _ret(terms, prob.host_arrays)
 
 
 def refine_logdet(prob: GraphGPProblem) -> float:
-    """``refine_logdet`` (src/api.jl:275-278); the sum is accumulated in double."""
+    """``refine_logdet`` (src/api.jl:24-28); the sum is accumulated in double."""
     out = C.c_double()
     _call("gpb2_refine_logdet", prob.handle, C.byref(out), _stream(prob))
     return out.value
@@ -202,7 +202,7 @@ def generate_logdet_and_grad_vals(prob: GraphGPProblem):
 
 
 def refine_inv_loss_grad_vals(prob: GraphGPProblem, values):
-    """(0.5*||refine_inv||^2, its vals-gradient) (src/grad.jl:630-671); values in tree order."""
+    """(0.5*||refine_inv||^2, its vals-gradient) (src/grad.jl:643-678); values in tree order."""
     v, host = _vec(prob, values, prob.npoints(), "values")
     out = _empty(prob, prob.nbins())
     loss = C.c_double()

@@ -82,7 +82,7 @@ class GraphGPProblem:
         self._handle = None
         self._finalizer = None
 
-    # -- sizes (src/types.jl:372-376) ----------------------------------------------------------
+    # -- sizes (src/types.jl:72-76) ----------------------------------------------------------
     def npoints(self) -> int:
         return self._N
 

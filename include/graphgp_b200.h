@@ -141,13 +141,13 @@ int gpb2_problem_check(gpb2_problem* prob, void* stream);
  * ---------------------------------------------------------------------------------------- */
 
 /* refine!: values_dev[0:n0] preset, values_dev[n0:N] written; xi_ref_dev has M entries.
- * Replaces the per-batch refine_apply_fused_kernel! launches of src/api.jl:364-392. */
+ * Replaces the per-batch refine_apply_fused_kernel! launches of src/api.jl:113-141. */
 int gpb2_refine(gpb2_problem* prob, void* values_dev, const void* xi_ref_dev, void* stream);
 
 /* Ranges of one depth batch, the building blocks of a level-sharded sweep over several GPUs
  * (each rank runs its slice of a batch, the caller exchanges the batch between ranks; the
  * exchange replaces the reference's MPI/serial level loop, src/distributed.jl:293-322 and
- * src/api.jl:364-392).  [lo, hi) are tree-order point indices inside one batch (n0 <= lo).
+ * src/api.jl:113-141).  [lo, hi) are tree-order point indices inside one batch (n0 <= lo).
  * Asynchronous on `stream` (no synchronisation; launch errors are returned).
  *   refine_range:          values[p] = std_p*xi_ref[p-n0] + sum_j mv_pj*values[nbr_pj]
  *                          (refine_apply_fused_kernel!, src/kernels.jl:101-119)
@@ -163,14 +163,14 @@ int gpb2_refine_reverse_range(gpb2_problem* prob, void* xg_dev, void* vb_dev, in
  * block is factorised (with the jitter ladder) if the table changed.  Synchronous. */
 int gpb2_dense_apply(gpb2_problem* prob, int trans, const void* x_dev, void* y_dev, void* stream);
 
-/* refine_inv!: xi_ref_dev[m] = (values[n0+m] - mean) / std.  Replaces src/api.jl:317-343
+/* refine_inv!: xi_ref_dev[m] = (values[n0+m] - mean) / std.  Replaces src/api.jl:66-97
  * (refine_inv_kernel!, src/kernels.jl:37-56) and gpcuda_refine_inv_f32 (csrc/graphgp_capi.cu:90-99). */
 int gpb2_refine_inv(gpb2_problem* prob, const void* values_dev, void* xi_ref_dev, void* stream);
 
-/* refine_logdet_terms: terms_dev[m] = log(std_m).  Replaces src/api.jl:281-308. */
+/* refine_logdet_terms: terms_dev[m] = log(std_m).  Replaces src/api.jl:30-57. */
 int gpb2_refine_logdet_terms(gpb2_problem* prob, void* terms_dev, void* stream);
 
-/* refine_logdet: sum of the terms, accumulated in double.  Replaces src/api.jl:275-278 and
+/* refine_logdet: sum of the terms, accumulated in double.  Replaces src/api.jl:24-28 and
  * gpcuda_refine_logdet_f32 (csrc/graphgp_capi.cu:76-88).  Synchronous. */
 int gpb2_refine_logdet(gpb2_problem* prob, double* logdet_host, void* stream);
 
@@ -193,7 +193,7 @@ int gpb2_refine_logdet_grad_vals_noalloc(gpb2_problem* prob, void* dvals_dev,
                                          double* logdet_host, void* stream);
 
 /* refine_inv_loss_grad_vals: loss = 0.5*||refine_inv(values)||^2 and its vals-gradient.
- * Replaces src/grad.jl:630-671 (refine_inv_loss_grad_hist_kernel!, src/kernels_adjoint.jl:155-221). */
+ * Replaces src/grad.jl:643-678 (refine_inv_loss_grad_hist_kernel!, src/kernels_adjoint.jl:155-221). */
 int gpb2_refine_inv_loss_grad_vals(gpb2_problem* prob, const void* values_dev, void* dvals_dev,
                                    double* loss_host, void* stream);
 

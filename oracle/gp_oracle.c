@@ -14,18 +14,18 @@
  * Every routine follows a named reference function (paths are inside the GraphGP.jl tree):
  *   cov_lookup            src/interp.jl:10-34
  *   cov_lookup_weights    src/interp.jl:62-83
- *   assemble_cov          src/linalg.jl:98-112   (exact Int64 squared distances)
- *   chol_lower            src/linalg.jl:121-156  (pivot floor eps(T)*A11, zeroed column)
- *   mean_vec_solve        src/linalg.jl:168-186  (weight zeroed at 1.5*sqrt(eps)*L11)
- *   chol_pullback         src/linalg.jl:195-217
- *   refine (forward)      src/kernels.jl:101-119 + src/api.jl:364-392 + src/cpu_native.jl:205-231
- *   refine_inv            src/kernels.jl:37-56, src/cpu_native.jl:165-182
- *   refine_logdet_terms   src/kernels.jl:25-35, src/cpu_native.jl:152-163
+ *   assemble_cov          src/linalg.jl:15-29   (exact Int64 squared distances)
+ *   chol_lower            src/linalg.jl:38-73  (pivot floor eps(T)*A11, zeroed column)
+ *   mean_vec_solve        src/linalg.jl:85-103  (weight zeroed at 1.5*sqrt(eps)*L11)
+ *   chol_pullback         src/linalg.jl:112-134
+ *   refine (forward)      src/kernels.jl:101-119 + src/api.jl:113-141 + src/cpu_native.jl:86-112
+ *   refine_inv            src/kernels.jl:37-56, src/cpu_native.jl:46-63
+ *   refine_logdet_terms   src/kernels.jl:25-35, src/cpu_native.jl:33-44
  *   generate_grad_xi core src/grad.jl:392-465 (materialised mean_vec/std + serial reverse sweep)
  *   generate_grad_vals    src/grad_generate_vals.jl:44-101,111-213 and the device per-point
  *                         body src/kernels_adjoint.jl:484-553 (pivfloor guard in the z-bar solve)
  *   refine_logdet_grad    src/grad.jl:32-87 (privatised per-chunk histograms)
- *   refine_inv_loss_grad  src/grad.jl:530-620
+ *   refine_inv_loss_grad  src/grad.jl:533-641
  *   dense layer           src/dense.jl:15-67,112-183,227-266 and chol_pullback_dyn!
  *                         src/grad_generate_vals.jl:18-39
  *
@@ -96,7 +96,7 @@ static inline int64_t cov_lookup_weights(T r, const T* bins, int64_t n, T* wlo, 
 }
 
 /* Radius between two lattice points: exact Int64 squared distance, then T(sq), sqrt, * scale
- * (src/linalg.jl:101-107). */
+ * (src/linalg.jl:19-24). */
 static inline T lattice_radius(const uint32_t* a, const uint32_t* b, int D, T scale) {
     int64_t sq = 0;
     for (int d = 0; d < D; d++) {
@@ -115,7 +115,7 @@ static inline void gather_joint(uint32_t* jc, const uint32_t* coords, const int6
     for (int d = 0; d < D; d++) jc[K * D + d] = coords[fine * D + d];
 }
 
-/* src/linalg.jl:98-112.  A is KP1 x KP1 row-major; only the lower triangle is written. */
+/* src/linalg.jl:15-29.  A is KP1 x KP1 row-major; only the lower triangle is written. */
 static inline void assemble_cov(T* A, const uint32_t* jc, int KP1, int D, T scale,
                                 const T* bins, const T* vals, int64_t nb) {
     for (int a = 0; a < KP1; a++) {
@@ -127,8 +127,10 @@ static inline void assemble_cov(T* A, const uint32_t* jc, int KP1, int D, T scal
     }
 }
 
-/* src/linalg.jl:121-156.  Left-looking Cholesky with the relative pivot floor. */
-static inline void chol_lower(T* A, int KP1) {
+/* src/linalg.jl:38-73.  Left-looking Cholesky with the relative pivot floor.  Returns the
+ * number of clamped pivots (diagnostics only). */
+static inline int chol_lower(T* A, int KP1) {
+    int clamped = 0;
     T pivmin = T_EPS * A[0];
     for (int j = 0; j < KP1; j++) {
         T s = A[j * KP1 + j];
@@ -144,14 +146,16 @@ static inline void chol_lower(T* A, int KP1) {
         } else {
             A[j * KP1 + j] = SQRT_T(pivmin);
             for (int i = j + 1; i < KP1; i++) A[i * KP1 + j] = (T)0;
+            clamped++;
         }
     }
+    return clamped;
 }
 
-/* The constant 1.5*sqrt(eps(T)) of src/linalg.jl:171, evaluated in T left to right. */
+/* The constant 1.5*sqrt(eps(T)) of src/linalg.jl:88, evaluated in T left to right. */
 static inline T pivfloor_coeff(void) { return (T)1.5 * SQRT_T(T_EPS); }
 
-/* src/linalg.jl:168-186.  Back substitution L[0:K,0:K]^T x = L[K, 0:K]. */
+/* src/linalg.jl:85-103.  Back substitution L[0:K,0:K]^T x = L[K, 0:K]. */
 static inline void mean_vec_solve(T* x, const T* L, int K) {
     int KP1 = K + 1;
     T pivfloor = pivfloor_coeff() * L[0];
@@ -167,7 +171,7 @@ static inline void mean_vec_solve(T* x, const T* L, int K) {
     }
 }
 
-/* src/linalg.jl:195-217.  Reverse of chol_lower; Lbar consumed, Abar lower triangle. */
+/* src/linalg.jl:112-134.  Reverse of chol_lower; Lbar consumed, Abar lower triangle. */
 static void chol_pullback(T* Abar, T* Lbar, const T* L, int n) {
     for (int j = n - 1; j >= 0; j--) {
         T ljj = L[j * n + j];
@@ -256,8 +260,8 @@ int SFX(gpo_chol_solve)(T* A, int KP1, T* mv) {
     return 0;
 }
 
-/* Forward refine over the depth batches (src/api.jl:364-392 with the fused CPU body of
- * src/cpu_native.jl:205-231).  values[0:n0] preset; xi_ref indexed by m. */
+/* Forward refine over the depth batches (src/api.jl:113-141 with the fused CPU body of
+ * src/cpu_native.jl:86-112).  values[0:n0] preset; xi_ref indexed by m. */
 int SFX(gpo_refine)(T* values, const T* xi_ref, const uint32_t* coords, const int64_t* nbrs,
                     const int64_t* offsets, int64_t n_off, int64_t n0, int K, int D, T scale,
                     const T* bins, const T* vals, int64_t nb, int nthreads) {
@@ -283,7 +287,48 @@ int SFX(gpo_refine)(T* values, const T* xi_ref, const uint32_t* coords, const in
     return 0;
 }
 
-/* Materialised mean_vec (M,K) and std (M) (src/kernels.jl:61-78, cpu_native.jl:184-201). */
+/* Diagnostics of the near-singular regime (no reference counterpart): over the refined points,
+ * out[0] = points whose chol_lower clamped at least one pivot, out[1] = clamped pivots in all,
+ * out[2] = points sharing a lattice site with one of their neighbours (a collision),
+ * out[3] = neighbour weights zeroed by mean_vec_solve's pivot floor. */
+int SFX(gpo_clamp_stats)(int64_t* out, const uint32_t* coords, const int64_t* nbrs, int64_t M,
+                         int64_t n0, int K, int D, T scale, const T* bins, const T* vals,
+                         int64_t nb, int nthreads) {
+    if (K > KMAX || D > DMAX) return 2;
+    int nt = nthreads_of(nthreads);
+    int64_t pts = 0, piv = 0, col = 0, zw = 0;
+#pragma omp parallel num_threads(nt) reduction(+ : pts, piv, col, zw)
+    {
+        T A[(KMAX + 1) * (KMAX + 1)], mv[KMAX];
+        uint32_t jc[(KMAX + 1) * DMAX];
+#pragma omp for schedule(static)
+        for (int64_t m = 0; m < M; m++) {
+            const int KP1 = K + 1;
+            gather_joint(jc, coords, nbrs + m * K, K, D, n0 + m);
+            int hit = 0;
+            for (int j = 0; j < K && !hit; j++) {
+                int same = 1;
+                for (int d = 0; d < D; d++) same &= jc[j * D + d] == jc[K * D + d];
+                hit = same;
+            }
+            col += hit;
+            assemble_cov(A, jc, KP1, D, scale, bins, vals, nb);
+            const int c = chol_lower(A, KP1);
+            pts += c > 0;
+            piv += c;
+            mean_vec_solve(mv, A, K);
+            const T pivfloor = pivfloor_coeff() * A[0];
+            for (int i = 0; i < K; i++) zw += !(A[i * KP1 + i] > pivfloor);
+        }
+    }
+    out[0] = pts;
+    out[1] = piv;
+    out[2] = col;
+    out[3] = zw;
+    return 0;
+}
+
+/* Materialised mean_vec (M,K) and std (M) (src/kernels.jl:61-78, src/cpu_native.jl:65-84). */
 int SFX(gpo_meanvec_std)(T* mean_vec, T* stdv, const uint32_t* coords, const int64_t* nbrs,
                          int64_t M, int64_t n0, int K, int D, T scale, const T* bins,
                          const T* vals, int64_t nb, int nthreads) {
@@ -340,7 +385,7 @@ int SFX(gpo_refine_logdet_terms)(T* terms, const uint32_t* coords, const int64_t
     return 0;
 }
 
-/* Reverse depth-batch sweep of generate_grad_xi in tree order (src/grad.jl:426-445): on entry
+/* Reverse depth-batch sweep of generate_grad_xi in tree order (src/grad.jl:430-446): on entry
  * vb is the field cotangent (tree order); on exit xg[n0:N] = std*vb and vb[0:n0] holds the
  * cotangent reaching the dense block.  Serial, latest batch first, as in the reference. */
 int SFX(gpo_reverse_sweep)(T* xg, T* vb, const T* mean_vec, const T* stdv, const int64_t* nbrs,
@@ -471,7 +516,7 @@ int SFX(gpo_refine_logdet_grad_vals)(double* dv_out, double* logdet_out, const u
     return 0;
 }
 
-/* refine_inv_loss_grad_vals (src/grad.jl:530-620): loss = 0.5*sum(xi^2) and its vals-gradient.
+/* refine_inv_loss_grad_vals (src/grad.jl:533-641): loss = 0.5*sum(xi^2) and its vals-gradient.
  * Note the reference's inverse-loss z-bar solve has NO pivfloor guard (src/grad.jl:574-580). */
 int SFX(gpo_refine_inv_loss_grad_vals)(double* dv_out, double* loss_out, const T* values,
                                        const uint32_t* coords, const int64_t* nbrs, int64_t M,
@@ -537,9 +582,11 @@ int SFX(gpo_refine_inv_loss_grad_vals)(double* dv_out, double* loss_out, const T
 /* L3: dense first layer (src/dense.jl)                                                      */
 /* ---------------------------------------------------------------------------------------- */
 
-/* _assemble_dense_cov (src/dense.jl:15-40): full symmetric n x n, row-major. */
+/* _assemble_dense_cov (src/dense.jl:15-40): full symmetric n x n, row-major.  Entries are
+ * independent, so the columns are spread over the host threads. */
 int SFX(gpo_dense_cov)(T* K, const uint32_t* coords, int64_t n, int D, T scale, const T* bins,
                        const T* vals, int64_t nb) {
+#pragma omp parallel for schedule(dynamic, 16)
     for (int64_t j = 0; j < n; j++) {
         K[j * n + j] = cov_lookup((T)0, bins, vals, nb);
         for (int64_t i = j + 1; i < n; i++) {
@@ -552,25 +599,75 @@ int SFX(gpo_dense_cov)(T* K, const uint32_t* coords, int64_t n, int D, T scale, 
     return 0;
 }
 
-/* Plain unblocked Cholesky (lower, row-major); returns 0 on success, j+1 at the first
- * non-positive (or NaN) pivot like LAPACK potrf's info. */
+/* Left-looking Cholesky (lower, row-major); returns 0 on success, j+1 at the first
+ * non-positive (or NaN) pivot like LAPACK potrf's info.  Every entry receives exactly the
+ * subtractions of the unblocked recurrence
+ *     L[i][j] = (A[i][j] - L[i][0]L[j][0] - L[i][1]L[j][1] - ... - L[i][j-1]L[j][j-1]) / L[j][j]
+ * in that order (p ascending, each product rounded, then the subtraction rounded), so the factor
+ * does not depend on the blocking or the thread count.  Columns are taken in panels of PB: the
+ * products with the finished columns p < j0 are subtracted first for the whole panel (the panel's
+ * rows read once per row below it, from a transposed copy), then the panel is finished column by
+ * column (p = j0 .. j-1).  Rows are independent and spread over the host threads. */
+#define PB 32
 static int64_t dense_potrf(T* L, int64_t n) {
-    for (int64_t j = 0; j < n; j++) {
-        T s = L[j * n + j];
-        for (int64_t p = 0; p < j; p++) s -= L[j * n + p] * L[j * n + p];
-        if (!(s > (T)0)) return j + 1;
-        T d = SQRT_T(s);
-        L[j * n + j] = d;
-        for (int64_t i = j + 1; i < n; i++) {
-            T t = L[i * n + j];
-            for (int64_t p = 0; p < j; p++) t -= L[i * n + p] * L[j * n + p];
-            L[i * n + j] = t / d;
+    T* Wt = (T*)malloc(sizeof(T) * (size_t)PB * (size_t)(n > 0 ? n : 1));
+    if (!Wt) return -1;
+    for (int64_t j0 = 0; j0 < n; j0 += PB) {
+        const int64_t nb = (n - j0) < PB ? (n - j0) : PB;
+        /* Wt[p][jj] = L[j0+jj][p] for the finished columns p < j0. */
+        for (int64_t p = 0; p < j0; p++)
+            for (int64_t jj = 0; jj < nb; jj++) Wt[p * PB + jj] = L[(j0 + jj) * n + p];
+        /* Phase 1: subtract the products with columns p < j0 from every entry (i, j) of the
+         * panel, i >= j >= j0. */
+#pragma omp parallel for schedule(static) if ((n - j0) * j0 > 65536)
+        for (int64_t i = j0; i < n; i++) {
+            T t[PB];
+            T* Li = L + i * n;
+            const int64_t w = (i - j0 + 1) < nb ? (i - j0 + 1) : nb;
+            for (int64_t jj = 0; jj < w; jj++) t[jj] = Li[j0 + jj];
+            for (int64_t p = 0; p < j0; p++) {
+                const T lip = Li[p];
+                const T* wp = Wt + p * PB;
+                for (int64_t jj = 0; jj < w; jj++) t[jj] -= lip * wp[jj];
+            }
+            for (int64_t jj = 0; jj < w; jj++) Li[j0 + jj] = t[jj];
+        }
+        /* Phase 2a: the diagonal block, column by column (p = j0 .. j-1). */
+        for (int64_t j = j0; j < j0 + nb; j++) {
+            T* Lj = L + j * n;
+            T s = Lj[j];
+            for (int64_t p = j0; p < j; p++) s -= Lj[p] * Lj[p];
+            if (!(s > (T)0)) {
+                free(Wt);
+                return j + 1;
+            }
+            const T d = SQRT_T(s);
+            Lj[j] = d;
+            for (int64_t i = j + 1; i < j0 + nb; i++) {
+                T* Li = L + i * n;
+                T t = Li[j];
+                for (int64_t p = j0; p < j; p++) t -= Li[p] * Lj[p];
+                Li[j] = t / d;
+            }
+        }
+        /* Phase 2b: the rows below the block, each finishing the panel's columns in order. */
+#pragma omp parallel for schedule(static) if ((n - j0 - nb) * nb > 4096)
+        for (int64_t i = j0 + nb; i < n; i++) {
+            T* Li = L + i * n;
+            for (int64_t j = j0; j < j0 + nb; j++) {
+                const T* Lj = L + j * n;
+                T t = Li[j];
+                for (int64_t p = j0; p < j; p++) t -= Li[p] * Lj[p];
+                Li[j] = t / Lj[j];
+            }
         }
     }
+    free(Wt);
     for (int64_t i = 0; i < n; i++)
         for (int64_t j = i + 1; j < n; j++) L[i * n + j] = (T)0;
     return 0;
 }
+#undef PB
 
 /* _dense_chol_L (src/dense.jl:46-67): factor, else retry with K + eps*mean(diag) for
  * eps = 1e-9, 1e-8, ..., 1e-2 (the sequence evaluated in T).  Returns 0, or 1 when even 1e-2
@@ -656,6 +753,35 @@ int SFX(gpo_dense_grad_vals)(double* dv, const T* L, const T* vb, const T* xi,
     }
     free(Lbar);
     free(Kbar);
+    return 0;
+}
+
+/* Scatter a dense cotangent given in double (G, n x n row-major: G[i][j], i > j, the pair's
+ * cotangent; G[i][i] the diagonal's) into dv through cov_lookup_weights of each pair's radius
+ * (the histogram step of src/grad_generate_vals.jl:252-280 and src/dense.jl:153-183).  Used by
+ * the blocked dense pullback of oracle.py for large first layers; rows are spread over the host
+ * threads, each with a private histogram. */
+int SFX(gpo_dense_scatter)(double* dv, const double* G, const uint32_t* coords, int64_t n, int D,
+                           T scale, const T* bins, int64_t nb) {
+#pragma omp parallel
+    {
+        double* h = (double*)calloc((size_t)nb, sizeof(double));
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t i = 0; i < n; i++) {
+            h[0] += G[i * n + i];
+            for (int64_t j = 0; j < i; j++) {
+                T r = lattice_radius(coords + i * D, coords + j * D, D, scale);
+                T wlo, whi;
+                int64_t lo = cov_lookup_weights(r, bins, nb, &wlo, &whi);
+                const double g = G[i * n + j];
+                h[lo] += g * (double)wlo;
+                h[lo + 1] += g * (double)whi;
+            }
+        }
+#pragma omp critical
+        for (int64_t b = 0; b < nb; b++) dv[b] += h[b];
+        free(h);
+    }
     return 0;
 }
 

@@ -122,7 +122,7 @@ def cov_lookup_weights(r, bins):
 
 
 def chol_solve(A, K):
-    """chol_lower! + mean_vec_solve! (src/linalg.jl:121-186) on one (K+1)x(K+1) matrix."""
+    """chol_lower! + mean_vec_solve! (src/linalg.jl:38-103) on one (K+1)x(K+1) matrix."""
     A = np.ascontiguousarray(A).copy()
     mv = np.empty(K, A.dtype)
     _fn("gpo_chol_solve", A.dtype)(_p(A), I32(K + 1), _p(mv))
@@ -134,7 +134,7 @@ def chol_solve(A, K):
 # ---------------------------------------------------------------------------------------------
 
 def refine(p, initial_values, xi_ref, nthreads=0):
-    """refine(prob, initial_values, xi) (src/api.jl:427-433)."""
+    """refine(prob, initial_values, xi) (src/api.jl:176-182)."""
     N, D, M, K = _dims(p)
     values = np.zeros(N, p.dtype)
     values[: p.n0] = initial_values
@@ -156,7 +156,7 @@ def meanvec_std(p, nthreads=0):
 
 
 def refine_inv(p, values, nthreads=0):
-    """refine_inv (src/api.jl:317-354)."""
+    """refine_inv (src/api.jl:66-103)."""
     N, D, M, K = _dims(p)
     values = np.ascontiguousarray(values, dtype=p.dtype)
     xi = np.empty(M, p.dtype)
@@ -176,7 +176,7 @@ def refine_logdet_terms(p, nthreads=0):
 
 
 def refine_logdet(p, nthreads=0):
-    """refine_logdet (src/api.jl:275-278); the sum is taken in float64."""
+    """refine_logdet (src/api.jl:24-28); the sum is taken in float64."""
     return float(np.sum(refine_logdet_terms(p, nthreads).astype(np.float64)))
 
 
@@ -195,7 +195,7 @@ def refine_logdet_grad_vals(p, nthreads=0, acc_t=False):
 
 
 def refine_inv_loss_grad_vals(p, values, nthreads=0, acc_t=False):
-    """refine_inv_loss_grad_vals (src/grad.jl:630-671): (loss, dvals float64)."""
+    """refine_inv_loss_grad_vals (src/grad.jl:643-678): (loss, dvals float64)."""
     N, D, M, K = _dims(p)
     values = np.ascontiguousarray(values, dtype=p.dtype)
     dv = np.zeros(len(p.bins), np.float64)
@@ -221,7 +221,18 @@ def dense_cov(p, n=None):
 
 
 def dense_chol(p):
-    """_dense_chol_L (src/dense.jl:46-67) -> (L, jitter_used)."""
+    """_dense_chol_L (src/dense.jl:46-67) -> (L, jitter_used).  The factor is kept on the
+    problem object for its table (a large first layer takes minutes on the host)."""
+    key = hash(p.vals.tobytes())
+    cached = getattr(p, "_dense_cache", None)
+    if cached is not None and cached[0] == key:
+        return cached[1], cached[2]
+    L, jit = _dense_chol(p)
+    p._dense_cache = (key, L, jit)
+    return L, jit
+
+
+def _dense_chol(p):
     Km = dense_cov(p)
     n = Km.shape[0]
     L = np.empty_like(Km)
@@ -342,9 +353,40 @@ def generate_grad_vals(p, xi, vbar, nthreads=0, acc_t=False):
     assert rc == 0
     vbd = np.ascontiguousarray(vb[: p.n0])
     xid = np.ascontiguousarray(xih[: p.n0])
+    if p.n0 > DENSE_BLOCKED_MIN:
+        dense_grad_vals_blocked(p, L, vbd, xid, dv)
+        return dv
     _fn("gpo_dense_grad_vals", p.dtype)(_p(dv), _p(L), _p(vbd), _p(xid), _p(p.coords),
                                         I64(p.n0), I32(D), _ct(p.dtype)(p.scale), _p(p.bins),
                                         I64(len(p.bins)), I32(1 if acc_t else 0))
+    return dv
+
+
+# First layers larger than this take the blocked dense pullback (the scalar recurrence is
+# O(n0^3) on one thread, and on the host slow in the subnormal range a short correlation
+# length drives the factor into).
+DENSE_BLOCKED_MIN = 2048
+
+
+def dense_grad_vals_blocked(p, L, vb, xi, dv):
+    """Dense block of generate_grad_vals (src/grad_generate_vals.jl:252-280) for a large first
+    layer, in float64: with Lbar = tril(vb xi^T), the pullback of chol_pullback_dyn!
+    (src/grad_generate_vals.jl:18-39) is the lower triangle of S = L^-T Phi(L^T Lbar) L^-1
+    (Phi: lower triangle, halved diagonal); the pair cotangent is S_ij + S_ji off the diagonal and
+    S_ii on it.  Accumulated into dv (float64, nbins)."""
+    from scipy.linalg import solve_triangular
+    N, D, M, K = _dims(p)
+    Lf = np.tril(np.asarray(L, np.float64))
+    X = Lf.T @ np.tril(np.outer(np.asarray(vb, np.float64), np.asarray(xi, np.float64)))
+    X = np.tril(X)
+    X[np.diag_indices_from(X)] *= 0.5
+    Y = solve_triangular(Lf, X, trans="T", lower=True)        # L^-T Phi
+    S = solve_triangular(Lf, Y.T, trans="T", lower=True).T    # (L^-T Phi) L^-1
+    G = np.tril(S, -1) + np.triu(S, 1).T
+    G[np.diag_indices_from(G)] = np.diag(S)
+    G = np.ascontiguousarray(G)
+    _fn("gpo_dense_scatter", p.dtype)(_p(dv), _p(G), _p(p.coords), I64(p.n0), I32(D),
+                                      _ct(p.dtype)(p.scale), _p(p.bins), I64(len(p.bins)))
     return dv
 
 
@@ -363,3 +405,107 @@ def generate_logdet_grad_vals(p, nthreads=0, acc_t=False):
     """generate_logdet_grad_vals (src/grad.jl:149-154)."""
     _, dv = refine_logdet_grad_vals(p, nthreads, acc_t)
     return dv + dense_logdet_grad_vals(p, acc_t)
+
+
+# ---------------------------------------------------------------------------------------------
+# Inputs: graph build and covariance tables, without the product library
+# ---------------------------------------------------------------------------------------------
+
+_GRAPH_PATH = os.path.join(_HERE, "libgp_graph.so")
+_glib = None
+
+
+def _graph_lib():
+    global _glib
+    if _glib is None:
+        if not os.path.exists(_GRAPH_PATH):
+            build()
+        g = C.CDLL(_GRAPH_PATH)
+        g.gpb2_build_graph.restype = I32
+        g.gpb2_build_graph.argtypes = [P, I64, I64, I64, I64, I64, I64, I64, C.POINTER(P)]
+        g.gpb2_graph_n_offsets.restype = I64
+        g.gpb2_graph_n_offsets.argtypes = [P]
+        g.gpb2_graph_n0.restype = I64
+        g.gpb2_graph_n0.argtypes = [P]
+        g.gpb2_graph_export.restype = I32
+        g.gpb2_graph_export.argtypes = [P, P, P, P, P, C.POINTER(C.c_double)]
+        g.gpb2_graph_free.restype = None
+        g.gpb2_graph_free.argtypes = [P]
+        g.gpo_graph_last_error.restype = C.c_char_p
+        _glib = g
+    return _glib
+
+
+def build_graph(points, n0, k, lattice_bits=21, nthreads=0):
+    """build_graph (src/graph_build.jl:256-288) on the host cores, through the oracle's own
+    copy of the host builder (libgp_graph.so): returns dict(coords (N,D) uint32, neighbors
+    (M,K) int64 0-based, offsets, n0, scale, indices 0-based tree->original)."""
+    pts = np.asfortranarray(np.asarray(points, dtype=np.float64))
+    N, D = pts.shape
+    L = _graph_lib()
+    g = P()
+    st = L.gpb2_build_graph(pts.ctypes.data_as(P), N, D, 1, int(n0), int(k), int(lattice_bits),
+                            int(nthreads), C.byref(g))
+    if st != 0:
+        raise RuntimeError(f"build_graph failed ({st}): {L.gpo_graph_last_error().decode()}")
+    try:
+        n_off = L.gpb2_graph_n_offsets(g)
+        n0f = L.gpb2_graph_n0(g)
+        coords = np.empty((N, D), np.uint32)
+        nbrs = np.empty((N - n0f, k), np.int64)
+        indices = np.empty(N, np.int64)
+        offsets = np.empty(n_off, np.int64)
+        scale = C.c_double()
+        L.gpb2_graph_export(g, coords.ctypes.data_as(P), nbrs.ctypes.data_as(P),
+                            indices.ctypes.data_as(P), offsets.ctypes.data_as(P), C.byref(scale))
+    finally:
+        L.gpb2_graph_free(g)
+    return dict(coords=coords, neighbors=nbrs, offsets=offsets, n0=int(n0f), scale=scale.value,
+                indices=indices)
+
+
+def make_cov_bins(r_min, r_max, n_bins):
+    """make_cov_bins (src/extras.jl:14-17): [0; 10 .^ range(log10 r_min, log10 r_max, n-1)]."""
+    import math
+    inner = 10.0 ** np.linspace(math.log10(float(r_min)), math.log10(float(r_max)), n_bins - 1)
+    return np.concatenate([[0.0], inner])
+
+
+def rbf_kernel(variance, scale, r_min, r_max, n_bins, jitter=0.0, dtype=np.float64):
+    """rbf_kernel (src/extras.jl:26-38): variance*exp(-r^2/(2 scale^2)), vals[0] *= 1+jitter."""
+    bins = make_cov_bins(r_min, r_max, n_bins)
+    r = bins.astype(dtype)
+    v = (np.asarray(variance, dtype) * np.exp(np.asarray(-0.5, dtype) * (r / np.asarray(scale, dtype)) ** 2)).astype(dtype)
+    v[0] = v[0] * (1 + np.asarray(jitter, dtype))
+    return bins, v
+
+
+def matern_kernel(p, variance, cutoff, r_min, r_max, n_bins, jitter=0.0, dtype=np.float64):
+    """matern_kernel (src/extras.jl:57-73), nu = p + 1/2: variance*exp(-x)*polyval(c, 2x) with
+    x = sqrt(2p+1) r / cutoff and c_i = exp(lgamma(p+1) + lgamma(p+i+1) - lgamma(i+1)
+    - lgamma(p-i+1) - lgamma(2p+1))."""
+    import math
+    bins = make_cov_bins(r_min, r_max, n_bins)
+    c = [math.exp(math.lgamma(p + 1.0) + math.lgamma(p + i + 1.0) - math.lgamma(i + 1.0)
+                  - math.lgamma(p - i + 1.0) - math.lgamma(2 * p + 1.0)) for i in range(p + 1)]
+    r = bins.astype(dtype)
+    x = dtype(math.sqrt(float(2 * p + 1))) * r / np.asarray(cutoff, dtype)
+    z = 2 * x
+    acc = np.full_like(z, c[0])
+    for ci in c[1:]:
+        acc = acc * z + dtype(ci)
+    v = (np.asarray(variance, dtype) * np.exp(-x) * acc).astype(dtype)
+    v[0] = v[0] * (1 + np.asarray(jitter, dtype))
+    return bins, v
+
+
+def clamp_stats(p, nthreads=0):
+    """Near-singular diagnostics over the refined points: dict(points_clamped, pivots_clamped,
+    collisions, weights_zeroed) (see gpo_clamp_stats in gp_oracle.c)."""
+    N, D, M, K = _dims(p)
+    out = np.zeros(4, np.int64)
+    _fn("gpo_clamp_stats", p.dtype)(_p(out), _p(p.coords), _p(p.nbrs), I64(M), I64(p.n0), I32(K),
+                                    I32(D), _ct(p.dtype)(p.scale), _p(p.bins), _p(p.vals),
+                                    I64(len(p.bins)), I32(nthreads))
+    return dict(points_clamped=int(out[0]), pivots_clamped=int(out[1]), collisions=int(out[2]),
+                weights_zeroed=int(out[3]))

@@ -46,3 +46,29 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda", 0)
+
+
+# Parity figures recorded by the tests (config, operation, size, norm-relative error, max-abs
+# error, note) and printed at the end of the run, so that a run's log carries the measured
+# errors next to the pass/fail status.
+PARITY = []
+
+
+def report(config: str, op: str, n: int, a, b, note: str = "") -> float:
+    """Record the error of `a` against the reference values `b` and return the norm-relative
+    error."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    rel = relerr(a, b)
+    mx = float(np.max(np.abs(a - b))) if a.size else 0.0
+    PARITY.append((config, op, int(n), rel, mx, note))
+    return rel
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    if not PARITY:
+        return
+    tr = terminalreporter
+    tr.write_sep("-", "parity against the oracle (norm-relative error, max-abs error)")
+    for cfg, op, n, rel, mx, note in PARITY:
+        tr.write_line(f"{cfg:<14} {op:<26} n={n:<11} rel={rel:.2e} maxabs={mx:.2e} {note}")
