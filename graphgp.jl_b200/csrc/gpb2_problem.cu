@@ -109,6 +109,25 @@ __global__ void k_convert_nbrs(const IT* __restrict__ src, int base, int64_t M, 
     }
 }
 
+// Device-side permutation check and conversion to int32 0-based: every value in [0, N) exactly
+// once (a bitmap of seen values).
+template <typename IT>
+__global__ void k_convert_perm(const IT* __restrict__ src, int base, int64_t n,
+                               unsigned* __restrict__ seen, int* __restrict__ dst,
+                               unsigned long long* __restrict__ bad) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const long long v = (long long)src[i] - base;
+        bool ok = v >= 0 && v < n;
+        if (ok) {
+            const unsigned bit = 1u << (v & 31);
+            ok = (atomicOr(&seen[v >> 5], bit) & bit) == 0;
+        }
+        dst[i] = ok ? (int)v : 0;
+        if (!ok) atomicAdd(bad, 1ull);
+    }
+}
+
 // ------------------------------------------------------------------------------------------
 // Interpolation table (see gpb2_device.cuh).
 // ------------------------------------------------------------------------------------------
@@ -261,12 +280,13 @@ int gpb2_version(void) { return GPB2_VERSION; }
 
 const char* gpb2_last_error(void) { return g_last_error.c_str(); }
 
-int gpb2_problem_create(gpb2_problem** out, int dtype, int device, const uint32_t* coords_dev,
-                        int64_t d, int64_t n, const void* neighbors_dev, int neighbor_bytes,
-                        int neighbor_base, int64_t k, const int64_t* offsets_host,
-                        int64_t n_offsets, int64_t n0, double scale, const void* bins_dev,
-                        const void* vals_dev, int64_t nbins, const int64_t* indices_host,
-                        int indices_base, void* stream) {
+static int create_impl(gpb2_problem** out, int dtype, int device, const uint32_t* coords_dev,
+                       int64_t d, int64_t n, const void* neighbors_dev, int neighbor_bytes,
+                       int neighbor_base, int64_t k, const int64_t* offsets_host,
+                       int64_t n_offsets, int64_t n0, double scale, const void* bins_dev,
+                       const void* vals_dev, int64_t nbins, const int64_t* indices_host,
+                       const void* indices_dev, int indices_bytes, int indices_base,
+                       void* stream) {
     clear_error();
     if (!out) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_create: out is NULL");
     *out = nullptr;
@@ -377,7 +397,44 @@ int gpb2_problem_create(gpb2_problem** out, int dtype, int device, const uint32_
             break;
         }
         // Permutation.
-        if (indices_host) {
+        if (indices_dev) {
+            if (indices_bytes != 4 && indices_bytes != 8) {
+                st = set_error(GPB2_ERR_INVALID_ARG, "indices_bytes must be 4 or 8");
+                break;
+            }
+            unsigned* seen = nullptr;
+            unsigned long long* pbad = nullptr;
+            if ((st = ensure_alloc(reinterpret_cast<void**>(&p->indices), sizeof(int) * n))) break;
+            if ((st = ensure_alloc(reinterpret_cast<void**>(&seen), sizeof(unsigned) * ((n + 31) / 32))))
+                break;
+            if ((st = ensure_alloc(reinterpret_cast<void**>(&pbad), sizeof(unsigned long long)))) {
+                cudaFree(seen);
+                break;
+            }
+            cudaMemsetAsync(seen, 0, sizeof(unsigned) * ((n + 31) / 32), s);
+            cudaMemsetAsync(pbad, 0, sizeof(unsigned long long), s);
+            const unsigned gp = (unsigned)std::min<int64_t>((n + 255) / 256, 65535);
+            if (indices_bytes == 8)
+                k_convert_perm<long long><<<gp, 256, 0, s>>>((const long long*)indices_dev,
+                                                             indices_base, n, seen, p->indices, pbad);
+            else
+                k_convert_perm<int><<<gp, 256, 0, s>>>((const int*)indices_dev, indices_base, n,
+                                                       seen, p->indices, pbad);
+            unsigned long long hb = 0;
+            cudaMemcpyAsync(&hb, pbad, sizeof(hb), cudaMemcpyDeviceToHost, s);
+            const cudaError_t e = cudaStreamSynchronize(s);
+            cudaFree(seen);
+            cudaFree(pbad);
+            if (e != cudaSuccess) {
+                st = set_error(GPB2_ERR_CUDA, "indices upload failed: %s", cudaGetErrorString(e));
+                break;
+            }
+            if (hb != 0) {
+                st = set_error(GPB2_ERR_INVALID_ARG,
+                               "indices is not a permutation of 0..N-1 (%llu bad entries)", hb);
+                break;
+            }
+        } else if (indices_host) {
             std::vector<int> idx(n);
             std::vector<unsigned char> seen(n, 0);
             for (int64_t i = 0; i < n; i++) {
@@ -418,6 +475,28 @@ int gpb2_problem_create(gpb2_problem** out, int dtype, int device, const uint32_
     }
     *out = p;
     return GPB2_OK;
+}
+
+int gpb2_problem_create(gpb2_problem** out, int dtype, int device, const uint32_t* coords_dev,
+                        int64_t d, int64_t n, const void* neighbors_dev, int neighbor_bytes,
+                        int neighbor_base, int64_t k, const int64_t* offsets_host,
+                        int64_t n_offsets, int64_t n0, double scale, const void* bins_dev,
+                        const void* vals_dev, int64_t nbins, const int64_t* indices_host,
+                        int indices_base, void* stream) {
+    return create_impl(out, dtype, device, coords_dev, d, n, neighbors_dev, neighbor_bytes,
+                       neighbor_base, k, offsets_host, n_offsets, n0, scale, bins_dev, vals_dev,
+                       nbins, indices_host, nullptr, 0, indices_base, stream);
+}
+
+int gpb2_problem_create_dev(gpb2_problem** out, int dtype, int device, const uint32_t* coords_dev,
+                            int64_t d, int64_t n, const void* neighbors_dev, int neighbor_bytes,
+                            int neighbor_base, int64_t k, const int64_t* offsets_host,
+                            int64_t n_offsets, int64_t n0, double scale, const void* bins_dev,
+                            const void* vals_dev, int64_t nbins, const void* indices_dev,
+                            int indices_bytes, int indices_base, void* stream) {
+    return create_impl(out, dtype, device, coords_dev, d, n, neighbors_dev, neighbor_bytes,
+                       neighbor_base, k, offsets_host, n_offsets, n0, scale, bins_dev, vals_dev,
+                       nbins, nullptr, indices_dev, indices_bytes, indices_base, stream);
 }
 
 int gpb2_problem_set_vals(gpb2_problem* p, const void* vals_dev, void* stream) {

@@ -14,11 +14,12 @@ from .api import (check_graph, generate, generate_grad_vals, generate_grad_xi, g
                   refine_logdet_grad_vals_noalloc, refine_logdet_terms, set_synchronous)
 from .autodiff import generate_of_vals, generate_t, inv_quadratic_loss_of_vals, logdet_of_vals
 from .extras import hyperparam_grad, make_cov_bins, matern_kernel, rbf_kernel
-from .graph import build_graph, build_graph_arrays, cached_graph
+from .graph import build_graph, build_graph_arrays, build_graph_device, cached_graph
 from .problem import GraphGPProblem, set_vals, to_backend
 
 __all__ = [
     "GraphGPProblem", "to_backend", "set_vals", "build_graph", "build_graph_arrays",
+    "build_graph_device",
     "cached_graph", "check_graph", "generate", "generate_inv", "generate_logdet",
     "generate_grad_xi", "generate_grad_vals", "refine", "refine_", "refine_inv", "refine_inv_",
     "refine_logdet", "refine_logdet_terms", "refine_logdet_grad_vals",

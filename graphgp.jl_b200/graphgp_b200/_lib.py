@@ -78,6 +78,8 @@ _SIGNATURES = {
     "gpb2_last_error": (C.c_char_p, []),
     "gpb2_problem_create": (I32, [C.POINTER(P), I32, I32, P, I64, I64, P, I32, I32, I64, PI64,
                                   I64, I64, C.c_double, P, P, I64, PI64, I32, P]),
+    "gpb2_problem_create_dev": (I32, [C.POINTER(P), I32, I32, P, I64, I64, P, I32, I32, I64,
+                                      PI64, I64, I64, C.c_double, P, P, I64, P, I32, I32, P]),
     "gpb2_problem_set_vals": (I32, [P, P, P]),
     "gpb2_problem_prefactor": (I32, [P, P]),
     "gpb2_problem_info": (I32, [P, PI64, PI64, PI64, PI64, PI64]),
@@ -113,6 +115,11 @@ _SIGNATURES = {
     "gpb2_graph_n0": (I64, [P]),
     "gpb2_graph_export": (I32, [P, P, P, P, P, PD]),
     "gpb2_graph_free": (None, [P]),
+    "gpb2_build_graph_device": (I32, [P, I64, I64, I64, I64, I64, I64, I32, P, C.POINTER(P)]),
+    "gpb2_dgraph_n_offsets": (I64, [P]),
+    "gpb2_dgraph_n0": (I64, [P]),
+    "gpb2_dgraph_export": (I32, [P, P, P, P, PI64, PD, P]),
+    "gpb2_dgraph_free": (None, [P]),
 }
 
 _lib = None

@@ -8,7 +8,7 @@ generator when the points are produced on a GPU (``device="cuda"``, for the 1e8 
 configurations whose host generation would take minutes).  Both are deterministic.
 
 Every generator accepts ``n`` to draw a smaller cloud of the same distribution (the parity
-tests run the configurations' distributions at sizes the CPU oracle finishes quickly).
+tests run the configurations' distributions at sizes the host checker finishes quickly).
 
 C1  F64, N=1e4, D=2, N(0,1) (seed 99), n0=100,  k=10, RBF(1, 0.3, [1e-4, 10], 1000 bins)
 C2  F32, N=1e6, D=2, N(0,1) (seed 1),  n0=1000, k=8,  RBF(1, 0.3, [1e-4, 10], 1000 bins)

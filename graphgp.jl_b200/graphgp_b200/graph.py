@@ -50,6 +50,50 @@ def build_graph_arrays(points, n0: int, k: int, lattice_bits: int = 21, nthreads
                 indices=indices)
 
 
+def build_graph_device(points, n0: int, k: int, lattice_bits: int = 21, device=None):
+    """build_graph on the GPU (gpb2_build_graph_device): the same graph, byte for byte, as
+    ``build_graph_arrays``.  ``points`` is an (N, D) float64 torch tensor on the device (or a host
+    array, copied there).  Returns dict(coords (N, D) int32 tensor holding the uint32 lattice
+    coordinates, neighbors (M, K) int32 tensor 0-based, indices (N) int32 tensor 0-based
+    tree->original, offsets int64 numpy array, n0, scale), all tensors on the device."""
+    import torch
+    if isinstance(points, torch.Tensor):
+        dev = points.device if points.is_cuda else torch.device(
+            "cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
+    else:
+        dev = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+    pts = torch.as_tensor(points, dtype=torch.float64).to(dev).contiguous()
+    if pts.ndim != 2:
+        raise ValueError("points must be (N, D)")
+    N, D = pts.shape
+    L = _lib.lib()
+    g = C.c_void_p()
+    with torch.cuda.device(dev):
+        stream = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(L.gpb2_build_graph_device(C.c_void_p(pts.data_ptr()), N, D, 0, int(n0), int(k),
+                                             int(lattice_bits), dev.index or 0, stream,
+                                             C.byref(g)), "build_graph_device")
+        try:
+            n_off = L.gpb2_dgraph_n_offsets(g)
+            n0f = L.gpb2_dgraph_n0(g)
+            coords = torch.empty((N, D), dtype=torch.int32, device=dev)
+            nbrs = torch.empty((N - n0f, k), dtype=torch.int32, device=dev)
+            indices = torch.empty(N, dtype=torch.int32, device=dev)
+            offsets = np.empty(n_off, np.int64)
+            scale = C.c_double()
+            _lib.check(L.gpb2_dgraph_export(g, C.c_void_p(coords.data_ptr()),
+                                            C.c_void_p(nbrs.data_ptr()),
+                                            C.c_void_p(indices.data_ptr()),
+                                            offsets.ctypes.data_as(_lib.PI64), C.byref(scale),
+                                            stream), "graph export")
+            torch.cuda.current_stream(dev).synchronize()
+        finally:
+            L.gpb2_dgraph_free(g)
+    return dict(coords=coords, neighbors=nbrs, offsets=offsets, n0=int(n0f), scale=scale.value,
+                indices=indices)
+
+
 def build_graph(points, n0: int, k: int, bins, vals, lattice_bits: int = 21, nthreads: int = 0,
                 dtype=None, device=None) -> GraphGPProblem:
     """``build_graph(points, n0, k, bins, vals; lattice_bits=21)`` -> GraphGPProblem with the

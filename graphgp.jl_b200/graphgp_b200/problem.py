@@ -64,7 +64,10 @@ class GraphGPProblem:
         self.scale = float(scale)
         self.bins = bins
         self.vals = vals
-        self.indices = None if indices is None else _host(indices, np.int64)
+        # A permutation already on the device (a graph built by build_graph_device) stays there.
+        self.indices = None if indices is None else (
+            indices if isinstance(indices, torch.Tensor) and indices.is_cuda
+            else _host(indices, np.int64))
         self.neighbor_base = int(neighbor_base)
         if device is None:
             device = coords.device if isinstance(coords, torch.Tensor) and coords.is_cuda \
@@ -135,17 +138,27 @@ class GraphGPProblem:
             bins = self._dev(self.bins, self.torch_dtype)
             vals = self._dev(self.vals, self.torch_dtype)
             offs = np.ascontiguousarray(self.offsets, dtype=np.int64)
-            idx = None if self.indices is None else np.ascontiguousarray(self.indices, np.int64)
             stream = torch.cuda.current_stream(self.device).cuda_stream
             h = C.c_void_p()
-            st = L.gpb2_problem_create(
-                C.byref(h), _DT[self.dtype], self.device.index or 0,
-                C.c_void_p(coords.data_ptr()), self._D, self._N,
-                C.c_void_p(nbd.data_ptr()), 4 if nb_dt == torch.int32 else 8, self.neighbor_base,
-                self._K, offs.ctypes.data_as(_lib.PI64), len(offs), self.n0, self.scale,
-                C.c_void_p(bins.data_ptr()), C.c_void_p(vals.data_ptr()), self.nbins(),
-                None if idx is None else idx.ctypes.data_as(_lib.PI64), 0,
-                C.c_void_p(stream))
+            common = (C.byref(h), _DT[self.dtype], self.device.index or 0,
+                      C.c_void_p(coords.data_ptr()), self._D, self._N,
+                      C.c_void_p(nbd.data_ptr()), 4 if nb_dt == torch.int32 else 8,
+                      self.neighbor_base, self._K, offs.ctypes.data_as(_lib.PI64), len(offs),
+                      self.n0, self.scale, C.c_void_p(bins.data_ptr()),
+                      C.c_void_p(vals.data_ptr()), self.nbins())
+            if isinstance(self.indices, torch.Tensor):
+                idx = self.indices.to(self.device).contiguous()
+                if idx.dtype not in (torch.int32, torch.int64):
+                    raise TypeError("indices must be int32 or int64")
+                st = L.gpb2_problem_create_dev(*common, C.c_void_p(idx.data_ptr()),
+                                               4 if idx.dtype == torch.int32 else 8, 0,
+                                               C.c_void_p(stream))
+            else:
+                idx = None if self.indices is None else np.ascontiguousarray(self.indices,
+                                                                             np.int64)
+                st = L.gpb2_problem_create(*common,
+                                           None if idx is None else idx.ctypes.data_as(_lib.PI64),
+                                           0, C.c_void_p(stream))
             _lib.check(st, "GraphGPProblem upload")
         return h
 

@@ -74,6 +74,19 @@ int gpb2_problem_create(gpb2_problem** out, int dtype, int device,
                         double scale, const void* bins_dev, const void* vals_dev, int64_t nbins,
                         const int64_t* indices_host, int indices_base, void* stream);
 
+/* gpb2_problem_create with the permutation given on the device: indices_dev holds N int32
+ * (indices_bytes = 4) or int64 (8) values, base 0 or 1, checked on the device to be a
+ * permutation.  For graphs built on the device (gpb2_build_graph_device), whose arrays never
+ * pass through host memory; the reference's problems keep `indices` on the host
+ * (src/types.jl:22-60), which gpb2_problem_create covers. */
+int gpb2_problem_create_dev(gpb2_problem** out, int dtype, int device,
+                            const uint32_t* coords_dev, int64_t d, int64_t n,
+                            const void* neighbors_dev, int neighbor_bytes, int neighbor_base,
+                            int64_t k, const int64_t* offsets_host, int64_t n_offsets, int64_t n0,
+                            double scale, const void* bins_dev, const void* vals_dev,
+                            int64_t nbins, const void* indices_dev, int indices_bytes,
+                            int indices_base, void* stream);
+
 /* Replace the covariance values (`_set_vals`, src/chainrules.jl:18-21). */
 int gpb2_problem_set_vals(gpb2_problem* prob, const void* vals_dev, void* stream);
 
@@ -245,6 +258,25 @@ int64_t gpb2_graph_n0(const gpb2_graph* g);
 int gpb2_graph_export(const gpb2_graph* g, uint32_t* coords, int64_t* nbrs, int64_t* indices,
                       int64_t* offsets, double* scale);
 void gpb2_graph_free(gpb2_graph* g);
+
+/* build_graph on the device: the same graph, byte for byte, as gpb2_build_graph (and so as the
+ * reference's build_graph), built by sm_100a kernels from points already on `device`
+ * (points_dev: N x D float64, dim-major when points_dim_major != 0, else point-major), ordered
+ * on `stream`; the call waits for its work.  k <= 32, N < 2^31.  Replaces the reference's
+ * device builder gpcuda_build_graph_f32 (csrc/graphgp_capi.cu:100-117), which does not
+ * reproduce build_graph's output; this one does.  The arrays stay on the device:
+ * gpb2_dgraph_export copies coords (N*D uint32, point-major), nbrs (M*K int32, 0-based, -1 =
+ * unset), indices (N int32, 0-based tree->original) into caller buffers on the same device (any
+ * pointer may be NULL) and the offsets and scale to the host. */
+typedef struct gpb2_dgraph gpb2_dgraph;
+int gpb2_build_graph_device(const double* points_dev, int64_t n, int64_t d,
+                            int64_t points_dim_major, int64_t n0, int64_t k, int64_t lattice_bits,
+                            int device, void* stream, gpb2_dgraph** out);
+int64_t gpb2_dgraph_n_offsets(const gpb2_dgraph* g);
+int64_t gpb2_dgraph_n0(const gpb2_dgraph* g);
+int gpb2_dgraph_export(const gpb2_dgraph* g, uint32_t* coords_dev, int32_t* nbrs_dev,
+                       int32_t* indices_dev, int64_t* offsets_host, double* scale, void* stream);
+void gpb2_dgraph_free(gpb2_dgraph* g);
 
 #ifdef __cplusplus
 }
