@@ -129,6 +129,12 @@ struct PointFactor {
 // Flat kernels.
 // ---------------------------------------------------------------------------------------------
 
+// The flat kernels visit `cnt` refined points: m = m0 + t, or m = mlist[t] when a list is given
+// (the points a rank owns in a level-sharded operation: one chunk of every depth batch).
+__device__ __forceinline__ int64_t point_of(int64_t t, int64_t m0, const int* __restrict__ mlist) {
+    return mlist ? (int64_t)mlist[t] : m0 + t;
+}
+
 // Conditional-mean weights and std of points [m_begin, m_end) (refine_meanvec_std_kernel!,
 // src/kernels.jl:61-78): mv is (M, K) point-major, sd is (M).
 template <typename T, int K, int D>
@@ -152,14 +158,16 @@ k_factor(PointArgs<T> a, int64_t m_begin, int64_t m_end, T* __restrict__ mv, T* 
 // refine_inv_kernel! (src/kernels.jl:37-56).
 template <typename T, int K, int D>
 __global__ void __launch_bounds__(kFlatThreads)
-k_inv(PointArgs<T> a, const T* __restrict__ values, T* __restrict__ xi_out, int64_t M) {
+k_inv(PointArgs<T> a, const T* __restrict__ values, T* __restrict__ xi_out, int64_t m0,
+      int64_t cnt, const int* __restrict__ mlist) {
     using N = Num<T>;
     extern __shared__ __align__(16) unsigned char smem[];
     SmemTable<T> tab;
     tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
     __syncthreads();
-    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
-         m += (int64_t)gridDim.x * blockDim.x) {
+    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
+         it += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = point_of(it, m0, mlist);
         PointFactor<T, K, D, false> f;
         f.compute(a, tab, m);
         T x[K];
@@ -176,7 +184,8 @@ k_inv(PointArgs<T> a, const T* __restrict__ values, T* __restrict__ xi_out, int6
 // refine_logdet_kernel! (src/kernels.jl:25-35) + the sum, accumulated in double.
 template <typename T, int K, int D>
 __global__ void __launch_bounds__(kFlatThreads)
-k_logdet(PointArgs<T> a, T* __restrict__ terms, double* __restrict__ acc, int64_t M) {
+k_logdet(PointArgs<T> a, T* __restrict__ terms, double* __restrict__ acc, int64_t m0,
+         int64_t cnt, const int* __restrict__ mlist) {
     using N = Num<T>;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ double red[32];
@@ -184,8 +193,9 @@ k_logdet(PointArgs<T> a, T* __restrict__ terms, double* __restrict__ acc, int64_
     tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
     __syncthreads();
     double s = 0.0;
-    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
-         m += (int64_t)gridDim.x * blockDim.x) {
+    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
+         it += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = point_of(it, m0, mlist);
         PointFactor<T, K, D, false> f;
         f.compute(a, tab, m);
         const T t = N::log(f.L[tri(K, K)]);
@@ -258,7 +268,7 @@ struct GradShape {
 template <typename T, int K, int D>
 __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld_acc,
-              T* __restrict__ terms, int64_t M) {
+              T* __restrict__ terms, int64_t m0, int64_t cnt, const int* __restrict__ mlist) {
     using N = Num<T>;
     using PM = PointMath<T, K, D>;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -272,8 +282,9 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
     __syncthreads();
     double bin0 = 0.0;  // this thread's share of histogram bin 0
     double s = 0.0;
-    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
-         m += (int64_t)gridDim.x * blockDim.x) {
+    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
+         it += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = point_of(it, m0, mlist);
         PointFactor<T, K, D, true, typename GradShape<T, K, D>::Store::type> f;
         f.R = GradShape<T, K, D>::Store::make(rbase);
         f.compute(a, tab, m);
@@ -308,7 +319,7 @@ template <typename T, int K, int D>
 __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
             const T* __restrict__ vb, const T* __restrict__ mv, double* __restrict__ gacc,
-            int64_t M) {
+            int64_t m0, int64_t cnt, const int* __restrict__ mlist) {
     using N = Num<T>;
     using PM = PointMath<T, K, D>;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -320,8 +331,9 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
     double bin0 = 0.0;  // this thread's share of histogram bin 0
-    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
-         m += (int64_t)gridDim.x * blockDim.x) {
+    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
+         it += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = point_of(it, m0, mlist);
         const int64_t p = a.n0 + m;
         const T vbp = vb[p];
         PointFactor<T, K, D, true, typename GradShape<T, K, D>::Store::type> f;
@@ -361,7 +373,8 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
 template <typename T, int K, int D>
 __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict__ gacc,
-                double* __restrict__ loss_acc, T* __restrict__ xi_out, int64_t M) {
+                double* __restrict__ loss_acc, T* __restrict__ xi_out, int64_t m0, int64_t cnt,
+                const int* __restrict__ mlist) {
     using N = Num<T>;
     using PM = PointMath<T, K, D>;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -375,8 +388,9 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
     __syncthreads();
     double bin0 = 0.0;  // this thread's share of histogram bin 0
     double ls = 0.0;
-    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < M;
-         m += (int64_t)gridDim.x * blockDim.x) {
+    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
+         it += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = point_of(it, m0, mlist);
         PointFactor<T, K, D, true, typename GradShape<T, K, D>::Store::type> f;
         f.R = GradShape<T, K, D>::Store::make(rbase);
         f.compute(a, tab, m);
@@ -713,15 +727,23 @@ int coop_grid(const void* kernel, int threads, size_t smem);
 // ---------------------------------------------------------------------------------------------
 // Launchers, bundled per (T, K, D) into an Ops table.
 // ---------------------------------------------------------------------------------------------
+// The refined points a flat kernel visits: [m0, m0 + cnt), or list[0 .. cnt) when list is set.
+struct Pts {
+    int64_t m0 = 0;
+    int64_t cnt = 0;
+    const int* list = nullptr;
+    static Pts all(int64_t M) { return Pts{0, M, nullptr}; }
+};
+
 template <typename T>
 struct Ops {
     cudaError_t (*factor)(const PointArgs<T>&, int64_t, int64_t, T*, T*, cudaStream_t);
-    cudaError_t (*inv)(const PointArgs<T>&, const T*, T*, int64_t, cudaStream_t);
-    cudaError_t (*logdet)(const PointArgs<T>&, T*, double*, int64_t, cudaStream_t);
-    cudaError_t (*logdet_grad)(const PointArgs<T>&, double*, double*, T*, int64_t, cudaStream_t);
+    cudaError_t (*inv)(const PointArgs<T>&, const T*, T*, Pts, cudaStream_t);
+    cudaError_t (*logdet)(const PointArgs<T>&, T*, double*, Pts, cudaStream_t);
+    cudaError_t (*logdet_grad)(const PointArgs<T>&, double*, double*, T*, Pts, cudaStream_t);
     cudaError_t (*grad_vals)(const PointArgs<T>&, const T*, const T*, const T*, const T*, double*,
-                             int64_t, cudaStream_t);
-    cudaError_t (*inv_loss_grad)(const PointArgs<T>&, const T*, double*, double*, T*, int64_t,
+                             Pts, cudaStream_t);
+    cudaError_t (*inv_loss_grad)(const PointArgs<T>&, const T*, double*, double*, T*, Pts,
                                  cudaStream_t);
     cudaError_t (*fused_fwd)(const PointArgs<T>&, T*, const T*, int64_t, int64_t, cudaStream_t);
     cudaError_t (*sweep_fwdrev_all)(T*, const T*, T*, const T*, const T*, const int*, int64_t,
@@ -759,43 +781,52 @@ struct Launch {
         return flat("factor", k_factor<T, K, D>, flat_smem(a, false), me - mb, s, a, mb, me, mv,
                     sd);
     }
-    static cudaError_t inv(const PointArgs<T>& a, const T* values, T* xi, int64_t M,
+    static cudaError_t inv(const PointArgs<T>& a, const T* values, T* xi, Pts r,
                            cudaStream_t s) {
-        return flat("inv", k_inv<T, K, D>, flat_smem(a, false), M, s, a, values, xi, M);
+        return flat("inv", k_inv<T, K, D>, flat_smem(a, false), r.cnt, s, a, values, xi, r.m0,
+                    r.cnt, r.list);
     }
-    static cudaError_t logdet(const PointArgs<T>& a, T* terms, double* acc, int64_t M,
+    static cudaError_t logdet(const PointArgs<T>& a, T* terms, double* acc, Pts r,
                               cudaStream_t s) {
-        return flat("logdet", k_logdet<T, K, D>, flat_smem(a, false), M, s, a, terms, acc, M);
+        return flat("logdet", k_logdet<T, K, D>, flat_smem(a, false), r.cnt, s, a, terms, acc,
+                    r.m0, r.cnt, r.list);
     }
     static cudaError_t logdet_grad(const PointArgs<T>& a, double* gacc, double* ld, T* terms,
-                                   int64_t M, cudaStream_t s) {
+                                   Pts r, cudaStream_t s) {
+        const int64_t M = r.cnt;
+        if (M <= 0) return cudaSuccess;
         using G = GradShape<T, K, D>;
         const size_t smem = flat_smem(a, true) + G::Store::bytes;
         cudaError_t e = prepare_kernel_smem((const void*)k_logdet_grad<T, K, D>, smem);
         if (e != cudaSuccess) return e;
         const int grid = flat_grid((const void*)k_logdet_grad<T, K, D>, G::kThreads, smem, M);
         return launch_prof("logdet_grad", k_logdet_grad<T, K, D>, dim3(grid), dim3(G::kThreads),
-                           smem, s, a, gacc, ld, terms, M);
+                           smem, s, a, gacc, ld, terms, r.m0, r.cnt, r.list);
     }
     static cudaError_t grad_vals(const PointArgs<T>& a, const T* v, const T* xih, const T* vb,
-                                 const T* mv, double* gacc, int64_t M, cudaStream_t s) {
+                                 const T* mv, double* gacc, Pts r, cudaStream_t s) {
+        const int64_t M = r.cnt;
+        if (M <= 0) return cudaSuccess;
         using G = GradShape<T, K, D>;
         const size_t smem = flat_smem(a, true) + G::Store::bytes;
         cudaError_t e = prepare_kernel_smem((const void*)k_grad_vals<T, K, D>, smem);
         if (e != cudaSuccess) return e;
         const int grid = flat_grid((const void*)k_grad_vals<T, K, D>, G::kThreads, smem, M);
         return launch_prof("grad_vals", k_grad_vals<T, K, D>, dim3(grid), dim3(G::kThreads), smem,
-                           s, a, v, xih, vb, mv, gacc, M);
+                           s, a, v, xih, vb, mv, gacc, r.m0, r.cnt, r.list);
     }
     static cudaError_t inv_loss_grad(const PointArgs<T>& a, const T* values, double* gacc,
-                                     double* loss, T* xi_out, int64_t M, cudaStream_t s) {
+                                     double* loss, T* xi_out, Pts r, cudaStream_t s) {
+        const int64_t M = r.cnt;
+        if (M <= 0) return cudaSuccess;
         using G = GradShape<T, K, D>;
         const size_t smem = flat_smem(a, true) + G::Store::bytes;
         cudaError_t e = prepare_kernel_smem((const void*)k_inv_loss_grad<T, K, D>, smem);
         if (e != cudaSuccess) return e;
         const int grid = flat_grid((const void*)k_inv_loss_grad<T, K, D>, G::kThreads, smem, M);
         return launch_prof("inv_loss_grad", k_inv_loss_grad<T, K, D>, dim3(grid),
-                           dim3(G::kThreads), smem, s, a, values, gacc, loss, xi_out, M);
+                           dim3(G::kThreads), smem, s, a, values, gacc, loss, xi_out, r.m0,
+                           r.cnt, r.list);
     }
     static cudaError_t fused_fwd(const PointArgs<T>& a, T* values, const T* xi_ref, int64_t lo,
                                  int64_t hi, cudaStream_t s) {

@@ -65,11 +65,13 @@ int run(gpb2_problem* p, T* dvals, double* ld, cudaStream_t s) {
     double* acc = nullptr;
     GPB2_TRY(noalloc_acc(p->device, &acc));
     GPB2_CUDA_TRY(cudaMemsetAsync(acc, 0, sizeof(double) * (p->nb + kNoAllocScalars), s));
-    cudaError_t e = ops_of<T>(p)->logdet_grad(point_args<T>(p), acc, acc + p->nb, nullptr, p->m, s);
+    cudaError_t e = ops_of<T>(p)->logdet_grad(point_args<T>(p), acc, acc + p->nb, nullptr,
+                                              Pts::all(p->m), s);
     if (e != cudaSuccess)
         return set_error(GPB2_ERR_CUDA, "noalloc logdet grad launch failed: %s",
                          cudaGetErrorString(e));
-    const int64_t g = std::min<int64_t>((p->nb + 255) / 256, 148);
+    // The same grid as the allocating form's conversion (grid-stride loop, 256 threads).
+    const int64_t g = std::min<int64_t>((p->nb + 255) / 256, 148 * 16);
     k_noalloc_hist_to_t<T><<<(unsigned)std::max<int64_t>(g, 1), 256, 0, s>>>(acc, dvals, p->nb);
     GPB2_CUDA_TRY(cudaGetLastError());
     double h = 0.0;

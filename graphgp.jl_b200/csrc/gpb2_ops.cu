@@ -256,7 +256,7 @@ struct Impl {
     }
 
     static int refine_inv(P* p, const T* values, T* xi_ref, cudaStream_t s) {
-        return check_launch(ops_of<T>(p)->inv(point_args<T>(p), values, xi_ref, p->m, s),
+        return check_launch(ops_of<T>(p)->inv(point_args<T>(p), values, xi_ref, Pts::all(p->m), s),
                             "refine_inv");
     }
 
@@ -264,7 +264,7 @@ struct Impl {
         GPB2_TRY(ensure_scratch(p, false));
         GPB2_TRY(zero_acc(p, s));
         GPB2_TRY(check_launch(
-            ops_of<T>(p)->logdet(point_args<T>(p), terms, p->dacc + p->nb, p->m, s), "logdet"));
+            ops_of<T>(p)->logdet(point_args<T>(p), terms, p->dacc + p->nb, Pts::all(p->m), s), "logdet"));
         if (out) {
             double h[4];
             GPB2_TRY(read_scalars(p, h, s));
@@ -277,7 +277,7 @@ struct Impl {
         GPB2_TRY(ensure_scratch(p, false));
         GPB2_TRY(zero_acc(p, s));
         GPB2_TRY(check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p), p->dacc,
-                                                        p->dacc + p->nb, nullptr, p->m, s),
+                                                        p->dacc + p->nb, nullptr, Pts::all(p->m), s),
                               "logdet grad"));
         GPB2_TRY(finish_hist(p, dvals, s));
         if (ld) {
@@ -293,7 +293,7 @@ struct Impl {
         GPB2_TRY(ensure_scratch(p, false));
         GPB2_TRY(zero_acc(p, s));
         GPB2_TRY(check_launch(ops_of<T>(p)->inv_loss_grad(point_args<T>(p), values, p->dacc,
-                                                          p->dacc + p->nb + 1, nullptr, p->m, s),
+                                                          p->dacc + p->nb + 1, nullptr, Pts::all(p->m), s),
                               "inverse-loss grad"));
         GPB2_TRY(finish_hist(p, dvals, s));
         if (loss) {
@@ -372,7 +372,7 @@ struct Impl {
         GPB2_TRY(Dense<T>::factor(p, s));
         GPB2_TRY(Dense<T>::logdet(p, p->dacc + p->nb + 2, s));
         GPB2_TRY(check_launch(
-            ops_of<T>(p)->logdet(point_args<T>(p), nullptr, p->dacc + p->nb, p->m, s), "logdet"));
+            ops_of<T>(p)->logdet(point_args<T>(p), nullptr, p->dacc + p->nb, Pts::all(p->m), s), "logdet"));
         double h[4];
         GPB2_TRY(read_scalars(p, h, s));
         *out = h[2] + h[0];
@@ -424,7 +424,7 @@ struct Impl {
         GPB2_TRY(zero_acc(p, s));
         auto per_point = [&](cudaStream_t st) {
             return check_launch(ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb,
-                                                        (const T*)p->mv, p->dacc, p->m, st),
+                                                        (const T*)p->mv, p->dacc, Pts::all(p->m), st),
                                 "grad_vals");
         };
         if (!g_overlap) {
@@ -453,7 +453,7 @@ struct Impl {
         GPB2_TRY(ensure_scratch(p, false));
         GPB2_TRY(zero_acc(p, s));
         GPB2_TRY(check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p), p->dacc,
-                                                        p->dacc + p->nb, nullptr, p->m, s),
+                                                        p->dacc + p->nb, nullptr, Pts::all(p->m), s),
                               "logdet grad"));
         GPB2_TRY(Dense<T>::factor(p, s));
         GPB2_TRY(Dense<T>::logdet(p, p->dacc + p->nb + 2, s));
@@ -477,7 +477,7 @@ struct Impl {
         }
         GPB2_TRY(zero_acc(p, s));
         GPB2_TRY(check_launch(ops_of<T>(p)->inv_loss_grad(point_args<T>(p), yt, p->dacc,
-                                                          p->dacc + p->nb + 1, nullptr, p->m, s),
+                                                          p->dacc + p->nb + 1, nullptr, Pts::all(p->m), s),
                               "inverse-loss grad"));
         GPB2_TRY(Dense<T>::factor(p, s));
         GPB2_TRY(Dense<T>::inv_loss_grad(p, yt, p->dacc, p->dacc + p->nb + 1, s));

@@ -226,6 +226,7 @@ static int load_table(gpb2_problem* p, const void* vals_dev, cudaStream_t s) {
     p->dense_valid = false;   // the dense factor belongs to the previous table
     p->dense_launched = false;
     p->factor_valid = false;  // and so do the per-point mean_vec / std
+    p->sh_factor_valid = false;
     GPB2_CUDA_TRY(cudaMemcpyAsync(p->vals, vals_dev, ts * p->nb, cudaMemcpyDeviceToDevice, s));
     // The bins do not change after creation: they are read back once, the values every time.
     const bool first = p->hbins.size() != ts * p->nb;
@@ -255,7 +256,8 @@ static void free_problem(gpb2_problem* p) {
                     p->start,  p->mv,   p->sd,      p->buf_a, p->buf_b, p->buf_c,
                     p->buf_d,  p->dacc, p->Lcand,   p->lad,  p->Wd,    p->Wd2,
                     p->dwork,  p->dinfo, p->d_offsets, p->dsync, p->Ld,    p->trace,
-                    p->Ldr,    p->Dinv,  p->Wtri, p->Ainv};
+                    p->Ldr,    p->Dinv,  p->Wtri, p->Ainv,  p->sh_v, p->sh_vb,
+                    p->sh_xg,  p->sh_own};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);

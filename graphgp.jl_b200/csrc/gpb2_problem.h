@@ -82,6 +82,18 @@ struct gpb2_problem {
 
     const gpb2::Ops<float>* ops32 = nullptr;
     const gpb2::Ops<double>* ops64 = nullptr;
+
+    // Level-sharded operations (gpb2_shard.cu): full-length buffers with slack for the
+    // collectives' spill, the list of refined points this rank owns, and which sharding they
+    // were built for.
+    void* sh_v = nullptr;        // (N + slack) T   field
+    void* sh_vb = nullptr;       // (N + slack) T   cotangent (partial per rank)
+    void* sh_xg = nullptr;       // (N + slack) T   xi-cotangent
+    int64_t sh_len = 0;          // entries of each of the three
+    int* sh_own = nullptr;       // refined points (m) this rank's kernels visit
+    int64_t sh_own_cnt = 0;
+    int64_t sh_key[3] = {-1, -1, -1};  // (ranks, rank, min_shard) of sh_own
+    bool sh_factor_valid = false;       // mv / sd hold this rank's points for the current table
 };
 
 namespace gpb2 {

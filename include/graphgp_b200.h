@@ -200,8 +200,11 @@ int gpb2_refine_logdet_grad_vals(gpb2_problem* prob, void* dvals_dev, double* lo
  * at the point of the call.  The histogram lives in a fixed __device__ array of 4096 + 8 doubles
  * per device, cleared by the call on `stream`.  Limits: nbins <= 4096 (else
  * GPB2_ERR_INVALID_ARG); calls that overlap in time on one device (other threads, streams or
- * problems) race on the shared array; the first call on each device must be made outside stream
- * capture (it resolves the array's address).  Synchronous, like the allocating form. */
+ * problems) race on the shared array.  The first call on each device resolves the array's address
+ * (cudaGetSymbolAddress): make it before any stream capture.  The call always waits for its own
+ * work before returning
+ * (whatever gpb2_set_synchronous says), and it does not read the status words that earlier
+ * asynchronous calls on the handle left behind: call gpb2_problem_check for those. */
 int gpb2_refine_logdet_grad_vals_noalloc(gpb2_problem* prob, void* dvals_dev,
                                          double* logdet_host, void* stream);
 

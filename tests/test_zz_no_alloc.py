@@ -62,3 +62,26 @@ def test_noalloc_rejects_oversize_table(cuda_device):
         gp.refine_logdet_grad_vals_noalloc(prob)
     # the allocating entry point still serves it
     assert np.all(np.isfinite(gp.refine_logdet_grad_vals(prob)))
+
+
+def test_noalloc_fresh_handle_allocates_nothing(cuda_device):
+    # A handle whose first operation is the no-allocation call (no scratch exists yet) gives the
+    # allocating entry point's result, and the device's free memory is the same before and after
+    # the call.  The library's module is loaded on the device by an earlier call first (module
+    # loading reserves the fixed array itself, once per device).
+    import torch
+    gp.refine_logdet_grad_vals_noalloc(_problem(np.float32, seed=6))
+    prob = _problem(np.float32, seed=7)
+    ref = gp.refine_logdet_grad_vals(_problem(np.float32, seed=7))
+    out = torch.empty(prob.nbins(), dtype=prob.torch_dtype, device=prob.device)
+    h = prob.handle
+    stream = C.c_void_p(torch.cuda.current_stream(prob.device).cuda_stream)
+    torch.cuda.synchronize(cuda_device)
+    free0 = torch.cuda.mem_get_info(cuda_device)[0]
+    st = _lib.lib().gpb2_refine_logdet_grad_vals_noalloc(h, C.c_void_p(out.data_ptr()), None,
+                                                         stream)
+    torch.cuda.synchronize(cuda_device)
+    free1 = torch.cuda.mem_get_info(cuda_device)[0]
+    _lib.check(st, "noalloc")
+    assert free1 == free0
+    assert relerr(out.cpu().numpy(), ref) < TOL[np.float32]
