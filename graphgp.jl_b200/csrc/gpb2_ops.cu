@@ -19,6 +19,7 @@
 #include <cstring>
 #include <string>
 
+#include "gpb2_comm.h"
 #include "gpb2_problem.h"
 
 namespace gpb2 {
@@ -540,6 +541,313 @@ static int finish_call(gpb2_problem* p, cudaStream_t s) {
     return GPB2_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Level-sharded operations over the ranks of a gpb2_comm (one process or thread per GPU).
+//
+// Every rank holds the same problem (graph, table, dense factor) and the whole field; inputs and
+// outputs are full length, in original order, on every rank.  Depth batch b = [lo, hi) of at
+// least min_shard points is cut into `ranks` chunks of c = ceil((hi - lo) / ranks) points;
+// rank r owns [lo + r c, lo + (r+1) c) (clipped to hi).  Smaller batches are not split for the
+// forward sweep (every rank computes them, no exchange).  This is the reference's distributed
+// per-level loop (src/distributed.jl:281-331), whose sum-Allreduce per level becomes an
+// in-place all-gather of the owners' chunks.
+//
+// Forward: per batch, the owners' chunks, then an in-place NCCL all-gather completes the batch
+// everywhere (the gather may spill past hi into later batches' slots, rewritten when they are
+// computed, and past N into slack).
+// Reverse (generate_grad_xi, and generate_grad_vals' cotangent sweep): each rank keeps a partial
+// cotangent vb; rank 0 starts with vbar, the others with 0.  Latest batch first: its segment is
+// summed over the ranks (in-place reduce-scatter for a sharded batch, all-reduce for a small
+// one), then every rank scatters the contributions of the points it owns (a small batch's points
+// are split for this step only, so that each is scattered once).  The dense block's cotangents
+// and the xi-cotangents are summed over the ranks at the end.
+// generate_grad_vals: every rank then runs the per-point vals-gradient on the points it owns
+// (their cotangents are complete there); the dense block's pullback runs on rank 0; one
+// all-reduce of the nbins double histogram.
+// Fitting reductions (scheme A of src/distributed.jl:129-247): the refined points are split into
+// contiguous per-rank ranges; one all-reduce of the nbins + 4 double accumulators.
+struct ShardBatch {
+    int64_t lo, hi, chunk;
+    bool sharded;
+};
+
+struct ShardPlan {
+    std::vector<ShardBatch> b;
+    int64_t slack = 0;
+    int ranks = 1, rank = 0;
+
+    static ShardPlan make(const std::vector<int64_t>& offs, int ranks, int rank, int64_t min_shard) {
+        ShardPlan pl;
+        pl.ranks = ranks;
+        pl.rank = rank;
+        const int64_t n = offs.back();
+        for (size_t i = 1; i < offs.size(); i++) {
+            const int64_t lo = offs[i - 1], hi = offs[i], size = hi - lo;
+            const bool sh = ranks > 1 && size >= std::max<int64_t>(min_shard, ranks);
+            const int64_t c = sh ? (size + ranks - 1) / ranks : size;
+            pl.b.push_back(ShardBatch{lo, hi, c, sh});
+            if (sh) pl.slack = std::max(pl.slack, lo + ranks * c - n);
+        }
+        return pl;
+    }
+    // The points of batch b this rank computes in the forward sweep.
+    void fwd_range(const ShardBatch& x, int64_t& a, int64_t& e) const {
+        if (!x.sharded) {
+            a = x.lo;
+            e = x.hi;
+            return;
+        }
+        a = std::min(x.hi, x.lo + rank * x.chunk);
+        e = std::min(x.hi, a + x.chunk);
+    }
+    // The points of batch b whose cotangents this rank scatters (each point on one rank).
+    void own_range(const ShardBatch& x, int64_t& a, int64_t& e) const {
+        const int64_t c = x.sharded ? x.chunk : (x.hi - x.lo + ranks - 1) / ranks;
+        a = std::min(x.hi, x.lo + rank * c);
+        e = std::min(x.hi, a + c);
+    }
+};
+
+template <typename T>
+struct Shard {
+    using P = gpb2_problem;
+    static constexpr bool kF64 = sizeof(T) == 8;
+
+    // Buffers with slack and the rank's own point list (built once per sharding).
+    static int prepare(P* p, gpb2_comm* c, const ShardPlan& pl) {
+        GPB2_TRY(ensure_scratch(p, true));
+        const int64_t len = p->n + pl.slack + 1;
+        if (p->sh_len < len) {
+            void* bufs[3] = {p->sh_v, p->sh_vb, p->sh_xg};
+            for (void* b : bufs)
+                if (b) cudaFree(b);
+            p->sh_v = p->sh_vb = p->sh_xg = nullptr;
+            p->sh_len = 0;
+            GPB2_TRY(ensure_alloc(&p->sh_v, sizeof(T) * len));
+            GPB2_TRY(ensure_alloc(&p->sh_vb, sizeof(T) * len));
+            GPB2_TRY(ensure_alloc(&p->sh_xg, sizeof(T) * len));
+            p->sh_len = len;
+        }
+        const int64_t key[3] = {pl.ranks, pl.rank, comm_min_shard(c)};
+        if (p->sh_own && std::equal(key, key + 3, p->sh_key)) return GPB2_OK;
+        std::vector<int> own;
+        own.reserve((size_t)(p->m / pl.ranks + p->offsets.size() + 16));
+        for (const ShardBatch& x : pl.b) {
+            int64_t a, e;
+            pl.own_range(x, a, e);
+            for (int64_t q = a; q < e; q++) own.push_back((int)(q - p->n0));
+        }
+        if (p->sh_own) cudaFree(p->sh_own);
+        p->sh_own = nullptr;
+        p->sh_own_cnt = 0;
+        GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&p->sh_own), sizeof(int) * std::max<size_t>(own.size(), 1)));
+        GPB2_CUDA_TRY(cudaMemcpy(p->sh_own, own.data(), sizeof(int) * own.size(),
+                                 cudaMemcpyHostToDevice));
+        p->sh_own_cnt = (int64_t)own.size();
+        std::copy(key, key + 3, p->sh_key);
+        p->sh_factor_valid = false;
+        return GPB2_OK;
+    }
+
+    // mean_vec / std of the points this rank's sweeps read: its forward ranges (which contain
+    // its reverse ranges).  Nothing when every point's factor is current.
+    static int factor(P* p, const ShardPlan& pl, cudaStream_t s) {
+        if (p->factor_valid || p->sh_factor_valid) return GPB2_OK;
+        const Ops<T>* o = ops_of<T>(p);
+        for (const ShardBatch& x : pl.b) {
+            int64_t a, e;
+            pl.fwd_range(x, a, e);
+            if (e > a)
+                GPB2_TRY(Impl<T>::check_launch(
+                    o->factor(point_args<T>(p), a - p->n0, e - p->n0, (T*)p->mv, (T*)p->sd, s),
+                    "factor"));
+        }
+        p->sh_factor_valid = true;
+        return GPB2_OK;
+    }
+
+    static int forward(P* p, gpb2_comm* c, const ShardPlan& pl, const T* xt, T* v,
+                       cudaStream_t s) {
+        const Ops<T>* o = ops_of<T>(p);
+        GPB2_TRY(Dense<T>::apply_L(p, xt, v, s));
+        for (const ShardBatch& x : pl.b) {
+            int64_t a, e;
+            pl.fwd_range(x, a, e);
+            GPB2_TRY(Impl<T>::check_launch(o->sweep_fwd(v, xt + p->n0, (const T*)p->mv,
+                                                        (const T*)p->sd, p->nbrs, p->n0, a, e, s),
+                                           "forward sweep"));
+            if (x.sharded) GPB2_TRY(comm_all_gather(c, v, x.lo, x.chunk, kF64, s));
+        }
+        return GPB2_OK;
+    }
+
+    // On entry vb holds this rank's share of the cotangent (full length); on exit the points this
+    // rank owns hold their complete cotangents, vb[0:n0] the dense block's (summed), and xg (if
+    // given) the xi-cotangents of the refined points, summed over the ranks.
+    static int reverse(P* p, gpb2_comm* c, const ShardPlan& pl, T* vb, T* xg, cudaStream_t s) {
+        const Ops<T>* o = ops_of<T>(p);
+        for (size_t i = pl.b.size(); i-- > 0;) {
+            const ShardBatch& x = pl.b[i];
+            if (x.hi <= x.lo) continue;
+            if (x.sharded)
+                GPB2_TRY(comm_reduce_scatter(c, vb, x.lo, x.chunk, kF64, s));
+            else
+                GPB2_TRY(comm_all_reduce(c, vb + x.lo, x.hi - x.lo, kF64, s));
+            int64_t a, e;
+            pl.own_range(x, a, e);
+            GPB2_TRY(Impl<T>::check_launch(o->sweep_rev(xg, vb, (const T*)p->mv, (const T*)p->sd,
+                                                        p->nbrs, p->n0, a, e, s),
+                                           "reverse sweep"));
+        }
+        GPB2_TRY(comm_all_reduce(c, vb, p->n0, kF64, s));
+        if (xg) GPB2_TRY(comm_all_reduce(c, xg + p->n0, p->m, kF64, s));
+        return GPB2_OK;
+    }
+
+    static const T* to_tree(P* p, const T* x, T* buf, cudaStream_t s, int* st) {
+        if (!p->indices) return x;
+        *st = Impl<T>::gather(p, x, buf, s);
+        return buf;
+    }
+
+    static int generate(P* p, gpb2_comm* c, const T* xi, T* out, cudaStream_t s) {
+        const ShardPlan pl = ShardPlan::make(p->offsets, comm_size(c), comm_rank(c),
+                                             comm_min_shard(c));
+        GPB2_TRY(prepare(p, c, pl));
+        int st = GPB2_OK;
+        const T* xt = to_tree(p, xi, (T*)p->buf_b, s, &st);
+        GPB2_TRY(st);
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(factor(p, pl, s));
+        T* v = (T*)p->sh_v;
+        GPB2_TRY(forward(p, c, pl, xt, v, s));
+        if (p->indices) return Impl<T>::scatter(p, v, out, s);
+        GPB2_CUDA_TRY(cudaMemcpyAsync(out, v, sizeof(T) * p->n, cudaMemcpyDeviceToDevice, s));
+        return GPB2_OK;
+    }
+
+    // The rank's share of the upstream cotangent in tree order: vbar on rank 0, zero elsewhere.
+    static int seed_cotangent(P* p, gpb2_comm* c, const T* vbar, T* vb, cudaStream_t s) {
+        GPB2_CUDA_TRY(cudaMemsetAsync(vb, 0, sizeof(T) * p->sh_len, s));
+        if (comm_rank(c) != 0) return GPB2_OK;
+        if (p->indices) return Impl<T>::gather(p, vbar, vb, s);
+        GPB2_CUDA_TRY(cudaMemcpyAsync(vb, vbar, sizeof(T) * p->n, cudaMemcpyDeviceToDevice, s));
+        return GPB2_OK;
+    }
+
+    static int grad_xi(P* p, gpb2_comm* c, const T* vbar, T* xbar, cudaStream_t s) {
+        const ShardPlan pl = ShardPlan::make(p->offsets, comm_size(c), comm_rank(c),
+                                             comm_min_shard(c));
+        GPB2_TRY(prepare(p, c, pl));
+        T* vb = (T*)p->sh_vb;
+        T* xg = (T*)p->sh_xg;
+        GPB2_TRY(seed_cotangent(p, c, vbar, vb, s));
+        GPB2_CUDA_TRY(cudaMemsetAsync(xg, 0, sizeof(T) * p->sh_len, s));
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(factor(p, pl, s));
+        GPB2_TRY(reverse(p, c, pl, vb, xg, s));
+        GPB2_TRY(Dense<T>::apply_Lt(p, vb, xg, s));
+        if (p->indices) return Impl<T>::scatter(p, xg, xbar, s);
+        GPB2_CUDA_TRY(cudaMemcpyAsync(xbar, xg, sizeof(T) * p->n, cudaMemcpyDeviceToDevice, s));
+        return GPB2_OK;
+    }
+
+    static int grad_vals(P* p, gpb2_comm* c, const T* xi, const T* vbar, T* dvals,
+                         cudaStream_t s) {
+        const ShardPlan pl = ShardPlan::make(p->offsets, comm_size(c), comm_rank(c),
+                                             comm_min_shard(c));
+        GPB2_TRY(prepare(p, c, pl));
+        int st = GPB2_OK;
+        const T* xt = to_tree(p, xi, (T*)p->buf_b, s, &st);
+        GPB2_TRY(st);
+        GPB2_TRY(Dense<T>::factor(p, s));
+        GPB2_TRY(factor(p, pl, s));
+        T* v = (T*)p->sh_v;
+        T* vb = (T*)p->sh_vb;
+        GPB2_TRY(forward(p, c, pl, xt, v, s));
+        GPB2_TRY(seed_cotangent(p, c, vbar, vb, s));
+        GPB2_TRY(reverse(p, c, pl, vb, nullptr, s));
+        GPB2_TRY(Impl<T>::zero_acc(p, s));
+        GPB2_TRY(Impl<T>::check_launch(
+            ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb, (const T*)p->mv, p->dacc,
+                                    Pts{0, p->sh_own_cnt, p->sh_own}, s),
+            "grad_vals"));
+        if (comm_rank(c) == 0) GPB2_TRY(Dense<T>::grad_vals(p, vb, xt, p->dacc, s));
+        GPB2_TRY(comm_all_reduce(c, p->dacc, p->nb, true, s));
+        return Impl<T>::finish_hist(p, dvals, s);
+    }
+
+    // Contiguous per-rank ranges of the refined points (scheme A): the first M mod ranks ranks
+    // take one point more (_balanced_range, ext/GraphGPMPIExt.jl:25-36).
+    static Pts flat_share(P* p, gpb2_comm* c) {
+        const int64_t W = comm_size(c), r = comm_rank(c);
+        const int64_t base = p->m / W, rem = p->m % W;
+        const int64_t a = r < rem ? r * (base + 1) : rem * (base + 1) + (r - rem) * base;
+        return Pts{a, r < rem ? base + 1 : base, nullptr};
+    }
+
+    static int logdet(P* p, gpb2_comm* c, double* out, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        GPB2_TRY(Impl<T>::zero_acc(p, s));
+        GPB2_TRY(Dense<T>::factor(p, s));
+        if (comm_rank(c) == 0) GPB2_TRY(Dense<T>::logdet(p, p->dacc + p->nb + 2, s));
+        GPB2_TRY(Impl<T>::check_launch(ops_of<T>(p)->logdet(point_args<T>(p), nullptr,
+                                                            p->dacc + p->nb, flat_share(p, c), s),
+                                       "logdet"));
+        GPB2_TRY(comm_all_reduce(c, p->dacc + p->nb, 4, true, s));
+        double h[4];
+        GPB2_TRY(Impl<T>::read_scalars(p, h, s));
+        *out = h[2] + h[0];
+        return GPB2_OK;
+    }
+
+    static int logdet_grad(P* p, gpb2_comm* c, T* dvals, double* ld, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        GPB2_TRY(Impl<T>::zero_acc(p, s));
+        GPB2_TRY(Impl<T>::check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p), p->dacc,
+                                                                 p->dacc + p->nb, nullptr,
+                                                                 flat_share(p, c), s),
+                                       "logdet grad"));
+        GPB2_TRY(Dense<T>::factor(p, s));
+        if (comm_rank(c) == 0) {
+            GPB2_TRY(Dense<T>::logdet(p, p->dacc + p->nb + 2, s));
+            GPB2_TRY(Dense<T>::logdet_grad(p, p->dacc, s));
+        }
+        GPB2_TRY(comm_all_reduce(c, p->dacc, p->nb + 4, true, s));
+        GPB2_TRY(Impl<T>::finish_hist(p, dvals, s));
+        if (ld) {
+            double h[4];
+            GPB2_TRY(Impl<T>::read_scalars(p, h, s));
+            *ld = h[2] + h[0];
+        }
+        return GPB2_OK;
+    }
+
+    static int inv_loss_grad(P* p, gpb2_comm* c, const T* data, T* dvals, double* loss,
+                             cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        int st = GPB2_OK;
+        const T* yt = to_tree(p, data, (T*)p->buf_a, s, &st);
+        GPB2_TRY(st);
+        GPB2_TRY(Impl<T>::zero_acc(p, s));
+        GPB2_TRY(Impl<T>::check_launch(
+            ops_of<T>(p)->inv_loss_grad(point_args<T>(p), yt, p->dacc, p->dacc + p->nb + 1,
+                                        nullptr, flat_share(p, c), s),
+            "inverse-loss grad"));
+        GPB2_TRY(Dense<T>::factor(p, s));
+        if (comm_rank(c) == 0)
+            GPB2_TRY(Dense<T>::inv_loss_grad(p, yt, p->dacc, p->dacc + p->nb + 1, s));
+        GPB2_TRY(comm_all_reduce(c, p->dacc, p->nb + 4, true, s));
+        GPB2_TRY(Impl<T>::finish_hist(p, dvals, s));
+        if (loss) {
+            double h[4];
+            GPB2_TRY(Impl<T>::read_scalars(p, h, s));
+            *loss = h[1];
+        }
+        return GPB2_OK;
+    }
+};
+
 }  // namespace gpb2
 
 using namespace gpb2;
@@ -726,6 +1034,76 @@ int gpb2_generate_inv_loss_grad_vals(gpb2_problem* p, const void* data, void* dv
     GPB2_TRY(need(data, "data") | need(dvals, "dvals"));
     GPB2_DISPATCH(p, Impl<float>::generate_inv_loss_grad_vals(p, CF32(data), F32(dvals), loss, s),
                   Impl<double>::generate_inv_loss_grad_vals(p, CF64(data), F64(dvals), loss, s));
+}
+
+// ------------------------------------------------------------------------------ level-sharded
+
+#define GPB2_SHARDED(p, c, CALL32, CALL64)                                                     \
+    do {                                                                                       \
+        if (!(c)) return set_error(GPB2_ERR_INVALID_ARG, "%s: NULL communicator", __func__);   \
+        GPB2_DISPATCH(p, CALL32, CALL64);                                                      \
+    } while (0)
+
+int gpb2_generate_sharded(gpb2_problem* p, gpb2_comm* c, const void* xi, void* out,
+                          void* stream) {
+    GPB2_TRY(need(xi, "xi") | need(out, "out"));
+    GPB2_SHARDED(p, c, Shard<float>::generate(p, c, CF32(xi), F32(out), s),
+                 Shard<double>::generate(p, c, CF64(xi), F64(out), s));
+}
+
+int gpb2_generate_grad_xi_sharded(gpb2_problem* p, gpb2_comm* c, const void* vbar, void* xbar,
+                                  void* stream) {
+    GPB2_TRY(need(vbar, "vbar") | need(xbar, "xbar"));
+    GPB2_SHARDED(p, c, Shard<float>::grad_xi(p, c, CF32(vbar), F32(xbar), s),
+                 Shard<double>::grad_xi(p, c, CF64(vbar), F64(xbar), s));
+}
+
+int gpb2_generate_grad_vals_sharded(gpb2_problem* p, gpb2_comm* c, const void* xi,
+                                    const void* vbar, void* dvals, void* stream) {
+    GPB2_TRY(need(xi, "xi") | need(vbar, "vbar") | need(dvals, "dvals"));
+    GPB2_SHARDED(p, c, Shard<float>::grad_vals(p, c, CF32(xi), CF32(vbar), F32(dvals), s),
+                 Shard<double>::grad_vals(p, c, CF64(xi), CF64(vbar), F64(dvals), s));
+}
+
+int gpb2_generate_logdet_sharded(gpb2_problem* p, gpb2_comm* c, double* out, void* stream) {
+    GPB2_TRY(need(out, "logdet_host"));
+    GPB2_SHARDED(p, c, Shard<float>::logdet(p, c, out, s), Shard<double>::logdet(p, c, out, s));
+}
+
+int gpb2_generate_logdet_grad_vals_sharded(gpb2_problem* p, gpb2_comm* c, void* dvals,
+                                           double* ld, void* stream) {
+    GPB2_TRY(need(dvals, "dvals"));
+    GPB2_SHARDED(p, c, Shard<float>::logdet_grad(p, c, F32(dvals), ld, s),
+                 Shard<double>::logdet_grad(p, c, F64(dvals), ld, s));
+}
+
+int gpb2_generate_inv_loss_grad_vals_sharded(gpb2_problem* p, gpb2_comm* c, const void* data,
+                                             void* dvals, double* loss, void* stream) {
+    GPB2_TRY(need(data, "data") | need(dvals, "dvals"));
+    GPB2_SHARDED(p, c, Shard<float>::inv_loss_grad(p, c, CF32(data), F32(dvals), loss, s),
+                 Shard<double>::inv_loss_grad(p, c, CF64(data), F64(dvals), loss, s));
+}
+
+int gpb2_shard_plan(const int64_t* offsets, int64_t n_offsets, int nranks, int rank,
+                    int64_t min_shard, int64_t* fwd_lo, int64_t* fwd_hi, int64_t* own_lo,
+                    int64_t* own_hi, int* sharded, int64_t* slack) {
+    clear_error();
+    if (!offsets || n_offsets < 1 || nranks < 1 || rank < 0 || rank >= nranks || min_shard < 1)
+        return set_error(GPB2_ERR_INVALID_ARG, "gpb2_shard_plan: invalid arguments");
+    const ShardPlan pl = ShardPlan::make(std::vector<int64_t>(offsets, offsets + n_offsets),
+                                         nranks, rank, min_shard);
+    for (size_t i = 0; i < pl.b.size(); i++) {
+        int64_t a, e;
+        pl.fwd_range(pl.b[i], a, e);
+        if (fwd_lo) fwd_lo[i] = a;
+        if (fwd_hi) fwd_hi[i] = e;
+        pl.own_range(pl.b[i], a, e);
+        if (own_lo) own_lo[i] = a;
+        if (own_hi) own_hi[i] = e;
+        if (sharded) sharded[i] = pl.b[i].sharded ? 1 : 0;
+    }
+    if (slack) *slack = pl.slack;
+    return GPB2_OK;
 }
 
 }  // extern "C"

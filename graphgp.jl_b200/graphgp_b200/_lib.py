@@ -115,6 +115,19 @@ _SIGNATURES = {
     "gpb2_graph_n0": (I64, [P]),
     "gpb2_graph_export": (I32, [P, P, P, P, P, PD]),
     "gpb2_graph_free": (None, [P]),
+    "gpb2_comm_unique_id": (I32, [P]),
+    "gpb2_comm_create": (I32, [C.POINTER(P), I32, I32, P, I32, C.c_double]),
+    "gpb2_comm_set_min_shard": (I32, [P, I64]),
+    "gpb2_comm_info": (I32, [P, C.POINTER(I32), C.POINTER(I32)]),
+    "gpb2_comm_destroy": (I32, [P]),
+    "gpb2_generate_sharded": (I32, [P, P, P, P, P]),
+    "gpb2_generate_grad_xi_sharded": (I32, [P, P, P, P, P]),
+    "gpb2_generate_grad_vals_sharded": (I32, [P, P, P, P, P, P]),
+    "gpb2_generate_logdet_sharded": (I32, [P, P, PD, P]),
+    "gpb2_generate_logdet_grad_vals_sharded": (I32, [P, P, P, PD, P]),
+    "gpb2_generate_inv_loss_grad_vals_sharded": (I32, [P, P, P, P, PD, P]),
+    "gpb2_shard_plan": (I32, [PI64, I64, I32, I32, I64, PI64, PI64, PI64, PI64,
+                              C.POINTER(I32), PI64]),
     "gpb2_build_graph_device": (I32, [P, I64, I64, I64, I64, I64, I64, I32, P, C.POINTER(P)]),
     "gpb2_dgraph_n_offsets": (I64, [P]),
     "gpb2_dgraph_n0": (I64, [P]),

@@ -15,9 +15,18 @@ batches, all-reduce for small ones), each rank then scatters the contributions o
 into its partial cotangent, and at the end the dense block's cotangents are all-reduced and the
 per-rank xbar pieces summed.
 
-The per-batch work goes through the C ABI's range entry points (gpb2_refine_range,
-gpb2_refine_reverse_range, gpb2_dense_apply); `ops` can be replaced (the CPU tests run the
-orchestration under gloo with a numpy implementation of the same ranges).
+Two forms:
+* ``LevelSharded`` (the product path): the whole per-batch schedule runs inside the library
+  (gpb2_*_sharded), with the library's own NCCL communicator (``Comm``) issuing the collectives
+  on the caller's stream between the batch kernels; one C call per operation.
+* ``ShardedGenerate``: the same schedule written out in Python over torch.distributed
+  collectives and the C ABI's range entry points (gpb2_refine_range, gpb2_refine_reverse_range,
+  gpb2_dense_apply).  Its `ops` can be replaced: the CPU tests run it under gloo with a numpy
+  implementation of the ranges, which checks the plan and the orchestration without a GPU.
+
+``DistributedGraphGPProblem`` is the reference's scheme-A fitting view (src/distributed.jl:34-44,
+129-247): generate_logdet, generate_logdet(_and)_grad_vals and generate_inv_loss_grad_vals over
+contiguous per-rank ranges of the refined points, with one all-reduce.
 """
 from __future__ import annotations
 
@@ -191,3 +200,177 @@ class ShardedGenerate:
         c = -(-size // self.world)
         a = min(b.hi, b.lo + self.rank * c)
         return a, min(b.hi, a + c)
+
+
+
+# ---------------------------------------------------------------------------------------------
+# The library path: NCCL inside libgraphgp_b200.so
+# ---------------------------------------------------------------------------------------------
+
+class Comm:
+    """The library's NCCL communicator (gpb2_comm) over the ranks of a torch.distributed group:
+    rank 0 of the group makes the unique id, the group broadcasts it, every rank joins."""
+
+    def __init__(self, group=None, device=None, min_shard: int = 65536, timeout_s: float = 300.0):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        L = _lib.lib()
+        uid = C.create_string_buffer(128)
+        if self.rank == 0:
+            _lib.check(L.gpb2_comm_unique_id(uid), "gpb2_comm_unique_id")
+        obj = [bytes(uid.raw) if self.rank == 0 else None]
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        dist.broadcast_object_list(obj, src=src, group=group)
+        uid = C.create_string_buffer(obj[0], 128)
+        h = C.c_void_p()
+        _lib.check(L.gpb2_comm_create(C.byref(h), self.world, self.rank, uid,
+                                      self.device.index or 0, float(timeout_s)),
+                   "gpb2_comm_create")
+        self._h = h
+        self.set_min_shard(min_shard)
+
+    @property
+    def handle(self) -> C.c_void_p:
+        if self._h is None:
+            raise RuntimeError("communicator is closed")
+        return self._h
+
+    def set_min_shard(self, min_shard: int) -> None:
+        _lib.check(_lib.lib().gpb2_comm_set_min_shard(self.handle, int(min_shard)),
+                   "gpb2_comm_set_min_shard")
+        self.min_shard = int(min_shard)
+
+    def close(self) -> None:
+        if self._h is not None:
+            _lib.check(_lib.lib().gpb2_comm_destroy(self._h), "gpb2_comm_destroy")
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def library_plan(offsets, world: int, rank: int, min_shard: int):
+    """The library's sharding plan of a rank (gpb2_shard_plan, host only): per depth batch
+    (forward range, own range, sharded) and the slack."""
+    offs = np.ascontiguousarray(offsets, np.int64)
+    nb = len(offs) - 1
+    fl, fh, ol, oh = (np.empty(nb, np.int64) for _ in range(4))
+    sh = np.empty(nb, np.int32)
+    slack = C.c_int64()
+    _lib.check(_lib.lib().gpb2_shard_plan(
+        offs.ctypes.data_as(_lib.PI64), len(offs), world, rank, int(min_shard),
+        fl.ctypes.data_as(_lib.PI64), fh.ctypes.data_as(_lib.PI64),
+        ol.ctypes.data_as(_lib.PI64), oh.ctypes.data_as(_lib.PI64),
+        sh.ctypes.data_as(C.POINTER(C.c_int)), C.byref(slack)), "gpb2_shard_plan")
+    return [((int(a), int(b)), (int(c), int(d)), bool(e))
+            for a, b, c, d, e in zip(fl, fh, ol, oh, sh)], int(slack.value)
+
+
+class LevelSharded:
+    """generate / generate_grad_xi / generate_grad_vals of `prob` with every depth batch split
+    over the ranks of `comm` (a library ``Comm``); the per-batch kernels and collectives run
+    inside the library, one C call per operation.  Inputs and outputs are full-length device
+    tensors in original order on every rank; the results equal the single-GPU operations'."""
+
+    def __init__(self, prob: GraphGPProblem, comm: Comm):
+        self.prob = prob
+        self.comm = comm
+
+    def _s(self):
+        return C.c_void_p(torch.cuda.current_stream(self.prob.device).cuda_stream)
+
+    def _vec(self, x, name):
+        t = torch.as_tensor(x, dtype=self.prob.torch_dtype, device=self.prob.device).contiguous()
+        if t.ndim != 1 or t.shape[0] != self.prob.npoints():
+            raise ValueError(f"{name} must have length {self.prob.npoints()}")
+        return t
+
+    def generate(self, xi, out=None) -> torch.Tensor:
+        x = self._vec(xi, "xi")
+        out = torch.empty_like(x) if out is None else out
+        _lib.check(_lib.lib().gpb2_generate_sharded(self.prob.handle, self.comm.handle,
+                                                    C.c_void_p(x.data_ptr()),
+                                                    C.c_void_p(out.data_ptr()), self._s()),
+                   "generate_sharded")
+        return out
+
+    def generate_grad_xi(self, vbar, out=None) -> torch.Tensor:
+        v = self._vec(vbar, "vbar")
+        out = torch.empty_like(v) if out is None else out
+        _lib.check(_lib.lib().gpb2_generate_grad_xi_sharded(
+            self.prob.handle, self.comm.handle, C.c_void_p(v.data_ptr()),
+            C.c_void_p(out.data_ptr()), self._s()), "generate_grad_xi_sharded")
+        return out
+
+    def generate_grad_vals(self, xi, vbar, out=None) -> torch.Tensor:
+        x = self._vec(xi, "xi")
+        v = self._vec(vbar, "vbar")
+        out = torch.empty(self.prob.nbins(), dtype=self.prob.torch_dtype,
+                          device=self.prob.device) if out is None else out
+        _lib.check(_lib.lib().gpb2_generate_grad_vals_sharded(
+            self.prob.handle, self.comm.handle, C.c_void_p(x.data_ptr()),
+            C.c_void_p(v.data_ptr()), C.c_void_p(out.data_ptr()), self._s()),
+            "generate_grad_vals_sharded")
+        return out
+
+
+class DistributedGraphGPProblem:
+    """Scheme-A fitting view of a problem (src/distributed.jl:34-44, 129-247): every rank holds
+    the whole problem; the refined points are split into contiguous per-rank ranges (the first
+    M mod ranks ranks take one more, _balanced_range, ext/GraphGPMPIExt.jl:25-36), rank 0 adds
+    the dense first layer, and one all-reduce of nbins + 4 doubles (the histogram and the
+    scalars, accumulated in float64) gives every rank the global result."""
+
+    def __init__(self, prob: GraphGPProblem, comm: Comm):
+        self.prob = prob
+        self.comm = comm
+        M, W, r = prob.nrefined(), comm.world, comm.rank
+        base, rem = divmod(M, W)
+        self.m_lo = r * (base + 1) if r < rem else rem * (base + 1) + (r - rem) * base
+        self.m_hi = self.m_lo + (base + 1 if r < rem else base)   # exclusive
+        self.is_root = r == 0
+
+    def nrefined_local(self) -> int:
+        return self.m_hi - self.m_lo
+
+    def _s(self):
+        return C.c_void_p(torch.cuda.current_stream(self.prob.device).cuda_stream)
+
+    def generate_logdet(self) -> float:
+        out = C.c_double()
+        _lib.check(_lib.lib().gpb2_generate_logdet_sharded(self.prob.handle, self.comm.handle,
+                                                           C.byref(out), self._s()),
+                   "generate_logdet_sharded")
+        return out.value
+
+    def generate_logdet_and_grad_vals(self):
+        out = torch.empty(self.prob.nbins(), dtype=self.prob.torch_dtype, device=self.prob.device)
+        ld = C.c_double()
+        _lib.check(_lib.lib().gpb2_generate_logdet_grad_vals_sharded(
+            self.prob.handle, self.comm.handle, C.c_void_p(out.data_ptr()), C.byref(ld),
+            self._s()), "generate_logdet_grad_vals_sharded")
+        return ld.value, out
+
+    def generate_logdet_grad_vals(self):
+        return self.generate_logdet_and_grad_vals()[1]
+
+    def generate_inv_loss_grad_vals(self, data):
+        d = torch.as_tensor(data, dtype=self.prob.torch_dtype, device=self.prob.device).contiguous()
+        out = torch.empty(self.prob.nbins(), dtype=self.prob.torch_dtype, device=self.prob.device)
+        loss = C.c_double()
+        _lib.check(_lib.lib().gpb2_generate_inv_loss_grad_vals_sharded(
+            self.prob.handle, self.comm.handle, C.c_void_p(d.data_ptr()),
+            C.c_void_p(out.data_ptr()), C.byref(loss), self._s()),
+            "generate_inv_loss_grad_vals_sharded")
+        return loss.value, out
+
+
+def distribute(prob: GraphGPProblem, comm: Comm) -> DistributedGraphGPProblem:
+    """``distribute(prob, comm)`` (ext/GraphGPMPIExt.jl:46-67): the scheme-A view of `prob`."""
+    return DistributedGraphGPProblem(prob, comm)

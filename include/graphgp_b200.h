@@ -245,6 +245,62 @@ int gpb2_generate_inv_loss_grad_vals(gpb2_problem* prob, const void* data_dev, v
                                      double* loss_host, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * Level-sharded operations over several GPUs, one process (or thread) per GPU.  Replaces the
+ * reference's distributed per-level loop (src/distributed.jl:281-331: a host loop over depth
+ * levels with an MPI sum-Allreduce of each level's new values, through the shims of
+ * ext/GraphGPMPIExt.jl:99-115) and its fitting reductions (scheme A, src/distributed.jl:129-247,
+ * ext/GraphGPMPIExt.jl:46-115).  The communicator is NCCL over NVLink, created by the library
+ * from a unique id that rank 0 makes and the caller distributes (MPI, a file, a store):
+ *   gpb2_comm_unique_id(id)                 on one rank; id has GPB2_COMM_ID_BYTES bytes
+ *   gpb2_comm_create(&c, nranks, rank, id, device, timeout_s)   on every rank (collective; a
+ *                                           rank missing after timeout_s ends it with
+ *                                           GPB2_ERR_TIMEOUT; timeout_s <= 0 waits without limit)
+ * Every rank holds the same problem and calls the same operations in the same order, with
+ * full-length inputs in original order; outputs are full length on every rank.  A depth batch of
+ * at least min_shard points (gpb2_comm_set_min_shard, default 65536) is split into one chunk per
+ * rank and completed by an in-place all-gather; smaller batches are computed by every rank.  The
+ * reverse sweeps sum the batch's cotangents over the ranks (reduce-scatter) before scattering;
+ * the vals-gradients end with one all-reduce of the double histogram.  The fitting reductions
+ * split the refined points into contiguous per-rank ranges and end with one all-reduce of
+ * nbins + 4 doubles.  Results equal the single-GPU operations' (the forward bit for bit; sums in
+ * another order within tolerance).
+ * ---------------------------------------------------------------------------------------- */
+#define GPB2_COMM_ID_BYTES 128
+typedef struct gpb2_comm gpb2_comm;
+int gpb2_comm_unique_id(unsigned char* id);
+int gpb2_comm_create(gpb2_comm** out, int nranks, int rank, const unsigned char* id, int device,
+                     double timeout_s);
+int gpb2_comm_set_min_shard(gpb2_comm* comm, int64_t min_shard);
+int gpb2_comm_info(const gpb2_comm* comm, int* nranks, int* rank);
+int gpb2_comm_destroy(gpb2_comm* comm);
+
+/* generate / generate_grad_xi / generate_grad_vals with level-sharded sweeps
+ * (src/distributed.jl:281-331; single-GPU forms src/orchestrate.jl:19-42, src/grad.jl:392-506,
+ * src/grad_generate_vals.jl:111-282). */
+int gpb2_generate_sharded(gpb2_problem* prob, gpb2_comm* comm, const void* xi_dev, void* out_dev,
+                          void* stream);
+int gpb2_generate_grad_xi_sharded(gpb2_problem* prob, gpb2_comm* comm, const void* vbar_dev,
+                                  void* xbar_dev, void* stream);
+int gpb2_generate_grad_vals_sharded(gpb2_problem* prob, gpb2_comm* comm, const void* xi_dev,
+                                    const void* vbar_dev, void* dvals_dev, void* stream);
+/* Fitting reductions, scheme A (src/distributed.jl:129-247): generate_logdet,
+ * generate_logdet_(and_)grad_vals, generate_inv_loss_grad_vals. */
+int gpb2_generate_logdet_sharded(gpb2_problem* prob, gpb2_comm* comm, double* logdet_host,
+                                 void* stream);
+int gpb2_generate_logdet_grad_vals_sharded(gpb2_problem* prob, gpb2_comm* comm, void* dvals_dev,
+                                           double* logdet_host, void* stream);
+int gpb2_generate_inv_loss_grad_vals_sharded(gpb2_problem* prob, gpb2_comm* comm,
+                                             const void* data_dev, void* dvals_dev,
+                                             double* loss_host, void* stream);
+/* The sharding plan of a rank (host only, no GPU): per depth batch b, the forward range
+ * [fwd_lo[b], fwd_hi[b]) the rank computes, the range [own_lo[b], own_hi[b]) whose cotangents it
+ * scatters, whether the batch is split (sharded[b]), and the slack past N the collectives may
+ * touch.  Arrays have n_offsets - 1 entries; any may be NULL. */
+int gpb2_shard_plan(const int64_t* offsets, int64_t n_offsets, int nranks, int rank,
+                    int64_t min_shard, int64_t* fwd_lo, int64_t* fwd_hi, int64_t* own_lo,
+                    int64_t* own_hi, int* sharded, int64_t* slack);
+
+/* ------------------------------------------------------------------------------------------
  * Graph build (host, the input producer of the path).  Restates build_graph
  * (src/graph_build.jl:256-288: special-order tree, preceding k-NN, depths, stable order by
  * depth, 21-bit quantisation, offsets); its output is byte-identical to the reference's.
