@@ -31,6 +31,7 @@
 #include <cooperative_groups.h>
 
 #include "gpb2_problem.h"
+#include "gpb2_sync.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -40,6 +41,7 @@ namespace {
 
 constexpr int kB = 32;          // panel width (= warp size: a lane per row or column)
 constexpr int kSpecMax = 4096;  // concurrent ladder up to this n0
+constexpr int kGridMin = 2048;  // one candidate at a time on the whole GPU above this n0
 
 template <typename T>
 __host__ __device__ constexpr int chol_threads() { return 512; }
@@ -68,6 +70,8 @@ struct CholArgs {
     int* err;         // error word: a bounded wait gave up
     int order[16];    // order[c]: ladder index of candidate slot c (a kernel argument)
     unsigned long long* trace;  // diagnostics (GPB2_TRACE_DENSE): phase timestamps, or NULL
+    GridSync gs;      // whole-grid form: barrier words
+    unsigned int* gctr;  // whole-grid form: the trailing-tile counters (by panel parity)
 };
 
 __device__ __forceinline__ void st_release_gpu(int* p, int v) {
@@ -457,15 +461,18 @@ __device__ __forceinline__ bool chol_stopped(const CholArgs<T>& a, int c, int64_
     return f != 0 && (int64_t)f - 1 < lim;
 }
 
-// One cluster per ladder candidate; the cluster's CTAs split each phase and meet at the
-// hardware cluster barrier (release/acquire at cluster scope), so no grid-wide barrier is
-// needed and candidates proceed independently.  One barrier per panel: rank 0 updates tile
-// (0, 0) -- which holds the next diagonal block -- factors that block, publishes it and solves
-// the tile's rows below it; the other CTAs take the remaining trailing tiles from an atomic
-// counter in rank 0's shared memory, the tiles of the first tile column (which hold the next
-// panel's rows) last, and whoever updates one of those then solves its rows against the
-// published block.  At the barrier the next panel is final.
-template <typename T, int TL>
+// One group of CTAs per ladder candidate.  kGrid = false: a thread-block cluster per candidate,
+// its CTAs meeting at the hardware cluster barrier (release/acquire at cluster scope), so
+// candidates proceed independently (the concurrent ladder of blocks up to a few thousand).
+// kGrid = true: one candidate per cooperative launch on every SM, meeting at the bounded grid
+// barrier (the first layers of the 1e8 / 1e9-point configurations, where one factorisation
+// has enough tiles for the whole GPU).  One barrier per panel: rank 0 updates tile (0, 0) --
+// which holds the next diagonal block -- factors that block, publishes it and solves the tile's
+// rows below it; the other CTAs take the remaining trailing tiles from an atomic counter (in
+// rank 0's shared memory, or in global memory for the grid), the tiles of the first tile column
+// (which hold the next panel's rows) last, and whoever updates one of those then solves its rows
+// against the published block.  At the barrier the next panel is final.
+template <typename T, int TL, bool kGrid>
 __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> a) {
     __shared__ __align__(16) T S[2 * TL][kB + 1];
     __shared__ __align__(16) T Dg[(kB + 1) * kB];
@@ -473,10 +480,33 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
     __shared__ unsigned int s_ctr[2];   // rank 0: next trailing tile (by panel parity)
     __shared__ unsigned int s_next[2];  // this CTA's next tile (double-buffered)
     __shared__ int s_dg;                // panel whose diagonal factor Dg holds (-1: none)
-    cg::cluster_group cl = cg::this_cluster();
-    const int CL = (int)cl.num_blocks();
-    const int rank = (int)cl.block_rank();
-    const int c = (int)(blockIdx.x / CL);
+    int CL, rank, c;
+    if constexpr (kGrid) {
+        CL = (int)gridDim.x;
+        rank = (int)blockIdx.x;
+        c = 0;
+    } else {
+        cg::cluster_group cl = cg::this_cluster();
+        CL = (int)cl.num_blocks();
+        rank = (int)cl.block_rank();
+        c = (int)(blockIdx.x / CL);
+    }
+    // The group's barrier; false when the grid form's bounded wait gave up (its error word is
+    // set and every CTA leaves).
+    auto group_sync = [&]() -> bool {
+        if constexpr (kGrid) {
+            return grid_sync(a.gs);
+        } else {
+            cg::this_cluster().sync();
+            return true;
+        }
+    };
+    auto tile_counter = [&](int parity) -> unsigned int* {
+        if constexpr (kGrid)
+            return a.gctr + parity;
+        else
+            return cg::this_cluster().map_shared_rank(&s_ctr[parity], 0);
+    };
     // A previous launch of the ladder already succeeded (sel is only written between launches).
     if (__ldcg(a.sel) >= 0) return;
     const int npanels = (int)((a.n + kB - 1) / kB);
@@ -497,13 +527,17 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
         s_ctr[0] = 1u;  // tile 0 of every panel is rank 0's
         s_ctr[1] = 1u;
         s_dg = -1;
+        if (kGrid && rank == 0) {
+            a.gctr[0] = 1u;
+            a.gctr[1] = 1u;
+        }
     }
     // Panel 0: its diagonal block, then its rows.
     if (rank == 0) chol_diag(a, c, 0, S, &s_bad);
-    cl.sync();
+    if (!group_sync()) return leave(3000);
     if (chol_stopped(a, c, kB)) return leave(1);
     chol_panel<T>(a, c, 0, rank, CL, Dg, nullptr);
-    cl.sync();
+    if (!group_sync()) return leave(3000);
     for (int k = 0; k < npanels; k++) {
         const int64_t p0 = (int64_t)k * kB;
         unsigned long long* st = tr ? tr + 8 * k : nullptr;
@@ -515,7 +549,7 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
         const int64_t nt = (rows + TL - 1) / TL;
         const unsigned int tiles = (unsigned int)(nt * (nt + 1) / 2);
         const unsigned int inner = (unsigned int)((nt - 1) * nt / 2);  // tiles with bj >= 1
-        unsigned int* ctr = cl.map_shared_rank(&s_ctr[k & 1], 0);
+        unsigned int* ctr = tile_counter(k & 1);
         unsigned int t = 0u;
         if (rank != 0) {
             if (threadIdx.x == 0) s_next[0] = atomicAdd(ctr, 1u);
@@ -584,6 +618,7 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
         }
         if (rank == 0 && threadIdx.x == 0) {
             s_ctr[(k + 1) & 1] = 1u;  // the next panel's counter
+            if (kGrid) a.gctr[(k + 1) & 1] = 1u;
             // Superseded: a smaller ladder step has already factorised, so this candidate can no
             // longer be selected -- stop (after the barrier, with the whole cluster) and free its
             // SMs for candidates still waiting for a slot.
@@ -593,7 +628,7 @@ __global__ void __launch_bounds__(chol_threads<T>()) k_chol_cluster(CholArgs<T> 
             if (sup && !__ldcg(a.fail + c)) a.fail[c] = (int)(p0 + kB) + 1;
         }
         if (st) st[7] = global_ns();
-        cl.sync();
+        if (!group_sync()) return leave(3000);
     }
     if (rank == 0 && threadIdx.x == 0 && !__ldcg(a.fail + c)) a.done[c] = 1;
     leave(1000);
@@ -669,7 +704,7 @@ __global__ void k_ladder_assemble(TableView<T> tv, const uint32_t* __restrict__ 
 template <typename T, int TL>
 int cluster_size() {
     static const int cs = [] {
-        cudaFuncSetAttribute((const void*)k_chol_cluster<T, TL>,
+        cudaFuncSetAttribute((const void*)k_chol_cluster<T, TL, false>,
                              cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         for (int c = 16; c >= 1; c /= 2) {
             cudaLaunchConfig_t cfg = {};
@@ -683,7 +718,7 @@ int cluster_size() {
             cfg.attrs = attr;
             cfg.numAttrs = 1;
             int nclusters = 0;
-            if (cudaOccupancyMaxActiveClusters(&nclusters, (const void*)k_chol_cluster<T, TL>, &cfg) ==
+            if (cudaOccupancyMaxActiveClusters(&nclusters, (const void*)k_chol_cluster<T, TL, false>, &cfg) ==
                     cudaSuccess &&
                 nclusters > 0)
                 return c;
@@ -695,6 +730,64 @@ int cluster_size() {
 }
 
 }  // namespace
+
+// Large first layers: the ladder's candidates one at a time in ladder order, each factorised by
+// the whole GPU (the grid form of k_chol_cluster, a cooperative launch) directly in the factor
+// buffer; once one succeeds the later launches return at once (they read the selection first),
+// so the usual case -- K itself factorises -- costs one factorisation and a few empty launches.
+template <typename T>
+int ladder_grid(gpb2_problem* p, cudaStream_t s, const std::vector<T>& jit, int ncand_used) {
+    const int64_t n = p->n0;
+    const size_t nn = (size_t)n * (size_t)n;
+    GPB2_TRY(ensure_alloc(&p->Ld, sizeof(T) * nn));
+    GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&p->lad), sizeof(int) * kLadInts + sizeof(T) * 16));
+    int* sel = p->lad + kLadSel;
+    T* base = static_cast<T*>(p->Ld);
+    const size_t smem = table_smem_bytes<T>((int)p->nb, p->nkeys);
+    GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_ladder_assemble<T>, smem));
+    constexpr int kTile = sizeof(T) == 4 ? 128 : 64;
+    void (*kern)(CholArgs<T>) = k_chol_cluster<T, kTile, true>;
+    const int grid = coop_grid((const void*)kern, chol_threads<T>(), 0);
+    if (grid <= 0) return set_error(GPB2_ERR_CUDA, "no resident grid for the dense factorisation");
+    GPB2_CUDA_TRY(cudaMemsetAsync(p->lad, 0, sizeof(int) * kLadInts, s));
+    GPB2_CUDA_TRY(cudaMemsetAsync(sel, 0xff, sizeof(int) * 2, s));
+    for (int c = 0; c < ncand_used; c++) {
+        // Per-candidate words (slot 0): failure column, completion, published panel, barrier.
+        GPB2_CUDA_TRY(cudaMemsetAsync(p->lad + kLadFail, 0, sizeof(int), s));
+        GPB2_CUDA_TRY(cudaMemsetAsync(p->lad + kLadDone, 0, sizeof(int), s));
+        GPB2_CUDA_TRY(cudaMemsetAsync(p->lad + kLadDflag, 0, sizeof(int), s));
+        GPB2_CUDA_TRY(cudaMemsetAsync(p->lad + kLadGridBar, 0, sizeof(int), s));
+        SlotJit<T> sj{};
+        sj.v[0] = jit[c];
+        GPB2_CUDA_TRY(launch_prof("dense_assemble", k_ladder_assemble<T>,
+                                  dim3((unsigned)std::min<int64_t>(n, 4 * 148)), dim3(256), smem,
+                                  s, table_view<T>(p), (const uint32_t*)p->coords, (int)p->d,
+                                  coord_stride((int)p->d), (T)p->scale, n, sj, 1, base,
+                                  (const int*)sel));
+        CholArgs<T> args{base, n, 1, c, p->lad + kLadFail, sel, p->lad + kLadDone,
+                         p->lad + kLadDflag, p->lad + kLadBarErr, {}, nullptr,
+                         GridSync{reinterpret_cast<unsigned int*>(p->lad + kLadGridBar),
+                                  p->lad + kLadBarErr},
+                         reinterpret_cast<unsigned int*>(p->lad + kLadGridCtr)};
+        args.order[0] = c;
+        void* argv[] = {(void*)&args};
+        const ProfToken t = prof_begin("dense_chol", s);
+        const cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, grid,
+                                                          chol_threads<T>(), argv, 0, s);
+        prof_end(t, s);
+        GPB2_CUDA_TRY(e);
+        SlotOrder so{};
+        so.v[0] = c;
+        GPB2_CUDA_TRY(launch_prof("dense_mark", k_ladder_mark, dim3(1), dim3(1), 0, s,
+                                  (const int*)(p->lad + kLadDone), so, 1, sel));
+    }
+    // No candidate factorised: the status word records it (the pick kernel copies nothing else:
+    // the factor already sits in its buffer).
+    GPB2_CUDA_TRY(launch_prof("dense_pick", k_ladder_pick<T>, dim3(1), dim3(32), 0, s,
+                              (const T*)base, (const int*)sel, (int64_t)0,
+                              static_cast<T*>(p->Ld), p->lad + kLadNotPD));
+    return GPB2_OK;
+}
 
 template <typename T>
 int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
@@ -712,6 +805,16 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
             epsv[ncand_used] = eps;
             jit[ncand_used++] = eps * dmean;
         }
+    }
+    // Whole-GPU factorisation above this size (GPB2_DENSE_GRID_MIN overrides it).
+    int64_t grid_min = kGridMin;
+    if (const char* e = std::getenv("GPB2_DENSE_GRID_MIN")) grid_min = std::atoll(e);
+    if (n > grid_min) {
+        GPB2_TRY(ladder_grid<T>(p, s, jit, ncand_used));
+        p->ladder_eps.assign(epsv.begin(), epsv.begin() + ncand_used);
+        p->dense_pending = true;  // outcome checked by the call's finishing synchronisation
+        p->dense_launched = true;
+        return GPB2_OK;
     }
     int64_t spec_max = kSpecMax;  // GPB2_DENSE_SPEC_MAX overrides it (tests: force sequential)
     if (const char* e = std::getenv("GPB2_DENSE_SPEC_MAX")) spec_max = std::atoll(e);
@@ -732,7 +835,7 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
     int tile = n <= 2048 ? kTileS : kTileL;
     if (const char* e = std::getenv("GPB2_CHOL_TILE")) tile = std::atoi(e) == kTileL ? kTileL : kTileS;
     void (*kern)(CholArgs<T>) =
-        tile == kTileS ? k_chol_cluster<T, kTileS> : k_chol_cluster<T, kTileL>;
+        tile == kTileS ? k_chol_cluster<T, kTileS, false> : k_chol_cluster<T, kTileL, false>;
     const int csize = tile == kTileS ? cluster_size<T, kTileS>() : cluster_size<T, kTileL>();
     if (csize <= 0) return set_error(GPB2_ERR_CUDA, "no thread-block cluster shape fits");
 

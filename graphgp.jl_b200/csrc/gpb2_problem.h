@@ -106,7 +106,9 @@ constexpr int kLadNotPD = 34;   // set when no candidate succeeded
 constexpr int kLadBarErr = 36;  // error word of the factorisation (0: none)
 constexpr int kLadDflag = 48;   // [48, 64): per-candidate last published diagonal panel
 constexpr int kLadOrder = 64;   // [64, 80): ladder index of each candidate slot of a launch
-constexpr int kLadInts = 80;
+constexpr int kLadGridBar = 80; // grid barrier word of the whole-GPU factorisation
+constexpr int kLadGridCtr = 84; // [84, 86): its trailing-tile counters (by panel parity)
+constexpr int kLadInts = 96;
 
 // RAII: make the problem's device current for the duration of a call, restore afterwards.
 struct DeviceGuard {

@@ -420,6 +420,30 @@ def test_dense_large_tile_and_ladder_switch(cuda_device, dt, monkeypatch):
         assert np.array_equal(prob.dense_factor(), np.tril(L_ora))
 
 
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_dense_whole_gpu_ladder(cuda_device, dt, monkeypatch):
+    # The whole-GPU form (one candidate per cooperative launch, every SM on its trailing
+    # update; the default above n0 = 2048) forced onto the config-2 root block: eight launches
+    # in ladder order, the same step and the same factor bit for bit as the oracle.
+    monkeypatch.setenv("GPB2_DENSE_GRID_MIN", "0")
+    prob, orc = _config_problem(20_000, 2, 1000, 8, dt, 1)
+    gp.generate_logdet(prob)
+    L_ora, jit = O.dense_chol(orc)
+    assert jit > 0
+    assert np.isclose(prob.dense_jitter(), jit, rtol=1e-6)
+    assert np.array_equal(prob.dense_factor(), np.tril(L_ora))
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_dense_whole_gpu_large(cuda_device, dt):
+    # A first layer above the switch (n0 = 3000, D = 3): bit for bit as the oracle.
+    prob, orc = _config_problem(60_000, 3, 3000, 8, dt, 21)
+    gp.generate_logdet(prob)
+    L_ora, jit = O.dense_chol(orc)
+    assert np.isclose(prob.dense_jitter(), jit, rtol=1e-6)
+    assert np.array_equal(prob.dense_factor(), np.tril(L_ora))
+
+
 def test_degenerate_duplicates(cuda_device):
     # test/test_degenerate.jl: 30 exact duplicate points must give finite results everywhere.
     rng = np.random.default_rng(0xDEAD)
