@@ -47,6 +47,18 @@ template <> struct Num<float> {
     // c - a*b with one rounding (adjoint arithmetic only: not part of any exact-order path)
     static __device__ __forceinline__ float fms(float a, float b, float c) { return fmaf(-a, b, c); }
     static __device__ __forceinline__ float div_fast(float a, float b) { return __fdividef(a, b); }
+    // a / b rounded to nearest, given r = RN(1/b): Markstein's correction q0 = RN(a r),
+    // e = a - q0 b (exact with one fused multiply-add), q = RN(q0 + e r) is the correctly rounded
+    // quotient when nothing over- or underflows; operands outside a safe exponent window (and a
+    // zero dividend, whose sign the sequence would lose) take the IEEE division itself.
+    static __device__ __forceinline__ float div_r(float a, float b, float r) {
+        const float q0 = __fmul_rn(a, r);
+        const float e = __fmaf_rn(-q0, b, a);
+        const float q = __fmaf_rn(e, r, q0);
+        const unsigned ea = (__float_as_uint(a) >> 23) & 0xffu, eb = (__float_as_uint(b) >> 23) & 0xffu;
+        const bool safe = (ea - 31u) < 130u && (eb - 97u) < 60u;  // |a| in [2^-96, 2^34), b in [2^-30, 2^30)
+        return safe ? q : __fdiv_rn(a, b);
+    }
     static __device__ __forceinline__ float log(float a) { return logf(a); }
     static __device__ __forceinline__ float from_i64(long long x) { return __ll2float_rn(x); }
     static __device__ __forceinline__ U bits(float x) { return __float_as_uint(x); }
@@ -64,6 +76,16 @@ template <> struct Num<double> {
         return fma(-a, b, c);
     }
     static __device__ __forceinline__ double div_fast(double a, double b) { return a / b; }
+    static __device__ __forceinline__ double div_r(double a, double b, double r) {
+        const double q0 = __dmul_rn(a, r);
+        const double e = __fma_rn(-q0, b, a);
+        const double q = __fma_rn(e, r, q0);
+        const unsigned long long ua = (unsigned long long)__double_as_longlong(a);
+        const unsigned long long ub = (unsigned long long)__double_as_longlong(b);
+        const unsigned ea = (unsigned)((ua >> 52) & 0x7ffu), eb = (unsigned)((ub >> 52) & 0x7ffu);
+        const bool safe = (ea - 223u) < 1024u && (eb - 923u) < 200u;  // |a| in [2^-800, 2^224), b in [2^-100, 2^100)
+        return safe ? q : __ddiv_rn(a, b);
+    }
     static __device__ __forceinline__ double log(double a) { return ::log(a); }
     static __device__ __forceinline__ double from_i64(long long x) { return __ll2double_rn(x); }
     static __device__ __forceinline__ U bits(double x) {
@@ -185,7 +207,7 @@ struct SmemTable {
         whi = t;
         return lo;
     }
-    // lookup() that also returns weights_fast()'s segment and fraction t (w_lo = 1 - t, w_hi = t),
+    // lookup() that also returns weights()'s segment and fraction t (w_lo = 1 - t, w_hi = t),
     // from the same segment search: the value and both weights bit for bit as the two calls.
     __device__ __forceinline__ T lookup_w(T r, int& lo_out, T& t_out) const {
         if (r <= b0) { lo_out = 0; t_out = T(0); return v0; }
@@ -196,21 +218,10 @@ struct SmemTable {
         const T y0 = seg[4 * lo + 2];
         const T slope = seg[4 * lo + 3];
         lo_out = lo;
-        t_out = N::div_fast(N::sub(r, x0), N::sub(x1, x0));
+        t_out = N::div(N::sub(r, x0), N::sub(x1, x0));
         return N::add(y0, N::mul(slope, N::sub(r, x0)));
     }
-    // The same with a fast (not correctly rounded) division: the gradient histograms' weights.
-    __device__ __forceinline__ int weights_fast(T r, T& wlo, T& whi) const {
-        if (r <= b0) { wlo = T(1); whi = T(0); return 0; }
-        if (r >= bN) { wlo = T(0); whi = T(1); return nb - 2; }
-        const int lo = locate(r);
-        const T x0 = seg[4 * lo + 0];
-        const T x1 = seg[4 * lo + 1];
-        const T t = N::div_fast(N::sub(r, x0), N::sub(x1, x0));
-        wlo = N::sub(T(1), t);
-        whi = t;
-        return lo;
-    }
+
 };
 
 // ------------------------------------------------------------------------------------------
@@ -433,9 +444,10 @@ struct PointMath {
 
     // Adjoint of mean_vec_solve!: forward substitution L[0:K,0:K] z = z_in, optionally with
     // the pivot guard (src/kernels_adjoint.jl:520-530) or without it (src/grad.jl:574-580).
-    // Adjoint arithmetic (here and in seed_from_solve / pullback): fused multiply-adds and
-    // multiplication by the pivot reciprocals, not the forward's exact order -- these feed
-    // gradients, which are compared within tolerance.
+    // The adjoint arithmetic (here and in seed_from_solve / pullback) is the reference's
+    // operation order with every operation rounded to nearest, as the forward's: each division
+    // by a pivot is the correctly rounded quotient (div_r, from the pivot's reciprocal), so a
+    // point's cotangents equal the CPU restatement's bit for bit.
     template <bool GUARD>
     static __device__ __forceinline__ void forward_subst(T (&z)[K], const T (&L)[NT],
                                                          const T (&rp)[KP1], T pivfloor) {
@@ -444,12 +456,12 @@ struct PointMath {
             T s = z[i];
             sfor<0, i>([&](auto q_) {
                 GPB2_CI(q);
-                s = N::fms(L[tri(i, q)], z[q], s);
+                s = N::sub(s, N::mul(L[tri(i, q)], z[q]));
             });
             if constexpr (GUARD)
-                z[i] = L[tri(i, i)] > pivfloor ? N::mul(s, rp[i]) : T(0);
+                z[i] = L[tri(i, i)] > pivfloor ? N::div_r(s, L[tri(i, i)], rp[i]) : T(0);
             else
-                z[i] = N::mul(s, rp[i]);
+                z[i] = N::div_r(s, L[tri(i, i)], rp[i]);
         });
     }
 
@@ -462,7 +474,7 @@ struct PointMath {
             B[tri(K, j)] = N::add(B[tri(K, j)], z[j]);
             sfor<0, j + 1>([&](auto i_) {
                 GPB2_CI(i);
-                B[tri(j, i)] = N::fms(z[i], x[j], B[tri(j, i)]);
+                B[tri(j, i)] = N::sub(B[tri(j, i)], N::mul(z[i], x[j]));
             });
         });
     }
@@ -474,24 +486,27 @@ struct PointMath {
                                                     const T (&rp)[KP1]) {
         sfor_down<0, KP1>([&](auto j_) {
             GPB2_CI(j);
+            const T ljj = L[tri(j, j)];
             const T rj = rp[j];
             sfor_down<j + 1, KP1>([&](auto i_) {
                 GPB2_CI(i);
-                const T tbar = N::mul(B[tri(i, j)], rj);  // L-bar[i][j] / L[j][j]
-                B[tri(j, j)] = N::fms(tbar, L[tri(i, j)], B[tri(j, j)]);
+                const T lbij = B[tri(i, j)];
+                const T tbar = N::div_r(lbij, ljj, rj);
+                B[tri(j, j)] = N::sub(B[tri(j, j)], N::div_r(N::mul(lbij, L[tri(i, j)]), ljj, rj));
                 B[tri(i, j)] = tbar;
                 sfor<0, j>([&](auto p_) {
                     GPB2_CI(p);
-                    B[tri(i, p)] = N::fms(tbar, L[tri(j, p)], B[tri(i, p)]);
-                    B[tri(j, p)] = N::fms(tbar, L[tri(i, p)], B[tri(j, p)]);
+                    B[tri(i, p)] = N::sub(B[tri(i, p)], N::mul(tbar, L[tri(j, p)]));
+                    B[tri(j, p)] = N::sub(B[tri(j, p)], N::mul(tbar, L[tri(i, p)]));
                 });
             });
-            const T sbar = N::mul(B[tri(j, j)], N::mul(T(0.5), rj));
+            // 1 / (2 ljj) rounded is rj / 2 exactly (a power-of-two scaling).
+            const T sbar = N::div_r(B[tri(j, j)], N::mul(T(2), ljj), N::mul(T(0.5), rj));
             B[tri(j, j)] = sbar;
             const T s2 = N::mul(T(2), sbar);
             sfor<0, j>([&](auto p_) {
                 GPB2_CI(p);
-                B[tri(j, p)] = N::fms(s2, L[tri(j, p)], B[tri(j, p)]);
+                B[tri(j, p)] = N::sub(B[tri(j, p)], N::mul(s2, L[tri(j, p)]));
             });
         });
     }

@@ -216,12 +216,10 @@ __device__ __forceinline__ void scatter_hist(double* hist, double& bin0,
                                              const SmemTable<T>& tab) {
     using N = Num<T>;
     constexpr int KP1 = K + 1;
-    T dsum = T(0);
     sfor<0, KP1>([&](auto a_) {
         GPB2_CI(a);
-        dsum = N::add(dsum, B[tri(a, a)]);
+        bin0 += (double)B[tri(a, a)];
     });
-    bin0 += (double)dsum;
     sfor<1, KP1>([&](auto a_) {
         GPB2_CI(a);
         sfor<0, a>([&](auto b_) {
@@ -235,7 +233,7 @@ __device__ __forceinline__ void scatter_hist(double* hist, double& bin0,
                 wlo = N::sub(T(1), t);
                 whi = t;
             } else {
-                lo = tab.weights_fast(R[tri(a - 1, b)], wlo, whi);
+                lo = tab.weights(R[tri(a - 1, b)], wlo, whi);
             }
             const T g = B[tri(a, b)];
             atomicAdd(&hist[lo], (double)N::mul(g, wlo));
