@@ -111,12 +111,14 @@ struct Impl {
 
     // original -> tree: dst[i] = src[indices[i]]
     static int gather(P* p, const T* src, T* dst, cudaStream_t s) {
+        if (perm_two_pass(p)) return perm_apply<T>(p, true, src, dst, s);
         return check_launch(launch_prof("gather", k_gather<T>, dim3(grid1d(p->n)), dim3(256), 0,
                                         s, src, (const int*)p->indices, dst, p->n),
                             "gather");
     }
     // tree -> original: dst[indices[i]] = src[i]
     static int scatter(P* p, const T* src, T* dst, cudaStream_t s) {
+        if (perm_two_pass(p)) return perm_apply<T>(p, false, src, dst, s);
         return check_launch(launch_prof("scatter", k_scatter<T>, dim3(grid1d(p->n)), dim3(256), 0,
                                         s, src, (const int*)p->indices, dst, p->n),
                             "scatter");

@@ -257,7 +257,8 @@ static void free_problem(gpb2_problem* p) {
                     p->buf_d,  p->dacc, p->Lcand,   p->lad,  p->Wd,    p->Wd2,
                     p->dwork,  p->dinfo, p->d_offsets, p->dsync, p->Ld,    p->trace,
                     p->Ldr,    p->Dinv,  p->Wtri, p->Ainv,  p->sh_v, p->sh_vb,
-                    p->sh_xg,  p->sh_own};
+                    p->sh_xg,  p->sh_own, p->perm_stage, p->perm_pos_g, p->perm_q_g,
+                    p->perm_pos_s, p->perm_q_s};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);

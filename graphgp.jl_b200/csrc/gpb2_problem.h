@@ -94,6 +94,16 @@ struct gpb2_problem {
     int64_t sh_own_cnt = 0;
     int64_t sh_key[3] = {-1, -1, -1};  // (ranks, rank, min_shard) of sh_own
     bool sh_factor_valid = false;       // mv / sd hold this rank's points for the current table
+
+    // Two-pass permutation plan of large problems (gpb2_perm.cu): staging buffer (N T) and, per
+    // direction (g: original -> tree, s: tree -> original), each input's staging slot and each
+    // output's rank in its destination block.
+    void* perm_stage = nullptr;
+    int* perm_pos_g = nullptr;
+    int* perm_q_g = nullptr;
+    int* perm_pos_s = nullptr;
+    int* perm_q_s = nullptr;
+    int perm_shift = 22;  // log2 of the values per destination block
 };
 
 namespace gpb2 {
@@ -165,6 +175,12 @@ int ensure_alloc(void** ptr, size_t bytes);
 int ensure_capacity(void** ptr, size_t* cap, size_t bytes);
 int ensure_scratch(gpb2_problem* p, bool need_mv);
 int ensure_dense(gpb2_problem* p);
+
+// The original <-> tree permutation in two streaming passes (gpb2_perm.cu), for problems whose
+// field outgrows the L2 (perm_two_pass); the plan is built on first use.
+bool perm_two_pass(const gpb2_problem* p);
+template <typename T>
+int perm_apply(gpb2_problem* p, bool to_tree, const T* in, T* out, cudaStream_t s);
 
 // Dense first layer (gpb2_dense.cu).  All on `s`; factor() synchronises once to read the
 // Cholesky status (the jitter ladder of src/dense.jl:46-67 branches on it).

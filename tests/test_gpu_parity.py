@@ -528,3 +528,21 @@ def test_large_roundtrip_and_linearity_f32(cuda_device):
     assert abs(lhs - rhs) <= 1e-4 * abs(lhs)
     dv = gp.generate_grad_vals(prob, xi, vb)
     assert torch.isfinite(dv).all()
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_two_pass_permutation(cuda_device, dt, monkeypatch):
+    # The two-pass original <-> tree permutation of large fields (forced here on a 3e5-point
+    # problem, with 4096-value destination blocks: 74 blocks, the last one partial) gives the
+    # direct gather / scatter's results bit for bit.
+    monkeypatch.setenv("GPB2_PERM_BLOCK_SHIFT", "12")
+    prob, orc = _config_problem(300_000, 2, 500, 8, dt, 9)
+    rng = np.random.default_rng(3)
+    xi = torch.from_numpy(rng.standard_normal(prob.npoints()).astype(dt)).to(cuda_device)
+    vb = torch.from_numpy(rng.standard_normal(prob.npoints()).astype(dt)).to(cuda_device)
+    monkeypatch.setenv("GPB2_PERM_TWO_PASS_MIN", str(1 << 40))
+    ref = (gp.generate(prob, xi), gp.generate_grad_xi(prob, vb), gp.generate_inv(prob, xi))
+    monkeypatch.setenv("GPB2_PERM_TWO_PASS_MIN", "0")
+    got = (gp.generate(prob, xi), gp.generate_grad_xi(prob, vb), gp.generate_inv(prob, xi))
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
