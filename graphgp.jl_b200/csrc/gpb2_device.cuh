@@ -406,6 +406,9 @@ struct PointMath {
             const bool ok = s > pivmin;
             const T d = N::sqrt(ok ? s : pivmin);
             L[tri(j, j)] = d;
+            // t / d for the column's entries: the correctly rounded quotients, from one rounded
+            // reciprocal of the pivot (div_r), the same bits as the IEEE divisions.
+            const T rd = N::div(T(1), d);
             sfor<j + 1, KP1>([&](auto i_) {
                 GPB2_CI(i);
                 T t = L[tri(i, j)];
@@ -413,7 +416,7 @@ struct PointMath {
                     GPB2_CI(p);
                     t = N::sub(t, N::mul(L[tri(i, p)], L[tri(j, p)]));
                 });
-                L[tri(i, j)] = ok ? N::div(t, d) : T(0);
+                L[tri(i, j)] = ok ? N::div_r(t, d, rd) : T(0);
             });
         });
     }

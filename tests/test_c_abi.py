@@ -8,6 +8,7 @@ import numpy as np
 import pytest
 
 from conftest import ROOT, relerr
+from oracle import oracle as O
 
 SRC = os.path.join(ROOT, "tests", "c", "abi_generate.c")
 LIBDIR = os.path.join(ROOT, "graphgp.jl_b200")
@@ -53,4 +54,7 @@ def test_c_program_generate(tmp_path, golden, cuda_device):
     assert r.returncode == 0, r.stderr
     out = np.fromfile(tmp_path / "out.f64", np.float64)
     assert relerr(out[:n], d["generate_field"]) < 1e-12
-    assert abs(out[n] - float(d["logdet64"])) < 1e-10 * abs(float(d["logdet64"]))
+    orc = O.make_problem(d["coords"], d["neighbors"], d["offsets"], d["n0"], d["scale"],
+                         d["cov_bins64"], d["cov_vals64"], d["indices"], np.float64)
+    ld = O.generate_logdet(orc)
+    assert abs(out[n] - ld) < 1e-12 * abs(ld)

@@ -541,8 +541,10 @@ def test_two_pass_permutation(cuda_device, dt, monkeypatch):
     xi = torch.from_numpy(rng.standard_normal(prob.npoints()).astype(dt)).to(cuda_device)
     vb = torch.from_numpy(rng.standard_normal(prob.npoints()).astype(dt)).to(cuda_device)
     monkeypatch.setenv("GPB2_PERM_TWO_PASS_MIN", str(1 << 40))
-    ref = (gp.generate(prob, xi), gp.generate_grad_xi(prob, vb), gp.generate_inv(prob, xi))
+    ref = (gp.generate(prob, xi), gp.generate_inv(prob, xi), gp.generate_grad_xi(prob, vb))
     monkeypatch.setenv("GPB2_PERM_TWO_PASS_MIN", "0")
-    got = (gp.generate(prob, xi), gp.generate_grad_xi(prob, vb), gp.generate_inv(prob, xi))
-    for a, b in zip(got, ref):
-        assert torch.equal(a, b)
+    got = (gp.generate(prob, xi), gp.generate_inv(prob, xi), gp.generate_grad_xi(prob, vb))
+    assert torch.equal(got[0], ref[0])
+    assert torch.equal(got[1], ref[1])
+    # The reverse sweep's atomic sums are not reproducible bit for bit from run to run.
+    assert relerr(got[2].cpu().numpy(), ref[2].cpu().numpy()) < TOL[dt]
