@@ -430,6 +430,14 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
     flush_hist(gacc, hist, a.tab.nb);
 }
 
+// Grid-wide lane index of the persistent sweeps: a warp takes 32 consecutive points (its loads
+// are contiguous and, in library order, its points' neighbours are close together), and
+// consecutive warps sit on consecutive CTAs (one per SM), so a small batch still spreads over
+// every SM's load units instead of queueing on the first few.
+__device__ __forceinline__ int64_t sweep_gtid() {
+    return ((int64_t)(threadIdx.x >> 5) * gridDim.x + blockIdx.x) * 32 + (threadIdx.x & 31);
+}
+
 // ---------------------------------------------------------------------------------------------
 // Per-batch kernels.
 // ---------------------------------------------------------------------------------------------
@@ -538,9 +546,7 @@ k_sweep_fwd_all(T* __restrict__ values, const T* __restrict__ xi_ref, const T* _
                 const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
                 const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
     using N = Num<T>;
-    // Consecutive points go to consecutive CTAs (one per SM), so a small batch is spread over
-    // every SM's load units instead of queueing on the first few.
-    const int64_t gtid = (int64_t)threadIdx.x * gridDim.x + blockIdx.x;
+    const int64_t gtid = sweep_gtid();
     const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
     SweepPoint<T, K> sp;
     int64_t p = offs[0] + gtid;
@@ -632,9 +638,7 @@ k_sweep_rev_all(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv
                 const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
                 const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
     using N = Num<T>;
-    // Consecutive points go to consecutive CTAs (one per SM), so a small batch is spread over
-    // every SM's load units instead of queueing on the first few.
-    const int64_t gtid = (int64_t)threadIdx.x * gridDim.x + blockIdx.x;
+    const int64_t gtid = sweep_gtid();
     const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
     SweepPoint<T, K> sp;
     int64_t p = offs[nbatch - 1] + gtid;
@@ -674,7 +678,7 @@ k_sweep_fwdrev_all(T* __restrict__ values, const T* __restrict__ xi_ref, T* __re
                    const int* __restrict__ nbrs, int64_t n0, const int64_t* __restrict__ offs,
                    int nbatch, GridSync gs) {
     using N = Num<T>;
-    const int64_t gtid = (int64_t)threadIdx.x * gridDim.x + blockIdx.x;
+    const int64_t gtid = sweep_gtid();
     const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
     SweepPoint<T, K> fp, rp;
     int64_t pf = offs[0] + gtid, pr = offs[nbatch - 1] + gtid;

@@ -42,6 +42,22 @@ __global__ void k_scatter(const T* __restrict__ src, const int* __restrict__ idx
         dst[idx[i]] = src[i];
 }
 
+// Between the reference's tree order and the library's (gpb2_order.cu), over positions
+// [base, base + n): to_lib: dst[q] = src[map[base + q] - base]; else dst[map[base + q] - base] =
+// src[q].
+template <typename T>
+__global__ void k_lib_move(const T* __restrict__ src, T* __restrict__ dst,
+                           const int* __restrict__ map, int64_t base, int64_t n, int to_lib) {
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n;
+         q += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = (int64_t)map[base + q] - base;
+        if (to_lib)
+            dst[q] = src[t];
+        else
+            dst[t] = src[q];
+    }
+}
+
 template <typename T>
 __global__ void k_hist_to_t(const double* __restrict__ acc, T* __restrict__ out, int64_t nb) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nb;
@@ -252,7 +268,52 @@ struct Impl {
         return GPB2_OK;
     }
 
-    // ---------------------------------------------------------------- refine layer (tree order)
+    // ---------------------------------------------------------------- tree order <-> library order
+    static int lib_move(P* p, const T* src, T* dst, int64_t base, int64_t n, bool to_lib,
+                        cudaStream_t s) {
+        return check_launch(launch_prof("order", k_lib_move<T>, dim3(grid1d(n)), dim3(256), 0, s,
+                                        src, dst, (const int*)p->lib_tree, base, n,
+                                        to_lib ? 1 : 0),
+                            "order");
+    }
+    // The reference's tree-order entry points: inputs into library order, the operation, outputs
+    // back (positions [0, n0) are the same in both orders).
+    static int refine_tree(P* p, T* values, const T* xi_ref, cudaStream_t s) {
+        if (!p->lib_tree) return refine(p, values, xi_ref, s);
+        GPB2_TRY(ensure_scratch(p, true));
+        T* vl = (T*)p->buf_a;
+        T* xl = (T*)p->buf_b;
+        GPB2_TRY(lib_move(p, xi_ref, xl, p->n0, p->m, true, s));
+        GPB2_CUDA_TRY(cudaMemcpyAsync(vl, values, sizeof(T) * p->n0, cudaMemcpyDeviceToDevice, s));
+        GPB2_TRY(refine(p, vl, xl, s));
+        return lib_move(p, vl + p->n0, values + p->n0, p->n0, p->m, false, s);
+    }
+    static int refine_inv_tree(P* p, const T* values, T* xi_ref, cudaStream_t s) {
+        if (!p->lib_tree) return refine_inv(p, values, xi_ref, s);
+        GPB2_TRY(ensure_scratch(p, false));
+        T* vl = (T*)p->buf_a;
+        T* xl = (T*)p->buf_b;
+        GPB2_TRY(lib_move(p, values, vl, 0, p->n, true, s));
+        GPB2_TRY(refine_inv(p, vl, xl, s));
+        return lib_move(p, xl, xi_ref, p->n0, p->m, false, s);
+    }
+    static int refine_logdet_tree(P* p, T* terms, double* out, cudaStream_t s) {
+        if (!p->lib_tree || !terms) return refine_logdet(p, terms, out, s);
+        GPB2_TRY(ensure_scratch(p, false));
+        T* tl = (T*)p->buf_b;
+        GPB2_TRY(refine_logdet(p, tl, out, s));
+        return lib_move(p, tl, terms, p->n0, p->m, false, s);
+    }
+    static int refine_inv_loss_tree(P* p, const T* values, T* dvals, double* loss,
+                                    cudaStream_t s) {
+        if (!p->lib_tree) return refine_inv_loss_grad_vals(p, values, dvals, loss, s);
+        GPB2_TRY(ensure_scratch(p, false));
+        T* vl = (T*)p->buf_b;
+        GPB2_TRY(lib_move(p, values, vl, 0, p->n, true, s));
+        return refine_inv_loss_grad_vals(p, vl, dvals, loss, s);
+    }
+
+    // ---------------------------------------------------------------- refine layer (library order)
     static int refine(P* p, T* values, const T* xi_ref, cudaStream_t s) {
         GPB2_TRY(ensure_scratch(p, true));
         return refine_sweep(p, values, xi_ref, false, s);
@@ -905,8 +966,8 @@ int gpb2_set_forward_mode(int mode) {
 
 int gpb2_refine(gpb2_problem* p, void* values, const void* xi_ref, void* stream) {
     GPB2_TRY(need(values, "values") | need(xi_ref, "xi_ref"));
-    GPB2_DISPATCH(p, Impl<float>::refine(p, F32(values), CF32(xi_ref), s),
-                  Impl<double>::refine(p, F64(values), CF64(xi_ref), s));
+    GPB2_DISPATCH(p, Impl<float>::refine_tree(p, F32(values), CF32(xi_ref), s),
+                  Impl<double>::refine_tree(p, F64(values), CF64(xi_ref), s));
 }
 
 // [lo, hi) must lie inside one depth batch (the ranges of a level-sharded sweep).
@@ -965,14 +1026,14 @@ int gpb2_dense_apply(gpb2_problem* p, int trans, const void* x, void* y, void* s
 
 int gpb2_refine_inv(gpb2_problem* p, const void* values, void* xi_ref, void* stream) {
     GPB2_TRY(need(values, "values") | need(xi_ref, "xi_ref"));
-    GPB2_DISPATCH(p, Impl<float>::refine_inv(p, CF32(values), F32(xi_ref), s),
-                  Impl<double>::refine_inv(p, CF64(values), F64(xi_ref), s));
+    GPB2_DISPATCH(p, Impl<float>::refine_inv_tree(p, CF32(values), F32(xi_ref), s),
+                  Impl<double>::refine_inv_tree(p, CF64(values), F64(xi_ref), s));
 }
 
 int gpb2_refine_logdet_terms(gpb2_problem* p, void* terms, void* stream) {
     GPB2_TRY(need(terms, "terms"));
-    GPB2_DISPATCH(p, Impl<float>::refine_logdet(p, F32(terms), nullptr, s),
-                  Impl<double>::refine_logdet(p, F64(terms), nullptr, s));
+    GPB2_DISPATCH(p, Impl<float>::refine_logdet_tree(p, F32(terms), nullptr, s),
+                  Impl<double>::refine_logdet_tree(p, F64(terms), nullptr, s));
 }
 
 int gpb2_refine_logdet(gpb2_problem* p, double* out, void* stream) {
@@ -990,8 +1051,8 @@ int gpb2_refine_logdet_grad_vals(gpb2_problem* p, void* dvals, double* ld, void*
 int gpb2_refine_inv_loss_grad_vals(gpb2_problem* p, const void* values, void* dvals,
                                    double* loss, void* stream) {
     GPB2_TRY(need(values, "values") | need(dvals, "dvals"));
-    GPB2_DISPATCH(p, Impl<float>::refine_inv_loss_grad_vals(p, CF32(values), F32(dvals), loss, s),
-                  Impl<double>::refine_inv_loss_grad_vals(p, CF64(values), F64(dvals), loss, s));
+    GPB2_DISPATCH(p, Impl<float>::refine_inv_loss_tree(p, CF32(values), F32(dvals), loss, s),
+                  Impl<double>::refine_inv_loss_tree(p, CF64(values), F64(dvals), loss, s));
 }
 
 int gpb2_generate(gpb2_problem* p, const void* xi, void* out, void* stream) {

@@ -258,7 +258,7 @@ static void free_problem(gpb2_problem* p) {
                     p->dwork,  p->dinfo, p->d_offsets, p->dsync, p->Ld,    p->trace,
                     p->Ldr,    p->Dinv,  p->Wtri, p->Ainv,  p->sh_v, p->sh_vb,
                     p->sh_xg,  p->sh_own, p->perm_stage, p->perm_pos_g, p->perm_q_g,
-                    p->perm_pos_s, p->perm_q_s};
+                    p->perm_pos_s, p->perm_q_s, p->lib_tree};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);
@@ -460,6 +460,8 @@ static int create_impl(gpb2_problem** out, int dtype, int device, const uint32_t
                 break;
             }
         }
+        // Library order: every depth batch sorted by Morton code (all arrays above).
+        if ((st = library_order(p, s))) break;
         // Table.
         const size_t ts = tsize(p);
         if ((st = ensure_alloc(&p->bins, ts * nbins))) break;
@@ -517,6 +519,32 @@ int gpb2_problem_info(const gpb2_problem* p, int64_t* n, int64_t* m, int64_t* k,
     if (k) *k = p->k;
     if (d) *d = p->d;
     if (n_batches) *n_batches = (int64_t)p->offsets.size() - 1;
+    return GPB2_OK;
+}
+
+int gpb2_problem_order(const gpb2_problem* p, int32_t* lib_tree_dev, int32_t* lib_orig_dev,
+                       void* stream) {
+    clear_error();
+    if (!p) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_order: NULL problem");
+    DeviceGuard dg(p->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    std::vector<int> iota;
+    auto fill = [&](int32_t* dst, const int* src) -> int {
+        if (!dst) return GPB2_OK;
+        if (src) {
+            GPB2_CUDA_TRY(cudaMemcpyAsync(dst, src, sizeof(int) * p->n, cudaMemcpyDeviceToDevice, s));
+            return GPB2_OK;
+        }
+        if (iota.empty()) {
+            iota.resize((size_t)p->n);
+            for (int64_t i = 0; i < p->n; i++) iota[(size_t)i] = (int)i;
+        }
+        GPB2_CUDA_TRY(cudaMemcpyAsync(dst, iota.data(), sizeof(int) * p->n, cudaMemcpyHostToDevice, s));
+        GPB2_CUDA_TRY(cudaStreamSynchronize(s));  // iota is a host temporary
+        return GPB2_OK;
+    };
+    GPB2_TRY(fill(lib_tree_dev, p->lib_tree));
+    GPB2_TRY(fill(lib_orig_dev, p->indices));
     return GPB2_OK;
 }
 

@@ -23,7 +23,9 @@ struct gpb2_problem {
     // Device copies owned by the handle.
     uint32_t* coords = nullptr;  // (N, coord_stride(D))
     int* nbrs = nullptr;         // (M, K) int32, 0-based
-    int* indices = nullptr;      // (N) tree -> original, 0-based; nullptr = identity
+    int* indices = nullptr;      // (N) library -> original, 0-based; nullptr = identity
+    int* lib_tree = nullptr;     // (N) library -> tree position (gpb2_order.cu); nullptr = the
+                                 // tree order itself (the arrays above are in library order)
     void* bins = nullptr;        // (nb) T
     void* vals = nullptr;        // (nb) T
     void* seg = nullptr;         // 4 * (nb - 1) T
@@ -179,6 +181,9 @@ int ensure_dense(gpb2_problem* p);
 // The original <-> tree permutation in two streaming passes (gpb2_perm.cu), for problems whose
 // field outgrows the L2 (perm_two_pass); the plan is built on first use.
 bool perm_two_pass(const gpb2_problem* p);
+
+// Re-sorts every depth batch of a freshly uploaded problem by Morton code (gpb2_order.cu).
+int library_order(gpb2_problem* p, cudaStream_t s);
 template <typename T>
 int perm_apply(gpb2_problem* p, bool to_tree, const T* in, T* out, cudaStream_t s);
 

@@ -80,6 +80,7 @@ _SIGNATURES = {
                                   I64, I64, C.c_double, P, P, I64, PI64, I32, P]),
     "gpb2_problem_create_dev": (I32, [C.POINTER(P), I32, I32, P, I64, I64, P, I32, I32, I64,
                                       PI64, I64, I64, C.c_double, P, P, I64, P, I32, I32, P]),
+    "gpb2_problem_order": (I32, [P, P, P, P]),
     "gpb2_problem_set_vals": (I32, [P, P, P]),
     "gpb2_problem_prefactor": (I32, [P, P]),
     "gpb2_problem_info": (I32, [P, PI64, PI64, PI64, PI64, PI64]),

@@ -115,9 +115,14 @@ class ShardedGenerate:
         self.device = torch.device(device) if device is not None else prob.device
         self.dtype = prob.torch_dtype
         self.n, self.n0 = prob.npoints(), int(prob.n0)
-        idx = prob.indices
-        self.indices = None if idx is None else torch.as_tensor(np.asarray(idx, np.int64),
-                                                                device=self.device)
+        if ops is None:
+            # The library's range entry points index in its internal order (every depth batch
+            # sorted by Morton code): map original <-> library positions.
+            self.indices = prob.library_order()[1].to(device=self.device, dtype=torch.int64)
+        else:
+            idx = prob.indices
+            self.indices = None if idx is None else torch.as_tensor(np.asarray(idx, np.int64),
+                                                                    device=self.device)
         self.nccl = dist.get_backend(group) == "nccl"
 
     # -- collectives --------------------------------------------------------------------------

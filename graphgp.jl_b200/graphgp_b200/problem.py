@@ -197,6 +197,19 @@ class GraphGPProblem:
         _lib.check(st, "check")
         return self
 
+    def library_order(self):
+        """(lib_tree, lib_orig): the library's internal point order (gpb2_problem_order) as two
+        int32 device tensors, library position -> tree position and -> original index.  Inside
+        the handle every depth batch is sorted by Morton code; the range entry points
+        (gpb2_refine_range, gpb2_refine_reverse_range) index in this order."""
+        lt = torch.empty(self._N, dtype=torch.int32, device=self.device)
+        lo = torch.empty(self._N, dtype=torch.int32, device=self.device)
+        st = _lib.lib().gpb2_problem_order(
+            self.handle, C.c_void_p(lt.data_ptr()), C.c_void_p(lo.data_ptr()),
+            C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        _lib.check(st, "library_order")
+        return lt, lo
+
     def dense_jitter(self) -> float:
         """Relative jitter of the dense block's last factorisation (0.0 = none needed, -1.0 =
         not factorised yet), the ladder of src/dense.jl:46-67."""

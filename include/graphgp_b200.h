@@ -87,6 +87,17 @@ int gpb2_problem_create_dev(gpb2_problem** out, int dtype, int device,
                             int64_t nbins, const void* indices_dev, int indices_bytes,
                             int indices_base, void* stream);
 
+/* The library's internal point order.  Inside the handle every depth batch is sorted by the
+ * Morton code of its points (the batches, the dense first layer's positions [0, n0) and every
+ * point's neighbour list are unchanged, so every result is the same; the gathers of a warp's
+ * points become coalesced).  The operations in original order and the tree-order refine entry
+ * points translate at the boundary; the range entry points (gpb2_refine_range,
+ * gpb2_refine_reverse_range) work in library order.  This call copies the two maps, N int32 each,
+ * into device buffers: lib_tree_dev[q] = tree position of library position q, lib_orig_dev[q] =
+ * original index (either may be NULL).  No reference counterpart. */
+int gpb2_problem_order(const gpb2_problem* prob, int32_t* lib_tree_dev, int32_t* lib_orig_dev,
+                       void* stream);
+
 /* Replace the covariance values (`_set_vals`, src/chainrules.jl:18-21). */
 int gpb2_problem_set_vals(gpb2_problem* prob, const void* vals_dev, void* stream);
 
@@ -161,6 +172,8 @@ int gpb2_refine(gpb2_problem* prob, void* values_dev, const void* xi_ref_dev, vo
  * (each rank runs its slice of a batch, the caller exchanges the batch between ranks; the
  * exchange replaces the reference's MPI/serial level loop, src/distributed.jl:293-322 and
  * src/api.jl:113-141).  [lo, hi) are tree-order point indices inside one batch (n0 <= lo).
+ * Positions are the library's order (gpb2_problem_order): the batches' bounds are the tree
+ * order's, the points inside a batch are permuted.
  * Asynchronous on `stream` (no synchronisation; launch errors are returned).
  *   refine_range:          values[p] = std_p*xi_ref[p-n0] + sum_j mv_pj*values[nbr_pj]
  *                          (refine_apply_fused_kernel!, src/kernels.jl:101-119)

@@ -548,3 +548,41 @@ def test_two_pass_permutation(cuda_device, dt, monkeypatch):
     assert torch.equal(got[1], ref[1])
     # The reverse sweep's atomic sums are not reproducible bit for bit from run to run.
     assert relerr(got[2].cpu().numpy(), ref[2].cpu().numpy()) < TOL[dt]
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_library_order(cuda_device, dt, monkeypatch):
+    # Inside the handle every depth batch is re-sorted by Morton code.  The maps are a
+    # within-batch permutation (identity on the dense block), and every result -- in original
+    # order and through the tree-order refine entry points -- is the one the reference's tree
+    # order gives, bit for bit where the arithmetic has a fixed order.
+    prob, orc = _config_problem(120_000, 3, 700, 8, dt, 13)
+    monkeypatch.setenv("GPB2_TREE_ORDER", "1")
+    ref = gp.GraphGPProblem(prob.coords, prob.neighbors, prob.offsets, prob.n0, prob.scale,
+                            prob.bins, prob.vals, prob.indices, dtype=dt)
+    ref.handle
+    monkeypatch.delenv("GPB2_TREE_ORDER")
+    lt, lo = (t.cpu().numpy() for t in prob.library_order())
+    n0 = prob.n0
+    assert np.array_equal(lt[:n0], np.arange(n0))
+    offs = prob.offsets
+    for a, b in zip(offs[:-1], offs[1:]):
+        assert np.array_equal(np.sort(lt[a:b]), np.arange(a, b))
+    assert np.array_equal(lo, prob.indices[lt])
+    assert not np.array_equal(lt, np.arange(len(lt)))  # the order did change
+    rng = np.random.default_rng(4)
+    xi = rng.standard_normal(prob.npoints()).astype(dt)
+    iv = rng.standard_normal(n0).astype(dt)
+    xr = rng.standard_normal(prob.nrefined()).astype(dt)
+    f = gp.generate(prob, xi)
+    assert np.array_equal(f, gp.generate(ref, xi))
+    assert np.array_equal(gp.generate_inv(prob, f), gp.generate_inv(ref, f))
+    v = gp.refine(prob, iv, xr)
+    assert np.array_equal(v, gp.refine(ref, iv, xr))
+    assert np.array_equal(v, O.refine(orc, iv, xr))
+    assert np.array_equal(gp.refine_inv(prob, v), gp.refine_inv(ref, v))
+    assert np.array_equal(gp.refine_logdet_terms(prob), gp.refine_logdet_terms(ref))
+    l1, l2 = gp.refine_inv_loss_grad_vals(prob, v), gp.refine_inv_loss_grad_vals(ref, v)
+    assert abs(l1[0] - l2[0]) <= TOL[dt] * abs(l2[0]) and relerr(l1[1], l2[1]) < TOL[dt]
+    assert abs(gp.generate_logdet(prob) - gp.generate_logdet(ref)) <= \
+        TOL[dt] * abs(gp.generate_logdet(ref))
