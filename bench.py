@@ -459,12 +459,16 @@ def run_b200(args):
                 else "fallback 6650 GB/s (of fallback)")
 
     def profile(fn, k):
+        # Kernels in sequence for the per-launch events (an event pair around a kernel that
+        # shares the GPU with another stream's would also time the wait for SMs).
+        L.gpb2_set_overlap(0)
         L.gpb2_profile_reset()
         L.gpb2_profile_enable(1)
         timed(fn, k)
         L.gpb2_profile_enable(0)
         prof = _lib.profile_report()
         L.gpb2_profile_reset()
+        L.gpb2_set_overlap(1)
         return prof
 
     def points_per_launch(kind, cnt, k):

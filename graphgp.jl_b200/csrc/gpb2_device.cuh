@@ -118,10 +118,20 @@ struct SmemWeights {
     uint16_t* lo = nullptr;
     int stride = 0;
 };
+// The same weights in the problem's factor cache: one slab of M entries per pair (entry i of
+// point m at [i * stride + m], so a warp's 32 points read one contiguous run per entry).
+template <typename T>
+struct SlabWeights {
+    T* t = nullptr;
+    uint16_t* lo = nullptr;
+    int64_t stride = 0;
+};
 template <typename RT>
 struct is_weight_store : std::false_type {};
 template <typename T>
 struct is_weight_store<SmemWeights<T>> : std::true_type {};
+template <typename T>
+struct is_weight_store<SlabWeights<T>> : std::true_type {};
 
 // ------------------------------------------------------------------------------------------
 // Interpolation table (built on the host by the problem handle, see gpb2_problem.cu).
@@ -381,7 +391,7 @@ struct PointMath {
                     int lo;
                     T t;
                     L[tri(a, b)] = tab.lookup_w(r, lo, t);
-                    const int i = tri(a - 1, b) * R.stride;
+                    const auto i = tri(a - 1, b) * R.stride;
                     R.lo[i] = (uint16_t)lo;
                     R.t[i] = t;
                 } else {

@@ -20,6 +20,21 @@
 
 namespace gpb2 {
 
+// Per-point factor cache of a problem (slab layout: entry e of point m at [e * stride + m], so a
+// warp's 32 consecutive points touch one contiguous run per entry): the packed Cholesky factor
+// of every refined point (NT slabs) and the interpolation segment and fraction of each of its
+// pair radii (NR slabs each).  The factor pass writes it; the vals-gradient kernels read it
+// instead of gathering coordinates, interpolating the covariance and factorising again.  The
+// entries are the bits the recomputation would produce (the same code writes them).  Null
+// pointers: no cache.
+template <typename T>
+struct FactorCache {
+    T* L = nullptr;
+    T* t = nullptr;
+    uint16_t* lo = nullptr;
+    int64_t stride = 0;
+};
+
 template <typename T>
 struct PointArgs {
     TableView<T> tab;
@@ -27,6 +42,7 @@ struct PointArgs {
     const int* nbrs;         // (M, K) int32, 0-based
     int64_t n0;
     T scale;
+    FactorCache<T> fc;  // write target of k_factor / source of the gradient kernels, or none
 };
 
 constexpr int kFlatThreads = 128;
@@ -123,6 +139,26 @@ struct PointFactor {
         PM::template assemble<KEEP_R>(L, R, jc, a.scale, tab);
         PM::chol(L);
     }
+    // The factor cache's slab columns of point m (R must be a SlabWeights).
+    __device__ __forceinline__ void bind_cache(const PointArgs<T>& a, int64_t m) {
+        R.t = a.fc.t + m;
+        R.lo = a.fc.lo + m;
+        R.stride = a.fc.stride;
+    }
+    __device__ __forceinline__ void load_cached(const PointArgs<T>& a, int64_t m) {
+        load_row_i32<K>(nb, a.nbrs + m * K);
+        sfor<0, PM::NT>([&](auto e_) {
+            GPB2_CI(e);
+            L[e] = __ldcs(a.fc.L + e * a.fc.stride + m);
+        });
+        bind_cache(a, m);
+    }
+    __device__ __forceinline__ void store_cached(const PointArgs<T>& a, int64_t m) const {
+        sfor<0, PM::NT>([&](auto e_) {
+            GPB2_CI(e);
+            a.fc.L[e * a.fc.stride + m] = L[e];
+        });
+    }
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -137,7 +173,8 @@ __device__ __forceinline__ int64_t point_of(int64_t t, int64_t m0, const int* __
 
 // Conditional-mean weights and std of points [m_begin, m_end) (refine_meanvec_std_kernel!,
 // src/kernels.jl:61-78): mv is (M, K) point-major, sd is (M).
-template <typename T, int K, int D>
+// With FILL the point's factor and pair weights also go to the factor cache (a.fc).
+template <typename T, int K, int D, bool FILL>
 __global__ void __launch_bounds__(kFlatThreads)
 k_factor(PointArgs<T> a, int64_t m_begin, int64_t m_end, T* __restrict__ mv, T* __restrict__ sd) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -146,8 +183,12 @@ k_factor(PointArgs<T> a, int64_t m_begin, int64_t m_end, T* __restrict__ mv, T* 
     __syncthreads();
     for (int64_t m = m_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < m_end;
          m += (int64_t)gridDim.x * blockDim.x) {
-        PointFactor<T, K, D, false> f;
+        using RT = typename std::conditional<FILL, SlabWeights<T>,
+                                             RegArr<T, PointMath<T, K, D>::NR>>::type;
+        PointFactor<T, K, D, FILL, RT> f;
+        if constexpr (FILL) f.bind_cache(a, m);
         f.compute(a, tab, m);
+        if constexpr (FILL) f.store_cached(a, m);
         T x[K];
         PointMath<T, K, D>::solve(x, f.L, a.tab.pivc);
         store_row_t<T, K>(mv + m * K, x);
@@ -227,7 +268,7 @@ __device__ __forceinline__ void scatter_hist(double* hist, double& bin0,
             T wlo, whi;
             int lo;
             if constexpr (is_weight_store<RT>::value) {
-                const int i = tri(a - 1, b) * R.stride;
+                const auto i = tri(a - 1, b) * R.stride;
                 const T t = R.t[i];
                 lo = R.lo[i];
                 wlo = N::sub(T(1), t);
@@ -261,9 +302,43 @@ struct GradShape {
     static constexpr int kThreads = kUse ? kWide : kFlatThreads;
     static constexpr int kMinBlocks = kUse ? 2 : 1;
     using Store = RadiusStore<T, K, D, kThreads, kUse ? 72 * 1024 : 36 * 1024>;
+    // The point factor of a histogram kernel: recomputed (pair weights in Store), or read from
+    // the factor cache (pair weights in its slabs).
+    template <bool CACHED>
+    using Factor = PointFactor<T, K, D, true,
+                               typename std::conditional<CACHED, SlabWeights<T>,
+                                                         typename Store::type>::type>;
 };
 
-template <typename T, int K, int D>
+// Shared-memory layout of the histogram kernels: [table][histogram][pair-weight store] when the
+// factor is recomputed, the histogram alone when it comes from the factor cache (the cached
+// weights replace every table search).
+template <typename T, bool CACHED>
+__device__ __forceinline__ void grad_smem(const PointArgs<T>& a, SmemTable<T>& tab,
+                                          unsigned char* smem, double*& hist,
+                                          unsigned char*& rbase) {
+    if constexpr (CACHED) {
+        hist = reinterpret_cast<double*>(smem);
+        rbase = nullptr;
+    } else {
+        tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
+        hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
+        rbase = smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys) + sizeof(double) * a.tab.nb;
+    }
+}
+
+template <typename T, int K, int D, bool CACHED, typename F>
+__device__ __forceinline__ void grad_factor(F& f, const PointArgs<T>& a, const SmemTable<T>& tab,
+                                            unsigned char* rbase, int64_t m) {
+    if constexpr (CACHED) {
+        f.load_cached(a, m);
+    } else {
+        f.R = GradShape<T, K, D>::Store::make(rbase);
+        f.compute(a, tab, m);
+    }
+}
+
+template <typename T, int K, int D, bool CACHED>
 __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld_acc,
               T* __restrict__ terms, int64_t m0, int64_t cnt, const int* __restrict__ mlist) {
@@ -272,10 +347,9 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ double red[32];
     SmemTable<T> tab;
-    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
-    double* hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
-    unsigned char* rbase = smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys) +
-                           sizeof(double) * a.tab.nb;
+    double* hist;
+    unsigned char* rbase;
+    grad_smem<T, CACHED>(a, tab, smem, hist, rbase);
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
     double bin0 = 0.0;  // this thread's share of histogram bin 0
@@ -283,9 +357,8 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
     for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
          it += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = point_of(it, m0, mlist);
-        PointFactor<T, K, D, true, typename GradShape<T, K, D>::Store::type> f;
-        f.R = GradShape<T, K, D>::Store::make(rbase);
-        f.compute(a, tab, m);
+        typename GradShape<T, K, D>::template Factor<CACHED> f;
+        grad_factor<T, K, D, CACHED>(f, a, tab, rbase, m);
         const T lkk = f.L[tri(K, K)];
         const T t = N::log(lkk);
         if (terms) terms[m] = t;
@@ -313,7 +386,7 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
 // vb: every point's cotangent seed (vb[p]*xi[p], vb[p]*v[nbr]) is then known, and the point's
 // pullback needs nothing else, so the batches need not be visited in order.
 
-template <typename T, int K, int D>
+template <typename T, int K, int D, bool CACHED>
 __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
             const T* __restrict__ vb, const T* __restrict__ mv, double* __restrict__ gacc,
@@ -322,10 +395,9 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
     using PM = PointMath<T, K, D>;
     extern __shared__ __align__(16) unsigned char smem[];
     SmemTable<T> tab;
-    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
-    double* hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
-    unsigned char* rbase = smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys) +
-                           sizeof(double) * a.tab.nb;
+    double* hist;
+    unsigned char* rbase;
+    grad_smem<T, CACHED>(a, tab, smem, hist, rbase);
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
     double bin0 = 0.0;  // this thread's share of histogram bin 0
@@ -334,9 +406,8 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
         const int64_t m = point_of(it, m0, mlist);
         const int64_t p = a.n0 + m;
         const T vbp = vb[p];
-        PointFactor<T, K, D, true, typename GradShape<T, K, D>::Store::type> f;
-        f.R = GradShape<T, K, D>::Store::make(rbase);
-        f.compute(a, tab, m);
+        typename GradShape<T, K, D>::template Factor<CACHED> f;
+        grad_factor<T, K, D, CACHED>(f, a, tab, rbase, m);
         const T pivfloor = N::mul(a.tab.pivc, f.L[0]);
         T B[PM::NT];
         sfor<0, PM::NT>([&](auto i_) {
@@ -368,7 +439,7 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
 
 // refine_inv_loss_grad_hist_kernel! (src/kernels_adjoint.jl:155-221): loss 0.5*sum(xi^2) and its
 // vals-gradient; the z-bar solve has no pivot guard, as in the reference.
-template <typename T, int K, int D>
+template <typename T, int K, int D, bool CACHED>
 __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict__ gacc,
                 double* __restrict__ loss_acc, T* __restrict__ xi_out, int64_t m0, int64_t cnt,
@@ -378,10 +449,9 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ double red[32];
     SmemTable<T> tab;
-    tab.stage(a.tab, smem, threadIdx.x, blockDim.x);
-    double* hist = reinterpret_cast<double*>(smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys));
-    unsigned char* rbase = smem + table_smem_bytes<T>(a.tab.nb, a.tab.nkeys) +
-                           sizeof(double) * a.tab.nb;
+    double* hist;
+    unsigned char* rbase;
+    grad_smem<T, CACHED>(a, tab, smem, hist, rbase);
     for (int i = threadIdx.x; i < a.tab.nb; i += blockDim.x) hist[i] = 0.0;
     __syncthreads();
     double bin0 = 0.0;  // this thread's share of histogram bin 0
@@ -389,9 +459,8 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
     for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
          it += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = point_of(it, m0, mlist);
-        PointFactor<T, K, D, true, typename GradShape<T, K, D>::Store::type> f;
-        f.R = GradShape<T, K, D>::Store::make(rbase);
-        f.compute(a, tab, m);
+        typename GradShape<T, K, D>::template Factor<CACHED> f;
+        grad_factor<T, K, D, CACHED>(f, a, tab, rbase, m);
         T x[K];
         PM::solve(x, f.L, a.tab.pivc);
         const T sd = f.L[tri(K, K)];
@@ -513,18 +582,173 @@ k_sweep_rev(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv,
 
 // ---------------------------------------------------------------------------------------------
 // Persistent sweeps: one cooperative launch per full sweep.  The grid walks the depth batches in
-// order with a grid barrier between consecutive batches; before each barrier every thread loads
-// the read-only inputs of its first point of the next batch (neighbour list, weights, std, xi),
-// so after the barrier only the dependent gathers remain.  Field values and cotangents cross
-// the barrier through L2 (ld/st .cg), never through an SM's L1.
+// order with a grid barrier between consecutive batches.  Each thread holds the read-only inputs
+// (weights, neighbour list, std, xi) of two points in registers: while the current point's
+// neighbour gathers are in flight, the next point's inputs are already being loaded, so a point
+// costs one round of memory latency instead of two chained ones.  The first point of the next
+// batch is loaded before the barrier.  Field values and cotangents cross the barrier through L2
+// (ld/st .cg), never through an SM's L1.
 // ---------------------------------------------------------------------------------------------
-constexpr int kPersistThreads = 1024;
+constexpr int kPersistThreads = 1024;  // k_sweep_fwd_flow
+
+// One point's read-only sweep inputs.
+template <typename T, int K>
+struct SweepIn {
+    int nb[K];
+    T w[K];
+    T sd;
+    T xi;  // forward only
+    __device__ __forceinline__ void load(const T* __restrict__ mv, const T* __restrict__ sdv,
+                                         const T* __restrict__ xiv, const int* __restrict__ nbrs,
+                                         int64_t m) {
+        load_row_i32<K>(nb, nbrs + m * K);
+        load_row_t<T, K>(w, mv + m * K);
+        sd = __ldg(sdv + m);
+        if (xiv) xi = __ldg(xiv + m);
+    }
+};
+
+// Block shape of the persistent sweeps: as many threads as the register file holds with two
+// points' inputs, K gathered values and ~16 registers of bookkeeping per thread.
+template <typename T, int K>
+struct SweepShape {
+    static constexpr int kWords = (int)sizeof(T) / 4;
+    static constexpr int kRegs = 2 * (K + K * kWords + 2 * kWords) + K * kWords + 16;
+    static constexpr int kThreads =
+        kRegs <= 56 ? 1024 : (kRegs <= 85 ? 768 : (kRegs <= 128 ? 512 : 256));
+};
+
+// Step i of a sweep visits forward batch i (F) and reverse batch nbatch-1-i (R); one grid
+// barrier per step.  A thread's tasks within a step are F_0, R_0, F_1, R_1, ... (F_k: point
+// offs[i] + gtid + k*gsz when below offs[i+1]; R_k likewise in the reverse batch), the absent
+// ones skipped; neither kind reads the other's output, so their interleaving is free.  Per
+// point the arithmetic and its order are those of the per-batch kernels k_sweep_fwd /
+// k_sweep_rev: forward values[p] = std*xi + sum_j mv[j]*values[nbr_j]; reverse
+// xg[p] = std*vb[p], vb[nbr_j] += mv[j]*vb[p] (atomic: batch-mates can share a neighbour).
+template <typename T, int K, bool F, bool R>
+__device__ __forceinline__ void sweep_pipe(T* __restrict__ values, const T* __restrict__ xi_ref,
+                                           T* __restrict__ vb, T* __restrict__ xg,
+                                           const T* __restrict__ mv, const T* __restrict__ sd,
+                                           const int* __restrict__ nbrs, int64_t n0,
+                                           const int64_t* __restrict__ offs, int nbatch,
+                                           GridSync gs) {
+    using N = Num<T>;
+    const int64_t gtid = sweep_gtid();
+    const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
+
+    int64_t f0 = 0, fhi = 0, r0 = 0, rhi = 0;  // this step's first points and batch ends
+    auto set_step = [&](int i) {
+        f0 = offs[i] + gtid;
+        fhi = offs[i + 1];
+        r0 = offs[nbatch - 1 - i] + gtid;
+        rhi = offs[nbatch - i];
+    };
+    auto has = [&](bool fwd, int64_t k) {
+        return fwd ? (F && f0 + k * gsz < fhi) : (R && r0 + k * gsz < rhi);
+    };
+    auto load = [&](SweepIn<T, K>& in, bool fwd, int64_t k) {
+        const int64_t p = (fwd ? f0 : r0) + k * gsz;
+        in.load(mv, sd, fwd ? xi_ref : nullptr, nbrs, p - n0);
+    };
+
+    SweepIn<T, K> cur, nxt;
+    bool fwd, valid;
+    int64_t k = 0;
+    set_step(0);
+    valid = has(true, 0) || has(false, 0);
+    fwd = has(true, 0);
+    if (valid) load(cur, fwd, 0);
+    for (int i = 0; i < nbatch; i++) {
+        while (valid) {
+            // The task after (fwd, k): R_k after F_k, else F_{k+1}, else R_{k+1}.
+            bool nfwd = false, nvalid = true;
+            int64_t nk = k;
+            if (fwd && has(false, k)) {
+                nfwd = false;
+            } else if (has(true, k + 1)) {
+                nfwd = true;
+                nk = k + 1;
+            } else if (has(false, k + 1)) {
+                nfwd = false;
+                nk = k + 1;
+            } else {
+                nvalid = false;
+            }
+            if (F && fwd) {
+                const int64_t p = f0 + k * gsz;
+                T v[K];
+                sfor<0, K>([&](auto j_) {
+                    GPB2_CI(j);
+                    v[j] = __ldcg(values + cur.nb[j]);
+                });
+                if (nvalid) load(nxt, nfwd, nk);
+                T acc = N::mul(cur.sd, cur.xi);
+                sfor<0, K>([&](auto j_) {
+                    GPB2_CI(j);
+                    acc = N::add(acc, N::mul(cur.w[j], v[j]));
+                });
+                __stcg(values + p, acc);
+            } else if (R) {
+                const int64_t p = r0 + k * gsz;
+                const T vbp = __ldcg(vb + p);
+                if (nvalid) load(nxt, nfwd, nk);
+                if (xg) xg[p] = N::mul(cur.sd, vbp);
+                sfor<0, K>([&](auto j_) {
+                    GPB2_CI(j);
+                    atomicAdd(vb + cur.nb[j], N::mul(cur.w[j], vbp));
+                });
+            }
+            cur = nxt;
+            fwd = nfwd;
+            k = nk;
+            valid = nvalid;
+        }
+        if (i + 1 < nbatch) {
+            set_step(i + 1);
+            k = 0;
+            valid = has(true, 0) || has(false, 0);
+            fwd = has(true, 0);
+            if (valid) load(cur, fwd, 0);
+            if (!grid_sync(gs)) return;
+        }
+    }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(SweepShape<T, K>::kThreads)
+k_sweep_fwd_all(T* __restrict__ values, const T* __restrict__ xi_ref, const T* __restrict__ mv,
+                const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
+                const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
+    sweep_pipe<T, K, true, false>(values, xi_ref, nullptr, nullptr, mv, sd, nbrs, n0, offs, nbatch,
+                                  gs);
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(SweepShape<T, K>::kThreads)
+k_sweep_rev_all(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv,
+                const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
+                const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
+    sweep_pipe<T, K, false, true>(nullptr, nullptr, vb, xg, mv, sd, nbrs, n0, offs, nbatch, gs);
+}
+
+// generate_grad_vals needs both the forward field v (from xi) and the reverse cotangent vb (from
+// vbar); neither sweep reads the other's output, so one persistent kernel runs them together:
+// step i sweeps forward batch i and reverse batch nbatch-1-i, one grid barrier per step instead
+// of one per batch of each sweep.
+template <typename T, int K>
+__global__ void __launch_bounds__(SweepShape<T, K>::kThreads)
+k_sweep_fwdrev_all(T* __restrict__ values, const T* __restrict__ xi_ref, T* __restrict__ vb,
+                   const T* __restrict__ mv, const T* __restrict__ sd,
+                   const int* __restrict__ nbrs, int64_t n0, const int64_t* __restrict__ offs,
+                   int nbatch, GridSync gs) {
+    sweep_pipe<T, K, true, true>(values, xi_ref, vb, nullptr, mv, sd, nbrs, n0, offs, nbatch, gs);
+}
 
 template <typename T, int K>
 struct SweepPoint {
     int nb[K];
     T w[K];
-    T a;  // forward: std * xi (the first product of the sum); reverse: std
+    T a;  // std * xi (the first product of the forward sum)
     __device__ __forceinline__ void load_fwd(const T* __restrict__ mv, const T* __restrict__ sd,
                                              const T* __restrict__ xi_ref,
                                              const int* __restrict__ nbrs, int64_t m) {
@@ -532,47 +756,7 @@ struct SweepPoint {
         load_row_t<T, K>(w, mv + m * K);
         a = Num<T>::mul(__ldg(sd + m), __ldg(xi_ref + m));
     }
-    __device__ __forceinline__ void load_rev(const T* __restrict__ mv, const T* __restrict__ sd,
-                                             const int* __restrict__ nbrs, int64_t m) {
-        load_row_i32<K>(nb, nbrs + m * K);
-        load_row_t<T, K>(w, mv + m * K);
-        a = __ldg(sd + m);
-    }
 };
-
-template <typename T, int K>
-__global__ void __launch_bounds__(kPersistThreads)
-k_sweep_fwd_all(T* __restrict__ values, const T* __restrict__ xi_ref, const T* __restrict__ mv,
-                const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
-                const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
-    using N = Num<T>;
-    const int64_t gtid = sweep_gtid();
-    const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
-    SweepPoint<T, K> sp;
-    int64_t p = offs[0] + gtid;
-    bool have = p < offs[1];
-    if (have) sp.load_fwd(mv, sd, xi_ref, nbrs, p - n0);
-    for (int b = 0; b < nbatch; b++) {
-        const int64_t hi = offs[b + 1];
-        while (have) {
-            T acc = sp.a;
-            sfor<0, K>([&](auto j_) {
-                GPB2_CI(j);
-                acc = N::add(acc, N::mul(sp.w[j], __ldcg(values + sp.nb[j])));
-            });
-            __stcg(values + p, acc);
-            p += gsz;
-            have = p < hi;
-            if (have) sp.load_fwd(mv, sd, xi_ref, nbrs, p - n0);
-        }
-        if (b + 1 < nbatch) {
-            p = offs[b + 1] + gtid;
-            have = p < offs[b + 2];
-            if (have) sp.load_fwd(mv, sd, xi_ref, nbrs, p - n0);
-            if (!grid_sync(gs)) return;
-        }
-    }
-}
 
 // Dataflow forward sweep: one cooperative launch and no barrier.  values[n0:N] are set to the
 // pending pattern before the launch; each point waits only for its own K neighbour values, so
@@ -628,97 +812,6 @@ k_sweep_fwd_flow(T* __restrict__ values, const T* __restrict__ xi_ref, const T* 
                     return;
                 }
             }
-        }
-    }
-}
-
-template <typename T, int K>
-__global__ void __launch_bounds__(kPersistThreads)
-k_sweep_rev_all(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv,
-                const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
-                const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
-    using N = Num<T>;
-    const int64_t gtid = sweep_gtid();
-    const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
-    SweepPoint<T, K> sp;
-    int64_t p = offs[nbatch - 1] + gtid;
-    bool have = p < offs[nbatch];
-    if (have) sp.load_rev(mv, sd, nbrs, p - n0);
-    for (int b = nbatch - 1; b >= 0; b--) {
-        const int64_t hi = offs[b + 1];
-        while (have) {
-            const T vbp = __ldcg(vb + p);
-            if (xg) xg[p] = N::mul(sp.a, vbp);
-            sfor<0, K>([&](auto j_) {
-                GPB2_CI(j);
-                atomicAdd(vb + sp.nb[j], N::mul(sp.w[j], vbp));
-            });
-            p += gsz;
-            have = p < hi;
-            if (have) sp.load_rev(mv, sd, nbrs, p - n0);
-        }
-        if (b > 0) {
-            p = offs[b - 1] + gtid;
-            have = p < offs[b];
-            if (have) sp.load_rev(mv, sd, nbrs, p - n0);
-            if (!grid_sync(gs)) return;
-        }
-    }
-}
-
-// generate_grad_vals needs both the forward field v (from xi) and the reverse cotangent vb (from
-// vbar); neither sweep reads the other's output, so one persistent kernel runs them together:
-// step i sweeps forward batch i and reverse batch nbatch-1-i, one grid barrier per step instead
-// of one per batch of each sweep.  Per point, the same arithmetic and order as
-// k_sweep_fwd_all / k_sweep_rev_all (the reverse accumulation order is atomic either way).
-template <typename T, int K>
-__global__ void __launch_bounds__(kPersistThreads)
-k_sweep_fwdrev_all(T* __restrict__ values, const T* __restrict__ xi_ref, T* __restrict__ vb,
-                   const T* __restrict__ mv, const T* __restrict__ sd,
-                   const int* __restrict__ nbrs, int64_t n0, const int64_t* __restrict__ offs,
-                   int nbatch, GridSync gs) {
-    using N = Num<T>;
-    const int64_t gtid = sweep_gtid();
-    const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
-    SweepPoint<T, K> fp, rp;
-    int64_t pf = offs[0] + gtid, pr = offs[nbatch - 1] + gtid;
-    bool hf = pf < offs[1], hr = pr < offs[nbatch];
-    if (hf) fp.load_fwd(mv, sd, xi_ref, nbrs, pf - n0);
-    if (hr) rp.load_rev(mv, sd, nbrs, pr - n0);
-    for (int i = 0; i < nbatch; i++) {
-        const int br = nbatch - 1 - i;
-        const int64_t hif = offs[i + 1], hir = offs[br + 1];
-        while (hf || hr) {
-            if (hf) {
-                T acc = fp.a;
-                sfor<0, K>([&](auto j_) {
-                    GPB2_CI(j);
-                    acc = N::add(acc, N::mul(fp.w[j], __ldcg(values + fp.nb[j])));
-                });
-                __stcg(values + pf, acc);
-                pf += gsz;
-                hf = pf < hif;
-                if (hf) fp.load_fwd(mv, sd, xi_ref, nbrs, pf - n0);
-            }
-            if (hr) {
-                const T vbp = __ldcg(vb + pr);
-                sfor<0, K>([&](auto j_) {
-                    GPB2_CI(j);
-                    atomicAdd(vb + rp.nb[j], N::mul(rp.w[j], vbp));
-                });
-                pr += gsz;
-                hr = pr < hir;
-                if (hr) rp.load_rev(mv, sd, nbrs, pr - n0);
-            }
-        }
-        if (i + 1 < nbatch) {
-            pf = offs[i + 1] + gtid;
-            hf = pf < offs[i + 2];
-            if (hf) fp.load_fwd(mv, sd, xi_ref, nbrs, pf - n0);
-            pr = offs[br - 1] + gtid;
-            hr = pr < offs[br];
-            if (hr) rp.load_rev(mv, sd, nbrs, pr - n0);
-            if (!grid_sync(gs)) return;
         }
     }
 }
@@ -780,8 +873,29 @@ struct Launch {
     }
     static cudaError_t factor(const PointArgs<T>& a, int64_t mb, int64_t me, T* mv, T* sd,
                               cudaStream_t s) {
-        return flat("factor", k_factor<T, K, D>, flat_smem(a, false), me - mb, s, a, mb, me, mv,
-                    sd);
+        if (a.fc.L)
+            return flat("factor", k_factor<T, K, D, true>, flat_smem(a, false), me - mb, s, a, mb,
+                        me, mv, sd);
+        return flat("factor", k_factor<T, K, D, false>, flat_smem(a, false), me - mb, s, a, mb, me,
+                    mv, sd);
+    }
+    // A histogram kernel (k_logdet_grad, k_grad_vals, k_inv_loss_grad) over r.cnt points: the
+    // instantiation that reads the factor cache when the arguments carry one.
+    template <class KernC, class KernR, class... Args>
+    static cudaError_t hist_kernel(const char* name, KernC kc, KernR kr, const PointArgs<T>& a,
+                                   int64_t work, cudaStream_t s, Args... args) {
+        if (work <= 0) return cudaSuccess;
+        using G = GradShape<T, K, D>;
+        const bool cached = a.fc.L != nullptr;
+        const void* kern = cached ? (const void*)kc : (const void*)kr;
+        const size_t smem = cached ? sizeof(double) * a.tab.nb
+                                   : flat_smem(a, true) + G::Store::bytes;
+        cudaError_t e = prepare_kernel_smem(kern, smem);
+        if (e != cudaSuccess) return e;
+        const int grid = flat_grid(kern, G::kThreads, smem, work);
+        if (cached)
+            return launch_prof(name, kc, dim3(grid), dim3(G::kThreads), smem, s, a, args...);
+        return launch_prof(name, kr, dim3(grid), dim3(G::kThreads), smem, s, a, args...);
     }
     static cudaError_t inv(const PointArgs<T>& a, const T* values, T* xi, Pts r,
                            cudaStream_t s) {
@@ -795,40 +909,20 @@ struct Launch {
     }
     static cudaError_t logdet_grad(const PointArgs<T>& a, double* gacc, double* ld, T* terms,
                                    Pts r, cudaStream_t s) {
-        const int64_t M = r.cnt;
-        if (M <= 0) return cudaSuccess;
-        using G = GradShape<T, K, D>;
-        const size_t smem = flat_smem(a, true) + G::Store::bytes;
-        cudaError_t e = prepare_kernel_smem((const void*)k_logdet_grad<T, K, D>, smem);
-        if (e != cudaSuccess) return e;
-        const int grid = flat_grid((const void*)k_logdet_grad<T, K, D>, G::kThreads, smem, M);
-        return launch_prof("logdet_grad", k_logdet_grad<T, K, D>, dim3(grid), dim3(G::kThreads),
-                           smem, s, a, gacc, ld, terms, r.m0, r.cnt, r.list);
+        return hist_kernel("logdet_grad", k_logdet_grad<T, K, D, true>,
+                           k_logdet_grad<T, K, D, false>, a, r.cnt, s, gacc, ld, terms, r.m0,
+                           r.cnt, r.list);
     }
     static cudaError_t grad_vals(const PointArgs<T>& a, const T* v, const T* xih, const T* vb,
                                  const T* mv, double* gacc, Pts r, cudaStream_t s) {
-        const int64_t M = r.cnt;
-        if (M <= 0) return cudaSuccess;
-        using G = GradShape<T, K, D>;
-        const size_t smem = flat_smem(a, true) + G::Store::bytes;
-        cudaError_t e = prepare_kernel_smem((const void*)k_grad_vals<T, K, D>, smem);
-        if (e != cudaSuccess) return e;
-        const int grid = flat_grid((const void*)k_grad_vals<T, K, D>, G::kThreads, smem, M);
-        return launch_prof("grad_vals", k_grad_vals<T, K, D>, dim3(grid), dim3(G::kThreads), smem,
-                           s, a, v, xih, vb, mv, gacc, r.m0, r.cnt, r.list);
+        return hist_kernel("grad_vals", k_grad_vals<T, K, D, true>, k_grad_vals<T, K, D, false>,
+                           a, r.cnt, s, v, xih, vb, mv, gacc, r.m0, r.cnt, r.list);
     }
     static cudaError_t inv_loss_grad(const PointArgs<T>& a, const T* values, double* gacc,
                                      double* loss, T* xi_out, Pts r, cudaStream_t s) {
-        const int64_t M = r.cnt;
-        if (M <= 0) return cudaSuccess;
-        using G = GradShape<T, K, D>;
-        const size_t smem = flat_smem(a, true) + G::Store::bytes;
-        cudaError_t e = prepare_kernel_smem((const void*)k_inv_loss_grad<T, K, D>, smem);
-        if (e != cudaSuccess) return e;
-        const int grid = flat_grid((const void*)k_inv_loss_grad<T, K, D>, G::kThreads, smem, M);
-        return launch_prof("inv_loss_grad", k_inv_loss_grad<T, K, D>, dim3(grid),
-                           dim3(G::kThreads), smem, s, a, values, gacc, loss, xi_out, r.m0,
-                           r.cnt, r.list);
+        return hist_kernel("inv_loss_grad", k_inv_loss_grad<T, K, D, true>,
+                           k_inv_loss_grad<T, K, D, false>, a, r.cnt, s, values, gacc, loss,
+                           xi_out, r.m0, r.cnt, r.list);
     }
     static cudaError_t fused_fwd(const PointArgs<T>& a, T* values, const T* xi_ref, int64_t lo,
                                  int64_t hi, cudaStream_t s) {
@@ -851,27 +945,33 @@ struct Launch {
                            dim3(kSweepThreads), 0, s, xg, vb, mv, sd, nbrs, n0, lo, hi);
     }
     template <class Kern, class... Args>
-    static cudaError_t coop(const char* name, Kern kern, cudaStream_t s, Args... args) {
-        const int grid = coop_grid((const void*)kern, kPersistThreads, 0);
+    static cudaError_t coop(const char* name, Kern kern, int threads, size_t smem, cudaStream_t s,
+                            Args... args) {
+        if (smem) {
+            const cudaError_t e = prepare_kernel_smem((const void*)kern, smem);
+            if (e != cudaSuccess) return e;
+        }
+        const int grid = coop_grid((const void*)kern, threads, smem);
         void* argv[] = {(void*)&args...};
         const ProfToken t = prof_begin(name, s);
         const cudaError_t e =
-            cudaLaunchCooperativeKernel((const void*)kern, grid, kPersistThreads, argv, 0, s);
+            cudaLaunchCooperativeKernel((const void*)kern, grid, threads, argv, smem, s);
         prof_end(t, s);
         return e;
     }
+    using SS = SweepShape<T, K>;
     static cudaError_t sweep_fwd_all(T* values, const T* xi_ref, const T* mv, const T* sd,
                                      const int* nbrs, int64_t n0, const int64_t* offs, int nbatch,
                                      GridSync gs, cudaStream_t s) {
         if (nbatch <= 0) return cudaSuccess;
-        return coop("sweep_fwd_all", k_sweep_fwd_all<T, K>, s, values, xi_ref, mv, sd, nbrs, n0,
+        return coop("sweep_fwd_all", k_sweep_fwd_all<T, K>, SS::kThreads, 0, s, values, xi_ref, mv, sd, nbrs, n0,
                     offs, nbatch, gs);
     }
     static cudaError_t sweep_fwd_flow(T* values, const T* xi_ref, const T* mv, const T* sd,
                                       const int* nbrs, int64_t n0, int64_t n, int* err,
                                       cudaStream_t s) {
         if (n <= n0) return cudaSuccess;
-        return coop("sweep_fwd_flow", k_sweep_fwd_flow<T, K>, s, values, xi_ref, mv, sd, nbrs,
+        return coop("sweep_fwd_flow", k_sweep_fwd_flow<T, K>, kPersistThreads, 0, s, values, xi_ref, mv, sd, nbrs,
                     n0, n, err);
     }
     static cudaError_t sweep_fwdrev_all(T* values, const T* xi_ref, T* vb, const T* mv,
@@ -879,14 +979,14 @@ struct Launch {
                                         const int64_t* offs, int nbatch, GridSync gs,
                                         cudaStream_t s) {
         if (nbatch <= 0) return cudaSuccess;
-        return coop("sweep_fwdrev_all", k_sweep_fwdrev_all<T, K>, s, values, xi_ref, vb, mv, sd,
+        return coop("sweep_fwdrev_all", k_sweep_fwdrev_all<T, K>, SS::kThreads, 0, s, values, xi_ref, vb, mv, sd,
                     nbrs, n0, offs, nbatch, gs);
     }
     static cudaError_t sweep_rev_all(T* xg, T* vb, const T* mv, const T* sd, const int* nbrs,
                                      int64_t n0, const int64_t* offs, int nbatch, GridSync gs,
                                      cudaStream_t s) {
         if (nbatch <= 0) return cudaSuccess;
-        return coop("sweep_rev_all", k_sweep_rev_all<T, K>, s, xg, vb, mv, sd, nbrs, n0, offs,
+        return coop("sweep_rev_all", k_sweep_rev_all<T, K>, SS::kThreads, 0, s, xg, vb, mv, sd, nbrs, n0, offs,
                     nbatch, gs);
     }
     static const Ops<T>* ops() {

@@ -93,12 +93,12 @@ std::atomic<int> g_sync{[] {
     return (e && std::strcmp(e, "0") == 0) ? 0 : 1;
 }()};
 
-// Whether the dense first-layer factor runs beside the per-point factor (GPB2_OVERLAP=0 at load
-// time runs them one after the other on the call's stream).
-const bool g_overlap = [] {
+// Whether the dense first-layer work runs beside the per-point kernels on the problem's second
+// stream (GPB2_OVERLAP=0 at load time, or gpb2_set_overlap(0), runs it on the call's stream).
+std::atomic<bool> g_overlap_flag{[] {
     const char* e = std::getenv("GPB2_OVERLAP");
     return !(e && std::strcmp(e, "0") == 0);
-}();
+}()};
 
 // The problem's high-priority stream and its two events, created on first use.
 static int ensure_dense_stream(gpb2_problem* p) {
@@ -142,12 +142,62 @@ struct Impl {
 
     // mean_vec / std of every refined point.  They depend only on the graph and the table, so
     // they are computed once per table and reused by every call until the table changes.
+    // With the factor cache allocated (mode 1 allocates it here), the same pass fills it.
     static int factor_all(P* p, cudaStream_t s) {
         if (p->factor_valid) return GPB2_OK;
-        GPB2_TRY(check_launch(ops_of<T>(p)->factor(point_args<T>(p), 0, p->m, (T*)p->mv,
-                                                   (T*)p->sd, s),
+        if (p->fc_mode == 1) GPB2_TRY(alloc_factor_cache(p));
+        GPB2_TRY(check_launch(ops_of<T>(p)->factor(point_args<T>(p, FcUse::Fill), 0, p->m,
+                                                   (T*)p->mv, (T*)p->sd, s),
                               "factor"));
         p->factor_valid = true;
+        p->fc_valid = p->fc_L != nullptr;
+        return GPB2_OK;
+    }
+
+    // The factor cache's buffers, as the mode allows: mode 1 always (an allocation failure is
+    // the caller's error), mode 2 only when the device keeps a margin of free memory beyond it
+    // (else, or on a failed allocation, nothing: the kernels recompute).
+    static int alloc_factor_cache(P* p) {
+        if (p->fc_L || p->fc_mode == 0 || p->m <= 0) return GPB2_OK;
+        const size_t ts = sizeof(T);
+        const size_t nt = (size_t)(p->k + 1) * (p->k + 2) / 2, nr = nt - (size_t)(p->k + 1);
+        if (p->fc_mode == 2) {
+            size_t fr = 0, tot = 0;
+            if (cudaMemGetInfo(&fr, &tot) != cudaSuccess) {
+                cudaGetLastError();
+                return GPB2_OK;
+            }
+            const size_t margin = std::max(tot / 10, (size_t)8 << 30);
+            if (fr < factor_cache_bytes(p) + margin) return GPB2_OK;
+        }
+        int st = ensure_alloc(&p->fc_L, ts * nt * p->m);
+        if (!st) st = ensure_alloc(&p->fc_t, ts * nr * p->m);
+        if (!st) st = ensure_alloc(reinterpret_cast<void**>(&p->fc_lo), 2 * nr * p->m);
+        if (st) {
+            for (void* b : {p->fc_L, p->fc_t, (void*)p->fc_lo})
+                if (b) cudaFree(b);
+            p->fc_L = p->fc_t = nullptr;
+            p->fc_lo = nullptr;
+            if (p->fc_mode == 1) return st;
+            clear_error();
+        }
+        return GPB2_OK;
+    }
+
+    // Before generate_grad_vals' per-point kernel: the factor cache of the current table,
+    // allocated as the mode allows and, when the factor pass of this table ran without it, filled
+    // by a second factor pass (mean_vec / std are written again with the same bits).  The later
+    // calls on the same table, and the factor passes of later tables, then read and fill it.
+    static int ensure_factor_cache(P* p, cudaStream_t s) {
+        if (p->fc_valid || p->fc_mode == 0 || p->m <= 0) return GPB2_OK;
+        GPB2_TRY(alloc_factor_cache(p));
+        if (!p->fc_L) return GPB2_OK;
+        GPB2_TRY(ensure_scratch(p, true));
+        GPB2_TRY(check_launch(ops_of<T>(p)->factor(point_args<T>(p, FcUse::Fill), 0, p->m,
+                                                   (T*)p->mv, (T*)p->sd, s),
+                              "factor cache"));
+        p->factor_valid = true;
+        p->fc_valid = true;
         return GPB2_OK;
     }
 
@@ -159,7 +209,7 @@ struct Impl {
     // the remaining SMs on the call's stream; the call's stream then waits for the ladder.
     // Neither kernel waits on the other, so any co-scheduling is correct.
     static int factor_both(P* p, cudaStream_t s) {
-        if (!g_overlap || p->dense_valid || p->factor_valid) {
+        if (!g_overlap_flag.load() || p->dense_valid || p->factor_valid) {
             GPB2_TRY(Dense<T>::factor(p, s));
             return factor_all(p, s);
         }
@@ -340,7 +390,7 @@ struct Impl {
     static int refine_logdet_grad_vals(P* p, T* dvals, double* ld, cudaStream_t s) {
         GPB2_TRY(ensure_scratch(p, false));
         GPB2_TRY(zero_acc(p, s));
-        GPB2_TRY(check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p), p->dacc,
+        GPB2_TRY(check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p, FcUse::Read), p->dacc,
                                                         p->dacc + p->nb, nullptr, Pts::all(p->m), s),
                               "logdet grad"));
         GPB2_TRY(finish_hist(p, dvals, s));
@@ -356,7 +406,7 @@ struct Impl {
                                          cudaStream_t s) {
         GPB2_TRY(ensure_scratch(p, false));
         GPB2_TRY(zero_acc(p, s));
-        GPB2_TRY(check_launch(ops_of<T>(p)->inv_loss_grad(point_args<T>(p), values, p->dacc,
+        GPB2_TRY(check_launch(ops_of<T>(p)->inv_loss_grad(point_args<T>(p, FcUse::Read), values, p->dacc,
                                                           p->dacc + p->nb + 1, nullptr, Pts::all(p->m), s),
                               "inverse-loss grad"));
         GPB2_TRY(finish_hist(p, dvals, s));
@@ -485,13 +535,14 @@ struct Impl {
             GPB2_TRY(refine_sweep(p, v, xt + p->n0, true, s));
             GPB2_TRY(reverse_sweep(p, nullptr, vb, s));
         }
+        GPB2_TRY(ensure_factor_cache(p, s));
         GPB2_TRY(zero_acc(p, s));
         auto per_point = [&](cudaStream_t st) {
-            return check_launch(ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb,
+            return check_launch(ops_of<T>(p)->grad_vals(point_args<T>(p, FcUse::Read), v, xt, vb,
                                                         (const T*)p->mv, p->dacc, Pts::all(p->m), st),
                                 "grad_vals");
         };
-        if (!g_overlap) {
+        if (!g_overlap_flag.load()) {
             GPB2_TRY(per_point(s));
             GPB2_TRY(Dense<T>::grad_vals(p, vb, xt, p->dacc, s));
             return finish_hist(p, dvals, s);
@@ -516,7 +567,7 @@ struct Impl {
     static int generate_logdet_grad_vals(P* p, T* dvals, double* ld, cudaStream_t s) {
         GPB2_TRY(ensure_scratch(p, false));
         GPB2_TRY(zero_acc(p, s));
-        GPB2_TRY(check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p), p->dacc,
+        GPB2_TRY(check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p, FcUse::Read), p->dacc,
                                                         p->dacc + p->nb, nullptr, Pts::all(p->m), s),
                               "logdet grad"));
         GPB2_TRY(Dense<T>::factor(p, s));
@@ -540,7 +591,7 @@ struct Impl {
             yt = (const T*)p->buf_a;
         }
         GPB2_TRY(zero_acc(p, s));
-        GPB2_TRY(check_launch(ops_of<T>(p)->inv_loss_grad(point_args<T>(p), yt, p->dacc,
+        GPB2_TRY(check_launch(ops_of<T>(p)->inv_loss_grad(point_args<T>(p, FcUse::Read), yt, p->dacc,
                                                           p->dacc + p->nb + 1, nullptr, Pts::all(p->m), s),
                               "inverse-loss grad"));
         GPB2_TRY(Dense<T>::factor(p, s));
@@ -832,7 +883,7 @@ struct Shard {
         GPB2_TRY(reverse(p, c, pl, vb, nullptr, s));
         GPB2_TRY(Impl<T>::zero_acc(p, s));
         GPB2_TRY(Impl<T>::check_launch(
-            ops_of<T>(p)->grad_vals(point_args<T>(p), v, xt, vb, (const T*)p->mv, p->dacc,
+            ops_of<T>(p)->grad_vals(point_args<T>(p, FcUse::Read), v, xt, vb, (const T*)p->mv, p->dacc,
                                     Pts{0, p->sh_own_cnt, p->sh_own}, s),
             "grad_vals"));
         if (comm_rank(c) == 0) GPB2_TRY(Dense<T>::grad_vals(p, vb, xt, p->dacc, s));
@@ -867,7 +918,7 @@ struct Shard {
     static int logdet_grad(P* p, gpb2_comm* c, T* dvals, double* ld, cudaStream_t s) {
         GPB2_TRY(ensure_scratch(p, false));
         GPB2_TRY(Impl<T>::zero_acc(p, s));
-        GPB2_TRY(Impl<T>::check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p), p->dacc,
+        GPB2_TRY(Impl<T>::check_launch(ops_of<T>(p)->logdet_grad(point_args<T>(p, FcUse::Read), p->dacc,
                                                                  p->dacc + p->nb, nullptr,
                                                                  flat_share(p, c), s),
                                        "logdet grad"));
@@ -894,7 +945,7 @@ struct Shard {
         GPB2_TRY(st);
         GPB2_TRY(Impl<T>::zero_acc(p, s));
         GPB2_TRY(Impl<T>::check_launch(
-            ops_of<T>(p)->inv_loss_grad(point_args<T>(p), yt, p->dacc, p->dacc + p->nb + 1,
+            ops_of<T>(p)->inv_loss_grad(point_args<T>(p, FcUse::Read), yt, p->dacc, p->dacc + p->nb + 1,
                                         nullptr, flat_share(p, c), s),
             "inverse-loss grad"));
         GPB2_TRY(Dense<T>::factor(p, s));
@@ -954,6 +1005,11 @@ int gpb2_problem_check(gpb2_problem* p, void* stream) {
     DeviceGuard dg(p->device);
     if (!dg.ok) return set_error(GPB2_ERR_NO_DEVICE, "cudaSetDevice(%d) failed", p->device);
     return finish_call(p, (cudaStream_t)stream);
+}
+
+int gpb2_set_overlap(int on) {
+    g_overlap_flag.store(on != 0);
+    return GPB2_OK;
 }
 
 int gpb2_set_forward_mode(int mode) {

@@ -1,6 +1,8 @@
 // gpb2_problem.cu -- problem handle: upload, layout conversion, graph validation, interpolation
 // table, scratch management, error plumbing.
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <string>
@@ -50,6 +52,12 @@ int ensure_capacity(void** ptr, size_t* cap, size_t bytes) {
 }
 
 static size_t tsize(const gpb2_problem* p) { return p->dtype == GPB2_F32 ? 4 : 8; }
+
+size_t factor_cache_bytes(const gpb2_problem* p) {
+    const size_t ts = tsize(p);
+    const size_t nt = (size_t)(p->k + 1) * (p->k + 2) / 2, nr = nt - (size_t)(p->k + 1);
+    return (size_t)p->m * (nt * ts + nr * (ts + 2));
+}
 
 int ensure_scratch(gpb2_problem* p, bool need_mv) {
     const size_t ts = tsize(p);
@@ -227,6 +235,7 @@ static int load_table(gpb2_problem* p, const void* vals_dev, cudaStream_t s) {
     p->dense_launched = false;
     p->factor_valid = false;  // and so do the per-point mean_vec / std
     p->sh_factor_valid = false;
+    p->fc_valid = false;      // and the factor cache
     GPB2_CUDA_TRY(cudaMemcpyAsync(p->vals, vals_dev, ts * p->nb, cudaMemcpyDeviceToDevice, s));
     // The bins do not change after creation: they are read back once, the values every time.
     const bool first = p->hbins.size() != ts * p->nb;
@@ -258,7 +267,7 @@ static void free_problem(gpb2_problem* p) {
                     p->dwork,  p->dinfo, p->d_offsets, p->dsync, p->Ld,    p->trace,
                     p->Ldr,    p->Dinv,  p->Wtri, p->Ainv,  p->sh_v, p->sh_vb,
                     p->sh_xg,  p->sh_own, p->perm_stage, p->perm_pos_g, p->perm_q_g,
-                    p->perm_pos_s, p->perm_q_s, p->lib_tree};
+                    p->perm_pos_s, p->perm_q_s, p->lib_tree, p->fc_L, p->fc_t, p->fc_lo};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);
@@ -317,6 +326,8 @@ static int create_impl(gpb2_problem** out, int dtype, int device, const uint32_t
     if (d < 1 || d > 8) return set_error(GPB2_ERR_UNSUPPORTED_D, "unsupported D=%lld", (long long)d);
 
     auto* p = new gpb2_problem();
+    if (const char* e = std::getenv("GPB2_FACTOR_CACHE"))  // default mode of new handles
+        p->fc_mode = std::min(std::max(std::atoi(e), 0), 2);
     p->dtype = dtype;
     p->device = device;
     p->n = n;
@@ -509,6 +520,31 @@ int gpb2_problem_set_vals(gpb2_problem* p, const void* vals_dev, void* stream) {
     if (!p || !vals_dev) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_set_vals: NULL");
     DeviceGuard dg(p->device);
     return load_table(p, vals_dev, (cudaStream_t)stream);
+}
+
+int gpb2_problem_set_factor_cache(gpb2_problem* p, int mode) {
+    clear_error();
+    if (!p) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_set_factor_cache: NULL problem");
+    if (mode < 0 || mode > 2)
+        return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_set_factor_cache: mode %d", mode);
+    p->fc_mode = mode;
+    if (mode == 0 && p->fc_L) {  // give the memory back (cudaFree waits for the device)
+        DeviceGuard dg(p->device);
+        for (void* b : {p->fc_L, p->fc_t, (void*)p->fc_lo})
+            if (b) cudaFree(b);
+        p->fc_L = p->fc_t = nullptr;
+        p->fc_lo = nullptr;
+        p->fc_valid = false;
+    }
+    return GPB2_OK;
+}
+
+int gpb2_problem_factor_cache(const gpb2_problem* p, int* mode, int* valid, int64_t* bytes) {
+    if (!p) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_factor_cache: NULL problem");
+    if (mode) *mode = p->fc_mode;
+    if (valid) *valid = p->fc_L && p->fc_valid ? 1 : 0;
+    if (bytes) *bytes = (int64_t)factor_cache_bytes(p);
+    return GPB2_OK;
 }
 
 int gpb2_problem_info(const gpb2_problem* p, int64_t* n, int64_t* m, int64_t* k, int64_t* d,

@@ -44,6 +44,15 @@ struct gpb2_problem {
     double* dacc = nullptr;  // nb histogram + 8 scalars (double accumulators)
     bool factor_valid = false;  // mv / sd hold the current table's per-point factors
 
+    // Per-point factor cache (FactorCache): the packed Cholesky factor and the pair weights of
+    // every refined point, in slabs of M entries.  Mode 0 off, 1 on, 2 (default) on from the
+    // first vals-gradient call when it fits in the device's free memory with a margin.
+    void* fc_L = nullptr;        // NT slabs of T
+    void* fc_t = nullptr;        // NR slabs of T
+    uint16_t* fc_lo = nullptr;   // NR slabs of uint16
+    int fc_mode = 2;
+    bool fc_valid = false;       // the cache holds the current table's factors of all points
+
     // Dense n0 block.
     void* Ld = nullptr;       // (n0, n0) column-major lower: the selected ladder candidate
     void* Lcand = nullptr;    // ladder candidates, each (n0, n0) column-major lower
@@ -102,10 +111,10 @@ struct gpb2_problem {
     // output's rank in its destination block.
     void* perm_stage = nullptr;
     int* perm_pos_g = nullptr;
-    int* perm_q_g = nullptr;
+    uint16_t* perm_q_g = nullptr;  // per destination: rank of its source in the block
     int* perm_pos_s = nullptr;
-    int* perm_q_s = nullptr;
-    int perm_shift = 22;  // log2 of the values per destination block
+    uint16_t* perm_q_s = nullptr;
+    int perm_shift = 14;  // log2 of the values per destination block (64 KB)
 };
 
 namespace gpb2 {
@@ -154,16 +163,34 @@ TableView<T> table_view(const gpb2_problem* p) {
     return tv;
 }
 
+// The kernels' view of the problem.  With a cache the arguments also carry the factor cache:
+// as the target of the factor pass (FcUse::Fill, when it is allocated) or as the source of the
+// vals-gradient kernels (FcUse::Read, when it holds the current table).
+enum class FcUse { None, Fill, Read };
+
 template <typename T>
-PointArgs<T> point_args(const gpb2_problem* p) {
+PointArgs<T> point_args(const gpb2_problem* p, FcUse fc = FcUse::None) {
     PointArgs<T> a;
     a.tab = table_view<T>(p);
     a.coords = p->coords;
     a.nbrs = p->nbrs;
     a.n0 = p->n0;
     a.scale = (T)p->scale;
+    if (p->fc_L && (fc == FcUse::Fill || (fc == FcUse::Read && p->fc_valid))) {
+        a.fc.L = static_cast<T*>(p->fc_L);
+        a.fc.t = static_cast<T*>(p->fc_t);
+        a.fc.lo = p->fc_lo;
+        a.fc.stride = p->m;
+    }
     return a;
 }
+
+// Allocate the factor cache as the mode allows (mode 2: if it fits in free memory with a margin)
+// and fill it for the current table; a no-op when it is valid or not to be used.  Called by the
+// vals-gradient operations before their per-point kernel.
+int ensure_factor_cache(gpb2_problem* p, cudaStream_t s);
+// Bytes of the factor cache of a problem.
+size_t factor_cache_bytes(const gpb2_problem* p);
 
 template <typename T>
 const Ops<T>* ops_of(const gpb2_problem* p);

@@ -84,6 +84,8 @@ _SIGNATURES = {
     "gpb2_problem_set_vals": (I32, [P, P, P]),
     "gpb2_problem_prefactor": (I32, [P, P]),
     "gpb2_problem_info": (I32, [P, PI64, PI64, PI64, PI64, PI64]),
+    "gpb2_problem_set_factor_cache": (I32, [P, I32]),
+    "gpb2_problem_factor_cache": (I32, [P, C.POINTER(I32), C.POINTER(I32), PI64]),
     "gpb2_problem_destroy": (I32, [P]),
     "gpb2_problem_dense_jitter": (I32, [P, PD]),
     "gpb2_problem_dense_factor": (I32, [P, P, P]),
@@ -92,6 +94,7 @@ _SIGNATURES = {
     "gpb2_profile_report": (I32, [C.c_char_p, I64]),
     "gpb2_launch_count": (I64, []),
     "gpb2_set_forward_mode": (I32, [I32]),
+    "gpb2_set_overlap": (I32, [I32]),
     "gpb2_set_synchronous": (I32, [I32]),
     "gpb2_problem_check": (I32, [P, P]),
     "gpb2_refine": (I32, [P, P, P, P]),

@@ -189,6 +189,23 @@ class GraphGPProblem:
         _lib.check(st, "prefactor")
         return self
 
+    def set_factor_cache(self, mode: int) -> "GraphGPProblem":
+        """Per-point factor cache (the packed Cholesky factor and pair weights of every refined
+        point, read by the vals-gradient kernels instead of recomputing them): 0 off (frees
+        it), 1 always, 2 (default) from the first generate_grad_vals when the device keeps a
+        margin of free memory beyond it.  Results are the same in every mode."""
+        _lib.check(_lib.lib().gpb2_problem_set_factor_cache(self.handle, int(mode)),
+                   "set_factor_cache")
+        return self
+
+    def factor_cache(self) -> dict:
+        """{"mode", "valid" (holds the current table), "bytes"} of the factor cache."""
+        mode, valid, nbytes = C.c_int32(), C.c_int32(), C.c_int64()
+        _lib.check(_lib.lib().gpb2_problem_factor_cache(self.handle, C.byref(mode),
+                                                         C.byref(valid), C.byref(nbytes)),
+                   "factor_cache")
+        return {"mode": mode.value, "valid": bool(valid.value), "bytes": nbytes.value}
+
     def check(self) -> "GraphGPProblem":
         """Wait for this handle's queued work on the current stream and raise its status (in
         the asynchronous call mode, `set_synchronous(False)`, operations do not wait)."""

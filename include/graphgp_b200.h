@@ -110,6 +110,22 @@ int gpb2_problem_set_vals(gpb2_problem* prob, const void* vals_dev, void* stream
  * factorises the dense block) is reported by the next operation that uses the factor. */
 int gpb2_problem_prefactor(gpb2_problem* prob, void* stream);
 
+/* Per-point factor cache: the packed (K+1)x(K+1) Cholesky factor of every refined point and
+ * the interpolation segment and fraction of each of its K(K+1)/2 pair radii, kept in device
+ * memory (M * (NT*sizeof(T) + NR*(sizeof(T)+2)) bytes, NT = (K+1)(K+2)/2, NR = NT - K - 1;
+ * 396 bytes per point at K = 8 in single precision) so that the vals-gradient kernels
+ * (generate_grad_vals, refine_logdet_grad_vals, refine_inv_loss_grad_vals and their generate_
+ * forms) read each point's factor instead of gathering its neighbours' coordinates,
+ * interpolating the covariance and factorising again.  The per-point factor pass of a table
+ * fills it; the cached entries are the bits the recomputation gives, so results do not depend
+ * on the mode.  mode 0: off (frees it); 1: always; 2 (default; GPB2_FACTOR_CACHE in the
+ * environment sets the default of new handles): allocated by the first generate_grad_vals
+ * when the device keeps max(10 %, 8 GB) of its memory free beyond it, else not used.  No
+ * reference counterpart (the reference recomputes every factor in every kernel). */
+int gpb2_problem_set_factor_cache(gpb2_problem* prob, int mode);
+/* The mode, whether the cache holds the current table (valid), and its size in bytes. */
+int gpb2_problem_factor_cache(const gpb2_problem* prob, int* mode, int* valid, int64_t* bytes);
+
 /* Sizes: N, M = N - n0, K, D, number of depth batches (n_offsets - 1). */
 int gpb2_problem_info(const gpb2_problem* prob, int64_t* n, int64_t* m, int64_t* k, int64_t* d,
                       int64_t* n_batches);
@@ -145,6 +161,12 @@ int64_t gpb2_launch_count(void);
  * (the reverse sweep then runs as in mode 0).  All four give bit-identical forward values.  A
  * barrier or wait that times out makes the call return GPB2_ERR_TIMEOUT. */
 int gpb2_set_forward_mode(int mode);
+
+/* Whether the dense first layer's work (the jitter ladder, the dense pullback) runs on the
+ * handle's second stream beside the per-point kernels (1, default; GPB2_OVERLAP=0 at load time
+ * sets 0) or in sequence on the call's stream (0: per-launch profiles then time each kernel
+ * alone).  Process-wide; results are the same either way.  No reference counterpart. */
+int gpb2_set_overlap(int on);
 
 /* Call mode, process-wide (default 1; GPB2_SYNC=0 in the environment at load time sets 0).
  * 1: every operation waits for its work and returns its status, including the numerical ones

@@ -531,19 +531,27 @@ def test_large_roundtrip_and_linearity_f32(cuda_device):
 
 
 @pytest.mark.parametrize("dt", [np.float64, np.float32])
-def test_two_pass_permutation(cuda_device, dt, monkeypatch):
-    # The two-pass original <-> tree permutation of large fields (forced here on a 3e5-point
-    # problem, with 4096-value destination blocks: 74 blocks, the last one partial) gives the
-    # direct gather / scatter's results bit for bit.
-    monkeypatch.setenv("GPB2_PERM_BLOCK_SHIFT", "12")
+@pytest.mark.parametrize("shift,offset", [("12", 0), (None, 0), (None, 1)])
+def test_two_pass_permutation(cuda_device, dt, shift, offset, monkeypatch):
+    # The two-pass original <-> library permutation of large fields (forced here on a 3e5-point
+    # problem; 4096-value destination blocks give 74 blocks, the default 64 KB ones 19 or 37, the
+    # last one partial) gives the direct gather / scatter's results bit for bit -- also from and
+    # into caller arrays that are not 16-byte aligned (offset 1: the element-wise form).
+    if shift is not None:
+        monkeypatch.setenv("GPB2_PERM_BLOCK_SHIFT", shift)
     prob, orc = _config_problem(300_000, 2, 500, 8, dt, 9)
     rng = np.random.default_rng(3)
-    xi = torch.from_numpy(rng.standard_normal(prob.npoints()).astype(dt)).to(cuda_device)
-    vb = torch.from_numpy(rng.standard_normal(prob.npoints()).astype(dt)).to(cuda_device)
+    n = prob.npoints()
+    xi = torch.from_numpy(rng.standard_normal(n + offset).astype(dt)).to(cuda_device)[offset:]
+    vb = torch.from_numpy(rng.standard_normal(n + offset).astype(dt)).to(cuda_device)[offset:]
     monkeypatch.setenv("GPB2_PERM_TWO_PASS_MIN", str(1 << 40))
     ref = (gp.generate(prob, xi), gp.generate_inv(prob, xi), gp.generate_grad_xi(prob, vb))
     monkeypatch.setenv("GPB2_PERM_TWO_PASS_MIN", "0")
-    got = (gp.generate(prob, xi), gp.generate_inv(prob, xi), gp.generate_grad_xi(prob, vb))
+    got = [torch.empty(n + offset, dtype=xi.dtype, device=cuda_device)[offset:] for _ in range(3)]
+    for fn, x, o in (("gpb2_generate", xi, got[0]), ("gpb2_generate_inv", xi, got[1]),
+                     ("gpb2_generate_grad_xi", vb, got[2])):
+        gp.api._call(fn, prob.handle, gp.api._ptr(x), gp.api._ptr(o), gp.api._stream(prob))
+    torch.cuda.synchronize(cuda_device)
     assert torch.equal(got[0], ref[0])
     assert torch.equal(got[1], ref[1])
     # The reverse sweep's atomic sums are not reproducible bit for bit from run to run.
@@ -586,3 +594,44 @@ def test_library_order(cuda_device, dt, monkeypatch):
     assert abs(l1[0] - l2[0]) <= TOL[dt] * abs(l2[0]) and relerr(l1[1], l2[1]) < TOL[dt]
     assert abs(gp.generate_logdet(prob) - gp.generate_logdet(ref)) <= \
         TOL[dt] * abs(gp.generate_logdet(ref))
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_factor_cache(cuda_device, dt):
+    # The vals-gradients that read each point's factor and pair weights from the factor cache
+    # agree with the ones that recompute them and with the host checker, before and after a
+    # table change (the cache is refilled by the new table's factor pass).  The cached entries
+    # are the recomputation's bits; the histogram sums are atomic, hence the tolerance.
+    prob, orc = _config_problem(60_000, 3, 300, 8, dt, 17)
+    rng = np.random.default_rng(5)
+    xi = rng.standard_normal(prob.npoints()).astype(dt)
+    vb = rng.standard_normal(prob.npoints()).astype(dt)
+    y = gp.generate(prob, xi)
+
+    def grads():
+        return (gp.generate_grad_vals(prob, xi, vb), gp.refine_logdet_grad_vals(prob),
+                gp.refine_inv_loss_grad_vals(prob, y))
+
+    prob.set_factor_cache(0)
+    assert not prob.factor_cache()["valid"]
+    ref = grads()
+    prob.set_factor_cache(1)
+    got = grads()
+    info = prob.factor_cache()
+    assert info["valid"] and info["mode"] == 1
+    assert info["bytes"] == (prob.npoints() - prob.n0) * (45 * dt().itemsize + 36 * (dt().itemsize + 2))
+    for a, b in zip(got, ref):
+        assert relerr(np.asarray(a), np.asarray(b)) < TOL[dt]
+    assert relerr(np.asarray(got[0]), O.generate_grad_vals(orc, xi, vb)) < TOL[dt]
+    # A new table: the factor pass of the next call refills the cache.
+    _, vals2 = gp.rbf_kernel(1.3, 0.25, 1e-4, 10.0, 1000, jitter=1e-5)
+    prob.update_vals(vals2.astype(dt))
+    assert not prob.factor_cache()["valid"]
+    got2 = gp.generate_grad_vals(prob, xi, vb)
+    assert prob.factor_cache()["valid"]
+    orc2 = O.make_problem(orc.coords, orc.nbrs, orc.offsets, orc.n0, orc.scale, orc.bins,
+                          vals2.astype(dt), orc.indices, dt)
+    assert relerr(np.asarray(got2), O.generate_grad_vals(orc2, xi, vb)) < TOL[dt]
+    prob.set_factor_cache(0)
+    assert not prob.factor_cache()["valid"]
+    assert relerr(np.asarray(gp.generate_grad_vals(prob, xi, vb)), np.asarray(got2)) < TOL[dt]
