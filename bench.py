@@ -73,7 +73,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c2", action="store_true")
     ap.add_argument("--ncu-case", action="store_true",
-                    help="profiling case: one untimed step of the workload, no JSON line")
+                    help="profiling case: one untimed step of the workload (factorising the "
+                         "table), then one more inside the NVTX range 'graphgp_step' (select "
+                         "it with ncu --nvtx --nvtx-include graphgp_step/); no JSON line")
     return ap.parse_args()
 
 
@@ -408,6 +410,10 @@ def run_b200(args):
     if args.ncu_case:
         step()
         torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("graphgp_step")
+        step()
+        torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_pop()
         prob.release()
         if comm is not None:
             comm.close()

@@ -20,6 +20,7 @@
 #include <string>
 
 #include "gpb2_comm.h"
+#include "gpb2_nvtx.h"
 #include "gpb2_problem.h"
 
 namespace gpb2 {
@@ -236,10 +237,12 @@ struct Impl {
         const Ops<T>* o = ops_of<T>(p);
         if (fwd_mode() == FwdMode::Fused && !have_factor) {
             const PointArgs<T> a = point_args<T>(p);
-            for (size_t b = 1; b < p->offsets.size(); b++)
+            for (size_t b = 1; b < p->offsets.size(); b++) {
+                NvtxRange r("forward", (long long)b - 1);
                 GPB2_TRY(check_launch(
                     o->fused_fwd(a, values, xi_ref, p->offsets[b - 1], p->offsets[b], s),
                     "fused forward"));
+            }
             return GPB2_OK;
         }
         if (!have_factor) GPB2_TRY(factor_all(p, s));
@@ -259,11 +262,13 @@ struct Impl {
                                   "forward sweep"));
             return GPB2_OK;  // the barrier's error word is read when the call finishes
         }
-        for (size_t b = 1; b < p->offsets.size(); b++)
+        for (size_t b = 1; b < p->offsets.size(); b++) {
+            NvtxRange r("forward", (long long)b - 1);
             GPB2_TRY(check_launch(o->sweep_fwd(values, xi_ref, (const T*)p->mv,
                                                (const T*)p->sd, p->nbrs, p->n0,
                                                p->offsets[b - 1], p->offsets[b], s),
                                   "forward sweep"));
+        }
         return GPB2_OK;
     }
 
@@ -278,10 +283,12 @@ struct Impl {
                                   "reverse sweep"));
             return GPB2_OK;
         }
-        for (size_t b = p->offsets.size() - 1; b >= 1; b--)
+        for (size_t b = p->offsets.size() - 1; b >= 1; b--) {
+            NvtxRange r("reverse", (long long)b - 1);
             GPB2_TRY(check_launch(o->sweep_rev(xg, vb, (const T*)p->mv, (const T*)p->sd, p->nbrs,
                                                p->n0, p->offsets[b - 1], p->offsets[b], s),
                                   "reverse sweep"));
+        }
         return GPB2_OK;
     }
 
@@ -785,6 +792,7 @@ struct Shard {
         const Ops<T>* o = ops_of<T>(p);
         GPB2_TRY(Dense<T>::apply_L(p, xt, v, s));
         for (const ShardBatch& x : pl.b) {
+            NvtxRange r("forward", (long long)(&x - pl.b.data()));
             int64_t a, e;
             pl.fwd_range(x, a, e);
             GPB2_TRY(Impl<T>::check_launch(o->sweep_fwd(v, xt + p->n0, (const T*)p->mv,
@@ -803,6 +811,7 @@ struct Shard {
         for (size_t i = pl.b.size(); i-- > 0;) {
             const ShardBatch& x = pl.b[i];
             if (x.hi <= x.lo) continue;
+            NvtxRange r("reverse", (long long)i);
             if (x.sharded)
                 GPB2_TRY(comm_reduce_scatter(c, vb, x.lo, x.chunk, kF64, s));
             else
@@ -972,6 +981,7 @@ using namespace gpb2;
         if (!(p)) return set_error(GPB2_ERR_INVALID_ARG, "%s: NULL problem", __func__);         \
         DeviceGuard _dg((p)->device);                                                          \
         if (!_dg.ok) return set_error(GPB2_ERR_NO_DEVICE, "cudaSetDevice(%d) failed", (p)->device); \
+        NvtxRange _nvtx(__func__);                                                             \
         cudaStream_t s = (cudaStream_t)stream;                                                 \
         const int _st = (p)->dtype == GPB2_F32 ? (CALL32) : (CALL64);                           \
         if (_st != GPB2_OK) {                                                                  \
@@ -1044,6 +1054,7 @@ static int check_range(const gpb2_problem* p, int64_t lo, int64_t hi, const char
     do {                                                                                       \
         DeviceGuard _dg((p)->device);                                                          \
         if (!_dg.ok) return set_error(GPB2_ERR_NO_DEVICE, "cudaSetDevice(%d) failed", (p)->device); \
+        NvtxRange _nvtx(__func__);                                                             \
         cudaStream_t s = (cudaStream_t)stream;                                                 \
         return (p)->dtype == GPB2_F32 ? (CALL32) : (CALL64);                                    \
     } while (0)

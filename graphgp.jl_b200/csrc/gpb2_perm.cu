@@ -5,20 +5,22 @@
 // Applied directly, a random permutation of N values costs a 32-byte sector per 4-byte value
 // (gathers) or a read-modify-write of one (scatters) once the field outgrows the L2.  Here each
 // direction is applied in two passes through a staging buffer split into destination blocks of
-// 2^shift values (64 KB: 2^14 floats or 2^13 doubles), so that a block fits in one CTA's shared
-// memory:
-//   pass 1 reads the input in order and writes value i to stage[pos[i]] -- the block of its
-//          destination, at the next free slot of that block, in input order, so every block is
-//          filled front to back (each block's write front advances by a few hundred contiguous
-//          values per grid sweep, combined into whole sectors in the L2);
-//   pass 2 gives each CTA whole blocks: it reads block b of the staging buffer into shared
-//          memory (contiguous, vectorised) and writes the output in order,
+// 2^shift values (128 KB: 2^15 floats or 2^14 doubles), each of which fits in one CTA's shared
+// memory.  Staging slot of input i: in the block of its destination, at the next free slot of
+// that block in input order.
+//   pass 1 gives each CTA whole source tiles of 2^shift inputs: it reads a tile into shared
+//          memory (contiguous, vectorised) and writes it out in slot order,
+//          stage[pos[k]] = tile[from[k]] for k = 0, 1, ... -- the tile's inputs that go to one
+//          block occupy consecutive slots, so consecutive threads store runs of consecutive
+//          slots (about N / 2^(2 shift) values per run: ~10 at 1e8 floats) rather than one
+//          scattered sector each;
+//   pass 2 gives each CTA whole destination blocks: it reads block b of the staging buffer into
+//          shared memory and writes the output in order,
 //          out[b * 2^shift + t] = block[q[b * 2^shift + t]] (q a 16-bit index into the block).
-// Both passes stream their inputs and output once; only pass 1's scattered stores touch the L2
-// one sector per value.  pos and q come from one stable sort of the inputs by destination block,
-// once per problem and direction: the sources of block b are exactly the destinations of block b,
-// so block b of the staging buffer is [b * 2^shift, (b + 1) * 2^shift) and q[d] is the rank of
-// d's source there.
+// Every array is streamed once.  The plan comes from two stable sorts per problem and
+// direction: the inputs by destination block (slots; q) and each tile's inputs by destination
+// block (the slot order of the tile: from, pos).  The sources of block b are exactly the
+// destinations of block b, so block b of the staging buffer is [b * 2^shift, (b + 1) * 2^shift).
 #include <cub/cub.cuh>
 
 #include <cstdlib>
@@ -32,9 +34,10 @@ cudaError_t prepare_kernel_smem(const void* kernel, size_t smem);
 
 namespace {
 
-constexpr int kThreads = 256;    // plan kernels and pass 1
-constexpr int kP2Threads = 512;  // pass 2
-constexpr int kBlockBytes = 64 * 1024;
+constexpr int kThreads = 256;     // plan kernels
+constexpr int kP1Threads = 1024;  // pass 1
+constexpr int kP2Threads = 1024;  // pass 2
+constexpr int kBlockBytes = 128 * 1024;  // a source tile (pass 1) or destination block (pass 2)
 
 inline unsigned grid_of(int64_t n) {
     const int64_t g = (n + kThreads - 1) / kThreads;
@@ -100,45 +103,45 @@ __device__ __forceinline__ void Quad<double>::store_stream(double* p) const {
     __stcs(reinterpret_cast<double2*>(p) + 1, make_double2(v[2], v[3]));
 }
 
-// Pass 1: groups of four consecutive inputs per thread, kUnroll groups in flight (their loads
-// all issued before the first store), a grid-stride walk over the groups; the last n % 4 inputs
-// go to the first threads of the grid.  The vector form needs a 16-byte aligned input, which the
-// launcher checks (else kVec = false: one input per step).
-constexpr int kUnroll = 2;
-
+// Load values [base, base + len) of src into shared memory (16-byte loads when aligned).
 template <typename T, bool kVec>
-__global__ void __launch_bounds__(kThreads)
-k_perm_pass1(const T* __restrict__ in, const int* __restrict__ pos, int64_t n,
-             T* __restrict__ stage) {
-    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+__device__ __forceinline__ void load_tile(T* __restrict__ tile, const T* __restrict__ src,
+                                          int64_t base, int len) {
+    int done = 0;
     if constexpr (kVec) {
-        const int64_t ng = n >> 2;
-        for (int64_t g0 = tid; g0 < ng; g0 += kUnroll * nth) {
-            Quad<T> v[kUnroll];
-            int4 ps[kUnroll];
+        const int nq = len >> 2;
+        for (int i = threadIdx.x; i < nq; i += blockDim.x) {
+            Quad<T> v;
+            v.load_stream(src + base + 4 * i);
 #pragma unroll
-            for (int u = 0; u < kUnroll; u++) {
-                const int64_t g = g0 + u * nth;
-                if (g < ng) {
-                    v[u].load_stream(in + 4 * g);
-                    ps[u] = __ldcs(reinterpret_cast<const int4*>(pos) + g);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kUnroll; u++) {
-                if (g0 + u * nth < ng) {
-                    stage[ps[u].x] = v[u].v[0];
-                    stage[ps[u].y] = v[u].v[1];
-                    stage[ps[u].z] = v[u].v[2];
-                    stage[ps[u].w] = v[u].v[3];
-                }
-            }
+            for (int u = 0; u < 4; u++) tile[4 * i + u] = v.v[u];
         }
-        const int64_t i = 4 * ng + tid;
-        if (i < n) stage[__ldcs(pos + i)] = __ldcs(in + i);
-    } else {
-        for (int64_t i = tid; i < n; i += nth) stage[__ldcs(pos + i)] = __ldcs(in + i);
+        done = 4 * nq;
+    }
+    for (int i = done + threadIdx.x; i < len; i += blockDim.x) tile[i] = __ldcs(src + base + i);
+}
+
+// Pass 1: CTA-wide, one source tile of 2^tshift values at a time (grid-stride over the tiles).
+// The tile is read into shared memory; then slot k of the tile's destination order (the
+// tile's values sorted by their staging position) is written: stage[dst[k]] = tile[from[k]].
+// Consecutive threads take consecutive k, so their stores fall in runs of consecutive staging
+// slots (one run per destination block the tile feeds) instead of one sector each.
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(kP1Threads)
+k_perm_pass1(const T* __restrict__ in, const uint16_t* __restrict__ from,
+             const int* __restrict__ dst, int64_t n, int tshift, T* __restrict__ stage) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    T* tile = reinterpret_cast<T*>(smem);
+    const int64_t tsz = 1ll << tshift;
+    const int64_t ntile = (n + tsz - 1) >> tshift;
+    for (int64_t t = blockIdx.x; t < ntile; t += gridDim.x) {
+        const int64_t base = t << tshift;
+        const int len = (int)(n - base < tsz ? n - base : tsz);
+        load_tile<T, kVec>(tile, in, base, len);
+        __syncthreads();
+        for (int k = threadIdx.x; k < len; k += blockDim.x)
+            stage[__ldcs(dst + base + k)] = tile[__ldcs(from + base + k)];
+        __syncthreads();  // the tile buffer is reused for the next tile
     }
 }
 
@@ -158,14 +161,7 @@ k_perm_pass2(const T* __restrict__ stage, const uint16_t* __restrict__ q, int64_
         const int64_t base = b << shift;
         const int len = (int)(n - base < bsz ? n - base : bsz);
         const int nq = len >> 2;  // whole quads; base is a multiple of 2^shift >= 16 values
-        for (int i = threadIdx.x; i < nq; i += blockDim.x) {
-            Quad<T> v;
-            v.load_stream(stage + base + 4 * i);
-#pragma unroll
-            for (int u = 0; u < 4; u++) blk[4 * i + u] = v.v[u];
-        }
-        for (int i = 4 * nq + threadIdx.x; i < len; i += blockDim.x)
-            blk[i] = __ldcs(stage + base + i);
+        load_tile<T, true>(blk, stage, base, len);
         __syncthreads();
         if constexpr (kVec) {
             for (int i = threadIdx.x; i < nq; i += blockDim.x) {
@@ -189,46 +185,90 @@ k_perm_pass2(const T* __restrict__ stage, const uint16_t* __restrict__ q, int64_
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Pass 1 runs on a grid of exactly the co-resident CTAs, so the whole grid walks the input front
-// to back together and every block's write front stays compact (its sectors are completed in the
-// L2 before they are written back).
-template <class Kern>
-unsigned resident_grid(Kern kern, int threads, size_t smem, int64_t work) {
-    const int64_t g = std::max<int64_t>(1, (work + threads - 1) / threads);
-    return (unsigned)std::min<int64_t>(g, coop_grid((const void*)kern, threads, smem));
+__global__ void k_tile_keys(const int* __restrict__ dmap, int64_t n, int shift, int bbits,
+                            unsigned long long* __restrict__ key, int* __restrict__ val) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        key[i] = ((unsigned long long)(i >> shift) << bbits) | (unsigned)(dmap[i] >> shift);
+        val[i] = (int)i;
+    }
 }
 
-// One direction's plan from its destination map.
-int make_plan(const int* dst, int64_t n, int shift, int* pos, uint16_t* q, cudaStream_t s) {
-    unsigned *k0 = nullptr, *k1 = nullptr;
-    int *v0 = nullptr, *v1 = nullptr;
+// From each tile's sources sorted by destination block (sorted[k], k in tile order): the
+// in-tile offset of the k-th source and its staging slot.
+__global__ void k_tile_plan(const int* __restrict__ sorted, const int* __restrict__ pos,
+                            int64_t n, int shift, uint16_t* __restrict__ from,
+                            int* __restrict__ dst) {
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n;
+         k += (int64_t)gridDim.x * blockDim.x) {
+        const int src = sorted[k];
+        from[k] = (uint16_t)(src & ((1 << shift) - 1));
+        dst[k] = pos[src];
+    }
+}
+
+template <typename K>
+int sort_pairs(cub::DoubleBuffer<K>& dk, cub::DoubleBuffer<int>& dv, int64_t n, int bits,
+               void*& tmp, size_t& tmp_bytes, cudaStream_t s) {
+    size_t tb = 0;
+    if (cub::DeviceRadixSort::SortPairs(nullptr, tb, dk, dv, n, 0, bits, s) != cudaSuccess)
+        return set_error(GPB2_ERR_CUDA, "permutation plan: sort sizing failed");
+    if (tb > tmp_bytes) {
+        if (tmp) cudaFree(tmp);
+        tmp = nullptr;
+        tmp_bytes = 0;
+        GPB2_TRY(ensure_alloc(&tmp, tb));
+        tmp_bytes = tb;
+    }
+    if (cub::DeviceRadixSort::SortPairs(tmp, tb, dk, dv, n, 0, bits, s) != cudaSuccess)
+        return set_error(GPB2_ERR_CUDA, "permutation plan: sort failed");
+    return GPB2_OK;
+}
+
+inline int bits_for(int64_t count) {  // bits of the largest index below count
+    int b = 1;
+    while (b < 62 && ((count - 1) >> b) != 0) b++;
+    return b;
+}
+
+// One direction's plan from its destination map (dmap[i]: where input i goes): pass 1's
+// (from, dst) in tile order and pass 2's q.
+int make_plan(const int* dmap, int64_t n, int shift, uint16_t* from, int* dst, uint16_t* q,
+              cudaStream_t s) {
+    unsigned long long *k0 = nullptr, *k1 = nullptr;
+    int *v0 = nullptr, *v1 = nullptr, *pos = nullptr;
     void* tmp = nullptr;
+    size_t tmp_bytes = 0;
     int st = GPB2_OK;
+    const int nb_bits = bits_for((n + (1ll << shift) - 1) >> shift);  // block (= tile) index
     do {
-        if ((st = ensure_alloc(reinterpret_cast<void**>(&k0), sizeof(unsigned) * n))) break;
-        if ((st = ensure_alloc(reinterpret_cast<void**>(&k1), sizeof(unsigned) * n))) break;
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&k0), sizeof(unsigned long long) * n))) break;
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&k1), sizeof(unsigned long long) * n))) break;
         if ((st = ensure_alloc(reinterpret_cast<void**>(&v0), sizeof(int) * n))) break;
         if ((st = ensure_alloc(reinterpret_cast<void**>(&v1), sizeof(int) * n))) break;
-        k_perm_keys<<<grid_of(n), kThreads, 0, s>>>(dst, n, shift, k0, v0);
-        cub::DoubleBuffer<unsigned> dk(k0, k1);
-        cub::DoubleBuffer<int> dv(v0, v1);
-        int bits = 1;
-        while (bits < 32 && ((n - 1) >> shift) >> bits) bits++;
-        size_t tb = 0;
-        if (cub::DeviceRadixSort::SortPairs(nullptr, tb, dk, dv, n, 0, bits, s) != cudaSuccess) {
-            st = set_error(GPB2_ERR_CUDA, "permutation plan: sort sizing failed");
-            break;
+        if ((st = ensure_alloc(reinterpret_cast<void**>(&pos), sizeof(int) * n))) break;
+        // Staging slots: the inputs stably sorted by destination block.
+        {
+            unsigned* kk0 = reinterpret_cast<unsigned*>(k0);
+            unsigned* kk1 = reinterpret_cast<unsigned*>(k1);
+            k_perm_keys<<<grid_of(n), kThreads, 0, s>>>(dmap, n, shift, kk0, v0);
+            cub::DoubleBuffer<unsigned> dk(kk0, kk1);
+            cub::DoubleBuffer<int> dv(v0, v1);
+            if ((st = sort_pairs(dk, dv, n, nb_bits, tmp, tmp_bytes, s))) break;
+            k_perm_plan<<<grid_of(n), kThreads, 0, s>>>(dv.Current(), dmap, n, shift, pos, q);
         }
-        if ((st = ensure_alloc(&tmp, tb))) break;
-        if (cub::DeviceRadixSort::SortPairs(tmp, tb, dk, dv, n, 0, bits, s) != cudaSuccess) {
-            st = set_error(GPB2_ERR_CUDA, "permutation plan: sort failed");
-            break;
+        // Pass 1's order: every tile's inputs stably sorted by destination block, i.e. by slot.
+        {
+            k_tile_keys<<<grid_of(n), kThreads, 0, s>>>(dmap, n, shift, nb_bits, k0, v0);
+            cub::DoubleBuffer<unsigned long long> dk(k0, k1);
+            cub::DoubleBuffer<int> dv(v0, v1);
+            if ((st = sort_pairs(dk, dv, n, 2 * nb_bits, tmp, tmp_bytes, s))) break;
+            k_tile_plan<<<grid_of(n), kThreads, 0, s>>>(dv.Current(), pos, n, shift, from, dst);
         }
-        k_perm_plan<<<grid_of(n), kThreads, 0, s>>>(dv.Current(), dst, n, shift, pos, q);
         const cudaError_t e = cudaStreamSynchronize(s);  // the temporaries are freed below
         if (e != cudaSuccess) st = set_error(GPB2_ERR_CUDA, "permutation plan: %s", cudaGetErrorString(e));
     } while (0);
-    for (void* b : {(void*)k0, (void*)k1, (void*)v0, (void*)v1, tmp})
+    for (void* b : {(void*)k0, (void*)k1, (void*)v0, (void*)v1, (void*)pos, tmp})
         if (b) cudaFree(b);
     return st;
 }
@@ -249,30 +289,33 @@ int ensure_perm_plan(gpb2_problem* p, cudaStream_t s) {
     const int64_t n = p->n;
     int* inv = nullptr;
     int st = GPB2_OK;
-    // 64 KB blocks; GPB2_PERM_BLOCK_SHIFT may only make them smaller (>= 16 values).
-    const int full = ts == 4 ? 14 : 13;
+    // 128 KB tiles and blocks; GPB2_PERM_BLOCK_SHIFT may only make them smaller (>= 16 values).
+    const int full = ts == 4 ? 15 : 14;
     int shift = full;
     if (const char* e = std::getenv("GPB2_PERM_BLOCK_SHIFT")) shift = std::atoi(e);
     shift = std::min(std::max(shift, 4), full);
     p->perm_shift = shift;
+    int* dst_g = nullptr;
     do {
         if ((st = ensure_alloc(&p->perm_stage, ts * n))) break;
-        if ((st = ensure_alloc(reinterpret_cast<void**>(&p->perm_pos_s), sizeof(int) * n))) break;
-        if ((st = ensure_alloc(reinterpret_cast<void**>(&p->perm_q_s), sizeof(uint16_t) * n))) break;
-        if ((st = ensure_alloc(reinterpret_cast<void**>(&p->perm_q_g), sizeof(uint16_t) * n))) break;
+        for (void** b : {(void**)&p->perm_pos_s, (void**)&dst_g})
+            if ((st = ensure_alloc(b, sizeof(int) * n))) break;
+        if (st) break;
+        for (void** b : {(void**)&p->perm_from_s, (void**)&p->perm_from_g, (void**)&p->perm_q_s,
+                         (void**)&p->perm_q_g})
+            if ((st = ensure_alloc(b, sizeof(uint16_t) * n))) break;
+        if (st) break;
         if ((st = ensure_alloc(reinterpret_cast<void**>(&inv), sizeof(int) * n))) break;
         // library -> original: input i (library), destination idx[i].
-        if ((st = make_plan(p->indices, n, shift, p->perm_pos_s, p->perm_q_s, s))) break;
+        if ((st = make_plan(p->indices, n, shift, p->perm_from_s, p->perm_pos_s, p->perm_q_s, s)))
+            break;
         // original -> library: input j (original), destination inv[j].
         k_perm_inverse<<<grid_of(n), kThreads, 0, s>>>(p->indices, n, inv);
-        int* pos_g = nullptr;
-        if ((st = ensure_alloc(reinterpret_cast<void**>(&pos_g), sizeof(int) * n))) break;
-        if ((st = make_plan(inv, n, shift, pos_g, p->perm_q_g, s))) {
-            cudaFree(pos_g);
-            break;
-        }
-        p->perm_pos_g = pos_g;  // set last: its presence marks a complete plan
+        if ((st = make_plan(inv, n, shift, p->perm_from_g, dst_g, p->perm_q_g, s))) break;
+        p->perm_pos_g = dst_g;  // set last: its presence marks a complete plan
+        dst_g = nullptr;
     } while (0);
+    if (dst_g) cudaFree(dst_g);
     if (inv) cudaFree(inv);
     return st;
 }
@@ -280,30 +323,29 @@ int ensure_perm_plan(gpb2_problem* p, cudaStream_t s) {
 template <typename T>
 int perm_apply(gpb2_problem* p, bool to_tree, const T* in, T* out, cudaStream_t s) {
     GPB2_TRY(ensure_perm_plan(p, s));
-    const int* pos = to_tree ? p->perm_pos_g : p->perm_pos_s;
+    const int* dst = to_tree ? p->perm_pos_g : p->perm_pos_s;
+    const uint16_t* from = to_tree ? p->perm_from_g : p->perm_from_s;
     const uint16_t* q = to_tree ? p->perm_q_g : p->perm_q_s;
     T* stage = static_cast<T*>(p->perm_stage);
     const char* name = to_tree ? "gather" : "scatter";
     const int64_t n = p->n;
-    // pos, q and the staging buffer come from cudaMalloc; the caller's arrays may not be aligned.
-    const int64_t nv = (n + 4 * kUnroll - 1) / (4 * kUnroll);
-    if (aligned16(in)) {
-        auto k = k_perm_pass1<T, true>;
-        GPB2_CUDA_TRY(launch_prof(name, k, dim3(resident_grid(k, kThreads, 0, nv)),
-                                  dim3(kThreads), 0, s, in, pos, n, stage));
-    } else {
-        auto k = k_perm_pass1<T, false>;
-        GPB2_CUDA_TRY(launch_prof(name, k, dim3(resident_grid(k, kThreads, 0, n)),
-                                  dim3(kThreads), 0, s, in, pos, n, stage));
-    }
-    const size_t smem = sizeof(T) << p->perm_shift;  // <= kBlockBytes
-    const int64_t nblk = (n + (1ll << p->perm_shift) - 1) >> p->perm_shift;
+    const int shift = p->perm_shift;
+    const size_t smem = sizeof(T) << shift;  // <= kBlockBytes
+    const int64_t nblk = (n + (1ll << shift) - 1) >> shift;  // tiles = blocks
+    // The staging buffer and the plan come from cudaMalloc; the caller's arrays may not be
+    // aligned (then the element-wise forms).
+    auto k1 = aligned16(in) ? k_perm_pass1<T, true> : k_perm_pass1<T, false>;
+    GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k1, kBlockBytes));
+    const unsigned g1 = (unsigned)std::min<int64_t>(
+        nblk, coop_grid((const void*)k1, kP1Threads, kBlockBytes));
+    GPB2_CUDA_TRY(launch_prof(name, k1, dim3(g1), dim3(kP1Threads), smem, s, in, from, dst, n,
+                              shift, stage));
     auto k2 = aligned16(out) ? k_perm_pass2<T, true> : k_perm_pass2<T, false>;
     GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k2, kBlockBytes));
     const unsigned g2 = (unsigned)std::min<int64_t>(
         nblk, coop_grid((const void*)k2, kP2Threads, kBlockBytes));
     GPB2_CUDA_TRY(launch_prof(name, k2, dim3(g2), dim3(kP2Threads), smem, s, (const T*)stage, q,
-                              n, p->perm_shift, out));
+                              n, shift, out));
     return GPB2_OK;
 }
 

@@ -267,7 +267,7 @@ static void free_problem(gpb2_problem* p) {
                     p->dwork,  p->dinfo, p->d_offsets, p->dsync, p->Ld,    p->trace,
                     p->Ldr,    p->Dinv,  p->Wtri, p->Ainv,  p->sh_v, p->sh_vb,
                     p->sh_xg,  p->sh_own, p->perm_stage, p->perm_pos_g, p->perm_q_g,
-                    p->perm_pos_s, p->perm_q_s, p->lib_tree, p->fc_L, p->fc_t, p->fc_lo};
+                    p->perm_pos_s, p->perm_q_s, p->perm_from_g, p->perm_from_s, p->lib_tree, p->fc_L, p->fc_t, p->fc_lo};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);

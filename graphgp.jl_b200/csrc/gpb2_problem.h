@@ -109,12 +109,17 @@ struct gpb2_problem {
     // Two-pass permutation plan of large problems (gpb2_perm.cu): staging buffer (N T) and, per
     // direction (g: original -> tree, s: tree -> original), each input's staging slot and each
     // output's rank in its destination block.
+    // Two-pass permutation plans, original -> library (_g) and library -> original (_s):
+    // pass 1 writes stage[pos[k]] = tile[from[k]] for slot k of each source tile, pass 2
+    // out[d] = block[q[d]] for each destination block (tiles and blocks of 2^perm_shift values).
     void* perm_stage = nullptr;
     int* perm_pos_g = nullptr;
-    uint16_t* perm_q_g = nullptr;  // per destination: rank of its source in the block
+    uint16_t* perm_from_g = nullptr;
+    uint16_t* perm_q_g = nullptr;
     int* perm_pos_s = nullptr;
+    uint16_t* perm_from_s = nullptr;
     uint16_t* perm_q_s = nullptr;
-    int perm_shift = 14;  // log2 of the values per destination block (64 KB)
+    int perm_shift = 15;
 };
 
 namespace gpb2 {
