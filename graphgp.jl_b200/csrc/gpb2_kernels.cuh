@@ -591,7 +591,17 @@ k_sweep_rev(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv,
 // ---------------------------------------------------------------------------------------------
 constexpr int kPersistThreads = 1024;  // k_sweep_fwd_flow
 
-// One point's read-only sweep inputs.
+// The transposed graph of the pull-form reverse sweep (built by gpb2_rev.cu): the edges of
+// point q are off[q] .. off[q + 1]; edge e comes from refined point mj[e] / K (slot
+// mj[e] % K) with weight w[e] = mean_vec of that slot.  off == nullptr: the atomic push.
+template <typename T>
+struct RevGraph {
+    const uint32_t* off = nullptr;
+    const int* mj = nullptr;
+    const T* w = nullptr;
+};
+
+// One point's read-only sweep inputs (a pulled reverse point keeps its edge range in nb[0..1]).
 template <typename T, int K>
 struct SweepIn {
     int nb[K];
@@ -606,6 +616,12 @@ struct SweepIn {
         sd = __ldg(sdv + m);
         if (xiv) xi = __ldg(xiv + m);
     }
+    __device__ __forceinline__ void load_pull(const RevGraph<T>& rg, const T* __restrict__ sdv,
+                                              int64_t p, int64_t n0) {
+        nb[0] = (int)__ldg(rg.off + p);
+        nb[1] = (int)__ldg(rg.off + p + 1);
+        sd = p >= n0 ? __ldg(sdv + (p - n0)) : T(0);
+    }
 };
 
 // Block shape of the persistent sweeps: as many threads as the register file holds with two
@@ -618,37 +634,72 @@ struct SweepShape {
         kRegs <= 56 ? 1024 : (kRegs <= 85 ? 768 : (kRegs <= 128 ? 512 : 256));
 };
 
+// The incoming terms of point p in the pull-form reverse sweep, in edge order (the serial
+// sweep's order): acc = vb[p] + w_0 vb[c_0] + w_1 vb[c_1] + ..., four edges' loads in flight.
+template <typename T, int K>
+__device__ __forceinline__ T pull_sum(T acc, const RevGraph<T>& rg, const T* __restrict__ vb,
+                                      int64_t n0, uint32_t e, uint32_t end) {
+    using N = Num<T>;
+    for (; e + 4 <= end; e += 4) {
+        int mj[4];
+        T w[4], v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            mj[u] = __ldg(rg.mj + e + u);
+            w[u] = __ldg(rg.w + e + u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) v[u] = __ldcg(vb + n0 + mj[u] / K);
+#pragma unroll
+        for (int u = 0; u < 4; u++) acc = N::add(acc, N::mul(w[u], v[u]));
+    }
+    for (; e < end; e++) acc = N::add(acc, N::mul(__ldg(rg.w + e), __ldcg(vb + n0 + __ldg(rg.mj + e) / K)));
+    return acc;
+}
+
 // Step i of a sweep visits forward batch i (F) and reverse batch nbatch-1-i (R); one grid
 // barrier per step.  A thread's tasks within a step are F_0, R_0, F_1, R_1, ... (F_k: point
 // offs[i] + gtid + k*gsz when below offs[i+1]; R_k likewise in the reverse batch), the absent
 // ones skipped; neither kind reads the other's output, so their interleaving is free.  Per
 // point the arithmetic and its order are those of the per-batch kernels k_sweep_fwd /
 // k_sweep_rev: forward values[p] = std*xi + sum_j mv[j]*values[nbr_j]; reverse
-// xg[p] = std*vb[p], vb[nbr_j] += mv[j]*vb[p] (atomic: batch-mates can share a neighbour).
-template <typename T, int K, bool F, bool R>
+// xg[p] = std*vb[p], vb[nbr_j] += mv[j]*vb[p] -- pushed as atomic additions, or, with PULL, as
+// every point's own sum of its incoming terms in the serial order (pull_sum), which needs one
+// more step for the dense block [0, n0) after batch 0.
+template <typename T, int K, bool F, bool R, bool PULL>
 __device__ __forceinline__ void sweep_pipe(T* __restrict__ values, const T* __restrict__ xi_ref,
                                            T* __restrict__ vb, T* __restrict__ xg,
                                            const T* __restrict__ mv, const T* __restrict__ sd,
                                            const int* __restrict__ nbrs, int64_t n0,
                                            const int64_t* __restrict__ offs, int nbatch,
-                                           GridSync gs) {
+                                           RevGraph<T> rg, GridSync gs) {
     using N = Num<T>;
     const int64_t gtid = sweep_gtid();
     const int64_t gsz = (int64_t)gridDim.x * blockDim.x;
+    const int nstep = nbatch + (R && PULL ? 1 : 0);
 
     int64_t f0 = 0, fhi = 0, r0 = 0, rhi = 0;  // this step's first points and batch ends
     auto set_step = [&](int i) {
-        f0 = offs[i] + gtid;
-        fhi = offs[i + 1];
-        r0 = offs[nbatch - 1 - i] + gtid;
-        rhi = offs[nbatch - i];
+        if (i < nbatch) {
+            f0 = offs[i] + gtid;
+            fhi = offs[i + 1];
+            r0 = offs[nbatch - 1 - i] + gtid;
+            rhi = offs[nbatch - i];
+        } else {  // the pulled dense block
+            f0 = fhi = 0;
+            r0 = gtid;
+            rhi = n0;
+        }
     };
     auto has = [&](bool fwd, int64_t k) {
         return fwd ? (F && f0 + k * gsz < fhi) : (R && r0 + k * gsz < rhi);
     };
     auto load = [&](SweepIn<T, K>& in, bool fwd, int64_t k) {
         const int64_t p = (fwd ? f0 : r0) + k * gsz;
-        in.load(mv, sd, fwd ? xi_ref : nullptr, nbrs, p - n0);
+        if (!fwd && PULL)
+            in.load_pull(rg, sd, p, n0);
+        else
+            in.load(mv, sd, fwd ? xi_ref : nullptr, nbrs, p - n0);
     };
 
     SweepIn<T, K> cur, nxt;
@@ -658,7 +709,7 @@ __device__ __forceinline__ void sweep_pipe(T* __restrict__ values, const T* __re
     valid = has(true, 0) || has(false, 0);
     fwd = has(true, 0);
     if (valid) load(cur, fwd, 0);
-    for (int i = 0; i < nbatch; i++) {
+    for (int i = 0; i < nstep; i++) {
         while (valid) {
             // The task after (fwd, k): R_k after F_k, else F_{k+1}, else R_{k+1}.
             bool nfwd = false, nvalid = true;
@@ -690,20 +741,29 @@ __device__ __forceinline__ void sweep_pipe(T* __restrict__ values, const T* __re
                 __stcg(values + p, acc);
             } else if (R) {
                 const int64_t p = r0 + k * gsz;
-                const T vbp = __ldcg(vb + p);
-                if (nvalid) load(nxt, nfwd, nk);
-                if (xg) xg[p] = N::mul(cur.sd, vbp);
-                sfor<0, K>([&](auto j_) {
-                    GPB2_CI(j);
-                    atomicAdd(vb + cur.nb[j], N::mul(cur.w[j], vbp));
-                });
+                if constexpr (PULL) {
+                    const T vb0 = __ldcg(vb + p);
+                    if (nvalid) load(nxt, nfwd, nk);
+                    const T acc = pull_sum<T, K>(vb0, rg, vb, n0, (uint32_t)cur.nb[0],
+                                                 (uint32_t)cur.nb[1]);
+                    __stcg(vb + p, acc);
+                    if (xg && p >= n0) xg[p] = N::mul(cur.sd, acc);
+                } else {
+                    const T vbp = __ldcg(vb + p);
+                    if (nvalid) load(nxt, nfwd, nk);
+                    if (xg) xg[p] = N::mul(cur.sd, vbp);
+                    sfor<0, K>([&](auto j_) {
+                        GPB2_CI(j);
+                        atomicAdd(vb + cur.nb[j], N::mul(cur.w[j], vbp));
+                    });
+                }
             }
             cur = nxt;
             fwd = nfwd;
             k = nk;
             valid = nvalid;
         }
-        if (i + 1 < nbatch) {
+        if (i + 1 < nstep) {
             set_step(i + 1);
             k = 0;
             valid = has(true, 0) || has(false, 0);
@@ -719,29 +779,31 @@ __global__ void __launch_bounds__(SweepShape<T, K>::kThreads)
 k_sweep_fwd_all(T* __restrict__ values, const T* __restrict__ xi_ref, const T* __restrict__ mv,
                 const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
                 const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
-    sweep_pipe<T, K, true, false>(values, xi_ref, nullptr, nullptr, mv, sd, nbrs, n0, offs, nbatch,
-                                  gs);
+    sweep_pipe<T, K, true, false, false>(values, xi_ref, nullptr, nullptr, mv, sd, nbrs, n0, offs,
+                                         nbatch, RevGraph<T>{}, gs);
 }
 
-template <typename T, int K>
+template <typename T, int K, bool PULL>
 __global__ void __launch_bounds__(SweepShape<T, K>::kThreads)
 k_sweep_rev_all(T* __restrict__ xg, T* __restrict__ vb, const T* __restrict__ mv,
                 const T* __restrict__ sd, const int* __restrict__ nbrs, int64_t n0,
-                const int64_t* __restrict__ offs, int nbatch, GridSync gs) {
-    sweep_pipe<T, K, false, true>(nullptr, nullptr, vb, xg, mv, sd, nbrs, n0, offs, nbatch, gs);
+                const int64_t* __restrict__ offs, int nbatch, RevGraph<T> rg, GridSync gs) {
+    sweep_pipe<T, K, false, true, PULL>(nullptr, nullptr, vb, xg, mv, sd, nbrs, n0, offs, nbatch,
+                                        rg, gs);
 }
 
 // generate_grad_vals needs both the forward field v (from xi) and the reverse cotangent vb (from
 // vbar); neither sweep reads the other's output, so one persistent kernel runs them together:
 // step i sweeps forward batch i and reverse batch nbatch-1-i, one grid barrier per step instead
 // of one per batch of each sweep.
-template <typename T, int K>
+template <typename T, int K, bool PULL>
 __global__ void __launch_bounds__(SweepShape<T, K>::kThreads)
 k_sweep_fwdrev_all(T* __restrict__ values, const T* __restrict__ xi_ref, T* __restrict__ vb,
                    const T* __restrict__ mv, const T* __restrict__ sd,
                    const int* __restrict__ nbrs, int64_t n0, const int64_t* __restrict__ offs,
-                   int nbatch, GridSync gs) {
-    sweep_pipe<T, K, true, true>(values, xi_ref, vb, nullptr, mv, sd, nbrs, n0, offs, nbatch, gs);
+                   int nbatch, RevGraph<T> rg, GridSync gs) {
+    sweep_pipe<T, K, true, true, PULL>(values, xi_ref, vb, nullptr, mv, sd, nbrs, n0, offs,
+                                       nbatch, rg, gs);
 }
 
 template <typename T, int K>
@@ -842,7 +904,7 @@ struct Ops {
                                  cudaStream_t);
     cudaError_t (*fused_fwd)(const PointArgs<T>&, T*, const T*, int64_t, int64_t, cudaStream_t);
     cudaError_t (*sweep_fwdrev_all)(T*, const T*, T*, const T*, const T*, const int*, int64_t,
-                                    const int64_t*, int, GridSync, cudaStream_t);
+                                    const int64_t*, int, RevGraph<T>, GridSync, cudaStream_t);
     cudaError_t (*sweep_fwd_flow)(T*, const T*, const T*, const T*, const int*, int64_t, int64_t,
                                   int*, cudaStream_t);
     cudaError_t (*sweep_fwd)(T*, const T*, const T*, const T*, const int*, int64_t, int64_t,
@@ -852,7 +914,7 @@ struct Ops {
     cudaError_t (*sweep_fwd_all)(T*, const T*, const T*, const T*, const int*, int64_t,
                                  const int64_t*, int, GridSync, cudaStream_t);
     cudaError_t (*sweep_rev_all)(T*, T*, const T*, const T*, const int*, int64_t, const int64_t*,
-                                 int, GridSync, cudaStream_t);
+                                 int, RevGraph<T>, GridSync, cudaStream_t);
 };
 
 template <typename T>
@@ -974,20 +1036,27 @@ struct Launch {
         return coop("sweep_fwd_flow", k_sweep_fwd_flow<T, K>, kPersistThreads, 0, s, values, xi_ref, mv, sd, nbrs,
                     n0, n, err);
     }
+    // rg.off set: the pull-form reverse sweep (an extra step for the dense block), else push.
     static cudaError_t sweep_fwdrev_all(T* values, const T* xi_ref, T* vb, const T* mv,
                                         const T* sd, const int* nbrs, int64_t n0,
-                                        const int64_t* offs, int nbatch, GridSync gs,
-                                        cudaStream_t s) {
+                                        const int64_t* offs, int nbatch, RevGraph<T> rg,
+                                        GridSync gs, cudaStream_t s) {
         if (nbatch <= 0) return cudaSuccess;
-        return coop("sweep_fwdrev_all", k_sweep_fwdrev_all<T, K>, SS::kThreads, 0, s, values, xi_ref, vb, mv, sd,
-                    nbrs, n0, offs, nbatch, gs);
+        if (rg.off)
+            return coop("sweep_fwdrev_all", k_sweep_fwdrev_all<T, K, true>, SS::kThreads, 0, s,
+                        values, xi_ref, vb, mv, sd, nbrs, n0, offs, nbatch, rg, gs);
+        return coop("sweep_fwdrev_all", k_sweep_fwdrev_all<T, K, false>, SS::kThreads, 0, s,
+                    values, xi_ref, vb, mv, sd, nbrs, n0, offs, nbatch, rg, gs);
     }
     static cudaError_t sweep_rev_all(T* xg, T* vb, const T* mv, const T* sd, const int* nbrs,
-                                     int64_t n0, const int64_t* offs, int nbatch, GridSync gs,
-                                     cudaStream_t s) {
+                                     int64_t n0, const int64_t* offs, int nbatch, RevGraph<T> rg,
+                                     GridSync gs, cudaStream_t s) {
         if (nbatch <= 0) return cudaSuccess;
-        return coop("sweep_rev_all", k_sweep_rev_all<T, K>, SS::kThreads, 0, s, xg, vb, mv, sd, nbrs, n0, offs,
-                    nbatch, gs);
+        if (rg.off)
+            return coop("sweep_rev_all", k_sweep_rev_all<T, K, true>, SS::kThreads, 0, s, xg, vb,
+                        mv, sd, nbrs, n0, offs, nbatch, rg, gs);
+        return coop("sweep_rev_all", k_sweep_rev_all<T, K, false>, SS::kThreads, 0, s, xg, vb, mv,
+                    sd, nbrs, n0, offs, nbatch, rg, gs);
     }
     static const Ops<T>* ops() {
         static const Ops<T> o = {factor,        inv,           logdet,

@@ -272,13 +272,29 @@ struct Impl {
         return GPB2_OK;
     }
 
+    // The transposed graph of the pull-form reverse sweep (built on first use, its weights once
+    // per table -- after the table's factor pass), or none: the atomic push.
+    static int rev_graph(P* p, RevGraph<T>& rg, cudaStream_t s) {
+        rg = RevGraph<T>{};
+        if (p->rev_mode == 0) return GPB2_OK;
+        GPB2_TRY(ensure_rev_graph(p, s));
+        if (!p->rev_off) return GPB2_OK;
+        GPB2_TRY(ensure_rev_weights<T>(p, s));
+        rg.off = p->rev_off;
+        rg.mj = p->rev_mj;
+        rg.w = static_cast<const T*>(p->rev_w);
+        return GPB2_OK;
+    }
+
     // Reverse sweep over the batches, latest first; xg may be NULL.
     static int reverse_sweep(P* p, T* xg, T* vb, cudaStream_t s) {
         const Ops<T>* o = ops_of<T>(p);
         if (fwd_mode() == FwdMode::Persistent || fwd_mode() == FwdMode::Flow) {
+            RevGraph<T> rg;
+            GPB2_TRY(rev_graph(p, rg, s));
             GPB2_TRY(arm_sync(p, s));
             GPB2_TRY(check_launch(o->sweep_rev_all(xg, vb, (const T*)p->mv, (const T*)p->sd,
-                                                   p->nbrs, p->n0, p->d_offsets, nbatch(p),
+                                                   p->nbrs, p->n0, p->d_offsets, nbatch(p), rg,
                                                    grid_sync_of(p), s),
                                   "reverse sweep"));
             return GPB2_OK;
@@ -533,10 +549,13 @@ struct Impl {
             GPB2_CUDA_TRY(
                 cudaMemcpyAsync(vb, vbar, sizeof(T) * p->n, cudaMemcpyDeviceToDevice, s));
         if (fwd_mode() == FwdMode::Persistent) {  // both sweeps in one persistent kernel
+            RevGraph<T> rg;
+            GPB2_TRY(rev_graph(p, rg, s));
             GPB2_TRY(arm_sync(p, s));
             GPB2_TRY(check_launch(ops_of<T>(p)->sweep_fwdrev_all(
                                       v, xt + p->n0, vb, (const T*)p->mv, (const T*)p->sd,
-                                      p->nbrs, p->n0, p->d_offsets, nbatch(p), grid_sync_of(p), s),
+                                      p->nbrs, p->n0, p->d_offsets, nbatch(p), rg,
+                                      grid_sync_of(p), s),
                                   "forward+reverse sweep"));
         } else {
             GPB2_TRY(refine_sweep(p, v, xt + p->n0, true, s));

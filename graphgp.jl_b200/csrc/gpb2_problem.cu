@@ -236,6 +236,7 @@ static int load_table(gpb2_problem* p, const void* vals_dev, cudaStream_t s) {
     p->factor_valid = false;  // and so do the per-point mean_vec / std
     p->sh_factor_valid = false;
     p->fc_valid = false;      // and the factor cache
+    p->rev_w_valid = false;   // and the transposed graph's weights
     GPB2_CUDA_TRY(cudaMemcpyAsync(p->vals, vals_dev, ts * p->nb, cudaMemcpyDeviceToDevice, s));
     // The bins do not change after creation: they are read back once, the values every time.
     const bool first = p->hbins.size() != ts * p->nb;
@@ -267,7 +268,8 @@ static void free_problem(gpb2_problem* p) {
                     p->dwork,  p->dinfo, p->d_offsets, p->dsync, p->Ld,    p->trace,
                     p->Ldr,    p->Dinv,  p->Wtri, p->Ainv,  p->sh_v, p->sh_vb,
                     p->sh_xg,  p->sh_own, p->perm_stage, p->perm_pos_g, p->perm_q_g,
-                    p->perm_pos_s, p->perm_q_s, p->perm_from_g, p->perm_from_s, p->lib_tree, p->fc_L, p->fc_t, p->fc_lo};
+                    p->perm_pos_s, p->perm_q_s, p->perm_from_g, p->perm_from_s, p->lib_tree, p->fc_L, p->fc_t, p->fc_lo,
+                    p->rev_off, p->rev_mj, p->rev_w};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);
@@ -328,6 +330,8 @@ static int create_impl(gpb2_problem** out, int dtype, int device, const uint32_t
     auto* p = new gpb2_problem();
     if (const char* e = std::getenv("GPB2_FACTOR_CACHE"))  // default mode of new handles
         p->fc_mode = std::min(std::max(std::atoi(e), 0), 2);
+    if (const char* e = std::getenv("GPB2_REVERSE_MODE"))  // likewise
+        p->rev_mode = std::min(std::max(std::atoi(e), 0), 2);
     p->dtype = dtype;
     p->device = device;
     p->n = n;
@@ -536,6 +540,32 @@ int gpb2_problem_set_factor_cache(gpb2_problem* p, int mode) {
         p->fc_lo = nullptr;
         p->fc_valid = false;
     }
+    return GPB2_OK;
+}
+
+int gpb2_problem_set_reverse_mode(gpb2_problem* p, int mode) {
+    clear_error();
+    if (!p) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_set_reverse_mode: NULL problem");
+    if (mode < 0 || mode > 2)
+        return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_set_reverse_mode: mode %d", mode);
+    p->rev_mode = mode;
+    if (mode == 0 && p->rev_off) {  // give the memory back (cudaFree waits for the device)
+        DeviceGuard dg(p->device);
+        for (void* b : {(void*)p->rev_off, (void*)p->rev_mj, p->rev_w})
+            if (b) cudaFree(b);
+        p->rev_off = nullptr;
+        p->rev_mj = nullptr;
+        p->rev_w = nullptr;
+        p->rev_w_valid = false;
+    }
+    return GPB2_OK;
+}
+
+int gpb2_problem_reverse_mode(const gpb2_problem* p, int* mode, int* built, int64_t* bytes) {
+    if (!p) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_reverse_mode: NULL problem");
+    if (mode) *mode = p->rev_mode;
+    if (built) *built = p->rev_off ? 1 : 0;
+    if (bytes) *bytes = (int64_t)rev_graph_bytes(p);
     return GPB2_OK;
 }
 

@@ -53,6 +53,16 @@ struct gpb2_problem {
     int fc_mode = 2;
     bool fc_valid = false;       // the cache holds the current table's factors of all points
 
+    // Transposed graph of the pull-form reverse sweep (gpb2_rev.cu): rev_off (N + 1) delimits
+    // each point's incoming edges in rev_mj (child m * K + slot j, in the serial sweep's order)
+    // and rev_w (that slot's mean_vec, per table).  Mode 0: atomic push; 1: pull; 2 (default):
+    // pull when the graph fits in free memory with a margin.
+    uint32_t* rev_off = nullptr;
+    int* rev_mj = nullptr;
+    void* rev_w = nullptr;
+    int rev_mode = 2;
+    bool rev_w_valid = false;    // rev_w holds the current table's weights
+
     // Dense n0 block.
     void* Ld = nullptr;       // (n0, n0) column-major lower: the selected ladder candidate
     void* Lcand = nullptr;    // ladder candidates, each (n0, n0) column-major lower
@@ -196,6 +206,14 @@ PointArgs<T> point_args(const gpb2_problem* p, FcUse fc = FcUse::None) {
 int ensure_factor_cache(gpb2_problem* p, cudaStream_t s);
 // Bytes of the factor cache of a problem.
 size_t factor_cache_bytes(const gpb2_problem* p);
+
+// The transposed graph of the pull-form reverse sweep: built once per problem when the mode
+// allows (mode 2: if it fits in free memory with a margin); its weights once per table, after
+// the table's per-point factor pass.
+int ensure_rev_graph(gpb2_problem* p, cudaStream_t s);
+template <typename T>
+int ensure_rev_weights(gpb2_problem* p, cudaStream_t s);
+size_t rev_graph_bytes(const gpb2_problem* p);
 
 template <typename T>
 const Ops<T>* ops_of(const gpb2_problem* p);

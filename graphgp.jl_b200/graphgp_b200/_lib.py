@@ -85,6 +85,8 @@ _SIGNATURES = {
     "gpb2_problem_prefactor": (I32, [P, P]),
     "gpb2_problem_info": (I32, [P, PI64, PI64, PI64, PI64, PI64]),
     "gpb2_problem_set_factor_cache": (I32, [P, I32]),
+    "gpb2_problem_set_reverse_mode": (I32, [P, I32]),
+    "gpb2_problem_reverse_mode": (I32, [P, C.POINTER(I32), C.POINTER(I32), PI64]),
     "gpb2_problem_factor_cache": (I32, [P, C.POINTER(I32), C.POINTER(I32), PI64]),
     "gpb2_problem_destroy": (I32, [P]),
     "gpb2_problem_dense_jitter": (I32, [P, PD]),

@@ -206,6 +206,22 @@ class GraphGPProblem:
                    "factor_cache")
         return {"mode": mode.value, "valid": bool(valid.value), "bytes": nbytes.value}
 
+    def set_reverse_mode(self, mode: int) -> "GraphGPProblem":
+        """Reverse sweep form: 0 atomic push (sums in no fixed order), 1 pull through the
+        transposed graph (the serial sweep's sums bit for bit), 2 (default) pull when the graph
+        fits in free device memory with a margin."""
+        _lib.check(_lib.lib().gpb2_problem_set_reverse_mode(self.handle, int(mode)),
+                   "set_reverse_mode")
+        return self
+
+    def reverse_mode(self) -> dict:
+        """{"mode", "built" (the transposed graph exists), "bytes"}."""
+        mode, built, nbytes = C.c_int32(), C.c_int32(), C.c_int64()
+        _lib.check(_lib.lib().gpb2_problem_reverse_mode(self.handle, C.byref(mode),
+                                                         C.byref(built), C.byref(nbytes)),
+                   "reverse_mode")
+        return {"mode": mode.value, "built": bool(built.value), "bytes": nbytes.value}
+
     def check(self) -> "GraphGPProblem":
         """Wait for this handle's queued work on the current stream and raise its status (in
         the asynchronous call mode, `set_synchronous(False)`, operations do not wait)."""

@@ -126,6 +126,19 @@ int gpb2_problem_set_factor_cache(gpb2_problem* prob, int mode);
 /* The mode, whether the cache holds the current table (valid), and its size in bytes. */
 int gpb2_problem_factor_cache(const gpb2_problem* prob, int* mode, int* valid, int64_t* bytes);
 
+/* Reverse sweep of generate_grad_xi / generate_grad_vals.  mode 0: every refined point pushes
+ * its K terms mean_vec[j] * vb[p] into its neighbours' cotangents with atomic additions (the
+ * reference's form; sums in no fixed order).  1: every point pulls its incoming terms through
+ * the transposed graph, in the serial sweep's order (descending tree order of the child, slot
+ * order) -- sums bit for bit those of the serial reference sweep and reproducible -- at the
+ * cost of (4 + sizeof(T)) bytes per edge plus 4 per point of device memory (the graph is built
+ * once, its weights once per table).  2 (default; GPB2_REVERSE_MODE in the environment sets the
+ * default of new handles): 1 when it fits with a margin of free memory, else 0.  The per-batch
+ * sweep modes and the level-sharded operations always push.  No reference counterpart. */
+int gpb2_problem_set_reverse_mode(gpb2_problem* prob, int mode);
+/* The mode, whether the transposed graph is built, and its size in bytes. */
+int gpb2_problem_reverse_mode(const gpb2_problem* prob, int* mode, int* built, int64_t* bytes);
+
 /* Sizes: N, M = N - n0, K, D, number of depth batches (n_offsets - 1). */
 int gpb2_problem_info(const gpb2_problem* prob, int64_t* n, int64_t* m, int64_t* k, int64_t* d,
                       int64_t* n_batches);

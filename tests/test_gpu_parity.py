@@ -639,3 +639,30 @@ def test_factor_cache(cuda_device, dt):
     prob.set_factor_cache(0)
     assert not prob.factor_cache()["valid"]
     assert relerr(np.asarray(gp.generate_grad_vals(prob, xi, vb)), np.asarray(got2)) < TOL[dt]
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_reverse_pull_bit_exact(cuda_device, dt):
+    # The pull-form reverse sweep adds every point's incoming terms in the serial reference
+    # sweep's order (descending tree order of the child, slot order), so generate_grad_xi is the
+    # host checker's bit for bit and the same from run to run; the atomic push agrees to the
+    # tolerance.  generate_grad_vals (atomic histogram) agrees to the tolerance in both forms.
+    prob, orc = _config_problem(80_000, 2, 400, 8, dt, 23)
+    rng = np.random.default_rng(8)
+    n = prob.npoints()
+    xi = rng.standard_normal(n).astype(dt)
+    vb = rng.standard_normal(n).astype(dt)
+    prob.set_reverse_mode(1)
+    g = np.asarray(gp.generate_grad_xi(prob, vb))
+    info = prob.reverse_mode()
+    assert info["built"] and info["mode"] == 1
+    assert info["bytes"] == (n - prob.n0) * 8 * (4 + dt().itemsize) + 4 * (n + 1)
+    ref = O.generate_grad_xi(orc, vb)
+    assert np.array_equal(g, ref), relerr(g, ref)
+    assert np.array_equal(np.asarray(gp.generate_grad_xi(prob, vb)), g)
+    dv = np.asarray(gp.generate_grad_vals(prob, xi, vb))
+    assert relerr(dv, O.generate_grad_vals(orc, xi, vb)) < TOL[dt]
+    prob.set_reverse_mode(0)
+    assert not prob.reverse_mode()["built"]
+    assert relerr(np.asarray(gp.generate_grad_xi(prob, vb)), ref) < TOL[dt]
+    assert relerr(np.asarray(gp.generate_grad_vals(prob, xi, vb)), dv) < TOL[dt]
