@@ -314,8 +314,12 @@ def algorithmic_bytes(kind: str, K: int, D: int, T: int = 4, I: int = 4) -> floa
     coords = 4 * D * (K + 1)
     if kind == "factor":      # nbrs + joint coords in, mean_vec + std out
         return I * K + coords + T * K + T
-    if kind == "grad_vals":   # nbrs + coords + vb[p] + xi[p] + v[nbr] in (histogram flush excluded)
-        return I * K + coords + 2 * T + T * K
+    if kind == "grad_vals":   # nbrs + coords + vb[p] + xi[p] + v[nbr] + mean_vec in (histogram
+        return I * K + coords + 2 * T + T * K + T * K  # flush excluded)
+    if kind == "grad_vals_cached":  # the factor cache's L + pair weights instead of the coords
+        nt = (K + 1) * (K + 2) // 2
+        nr = nt - (K + 1)
+        return I * K + nt * T + nr * (T + 2) + 2 * T + T * K + T * K
     if kind == "sweep_fwd":   # nbrs + mean_vec + std + xi + values[nbr] in, values[p] out
         return I * K + T * K + T + T + T * K + T
     if kind == "sweep_rev":   # nbrs + mean_vec + std + vb[p] in, xg[p] out, K atomics (RMW)
@@ -324,10 +328,17 @@ def algorithmic_bytes(kind: str, K: int, D: int, T: int = 4, I: int = 4) -> floa
         return I * K + coords + T * (K + 2)
     if kind == "sweep_fwd_all":
         return algorithmic_bytes("sweep_fwd", K, D, T, I)
+    if kind == "sweep_rev_pull":  # its edge range + std + vb[p] in and out + xg[p] out; per
+        return I + T + 2 * T + T + K * (I + T + T)  # incoming edge: child, weight, vb[child]
     if kind == "sweep_rev_all":
         return algorithmic_bytes("sweep_rev", K, D, T, I)
     if kind == "sweep_fwdrev_all":
         return algorithmic_bytes("sweep_fwd", K, D, T, I) + algorithmic_bytes("sweep_rev", K, D, T, I)
+    if kind == "sweep_rev_all_pull":
+        return algorithmic_bytes("sweep_rev_pull", K, D, T, I)
+    if kind == "sweep_fwdrev_all_pull":  # no xg output in generate_grad_vals' joint sweep
+        return (algorithmic_bytes("sweep_fwd", K, D, T, I)
+                + algorithmic_bytes("sweep_rev_pull", K, D, T, I) - T)
     return float("nan")
 
 
@@ -484,17 +495,28 @@ def run_b200(args):
         per_step = cnt / k
         return share / per_step if kind in PER_BATCH else share
 
+    def form(kind):
+        # The form a kernel ran in: k_grad_vals reading the factor cache, the persistent reverse
+        # sweeps pulling through the transposed graph (their bytes differ from the other form).
+        if kind == "grad_vals" and prob.factor_cache()["valid"]:
+            return "grad_vals_cached"
+        if kind in ("sweep_rev_all", "sweep_fwdrev_all") and prob.reverse_mode()["built"]:
+            return kind + "_pull"
+        return kind
+
     def roofline_of(prof, k, kinds=None):
         refine = {kk: v for kk, v in prof.items()
                   if not np.isnan(algorithmic_bytes(kk, K, D)) and (kinds is None or kk in kinds)}
         kind, (cnt, tot) = max(refine.items(), key=lambda kv: kv[1][1])
         ppl = points_per_launch(kind, cnt, k)
         launch_ms = tot / cnt
-        ach = algorithmic_bytes(kind, K, D) * ppl / (launch_ms / 1e3) / 1e9
-        return {"bound": "hbm", "kernel": kind, "achieved": ach, "peak": peak, "unit": "GB/s",
-                "frac": ach / peak, "traffic": NCU_TRAFFIC.get(kind), "peak_source": peak_src,
-                "traffic_source": NCU_SOURCE if kind in NCU_TRAFFIC else None,
-                "bytes_per_point": algorithmic_bytes(kind, K, D),
+        bpp = algorithmic_bytes(form(kind), K, D)
+        ach = bpp * ppl / (launch_ms / 1e3) / 1e9
+        return {"bound": "hbm", "kernel": kind, "form": form(kind), "achieved": ach, "peak": peak,
+                "unit": "GB/s", "frac": ach / peak, "traffic": NCU_TRAFFIC.get(form(kind)),
+                "peak_source": peak_src,
+                "traffic_source": NCU_SOURCE if form(kind) in NCU_TRAFFIC else None,
+                "bytes_per_point": bpp,
                 "points_per_launch": ppl, "launches_per_step": cnt / k, "ms_per_launch": launch_ms,
                 "kernels": {kk: {"launches": v[0], "ms": round(v[1], 4)} for kk, v in prof.items()}}
 

@@ -243,6 +243,57 @@ __global__ void k_dense_scatter(TableView<T> tv, const uint32_t* __restrict__ co
     }
 }
 
+// Position gradient of the dense block (_dense_logdet_grad_points / _dense_inv_loss_grad_points,
+// src/dense.jl:188-225, 271-297): pair (i, j), i > j, cotangent g (mode 1: Kinv_ij from the
+// lower triangle of the column-major K^-1; mode 2: -alpha_i * alpha_j) times k'(r) / r times
+// scale * (x_i - x_j) added to point i and subtracted from point j (coincident points and flat
+// table segments add nothing).  dp is (N, D) row-major, double atomics.
+template <typename T>
+__global__ void __launch_bounds__(kDenseThreads)
+k_dense_points(TableView<T> tv, const uint32_t* __restrict__ coords, int D, int DS, T scale,
+               int64_t n, int mode, const T* __restrict__ A, double* __restrict__ dp) {
+    using N = Num<T>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    SmemTable<T> tab;
+    tab.stage(tv, smem, threadIdx.x, blockDim.x);
+    __syncthreads();
+    for (int64_t j = blockIdx.x; j < n; j += gridDim.x) {
+        for (int64_t i = j + 1 + threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t* ci = coords + i * DS;
+            const uint32_t* cj = coords + j * DS;
+            unsigned long long sq = 0;
+            for (int d = 0; d < D; d++) {
+                const uint32_t di = ci[d] > cj[d] ? ci[d] - cj[d] : cj[d] - ci[d];
+                sq += (unsigned long long)di * di;
+            }
+            if (sq == 0) continue;
+            const T r = N::mul(N::sqrt(N::from_i64((long long)sq)), scale);
+            const T dcov = tab.dr(r);
+            if (dcov == T(0)) continue;
+            const T g = mode == 1 ? A[j * n + i] : N::mul(-A[i], A[j]);
+            const T factor = N::div(N::mul(g, dcov), r);
+            for (int d = 0; d < D; d++) {
+                const T diff = N::mul(scale, N::sub(N::from_i64((long long)ci[d]),
+                                                    N::from_i64((long long)cj[d])));
+                const T c = N::mul(factor, diff);
+                atomicAdd(dp + i * D + d, (double)c);
+                atomicAdd(dp + j * D + d, -(double)c);
+            }
+        }
+    }
+}
+
+template <typename T>
+int scatter_points(gpb2_problem* p, int mode, const T* A, double* dp, cudaStream_t s) {
+    const size_t smem = table_smem_bytes<T>((int)p->nb, p->nkeys);
+    GPB2_CUDA_TRY(prepare_kernel_smem((const void*)k_dense_points<T>, smem));
+    const int grid = (int)std::min<int64_t>(p->n0, 2 * 148);
+    GPB2_CUDA_TRY(launch_prof("dense_points", k_dense_points<T>, dim3(grid), dim3(kDenseThreads),
+                              smem, s, table_view<T>(p), (const uint32_t*)p->coords, (int)p->d,
+                              coord_stride((int)p->d), (T)p->scale, p->n0, mode, A, dp));
+    return GPB2_OK;
+}
+
 template <typename T>
 int grid_for(int64_t n) {
     int64_t g = (n + kDenseThreads - 1) / kDenseThreads;
@@ -411,8 +462,9 @@ int Dense<T>::grad_vals(gpb2_problem* p, const T* vb, const T* xi, double* hist,
     return scatter<T>(p, 0, X, hist, s);
 }
 
+// K^-1 (column-major, lower triangle valid) into p->Wd.
 template <typename T>
-int Dense<T>::logdet_grad(gpb2_problem* p, double* hist, cudaStream_t s) {
+static int dense_kinv(gpb2_problem* p, cudaStream_t s) {
     const int n = (int)p->n0;
     T* W = static_cast<T*>(p->Wd);
     if (p->tri_ready) {
@@ -421,19 +473,33 @@ int Dense<T>::logdet_grad(gpb2_problem* p, double* hist, cudaStream_t s) {
         GPB2_TRY(wait_tri(p, s, true));
         GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
         GPB2_BLAS_TRY(syrk_tn(p->blas, n, static_cast<const T*>(p->Ainv), W));
-        return scatter<T>(p, 1, W, hist, s);
+        return GPB2_OK;
     }
     GPB2_CUDA_TRY(cudaMemcpyAsync(W, p->Ld, sizeof(T) * (size_t)n * n, cudaMemcpyDeviceToDevice,
                                   s));
     GPB2_SOLVER_TRY(cusolverDnSetStream(p->solver, s));
     GPB2_SOLVER_TRY(potri(p->solver, n, W, static_cast<T*>(p->dwork),
                           (int)(p->dwork_bytes / sizeof(T)), p->dinfo));
-    return scatter<T>(p, 1, W, hist, s);
+    return GPB2_OK;
 }
 
 template <typename T>
-int Dense<T>::inv_loss_grad(gpb2_problem* p, const T* y, double* hist, double* loss,
-                            cudaStream_t s) {
+int Dense<T>::logdet_grad(gpb2_problem* p, double* hist, cudaStream_t s) {
+    GPB2_TRY(dense_kinv<T>(p, s));
+    return scatter<T>(p, 1, static_cast<const T*>(p->Wd), hist, s);
+}
+
+template <typename T>
+int Dense<T>::logdet_points(gpb2_problem* p, double* dp, cudaStream_t s) {
+    GPB2_TRY(dense_kinv<T>(p, s));
+    return scatter_points<T>(p, 1, static_cast<const T*>(p->Wd), dp, s);
+}
+
+// z = L^-1 y (its half squared norm into *loss when loss is set) and alpha = L^-T z = K^-1 y;
+// returns alpha (in p->Wd).
+template <typename T>
+static int dense_alpha(gpb2_problem* p, const T* y, double* loss, const T** alpha_out,
+                       cudaStream_t s) {
     const int n = (int)p->n0;
     T* z = static_cast<T*>(p->Wd);
     if (p->tri_ready) {
@@ -443,16 +509,35 @@ int Dense<T>::inv_loss_grad(gpb2_problem* p, const T* y, double* hist, double* l
         T* alpha = z + n;
         GPB2_BLAS_TRY(cublasSetStream(p->blas, s));
         GPB2_BLAS_TRY(gemv(p->blas, CUBLAS_OP_N, n, static_cast<const T*>(p->Ainv), y, z));
+        if (loss)
+            GPB2_CUDA_TRY(launch_prof("dense_sumsq", k_sum_sq_half<T>, dim3(1),
+                                      dim3(kDenseThreads), 0, s, (const T*)z, (int64_t)n, loss));
+        GPB2_BLAS_TRY(gemv(p->blas, CUBLAS_OP_T, n, static_cast<const T*>(p->Ainv), z, alpha));
+        *alpha_out = alpha;
+        return GPB2_OK;
+    }
+    GPB2_TRY(Dense<T>::solve_L(p, y, z, s));  // z = L \ y  (generate_dense_inv)
+    if (loss)
         GPB2_CUDA_TRY(launch_prof("dense_sumsq", k_sum_sq_half<T>, dim3(1), dim3(kDenseThreads),
                                   0, s, (const T*)z, (int64_t)n, loss));
-        GPB2_BLAS_TRY(gemv(p->blas, CUBLAS_OP_T, n, static_cast<const T*>(p->Ainv), z, alpha));
-        return scatter<T>(p, 2, alpha, hist, s);
-    }
-    GPB2_TRY(solve_L(p, y, z, s));  // z = L \ y  (generate_dense_inv)
-    GPB2_CUDA_TRY(launch_prof("dense_sumsq", k_sum_sq_half<T>, dim3(1), dim3(kDenseThreads), 0, s,
-                              (const T*)z, (int64_t)n, loss));
     GPB2_BLAS_TRY(trsv(p->blas, CUBLAS_OP_T, n, static_cast<const T*>(p->Ld), z));  // alpha
-    return scatter<T>(p, 2, z, hist, s);
+    *alpha_out = z;
+    return GPB2_OK;
+}
+
+template <typename T>
+int Dense<T>::inv_loss_grad(gpb2_problem* p, const T* y, double* hist, double* loss,
+                            cudaStream_t s) {
+    const T* alpha = nullptr;
+    GPB2_TRY(dense_alpha<T>(p, y, loss, &alpha, s));
+    return scatter<T>(p, 2, alpha, hist, s);
+}
+
+template <typename T>
+int Dense<T>::inv_loss_points(gpb2_problem* p, const T* y, double* dp, cudaStream_t s) {
+    const T* alpha = nullptr;
+    GPB2_TRY(dense_alpha<T>(p, y, nullptr, &alpha, s));
+    return scatter_points<T>(p, 2, alpha, dp, s);
 }
 
 template struct Dense<float>;

@@ -205,6 +205,13 @@ struct SmemTable {
         return N::add(y0, N::mul(slope, N::sub(r, x0)));
     }
 
+    // cov_lookup_dr (src/interp.jl:43-60): the slope of the segment holding r, 0 at and beyond
+    // both ends of the table.
+    __device__ __forceinline__ T dr(T r) const {
+        if (r <= b0 || r >= bN) return T(0);
+        return seg[4 * locate(r) + 3];
+    }
+
     // cov_lookup_weights (src/interp.jl:62-83): returns lo, writes w_lo and w_hi.
     __device__ __forceinline__ int weights(T r, T& wlo, T& whi) const {
         if (r <= b0) { wlo = T(1); whi = T(0); return 0; }

@@ -499,6 +499,89 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
     flush_hist(gacc, hist, a.tab.nb);
 }
 
+// Point-position gradients of the refined points (refine_logdet_grad_points_kernel! and
+// refine_inv_loss_grad_points_kernel!, src/kernels_adjoint.jl:254-324; INV: the inverse loss
+// with `values`, else the log-determinant): the point's Abar, then every off-diagonal pair's
+// Abar * k'(r) / r * scale * (x_a - x_b) added to point a and subtracted from point b
+// (_scatter_Abar_points_atomic!, src/kernels_adjoint.jl:226-251; coincident points and flat
+// table segments add nothing).  dp is (N, D) row-major in library positions, double atomics
+// (the terms are T products, summed in double as the d(vals) histogram is).
+template <typename T, int K, int D, bool INV>
+__global__ void __launch_bounds__(kFlatThreads)
+k_points_grad(PointArgs<T> pa, const T* __restrict__ values, double* __restrict__ dp, int64_t m0,
+              int64_t cnt, const int* __restrict__ mlist) {
+    using N = Num<T>;
+    using PM = PointMath<T, K, D>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    SmemTable<T> tab;
+    tab.stage(pa.tab, smem, threadIdx.x, blockDim.x);
+    __syncthreads();
+    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
+         it += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = point_of(it, m0, mlist);
+        int nb[K];
+        load_row_i32<K>(nb, pa.nbrs + m * K);
+        uint32_t jc[PM::KP1][D];
+        PM::gather(jc, pa.coords, nb, pa.n0 + m);
+        T L[PM::NT];
+        RegArr<T, PM::NR> R;
+        PM::template assemble<false>(L, R, jc, pa.scale, tab);
+        PM::chol(L);
+        T B[PM::NT];
+        sfor<0, PM::NT>([&](auto i_) {
+            GPB2_CI(i);
+            B[i] = T(0);
+        });
+        T rp[PM::KP1];
+        PM::pivot_recips(rp, L);
+        if constexpr (INV) {
+            T x[K];
+            PM::solve(x, L, pa.tab.pivc);
+            const T sd = L[tri(K, K)];
+            T vn[K];
+            T mean = T(0);
+            sfor<0, K>([&](auto j_) {
+                GPB2_CI(j);
+                vn[j] = values[nb[j]];
+                mean = N::add(mean, N::mul(x[j], vn[j]));
+            });
+            const T xim = N::div(N::sub(values[pa.n0 + m], mean), sd);
+            B[tri(K, K)] = N::div(N::mul(-xim, xim), sd);
+            T z[K];
+            sfor<0, K>([&](auto j_) {
+                GPB2_CI(j);
+                z[j] = N::div(N::mul(-xim, vn[j]), sd);
+            });
+            PM::template forward_subst<false>(z, L, rp, T(0));
+            PM::seed_from_solve(B, z, x);
+        } else {
+            B[tri(K, K)] = rp[K];  // chol_logdet_pullback! seed 1/L[K][K]
+        }
+        PM::pullback(B, L, rp);
+        sfor<1, PM::KP1>([&](auto a_) {
+            GPB2_CI(a);
+            const int64_t ga = a < K ? (int64_t)nb[a] : pa.n0 + m;
+            sfor<0, a>([&](auto b_) {
+                GPB2_CI(b);
+                const T r = PM::radius(jc[a], jc[b], pa.scale);
+                if (r == T(0)) return;
+                const T dcov = tab.dr(r);
+                if (dcov == T(0)) return;
+                const int64_t gb = (int64_t)nb[b];  // b < a <= K: always a neighbour
+                const T factor = N::div(N::mul(B[tri(a, b)], dcov), r);
+                sfor<0, D>([&](auto d_) {
+                    GPB2_CI(d);
+                    const T diff = N::mul(pa.scale, N::sub(N::from_i64((long long)jc[a][d]),
+                                                           N::from_i64((long long)jc[b][d])));
+                    const T c = N::mul(factor, diff);
+                    atomicAdd(dp + ga * D + d, (double)c);
+                    atomicAdd(dp + gb * D + d, -(double)c);
+                });
+            });
+        });
+    }
+}
+
 // Grid-wide lane index of the persistent sweeps: a warp takes 32 consecutive points (its loads
 // are contiguous and, in library order, its points' neighbours are close together), and
 // consecutive warps sit on consecutive CTAs (one per SM), so a small batch still spreads over
@@ -915,6 +998,7 @@ struct Ops {
                                  const int64_t*, int, GridSync, cudaStream_t);
     cudaError_t (*sweep_rev_all)(T*, T*, const T*, const T*, const int*, int64_t, const int64_t*,
                                  int, RevGraph<T>, GridSync, cudaStream_t);
+    cudaError_t (*points_grad)(const PointArgs<T>&, const T*, double*, Pts, cudaStream_t);
 };
 
 template <typename T>
@@ -1058,12 +1142,21 @@ struct Launch {
         return coop("sweep_rev_all", k_sweep_rev_all<T, K, false>, SS::kThreads, 0, s, xg, vb, mv,
                     sd, nbrs, n0, offs, nbatch, rg, gs);
     }
+    // values != nullptr: the inverse-loss position gradient, else the log-determinant's.
+    static cudaError_t points_grad(const PointArgs<T>& a, const T* values, double* dp, Pts r,
+                                   cudaStream_t s) {
+        if (values)
+            return flat("points_grad", k_points_grad<T, K, D, true>, flat_smem(a, false), r.cnt,
+                        s, a, values, dp, r.m0, r.cnt, r.list);
+        return flat("points_grad", k_points_grad<T, K, D, false>, flat_smem(a, false), r.cnt, s,
+                    a, values, dp, r.m0, r.cnt, r.list);
+    }
     static const Ops<T>* ops() {
         static const Ops<T> o = {factor,        inv,           logdet,
                                  logdet_grad,   grad_vals,     inv_loss_grad,
                                  fused_fwd,     sweep_fwdrev_all, sweep_fwd_flow,
                                  sweep_fwd,     sweep_rev,     sweep_fwd_all,
-                                 sweep_rev_all};
+                                 sweep_rev_all, points_grad};
         return &o;
     }
 };

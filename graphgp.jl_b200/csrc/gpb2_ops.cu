@@ -46,6 +46,18 @@ __global__ void k_scatter(const T* __restrict__ src, const int* __restrict__ idx
 // Between the reference's tree order and the library's (gpb2_order.cu), over positions
 // [base, base + n): to_lib: dst[q] = src[map[base + q] - base]; else dst[map[base + q] - base] =
 // src[q].
+// (N, D) rows from library positions to tree positions, rounded to T:
+// dst[lib_tree[q]] = src[q] (the identity without a library order).
+template <typename T>
+__global__ void k_rows_to_tree(const double* __restrict__ src, T* __restrict__ dst,
+                               const int* __restrict__ lib_tree, int64_t n, int D) {
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n;
+         q += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = lib_tree ? (int64_t)lib_tree[q] : q;
+        for (int d = 0; d < D; d++) dst[t * D + d] = (T)src[q * D + d];
+    }
+}
+
 template <typename T>
 __global__ void k_lib_move(const T* __restrict__ src, T* __restrict__ dst,
                            const int* __restrict__ map, int64_t base, int64_t n, int to_lib) {
@@ -377,6 +389,57 @@ struct Impl {
         GPB2_TRY(refine_logdet(p, tl, out, s));
         return lib_move(p, tl, terms, p->n0, p->m, false, s);
     }
+    // ------------------------------------------------- point-position gradients, tree order
+    // (src/grad.jl:168-377).  Accumulated in library positions (N, D), the refined points'
+    // part (values_lib: the inverse loss, else the log-determinant) and, with `dense`, the dense
+    // block's (y_dense: its first n0 values); then the rows go to tree order.
+    static int points_grad(P* p, const T* values_lib, bool dense, const T* y_dense, T* dp_tree,
+                           cudaStream_t s) {
+        const int D = (int)p->d;
+        const size_t bytes = sizeof(double) * (size_t)p->n * D;
+        GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&p->dpts), bytes));
+        double* dl = p->dpts;
+        GPB2_CUDA_TRY(cudaMemsetAsync(dl, 0, bytes, s));
+        GPB2_TRY(check_launch(ops_of<T>(p)->points_grad(point_args<T>(p), values_lib, dl,
+                                                        Pts::all(p->m), s),
+                              "points grad"));
+        if (dense) {
+            GPB2_TRY(Dense<T>::factor(p, s));
+            if (values_lib)
+                GPB2_TRY(Dense<T>::inv_loss_points(p, y_dense, dl, s));
+            else
+                GPB2_TRY(Dense<T>::logdet_points(p, dl, s));
+        }
+        return check_launch(launch_prof("order", k_rows_to_tree<T>, dim3(grid1d(p->n)), dim3(256),
+                                        0, s, (const double*)dl, dp_tree, (const int*)p->lib_tree,
+                                        p->n, D),
+                            "order");
+    }
+    static int refine_logdet_grad_points(P* p, T* dp, cudaStream_t s) {
+        return points_grad(p, nullptr, false, nullptr, dp, s);
+    }
+    static int generate_logdet_grad_points(P* p, T* dp, cudaStream_t s) {
+        return points_grad(p, nullptr, true, nullptr, dp, s);
+    }
+    static int refine_inv_loss_grad_points(P* p, const T* values, T* dp, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        const T* vl = values;
+        if (p->lib_tree) {
+            GPB2_TRY(lib_move(p, values, (T*)p->buf_b, 0, p->n, true, s));
+            vl = (const T*)p->buf_b;
+        }
+        return points_grad(p, vl, false, nullptr, dp, s);
+    }
+    static int generate_inv_loss_grad_points(P* p, const T* data, T* dp, cudaStream_t s) {
+        GPB2_TRY(ensure_scratch(p, false));
+        const T* yl = data;
+        if (p->indices) {
+            GPB2_TRY(gather(p, data, (T*)p->buf_a, s));
+            yl = (const T*)p->buf_a;
+        }
+        return points_grad(p, yl, true, yl, dp, s);
+    }
+
     static int refine_inv_loss_tree(P* p, const T* values, T* dvals, double* loss,
                                     cudaStream_t s) {
         if (!p->lib_tree) return refine_inv_loss_grad_vals(p, values, dvals, loss, s);
@@ -568,14 +631,22 @@ struct Impl {
                                                         (const T*)p->mv, p->dacc, Pts::all(p->m), st),
                                 "grad_vals");
         };
+        GPB2_TRY(hist_and_dense(p, per_point, true, vb, xt, s));
+        return finish_hist(p, dvals, s);
+    }
+
+    // The per-point histogram kernel and (when `dense`) the dense block's pullback: independent,
+    // both adding into p->dacc.  The dense chain (a short run of small kernels) goes first, on
+    // the high-priority stream, and runs beside the per-point kernel (one after the other with
+    // the overlap off: GPB2_OVERLAP=0, gpb2_set_overlap(0)).
+    template <class PerPoint>
+    static int hist_and_dense(P* p, PerPoint per_point, bool dense, const T* vb, const T* xt,
+                              cudaStream_t s) {
+        if (!dense) return per_point(s);
         if (!g_overlap_flag.load()) {
             GPB2_TRY(per_point(s));
-            GPB2_TRY(Dense<T>::grad_vals(p, vb, xt, p->dacc, s));
-            return finish_hist(p, dvals, s);
+            return Dense<T>::grad_vals(p, vb, xt, p->dacc, s);
         }
-        // The dense block's pullback (a short chain of small kernels) and the per-point kernel
-        // are independent and both add into the histogram: the chain goes first, on the
-        // high-priority stream, and runs beside the per-point kernel.
         GPB2_TRY(ensure_dense_stream(p));
         GPB2_CUDA_TRY(cudaEventRecord(p->ev_fork, s));
         GPB2_CUDA_TRY(cudaStreamWaitEvent(p->dstream, p->ev_fork, 0));
@@ -587,7 +658,7 @@ struct Impl {
         GPB2_TRY(sp);
         GPB2_CUDA_TRY(e1);
         GPB2_CUDA_TRY(e2);
-        return finish_hist(p, dvals, s);
+        return GPB2_OK;
     }
 
     static int generate_logdet_grad_vals(P* p, T* dvals, double* ld, cudaStream_t s) {
@@ -786,23 +857,29 @@ struct Shard {
         p->sh_own_cnt = (int64_t)own.size();
         std::copy(key, key + 3, p->sh_key);
         p->sh_factor_valid = false;
+        p->fc_sh_valid = false;
         return GPB2_OK;
     }
 
     // mean_vec / std of the points this rank's sweeps read: its forward ranges (which contain
-    // its reverse ranges).  Nothing when every point's factor is current.
-    static int factor(P* p, const ShardPlan& pl, cudaStream_t s) {
-        if (p->factor_valid || p->sh_factor_valid) return GPB2_OK;
+    // its reverse ranges and the points it owns).  Nothing when every point's factor is current
+    // -- unless the vals-gradient wants the factor cache (allocated as its mode allows), which
+    // the same pass then fills for those ranges.
+    static int factor(P* p, const ShardPlan& pl, cudaStream_t s, bool want_cache = false) {
+        if (want_cache) GPB2_TRY(Impl<T>::alloc_factor_cache(p));
+        const bool fill = want_cache && p->fc_L && !p->fc_valid && !p->fc_sh_valid;
+        if ((p->factor_valid || p->sh_factor_valid) && !fill) return GPB2_OK;
         const Ops<T>* o = ops_of<T>(p);
+        const PointArgs<T> a = point_args<T>(p, fill ? FcUse::Fill : FcUse::None);
         for (const ShardBatch& x : pl.b) {
-            int64_t a, e;
-            pl.fwd_range(x, a, e);
-            if (e > a)
+            int64_t lo, hi;
+            pl.fwd_range(x, lo, hi);
+            if (hi > lo)
                 GPB2_TRY(Impl<T>::check_launch(
-                    o->factor(point_args<T>(p), a - p->n0, e - p->n0, (T*)p->mv, (T*)p->sd, s),
-                    "factor"));
+                    o->factor(a, lo - p->n0, hi - p->n0, (T*)p->mv, (T*)p->sd, s), "factor"));
         }
-        p->sh_factor_valid = true;
+        if (!p->factor_valid) p->sh_factor_valid = true;
+        if (fill) p->fc_sh_valid = true;
         return GPB2_OK;
     }
 
@@ -903,18 +980,22 @@ struct Shard {
         const T* xt = to_tree(p, xi, (T*)p->buf_b, s, &st);
         GPB2_TRY(st);
         GPB2_TRY(Dense<T>::factor(p, s));
-        GPB2_TRY(factor(p, pl, s));
+        GPB2_TRY(factor(p, pl, s, true));
         T* v = (T*)p->sh_v;
         T* vb = (T*)p->sh_vb;
         GPB2_TRY(forward(p, c, pl, xt, v, s));
         GPB2_TRY(seed_cotangent(p, c, vbar, vb, s));
         GPB2_TRY(reverse(p, c, pl, vb, nullptr, s));
         GPB2_TRY(Impl<T>::zero_acc(p, s));
-        GPB2_TRY(Impl<T>::check_launch(
-            ops_of<T>(p)->grad_vals(point_args<T>(p, FcUse::Read), v, xt, vb, (const T*)p->mv, p->dacc,
-                                    Pts{0, p->sh_own_cnt, p->sh_own}, s),
-            "grad_vals"));
-        if (comm_rank(c) == 0) GPB2_TRY(Dense<T>::grad_vals(p, vb, xt, p->dacc, s));
+        auto per_point = [&](cudaStream_t st) {
+            return Impl<T>::check_launch(
+                ops_of<T>(p)->grad_vals(point_args<T>(p, FcUse::ReadShard), v, xt, vb,
+                                        (const T*)p->mv, p->dacc,
+                                        Pts{0, p->sh_own_cnt, p->sh_own}, st),
+                "grad_vals");
+        };
+        // The dense block's pullback on rank 0 only (the all-reduce below adds it in once).
+        GPB2_TRY(Impl<T>::hist_and_dense(p, per_point, comm_rank(c) == 0, vb, xt, s));
         GPB2_TRY(comm_all_reduce(c, p->dacc, p->nb, true, s));
         return Impl<T>::finish_hist(p, dvals, s);
     }
@@ -1183,6 +1264,32 @@ int gpb2_generate_inv_loss_grad_vals(gpb2_problem* p, const void* data, void* dv
     GPB2_TRY(need(data, "data") | need(dvals, "dvals"));
     GPB2_DISPATCH(p, Impl<float>::generate_inv_loss_grad_vals(p, CF32(data), F32(dvals), loss, s),
                   Impl<double>::generate_inv_loss_grad_vals(p, CF64(data), F64(dvals), loss, s));
+}
+
+int gpb2_refine_logdet_grad_points(gpb2_problem* p, void* d_points, void* stream) {
+    GPB2_TRY(need(d_points, "d_points"));
+    GPB2_DISPATCH(p, Impl<float>::refine_logdet_grad_points(p, F32(d_points), s),
+                  Impl<double>::refine_logdet_grad_points(p, F64(d_points), s));
+}
+
+int gpb2_generate_logdet_grad_points(gpb2_problem* p, void* d_points, void* stream) {
+    GPB2_TRY(need(d_points, "d_points"));
+    GPB2_DISPATCH(p, Impl<float>::generate_logdet_grad_points(p, F32(d_points), s),
+                  Impl<double>::generate_logdet_grad_points(p, F64(d_points), s));
+}
+
+int gpb2_refine_inv_loss_grad_points(gpb2_problem* p, const void* values, void* d_points,
+                                     void* stream) {
+    GPB2_TRY(need(values, "values") | need(d_points, "d_points"));
+    GPB2_DISPATCH(p, Impl<float>::refine_inv_loss_grad_points(p, CF32(values), F32(d_points), s),
+                  Impl<double>::refine_inv_loss_grad_points(p, CF64(values), F64(d_points), s));
+}
+
+int gpb2_generate_inv_loss_grad_points(gpb2_problem* p, const void* data, void* d_points,
+                                       void* stream) {
+    GPB2_TRY(need(data, "data") | need(d_points, "d_points"));
+    GPB2_DISPATCH(p, Impl<float>::generate_inv_loss_grad_points(p, CF32(data), F32(d_points), s),
+                  Impl<double>::generate_inv_loss_grad_points(p, CF64(data), F64(d_points), s));
 }
 
 // ------------------------------------------------------------------------------ level-sharded

@@ -236,6 +236,7 @@ static int load_table(gpb2_problem* p, const void* vals_dev, cudaStream_t s) {
     p->factor_valid = false;  // and so do the per-point mean_vec / std
     p->sh_factor_valid = false;
     p->fc_valid = false;      // and the factor cache
+    p->fc_sh_valid = false;
     p->rev_w_valid = false;   // and the transposed graph's weights
     GPB2_CUDA_TRY(cudaMemcpyAsync(p->vals, vals_dev, ts * p->nb, cudaMemcpyDeviceToDevice, s));
     // The bins do not change after creation: they are read back once, the values every time.
@@ -269,7 +270,7 @@ static void free_problem(gpb2_problem* p) {
                     p->Ldr,    p->Dinv,  p->Wtri, p->Ainv,  p->sh_v, p->sh_vb,
                     p->sh_xg,  p->sh_own, p->perm_stage, p->perm_pos_g, p->perm_q_g,
                     p->perm_pos_s, p->perm_q_s, p->perm_from_g, p->perm_from_s, p->lib_tree, p->fc_L, p->fc_t, p->fc_lo,
-                    p->rev_off, p->rev_mj, p->rev_w};
+                    p->rev_off, p->rev_mj, p->rev_w, p->dpts};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);
@@ -539,6 +540,7 @@ int gpb2_problem_set_factor_cache(gpb2_problem* p, int mode) {
         p->fc_L = p->fc_t = nullptr;
         p->fc_lo = nullptr;
         p->fc_valid = false;
+        p->fc_sh_valid = false;
     }
     return GPB2_OK;
 }
@@ -572,7 +574,7 @@ int gpb2_problem_reverse_mode(const gpb2_problem* p, int* mode, int* built, int6
 int gpb2_problem_factor_cache(const gpb2_problem* p, int* mode, int* valid, int64_t* bytes) {
     if (!p) return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_factor_cache: NULL problem");
     if (mode) *mode = p->fc_mode;
-    if (valid) *valid = p->fc_L && p->fc_valid ? 1 : 0;
+    if (valid) *valid = !p->fc_L ? 0 : (p->fc_valid ? 1 : (p->fc_sh_valid ? 2 : 0));
     if (bytes) *bytes = (int64_t)factor_cache_bytes(p);
     return GPB2_OK;
 }

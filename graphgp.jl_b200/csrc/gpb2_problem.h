@@ -42,6 +42,7 @@ struct gpb2_problem {
     void* buf_c = nullptr;   // (N) T   tree-order cotangent
     void* buf_d = nullptr;   // (N) T   tree-order xbar
     double* dacc = nullptr;  // nb histogram + 8 scalars (double accumulators)
+    double* dpts = nullptr;  // (N, D) point-position gradient, library positions
     bool factor_valid = false;  // mv / sd hold the current table's per-point factors
 
     // Per-point factor cache (FactorCache): the packed Cholesky factor and the pair weights of
@@ -52,6 +53,7 @@ struct gpb2_problem {
     uint16_t* fc_lo = nullptr;   // NR slabs of uint16
     int fc_mode = 2;
     bool fc_valid = false;       // the cache holds the current table's factors of all points
+    bool fc_sh_valid = false;    // ... of the points of this rank's level-sharded forward ranges
 
     // Transposed graph of the pull-form reverse sweep (gpb2_rev.cu): rev_off (N + 1) delimits
     // each point's incoming edges in rev_mj (child m * K + slot j, in the serial sweep's order)
@@ -181,7 +183,7 @@ TableView<T> table_view(const gpb2_problem* p) {
 // The kernels' view of the problem.  With a cache the arguments also carry the factor cache:
 // as the target of the factor pass (FcUse::Fill, when it is allocated) or as the source of the
 // vals-gradient kernels (FcUse::Read, when it holds the current table).
-enum class FcUse { None, Fill, Read };
+enum class FcUse { None, Fill, Read, ReadShard };
 
 template <typename T>
 PointArgs<T> point_args(const gpb2_problem* p, FcUse fc = FcUse::None) {
@@ -191,7 +193,10 @@ PointArgs<T> point_args(const gpb2_problem* p, FcUse fc = FcUse::None) {
     a.nbrs = p->nbrs;
     a.n0 = p->n0;
     a.scale = (T)p->scale;
-    if (p->fc_L && (fc == FcUse::Fill || (fc == FcUse::Read && p->fc_valid))) {
+    // ReadShard: a level-sharded kernel over this rank's points, which the rank's own factor
+    // pass may have filled.
+    if (p->fc_L && (fc == FcUse::Fill || (fc == FcUse::Read && p->fc_valid) ||
+                    (fc == FcUse::ReadShard && (p->fc_valid || p->fc_sh_valid)))) {
         a.fc.L = static_cast<T*>(p->fc_L);
         a.fc.t = static_cast<T*>(p->fc_t);
         a.fc.lo = p->fc_lo;
@@ -264,6 +269,9 @@ struct Dense {
     static int solve_L(gpb2_problem* p, const T* b, T* y, cudaStream_t s);   // y = L \ b
     static int logdet(gpb2_problem* p, double* acc, cudaStream_t s);         // acc += sum log diag
     static int grad_vals(gpb2_problem* p, const T* vb, const T* xi, double* hist, cudaStream_t s);
+    // Position gradients of the dense block into dp ((N, D) row-major, added).
+    static int logdet_points(gpb2_problem* p, double* dp, cudaStream_t s);
+    static int inv_loss_points(gpb2_problem* p, const T* y, double* dp, cudaStream_t s);
     static int logdet_grad(gpb2_problem* p, double* hist, cudaStream_t s);
     static int inv_loss_grad(gpb2_problem* p, const T* y, double* hist, double* loss,
                              cudaStream_t s);

@@ -8,9 +8,11 @@ from . import _lib
 from ._lib import (GraphGPError, GraphInvariantError, NotPositiveDefiniteError,
                    UnsupportedError)
 from .api import (check_graph, generate, generate_grad_vals, generate_grad_xi, generate_inv,
-                  generate_inv_loss_grad_vals, generate_logdet, generate_logdet_and_grad_vals,
+                  generate_inv_loss_grad_points, generate_inv_loss_grad_vals, generate_logdet,
+                  generate_logdet_and_grad_vals, generate_logdet_grad_points,
                   generate_logdet_grad_vals, refine, refine_, refine_inv, refine_inv_,
-                  refine_inv_loss_grad_vals, refine_logdet, refine_logdet_grad_vals,
+                  refine_inv_loss_grad_points, refine_inv_loss_grad_vals, refine_logdet,
+                  refine_logdet_grad_points, refine_logdet_grad_vals,
                   refine_logdet_grad_vals_noalloc, refine_logdet_terms, set_synchronous)
 from .autodiff import generate_of_vals, generate_t, inv_quadratic_loss_of_vals, logdet_of_vals
 from .extras import hyperparam_grad, make_cov_bins, matern_kernel, rbf_kernel

@@ -116,6 +116,10 @@ _SIGNATURES = {
     "gpb2_generate_grad_vals": (I32, [P, P, P, P, P]),
     "gpb2_generate_logdet_grad_vals": (I32, [P, P, PD, P]),
     "gpb2_generate_inv_loss_grad_vals": (I32, [P, P, P, PD, P]),
+    "gpb2_refine_logdet_grad_points": (I32, [P, P, P]),
+    "gpb2_generate_logdet_grad_points": (I32, [P, P, P]),
+    "gpb2_refine_inv_loss_grad_points": (I32, [P, P, P, P]),
+    "gpb2_generate_inv_loss_grad_points": (I32, [P, P, P, P]),
     "gpb2_build_graph": (I32, [P, I64, I64, I64, I64, I64, I64, I64, C.POINTER(P)]),
     "gpb2_graph_n_offsets": (I64, [P]),
     "gpb2_graph_n0": (I64, [P]),

@@ -221,6 +221,47 @@ def generate_inv_loss_grad_vals(prob: GraphGPProblem, data):
     return loss.value, _ret(out, host)
 
 
+# ---------------------------------------------------------------------------------------------
+# Point-position gradients: src/grad.jl:168-377 -- (N, D) in tree order (Julia's (D, N))
+# ---------------------------------------------------------------------------------------------
+
+def _points_out(prob: GraphGPProblem) -> torch.Tensor:
+    return torch.empty((prob.npoints(), prob.ndims_space()), dtype=prob.torch_dtype,
+                       device=prob.device)
+
+
+def refine_logdet_grad_points(prob: GraphGPProblem):
+    """``refine_logdet_grad_points(prob)`` (src/grad.jl:168-233)."""
+    out = _points_out(prob)
+    _call("gpb2_refine_logdet_grad_points", prob.handle, _ptr(out), _stream(prob))
+    return _ret(out, prob.host_arrays)
+
+
+def generate_logdet_grad_points(prob: GraphGPProblem):
+    """``generate_logdet_grad_points(prob)`` (src/grad.jl:234-247): refinement + dense block."""
+    out = _points_out(prob)
+    _call("gpb2_generate_logdet_grad_points", prob.handle, _ptr(out), _stream(prob))
+    return _ret(out, prob.host_arrays)
+
+
+def refine_inv_loss_grad_points(prob: GraphGPProblem, values):
+    """``refine_inv_loss_grad_points(prob, values)`` (src/grad.jl:259-358); values in tree
+    order."""
+    v, host = _vec(prob, values, prob.npoints(), "values")
+    out = _points_out(prob)
+    _call("gpb2_refine_inv_loss_grad_points", prob.handle, _ptr(v), _ptr(out), _stream(prob))
+    return _ret(out, host)
+
+
+def generate_inv_loss_grad_points(prob: GraphGPProblem, data):
+    """``generate_inv_loss_grad_points(prob, data)`` (src/grad.jl:360-377); data in the
+    original order."""
+    d, host = _vec(prob, data, prob.npoints(), "data")
+    out = _points_out(prob)
+    _call("gpb2_generate_inv_loss_grad_points", prob.handle, _ptr(d), _ptr(out), _stream(prob))
+    return _ret(out, host)
+
+
 def set_synchronous(on: bool) -> None:
     """Process-wide call mode.  True (the default): every operation waits for its work and
     raises its numerical status (NotPositiveDefiniteError, barrier timeouts).  False: operations

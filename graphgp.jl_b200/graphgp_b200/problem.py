@@ -199,12 +199,13 @@ class GraphGPProblem:
         return self
 
     def factor_cache(self) -> dict:
-        """{"mode", "valid" (holds the current table), "bytes"} of the factor cache."""
+        """{"mode", "valid" (0: nothing current, 1: the current table's factors of every point,
+        2: those of this rank's level-sharded ranges), "bytes"} of the factor cache."""
         mode, valid, nbytes = C.c_int32(), C.c_int32(), C.c_int64()
         _lib.check(_lib.lib().gpb2_problem_factor_cache(self.handle, C.byref(mode),
                                                          C.byref(valid), C.byref(nbytes)),
                    "factor_cache")
-        return {"mode": mode.value, "valid": bool(valid.value), "bytes": nbytes.value}
+        return {"mode": mode.value, "valid": valid.value, "bytes": nbytes.value}
 
     def set_reverse_mode(self, mode: int) -> "GraphGPProblem":
         """Reverse sweep form: 0 atomic push (sums in no fixed order), 1 pull through the

@@ -5,7 +5,8 @@ module GraphGPB200Ext
 # arrays are CuArrays, the extension adds methods of GraphGP's own functions -- refine!,
 # refine_inv!, refine_logdet(_terms), refine_logdet_grad_vals, refine_inv_loss_grad_vals,
 # generate, generate_inv, generate_logdet, generate_grad_xi, generate_grad_vals,
-# generate_logdet(_and)_grad_vals, generate_inv_loss_grad_vals -- that are more specific than
+# generate_logdet(_and)_grad_vals, generate_inv_loss_grad_vals and the point-position gradients
+# ({refine,generate}_{logdet,inv_loss}_grad_points) -- that are more specific than
 # the generic ones (CuArray problem, CuArray vectors), so every caller, the ChainRules rrules of
 # src/chainrules.jl:31-72 and src/grad_generate_vals.jl:291-305 included, reaches the library
 # instead of the KernelAbstractions launches (src/api.jl:52-55,87-90,126-138,
@@ -200,6 +201,37 @@ function GraphGP.generate_inv_loss_grad_vals(prob::CuProblem{T}, data::CuVector{
     _check(ccall(_sym(:gpb2_generate_inv_loss_grad_vals), Cint, (V, D, D, Ref{Cdouble}, V),
         _handle(prob), _ptr(data), _ptr(out), loss, _stream()), "gpb2_generate_inv_loss_grad_vals")
     return T(loss[]), out
+end
+
+# --- point-position gradients, (D, N) in TREE order (src/grad.jl:168-377) -------------------
+function GraphGP.refine_logdet_grad_points(prob::CuProblem{T}; backend = nothing) where {T}
+    out = CUDA.zeros(T, ndims_space(prob), npoints(prob))
+    _check(ccall(_sym(:gpb2_refine_logdet_grad_points), Cint, (V, D, V), _handle(prob),
+        _ptr(out), _stream()), "gpb2_refine_logdet_grad_points")
+    return out
+end
+
+function GraphGP.generate_logdet_grad_points(prob::CuProblem{T}; backend = nothing) where {T}
+    out = CUDA.zeros(T, ndims_space(prob), npoints(prob))
+    _check(ccall(_sym(:gpb2_generate_logdet_grad_points), Cint, (V, D, V), _handle(prob),
+        _ptr(out), _stream()), "gpb2_generate_logdet_grad_points")
+    return out
+end
+
+function GraphGP.refine_inv_loss_grad_points(prob::CuProblem{T}, values::CuVector{T};
+                                             backend = nothing) where {T}
+    out = CUDA.zeros(T, ndims_space(prob), npoints(prob))
+    _check(ccall(_sym(:gpb2_refine_inv_loss_grad_points), Cint, (V, D, D, V), _handle(prob),
+        _ptr(values), _ptr(out), _stream()), "gpb2_refine_inv_loss_grad_points")
+    return out
+end
+
+function GraphGP.generate_inv_loss_grad_points(prob::CuProblem{T}, data::CuVector{T};
+                                               backend = nothing) where {T}
+    out = CUDA.zeros(T, ndims_space(prob), npoints(prob))
+    _check(ccall(_sym(:gpb2_generate_inv_loss_grad_points), Cint, (V, D, D, V), _handle(prob),
+        _ptr(data), _ptr(out), _stream()), "gpb2_generate_inv_loss_grad_points")
+    return out
 end
 
 # --- several GPUs: level-sharded operations and scheme-A fitting reductions ------------------

@@ -123,7 +123,8 @@ int gpb2_problem_prefactor(gpb2_problem* prob, void* stream);
  * when the device keeps max(10 %, 8 GB) of its memory free beyond it, else not used.  No
  * reference counterpart (the reference recomputes every factor in every kernel). */
 int gpb2_problem_set_factor_cache(gpb2_problem* prob, int mode);
-/* The mode, whether the cache holds the current table (valid), and its size in bytes. */
+/* The mode, what the cache holds (valid: 0 nothing current, 1 the current table's factors of
+ * every point, 2 those of this rank's level-sharded ranges), and its size in bytes. */
 int gpb2_problem_factor_cache(const gpb2_problem* prob, int* mode, int* valid, int64_t* bytes);
 
 /* Reverse sweep of generate_grad_xi / generate_grad_vals.  mode 0: every refined point pushes
@@ -291,6 +292,29 @@ int gpb2_generate_logdet_grad_vals(gpb2_problem* prob, void* dvals_dev, double* 
  * 0.5*||generate_inv(data)||^2; data in original order. */
 int gpb2_generate_inv_loss_grad_vals(gpb2_problem* prob, const void* data_dev, void* dvals_dev,
                                      double* loss_host, void* stream);
+
+/* Point-position gradients: d/dx of the log-determinant or of the inverse loss
+ * 0.5*||xi||^2 for the continuous positions x = scale * coords (the lattice enters only
+ * through the radii: the reference's straight-through convention).  d_points_dev is (D, N)
+ * column-major = (N, D) row-major T in TREE order, overwritten.  Every off-diagonal pair of a
+ * point's (K+1)x(K+1) block (and of the dense block, generate_ forms) adds
+ * Abar * k'(r) / r * scale * (x_a - x_b) to point a and subtracts it from point b, k' the
+ * table's segment slope (0 at and beyond both ends; coincident points add nothing); the
+ * additions are atomic.
+ * refine_logdet_grad_points (src/grad.jl:168-233, kernel src/kernels_adjoint.jl:254-270). */
+int gpb2_refine_logdet_grad_points(gpb2_problem* prob, void* d_points_dev, void* stream);
+/* generate_logdet_grad_points (src/grad.jl:234-247): plus the dense block's
+ * (_dense_logdet_grad_points, src/dense.jl:188-225: cotangent K^-1[a][b]). */
+int gpb2_generate_logdet_grad_points(gpb2_problem* prob, void* d_points_dev, void* stream);
+/* refine_inv_loss_grad_points (src/grad.jl:259-358, kernel src/kernels_adjoint.jl:273-324);
+ * values_dev: the field in tree order. */
+int gpb2_refine_inv_loss_grad_points(gpb2_problem* prob, const void* values_dev,
+                                     void* d_points_dev, void* stream);
+/* generate_inv_loss_grad_points (src/grad.jl:360-377): plus the dense block's
+ * (_dense_inv_loss_grad_points, src/dense.jl:271-297: cotangent -alpha_a * alpha_b,
+ * alpha = K^-1 y); data_dev in the original order. */
+int gpb2_generate_inv_loss_grad_points(gpb2_problem* prob, const void* data_dev,
+                                       void* d_points_dev, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Level-sharded operations over several GPUs, one process (or thread) per GPU.  Replaces the

@@ -824,3 +824,165 @@ double SFX(gpo_dense_logdet)(const T* L, int64_t n) {
     for (int64_t i = 0; i < n; i++) s += LOG_T(L[i * n + i]);
     return (double)s;
 }
+
+/* ---------------------------------------------------------------------------------------- */
+/* Point-position gradients (src/grad.jl:168-377, src/kernels_adjoint.jl:226-324,            */
+/* src/dense.jl:184-297).  d(.)/dx for the continuous positions x = scale * coords, tree      */
+/* order, (N, D) row-major (Julia's (D, N) column-major), accumulated in double.               */
+/* ---------------------------------------------------------------------------------------- */
+
+/* cov_lookup_dr (src/interp.jl:43-60): the slope of the segment holding r; 0 at and beyond
+ * both ends of the table. */
+static inline T cov_lookup_dr(T r, const T* bins, const T* vals, int64_t n) {
+    if (r <= bins[0] || r >= bins[n - 1]) return (T)0;
+    int64_t lo = 0, hi = n - 1;
+    while (hi - lo > 1) {
+        int64_t mid = (lo + hi) >> 1;
+        if (bins[mid] <= r) lo = mid; else hi = mid;
+    }
+    return (vals[lo + 1] - vals[lo]) / (bins[lo + 1] - bins[lo]);
+}
+
+/* One pair's term (src/kernels_adjoint.jl:226-251): c_d = (g * k'(r) / r) * scale * (x_a - x_b)
+ * into point a, -c_d into point b; coincident points and flat segments contribute nothing. */
+static inline void pair_points(double* dp, T g, const uint32_t* xa, const uint32_t* xb,
+                               int64_t ga, int64_t gb, int D, T scale, const T* bins,
+                               const T* vals, int64_t nb) {
+    int64_t sq = 0;
+    for (int d = 0; d < D; d++) {
+        int64_t di = (int64_t)xa[d] - (int64_t)xb[d];
+        sq += di * di;
+    }
+    if (sq == 0) return;
+    T r = SQRT_T((T)sq) * scale;
+    T dcov = cov_lookup_dr(r, bins, vals, nb);
+    if (dcov == (T)0) return;
+    T factor = g * dcov / r;
+    for (int d = 0; d < D; d++) {
+        T diff = scale * ((T)(int64_t)xa[d] - (T)(int64_t)xb[d]);
+        T c = factor * diff;
+        dp[ga * D + d] += (double)c;
+        dp[gb * D + d] -= (double)c;
+    }
+}
+
+/* A refined point's off-diagonal Abar through k'(r) into its K + 1 points (rows 0..K-1 the
+ * neighbours, row K the point itself). */
+static void scatter_abar_points(double* dp, const T* Abar, const uint32_t* jc, const int64_t* nbm,
+                                int64_t fine, int KP1, int D, T scale, const T* bins,
+                                const T* vals, int64_t nb) {
+    int K = KP1 - 1;
+    for (int a = 1; a < KP1; a++) {
+        int64_t ga = a < K ? nbm[a] : fine;
+        for (int b = 0; b < a; b++) {
+            int64_t gb = b < K ? nbm[b] : fine;
+            pair_points(dp, Abar[a * KP1 + b], jc + a * D, jc + b * D, ga, gb, D, scale, bins,
+                        vals, nb);
+        }
+    }
+}
+
+/* refine_logdet_grad_points (src/grad.jl:186-233): seed 1 / L[K][K], chol_pullback, scatter. */
+int SFX(gpo_refine_logdet_grad_points)(double* dp, const uint32_t* coords, const int64_t* nbrs,
+                                       int64_t M, int64_t n0, int K, int D, T scale,
+                                       const T* bins, const T* vals, int64_t nb) {
+    if (K > KMAX || D > DMAX) return 2;
+    int KP1 = K + 1;
+    T* A = (T*)malloc(sizeof(T) * KP1 * KP1 * 3);
+    T* Abar = A + KP1 * KP1;
+    T* Lbar = Abar + KP1 * KP1;
+    uint32_t jc[(KMAX + 1) * DMAX];
+    for (int64_t m = 0; m < M; m++) {
+        point_factor(A, NULL, jc, coords, nbrs, m, n0, K, D, scale, bins, vals, nb);
+        for (int i = 0; i < KP1 * KP1; i++) Lbar[i] = (T)0;
+        Lbar[K * KP1 + K] = (T)1 / A[K * KP1 + K];
+        chol_pullback(Abar, Lbar, A, KP1);
+        scatter_abar_points(dp, Abar, jc, nbrs + m * K, n0 + m, KP1, D, scale, bins, vals, nb);
+    }
+    free(A);
+    return 0;
+}
+
+/* refine_inv_loss_grad_points (src/grad.jl:259-358): the seeds of the inverse-loss vals
+ * gradient (no pivot guard in the z-bar solve), chol_pullback, scatter into the points. */
+int SFX(gpo_refine_inv_loss_grad_points)(double* dp, const T* values, const uint32_t* coords,
+                                         const int64_t* nbrs, int64_t M, int64_t n0, int K, int D,
+                                         T scale, const T* bins, const T* vals, int64_t nb) {
+    if (K > KMAX || D > DMAX) return 2;
+    int KP1 = K + 1;
+    T* A = (T*)malloc(sizeof(T) * KP1 * KP1 * 3);
+    T* Abar = A + KP1 * KP1;
+    T* Lbar = Abar + KP1 * KP1;
+    T mv[KMAX], zbar[KMAX];
+    uint32_t jc[(KMAX + 1) * DMAX];
+    for (int64_t m = 0; m < M; m++) {
+        T sd = point_factor(A, mv, jc, coords, nbrs, m, n0, K, D, scale, bins, vals, nb);
+        T mean = (T)0;
+        for (int j = 0; j < K; j++) mean += mv[j] * values[nbrs[m * K + j]];
+        T xim = (values[n0 + m] - mean) / sd;
+        for (int i = 0; i < KP1 * KP1; i++) Lbar[i] = (T)0;
+        Lbar[K * KP1 + K] = -xim * xim / sd;
+        for (int j = 0; j < K; j++) zbar[j] = -xim * values[nbrs[m * K + j]] / sd;
+        for (int i = 0; i < K; i++) {
+            T s = zbar[i];
+            for (int p = 0; p < i; p++) s -= A[i * KP1 + p] * zbar[p];
+            zbar[i] = s / A[i * KP1 + i];
+        }
+        for (int j = 0; j < K; j++) {
+            Lbar[K * KP1 + j] += zbar[j];
+            for (int i = 0; i <= j; i++) Lbar[j * KP1 + i] -= zbar[i] * mv[j];
+        }
+        chol_pullback(Abar, Lbar, A, KP1);
+        scatter_abar_points(dp, Abar, jc, nbrs + m * K, n0 + m, KP1, D, scale, bins, vals, nb);
+    }
+    free(A);
+    return 0;
+}
+
+/* The dense block's position gradients (src/dense.jl:188-225, 271-297): the off-diagonal
+ * cotangent g[a][b] (a > b) through k'(r) into points a and b.  mode 0: g = K^{-1}[a][b] from
+ * the block's factor L (row-major lower); mode 1: g = -alpha[a] * alpha[b] with
+ * alpha = L^{-T} L^{-1} y. */
+int SFX(gpo_dense_grad_points)(double* dp, const T* L, const T* y, const uint32_t* coords,
+                               int64_t n, int D, T scale, const T* bins, const T* vals,
+                               int64_t nb, int mode) {
+    T* Li = NULL;
+    T* alpha = NULL;
+    if (mode == 0) {
+        Li = (T*)calloc((size_t)n * n, sizeof(T));
+        for (int64_t j = 0; j < n; j++)
+            for (int64_t i = j; i < n; i++) {
+                T s = (i == j) ? (T)1 : (T)0;
+                for (int64_t p = j; p < i; p++) s -= L[i * n + p] * Li[p * n + j];
+                Li[i * n + j] = s / L[i * n + i];
+            }
+    } else {
+        T* xi = (T*)malloc(sizeof(T) * n);
+        alpha = (T*)malloc(sizeof(T) * n);
+        for (int64_t i = 0; i < n; i++) {
+            T s = y[i];
+            for (int64_t p = 0; p < i; p++) s -= L[i * n + p] * xi[p];
+            xi[i] = s / L[i * n + i];
+        }
+        for (int64_t i = n - 1; i >= 0; i--) {
+            T s = xi[i];
+            for (int64_t p = i + 1; p < n; p++) s -= L[p * n + i] * alpha[p];
+            alpha[i] = s / L[i * n + i];
+        }
+        free(xi);
+    }
+    for (int64_t b = 0; b < n; b++)
+        for (int64_t a = b + 1; a < n; a++) {
+            T g;
+            if (mode == 0) {
+                g = (T)0;
+                for (int64_t kk = 0; kk < n; kk++) g += Li[kk * n + a] * Li[kk * n + b];
+            } else {
+                g = -alpha[a] * alpha[b];
+            }
+            pair_points(dp, g, coords + a * D, coords + b * D, a, b, D, scale, bins, vals, nb);
+        }
+    free(Li);
+    free(alpha);
+    return 0;
+}

@@ -408,6 +408,57 @@ def generate_logdet_grad_vals(p, nthreads=0, acc_t=False):
 
 
 # ---------------------------------------------------------------------------------------------
+# Point-position gradients (src/grad.jl:168-377, src/dense.jl:184-297): (N, D) in tree order,
+# d(.)/dx for the continuous positions x = scale * coords (Julia's (D, N))
+# ---------------------------------------------------------------------------------------------
+
+def refine_logdet_grad_points(p):
+    """refine_logdet_grad_points (src/grad.jl:168-233)."""
+    N, D, M, K = _dims(p)
+    dp = np.zeros((N, D), np.float64)
+    rc = _fn("gpo_refine_logdet_grad_points", p.dtype)(_p(dp), _p(p.coords), _p(p.nbrs), I64(M),
+                                                        *_common(p))
+    assert rc == 0
+    return dp.astype(p.dtype)
+
+
+def refine_inv_loss_grad_points(p, values):
+    """refine_inv_loss_grad_points (src/grad.jl:259-358); values in tree order."""
+    N, D, M, K = _dims(p)
+    values = np.ascontiguousarray(values, dtype=p.dtype)
+    dp = np.zeros((N, D), np.float64)
+    rc = _fn("gpo_refine_inv_loss_grad_points", p.dtype)(_p(dp), _p(values), _p(p.coords),
+                                                          _p(p.nbrs), I64(M), *_common(p))
+    assert rc == 0
+    return dp.astype(p.dtype)
+
+
+def dense_grad_points(p, y=None):
+    """_dense_logdet_grad_points (y None) / _dense_inv_loss_grad_points (y = the first n0
+    values in tree order) (src/dense.jl:188-225, 271-297): (N, D), zero past n0."""
+    N, D, M, K = _dims(p)
+    L, _ = dense_chol(p)
+    dp = np.zeros((N, D), np.float64)
+    yy = np.zeros(p.n0, p.dtype) if y is None else np.ascontiguousarray(y, dtype=p.dtype)
+    _fn("gpo_dense_grad_points", p.dtype)(_p(dp), _p(L), _p(yy), _p(p.coords), I64(p.n0),
+                                          I32(D), _ct(p.dtype)(p.scale), _p(p.bins), _p(p.vals),
+                                          I64(len(p.bins)), I32(0 if y is None else 1))
+    return dp.astype(p.dtype)
+
+
+def generate_logdet_grad_points(p):
+    """generate_logdet_grad_points (src/grad.jl:234-247): refinement + dense block."""
+    return refine_logdet_grad_points(p) + dense_grad_points(p)
+
+
+def generate_inv_loss_grad_points(p, data):
+    """generate_inv_loss_grad_points (src/grad.jl:360-377); data in the original order."""
+    d = np.asarray(data, p.dtype)
+    dord = d if p.indices is None else d[p.indices]
+    return refine_inv_loss_grad_points(p, dord) + dense_grad_points(p, dord[: p.n0])
+
+
+# ---------------------------------------------------------------------------------------------
 # Inputs: graph build and covariance tables, without the product library
 # ---------------------------------------------------------------------------------------------
 

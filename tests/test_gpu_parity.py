@@ -666,3 +666,25 @@ def test_reverse_pull_bit_exact(cuda_device, dt):
     assert not prob.reverse_mode()["built"]
     assert relerr(np.asarray(gp.generate_grad_xi(prob, vb)), ref) < TOL[dt]
     assert relerr(np.asarray(gp.generate_grad_vals(prob, xi, vb)), dv) < TOL[dt]
+
+
+@pytest.mark.parametrize("dt", [np.float64, np.float32])
+def test_points_gradients(cuda_device, dt):
+    # Point-position gradients -- refine_ and generate_ forms of the log-determinant's and of
+    # the inverse loss's -- against the host checker (itself pinned by finite differences of a
+    # continuous-position forward), (N, D) in tree order.  The pairs' terms are added
+    # atomically, hence the tolerance.
+    prob, orc = _config_problem(30_000, 3, 200, 8, dt, 31)
+    rng = np.random.default_rng(9)
+    n = prob.npoints()
+    data = rng.standard_normal(n).astype(dt)
+    vt = data[orc.indices]
+    g = np.asarray(gp.refine_logdet_grad_points(prob))
+    assert g.shape == (n, 3)
+    assert relerr(g, O.refine_logdet_grad_points(orc)) < TOL[dt]
+    assert relerr(np.asarray(gp.generate_logdet_grad_points(prob)),
+                  O.generate_logdet_grad_points(orc)) < TOL[dt]
+    assert relerr(np.asarray(gp.refine_inv_loss_grad_points(prob, vt)),
+                  O.refine_inv_loss_grad_points(orc, vt)) < TOL[dt]
+    assert relerr(np.asarray(gp.generate_inv_loss_grad_points(prob, data)),
+                  O.generate_inv_loss_grad_points(orc, data)) < TOL[dt]
