@@ -667,16 +667,19 @@ __global__ void k_ladder_pick(const T* __restrict__ base, const int* __restrict_
 // Candidates 0..nc-1 of the ladder: K with jit[c] added to the diagonal (exact T sum).  Only the
 // lower triangle is written: nothing downstream reads the upper one.
 template <typename T>
-__global__ void k_ladder_assemble(TableView<T> tv, const uint32_t* __restrict__ coords, int D,
-                                  int DS, T scale, int64_t n, SlotJit<T> jit, int nc,
-                                  T* __restrict__ base, const int* __restrict__ sel) {
+__global__ void k_ladder_assemble(TableView<T> tv, AnisoView<T> av,
+                                  const uint32_t* __restrict__ coords, int D, int DS, T scale,
+                                  int64_t n, SlotJit<T> jit, int nc, T* __restrict__ base,
+                                  const int* __restrict__ sel) {
     // A later launch of the ladder must not overwrite the slots once a candidate is selected.
     if (__ldcg(sel) >= 0) return;
     extern __shared__ __align__(16) unsigned char smem[];
     SmemTable<T> tab;
     tab.stage(tv, smem, threadIdx.x, blockDim.x);
     __syncthreads();
-    const T diag = tab.lookup(T(0));
+    // An anisotropic covariance (av.grid set) replaces the table (_assemble_dense_cov_aniso,
+    // src/aniso.jl:218-244).
+    const T diag = av.grid ? av.lookup(T(0), T(0)) : tab.lookup(T(0));
     const int64_t nn = n * n;
     for (int64_t j = blockIdx.x; j < n; j += gridDim.x) {
         for (int64_t i = j + threadIdx.x; i < n; i += blockDim.x) {
@@ -684,6 +687,9 @@ __global__ void k_ladder_assemble(TableView<T> tv, const uint32_t* __restrict__ 
                 for (int c = 0; c < nc; c++)
                     base[c * nn + j * n + j] =
                         jit.v[c] == T(0) ? diag : Num<T>::add(diag, jit.v[c]);
+            } else if (av.grid) {
+                const T v = av.pair_rt(coords + i * DS, coords + j * DS, D, scale);
+                for (int c = 0; c < nc; c++) base[c * nn + j * n + i] = v;
             } else {
                 long long sq = 0;
                 for (int d = 0; d < D; d++) {
@@ -761,7 +767,8 @@ int ladder_grid(gpb2_problem* p, cudaStream_t s, const std::vector<T>& jit, int 
         sj.v[0] = jit[c];
         GPB2_CUDA_TRY(launch_prof("dense_assemble", k_ladder_assemble<T>,
                                   dim3((unsigned)std::min<int64_t>(n, 4 * 148)), dim3(256), smem,
-                                  s, table_view<T>(p), (const uint32_t*)p->coords, (int)p->d,
+                                  s, table_view<T>(p), aniso_view<T>(p),
+                                  (const uint32_t*)p->coords, (int)p->d,
                                   coord_stride((int)p->d), (T)p->scale, n, sj, 1, base,
                                   (const int*)sel));
         CholArgs<T> args{base, n, 1, c, p->lad + kLadFail, sel, p->lad + kLadDone,
@@ -798,7 +805,8 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
     int ncand_used = 1;
     {
         T dmean = T(0);
-        const T v0 = (T)p->v0;  // every diagonal entry is cov_lookup(0)
+        // every diagonal entry is cov_lookup(0) (aniso_lookup(0, 0) for an anisotropic model)
+        const T v0 = (T)(p->an_grid ? p->an_diag : p->v0);
         for (int64_t i = 0; i < n; i++) dmean = dmean + v0;
         dmean = dmean / (T)(n > 1 ? n : 1);
         for (T eps = T(1e-9); eps <= T(1e-2) && ncand_used < ncand; eps *= T(10)) {
@@ -898,7 +906,8 @@ int dense_cholesky_ladder(gpb2_problem* p, cudaStream_t s) {
         }
         GPB2_CUDA_TRY(launch_prof("dense_assemble", k_ladder_assemble<T>,
                                   dim3((unsigned)std::min<int64_t>(n, 4 * 148)), dim3(256), smem,
-                                  s, table_view<T>(p), (const uint32_t*)p->coords, (int)p->d,
+                                  s, table_view<T>(p), aniso_view<T>(p),
+                                  (const uint32_t*)p->coords, (int)p->d,
                                   coord_stride((int)p->d), (T)p->scale, n,
                                   slot_jit(first, nc), nc, base, (const int*)sel));
         unsigned long long* trace = nullptr;

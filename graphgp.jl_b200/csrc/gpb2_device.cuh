@@ -146,6 +146,79 @@ struct TableView {
     T pivc;                    // T(1.5) * sqrt(eps(T)), evaluated in T on the host
 };
 
+// Anisotropic covariance K(d_spatial, d_z) (src/aniso.jl): grid[i + j * ns] =
+// K(spatial_bins[i], z_bins[j]) (the reference's (ns, nz) column-major grid), bilinear at the
+// fractional bin indices of the two separations.  grid == nullptr: the isotropic table.
+template <typename T>
+struct AnisoView {
+    const T* sb = nullptr;
+    const T* zb = nullptr;
+    const T* grid = nullptr;
+    int ns = 0, nz = 0;
+    T alpha = T(1);
+
+    // _frac_index (src/aniso.jl:42-57): 0-based, clamped to [0, n - 1].
+    static __device__ __forceinline__ T frac_index(T d, const T* __restrict__ bins, int n) {
+        using N = Num<T>;
+        if (d <= __ldg(bins)) return T(0);
+        if (d >= __ldg(bins + n - 1)) return T(n - 1);
+        int lo = 0, hi = n - 1;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (__ldg(bins + mid) <= d) lo = mid; else hi = mid;
+        }
+        const T x0 = __ldg(bins + lo), x1 = __ldg(bins + lo + 1);
+        return N::add(T(lo), N::div(N::sub(d, x0), N::sub(x1, x0)));
+    }
+
+    // aniso_lookup (src/aniso.jl:67-85), in its operation order.
+    __device__ __forceinline__ T lookup(T ds, T dz) const {
+        using N = Num<T>;
+        const T fx = frac_index(ds, sb, ns), fz = frac_index(dz, zb, nz);
+        const int i0 = (int)fx, j0 = (int)fz;  // truncation = floor: both are >= 0
+        const int i1 = i0 + 1 < ns ? i0 + 1 : ns - 1;
+        const int j1 = j0 + 1 < nz ? j0 + 1 : nz - 1;
+        const T tx = N::sub(fx, T(i0)), tz = N::sub(fz, T(j0));
+        const T ux = N::sub(T(1), tx), uz = N::sub(T(1), tz);
+        const T g00 = __ldg(grid + i0 + j0 * ns), g10 = __ldg(grid + i1 + j0 * ns);
+        const T g01 = __ldg(grid + i0 + j1 * ns), g11 = __ldg(grid + i1 + j1 * ns);
+        return N::add(N::mul(N::add(N::mul(g00, ux), N::mul(g10, tx)), uz),
+                      N::mul(N::add(N::mul(g01, ux), N::mul(g11, tx)), tz));
+    }
+
+    // The pair's separations (src/aniso.jl:88-105): spatial over the first D - 1 coordinates,
+    // radial |dz| * scale / alpha over the last; squares summed exactly (modulo 2^64, as Int64).
+    template <int D>
+    __device__ __forceinline__ T pair(const uint32_t (&a)[D], const uint32_t (&b)[D],
+                                      T scale) const {
+        using N = Num<T>;
+        unsigned long long sq = 0;
+#pragma unroll
+        for (int d = 0; d < D - 1; d++) {
+            const uint32_t di = a[d] > b[d] ? a[d] - b[d] : b[d] - a[d];
+            sq += (unsigned long long)di * di;
+        }
+        const long long dzi = (long long)a[D - 1] - (long long)b[D - 1];
+        const T ds = N::mul(N::sqrt(N::from_i64((long long)sq)), scale);
+        const T dz = N::div(N::mul(N::from_i64(dzi < 0 ? -dzi : dzi), scale), alpha);
+        return lookup(ds, dz);
+    }
+    // The same for coordinates in memory and a run-time D (the dense block's assembly).
+    __device__ __forceinline__ T pair_rt(const uint32_t* __restrict__ a,
+                                         const uint32_t* __restrict__ b, int D, T scale) const {
+        using N = Num<T>;
+        unsigned long long sq = 0;
+        for (int d = 0; d < D - 1; d++) {
+            const uint32_t di = a[d] > b[d] ? a[d] - b[d] : b[d] - a[d];
+            sq += (unsigned long long)di * di;
+        }
+        const long long dzi = (long long)a[D - 1] - (long long)b[D - 1];
+        const T ds = N::mul(N::sqrt(N::from_i64((long long)sq)), scale);
+        const T dz = N::div(N::mul(N::from_i64(dzi < 0 ? -dzi : dzi), scale), alpha);
+        return lookup(ds, dz);
+    }
+};
+
 // Bytes of dynamic shared memory a kernel needs for the staged table.
 template <typename T>
 __host__ __device__ inline size_t table_smem_bytes(int nb, int nkeys) {
@@ -405,6 +478,20 @@ struct PointMath {
                     if constexpr (KEEP_R) R[tri(a - 1, b)] = r;
                     L[tri(a, b)] = tab.lookup(r);
                 }
+            });
+        });
+    }
+
+    // assemble_cov! for an anisotropic covariance (src/aniso.jl:88-105).
+    static __device__ __forceinline__ void assemble_aniso(T (&L)[NT], const uint32_t (&jc)[KP1][D],
+                                                          T scale, const AnisoView<T>& av) {
+        const T diag = av.lookup(T(0), T(0));
+        sfor<0, KP1>([&](auto a_) {
+            GPB2_CI(a);
+            L[tri(a, a)] = diag;
+            sfor<0, a>([&](auto b_) {
+                GPB2_CI(b);
+                L[tri(a, b)] = av.template pair<D>(jc[a], jc[b], scale);
             });
         });
     }

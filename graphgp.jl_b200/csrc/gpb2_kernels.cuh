@@ -43,6 +43,7 @@ struct PointArgs {
     int64_t n0;
     T scale;
     FactorCache<T> fc;  // write target of k_factor / source of the gradient kernels, or none
+    AnisoView<T> an;    // an anisotropic covariance (forward kernels), or none: the table
 };
 
 constexpr int kFlatThreads = 128;
@@ -139,6 +140,22 @@ struct PointFactor {
         PM::template assemble<KEEP_R>(L, R, jc, a.scale, tab);
         PM::chol(L);
     }
+    // The same with the anisotropic covariance of a.an (src/aniso.jl: forward only).
+    __device__ __forceinline__ void compute_aniso(const PointArgs<T>& a, int64_t m) {
+        load_row_i32<K>(nb, a.nbrs + m * K);
+        uint32_t jc[PM::KP1][D];
+        PM::gather(jc, a.coords, nb, a.n0 + m);
+        PM::assemble_aniso(L, jc, a.scale, a.an);
+        PM::chol(L);
+    }
+    // Either covariance, for the forward kernels.
+    __device__ __forceinline__ void compute_any(const PointArgs<T>& a, const SmemTable<T>& tab,
+                                                int64_t m) {
+        if (a.an.grid)
+            compute_aniso(a, m);
+        else
+            compute(a, tab, m);
+    }
     // The factor cache's slab columns of point m (R must be a SlabWeights).
     __device__ __forceinline__ void bind_cache(const PointArgs<T>& a, int64_t m) {
         R.t = a.fc.t + m;
@@ -186,9 +203,13 @@ k_factor(PointArgs<T> a, int64_t m_begin, int64_t m_end, T* __restrict__ mv, T* 
         using RT = typename std::conditional<FILL, SlabWeights<T>,
                                              RegArr<T, PointMath<T, K, D>::NR>>::type;
         PointFactor<T, K, D, FILL, RT> f;
-        if constexpr (FILL) f.bind_cache(a, m);
-        f.compute(a, tab, m);
-        if constexpr (FILL) f.store_cached(a, m);
+        if constexpr (FILL) {  // the cache is never allocated for an anisotropic problem
+            f.bind_cache(a, m);
+            f.compute(a, tab, m);
+            f.store_cached(a, m);
+        } else {
+            f.compute_any(a, tab, m);
+        }
         T x[K];
         PointMath<T, K, D>::solve(x, f.L, a.tab.pivc);
         store_row_t<T, K>(mv + m * K, x);
@@ -210,7 +231,7 @@ k_inv(PointArgs<T> a, const T* __restrict__ values, T* __restrict__ xi_out, int6
          it += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = point_of(it, m0, mlist);
         PointFactor<T, K, D, false> f;
-        f.compute(a, tab, m);
+        f.compute_any(a, tab, m);
         T x[K];
         PointMath<T, K, D>::solve(x, f.L, a.tab.pivc);
         T mean = T(0);
@@ -238,7 +259,7 @@ k_logdet(PointArgs<T> a, T* __restrict__ terms, double* __restrict__ acc, int64_
          it += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = point_of(it, m0, mlist);
         PointFactor<T, K, D, false> f;
-        f.compute(a, tab, m);
+        f.compute_any(a, tab, m);
         const T t = N::log(f.L[tri(K, K)]);
         if (terms) terms[m] = t;
         s += (double)t;
@@ -609,7 +630,7 @@ k_fused_fwd(PointArgs<T> a, T* __restrict__ values, const T* __restrict__ xi_ref
          p += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = p - a.n0;
         PointFactor<T, K, D, false> f;
-        f.compute(a, tab, m);
+        f.compute_any(a, tab, m);
         T x[K];
         PointMath<T, K, D>::solve(x, f.L, a.tab.pivc);
         T acc = N::mul(f.L[tri(K, K)], xi_ref[m]);
@@ -718,23 +739,24 @@ struct SweepShape {
 };
 
 // The incoming terms of point p in the pull-form reverse sweep, in edge order (the serial
-// sweep's order): acc = vb[p] + w_0 vb[c_0] + w_1 vb[c_1] + ..., four edges' loads in flight.
+// sweep's order): acc = vb[p] + w_0 vb[c_0] + w_1 vb[c_1] + ..., eight edges' loads in flight.
 template <typename T, int K>
 __device__ __forceinline__ T pull_sum(T acc, const RevGraph<T>& rg, const T* __restrict__ vb,
                                       int64_t n0, uint32_t e, uint32_t end) {
     using N = Num<T>;
-    for (; e + 4 <= end; e += 4) {
-        int mj[4];
-        T w[4], v[4];
+    constexpr int U = 8;
+    for (; e + U <= end; e += U) {
+        int mj[U];
+        T w[U], v[U];
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
+        for (int u = 0; u < U; u++) {
             mj[u] = __ldg(rg.mj + e + u);
             w[u] = __ldg(rg.w + e + u);
         }
 #pragma unroll
-        for (int u = 0; u < 4; u++) v[u] = __ldcg(vb + n0 + mj[u] / K);
+        for (int u = 0; u < U; u++) v[u] = __ldcg(vb + n0 + mj[u] / K);
 #pragma unroll
-        for (int u = 0; u < 4; u++) acc = N::add(acc, N::mul(w[u], v[u]));
+        for (int u = 0; u < U; u++) acc = N::add(acc, N::mul(w[u], v[u]));
     }
     for (; e < end; e++) acc = N::add(acc, N::mul(__ldg(rg.w + e), __ldcg(vb + n0 + __ldg(rg.mj + e) / K)));
     return acc;

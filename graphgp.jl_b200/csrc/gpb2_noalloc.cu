@@ -92,6 +92,10 @@ int gpb2_refine_logdet_grad_vals_noalloc(gpb2_problem* p, void* dvals, double* l
     clear_error();
     if (!p || !dvals)
         return set_error(GPB2_ERR_INVALID_ARG, "gpb2_refine_logdet_grad_vals_noalloc: NULL");
+    if (p->an_grid)
+        return set_error(GPB2_ERR_INVALID_ARG,
+                         "gpb2_refine_logdet_grad_vals_noalloc: the anisotropic covariance "
+                         "supports the forward operations only");
     if (p->nb > kNoAllocMaxBins)
         return set_error(GPB2_ERR_INVALID_ARG,
                          "gpb2_refine_logdet_grad_vals_noalloc: %lld bins exceed the fixed "

@@ -171,7 +171,7 @@ struct Impl {
     // the caller's error), mode 2 only when the device keeps a margin of free memory beyond it
     // (else, or on a failed allocation, nothing: the kernels recompute).
     static int alloc_factor_cache(P* p) {
-        if (p->fc_L || p->fc_mode == 0 || p->m <= 0) return GPB2_OK;
+        if (p->fc_L || p->fc_mode == 0 || p->m <= 0 || p->an_grid) return GPB2_OK;
         const size_t ts = sizeof(T);
         const size_t nt = (size_t)(p->k + 1) * (p->k + 2) / 2, nr = nt - (size_t)(p->k + 1);
         if (p->fc_mode == 2) {
@@ -1098,6 +1098,15 @@ using namespace gpb2;
 #define CF32(x) static_cast<const float*>(x)
 #define CF64(x) static_cast<const double*>(x)
 
+// The vals and position gradients are defined for the isotropic table only: the reference's
+// anisotropic covariance is forward-only (src/aniso.jl:17).
+static int iso_only(const gpb2_problem* p, const char* fn) {
+    if (p && p->an_grid)
+        return set_error(GPB2_ERR_INVALID_ARG,
+                         "%s: the anisotropic covariance supports the forward operations only", fn);
+    return GPB2_OK;
+}
+
 static int need(const void* ptr, const char* name) {
     return ptr ? GPB2_OK : set_error(GPB2_ERR_INVALID_ARG, "%s is NULL", name);
 }
@@ -1210,6 +1219,7 @@ int gpb2_refine_logdet(gpb2_problem* p, double* out, void* stream) {
 }
 
 int gpb2_refine_logdet_grad_vals(gpb2_problem* p, void* dvals, double* ld, void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(dvals, "dvals"));
     GPB2_DISPATCH(p, Impl<float>::refine_logdet_grad_vals(p, F32(dvals), ld, s),
                   Impl<double>::refine_logdet_grad_vals(p, F64(dvals), ld, s));
@@ -1217,6 +1227,7 @@ int gpb2_refine_logdet_grad_vals(gpb2_problem* p, void* dvals, double* ld, void*
 
 int gpb2_refine_inv_loss_grad_vals(gpb2_problem* p, const void* values, void* dvals,
                                    double* loss, void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(values, "values") | need(dvals, "dvals"));
     GPB2_DISPATCH(p, Impl<float>::refine_inv_loss_tree(p, CF32(values), F32(dvals), loss, s),
                   Impl<double>::refine_inv_loss_tree(p, CF64(values), F64(dvals), loss, s));
@@ -1248,12 +1259,14 @@ int gpb2_generate_grad_xi(gpb2_problem* p, const void* vbar, void* xbar, void* s
 
 int gpb2_generate_grad_vals(gpb2_problem* p, const void* xi, const void* vbar, void* dvals,
                             void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(xi, "xi") | need(vbar, "vbar") | need(dvals, "dvals"));
     GPB2_DISPATCH(p, Impl<float>::generate_grad_vals(p, CF32(xi), CF32(vbar), F32(dvals), s),
                   Impl<double>::generate_grad_vals(p, CF64(xi), CF64(vbar), F64(dvals), s));
 }
 
 int gpb2_generate_logdet_grad_vals(gpb2_problem* p, void* dvals, double* ld, void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(dvals, "dvals"));
     GPB2_DISPATCH(p, Impl<float>::generate_logdet_grad_vals(p, F32(dvals), ld, s),
                   Impl<double>::generate_logdet_grad_vals(p, F64(dvals), ld, s));
@@ -1261,18 +1274,21 @@ int gpb2_generate_logdet_grad_vals(gpb2_problem* p, void* dvals, double* ld, voi
 
 int gpb2_generate_inv_loss_grad_vals(gpb2_problem* p, const void* data, void* dvals,
                                      double* loss, void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(data, "data") | need(dvals, "dvals"));
     GPB2_DISPATCH(p, Impl<float>::generate_inv_loss_grad_vals(p, CF32(data), F32(dvals), loss, s),
                   Impl<double>::generate_inv_loss_grad_vals(p, CF64(data), F64(dvals), loss, s));
 }
 
 int gpb2_refine_logdet_grad_points(gpb2_problem* p, void* d_points, void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(d_points, "d_points"));
     GPB2_DISPATCH(p, Impl<float>::refine_logdet_grad_points(p, F32(d_points), s),
                   Impl<double>::refine_logdet_grad_points(p, F64(d_points), s));
 }
 
 int gpb2_generate_logdet_grad_points(gpb2_problem* p, void* d_points, void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(d_points, "d_points"));
     GPB2_DISPATCH(p, Impl<float>::generate_logdet_grad_points(p, F32(d_points), s),
                   Impl<double>::generate_logdet_grad_points(p, F64(d_points), s));
@@ -1280,6 +1296,7 @@ int gpb2_generate_logdet_grad_points(gpb2_problem* p, void* d_points, void* stre
 
 int gpb2_refine_inv_loss_grad_points(gpb2_problem* p, const void* values, void* d_points,
                                      void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(values, "values") | need(d_points, "d_points"));
     GPB2_DISPATCH(p, Impl<float>::refine_inv_loss_grad_points(p, CF32(values), F32(d_points), s),
                   Impl<double>::refine_inv_loss_grad_points(p, CF64(values), F64(d_points), s));
@@ -1287,6 +1304,7 @@ int gpb2_refine_inv_loss_grad_points(gpb2_problem* p, const void* values, void* 
 
 int gpb2_generate_inv_loss_grad_points(gpb2_problem* p, const void* data, void* d_points,
                                        void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(data, "data") | need(d_points, "d_points"));
     GPB2_DISPATCH(p, Impl<float>::generate_inv_loss_grad_points(p, CF32(data), F32(d_points), s),
                   Impl<double>::generate_inv_loss_grad_points(p, CF64(data), F64(d_points), s));
@@ -1316,6 +1334,7 @@ int gpb2_generate_grad_xi_sharded(gpb2_problem* p, gpb2_comm* c, const void* vba
 
 int gpb2_generate_grad_vals_sharded(gpb2_problem* p, gpb2_comm* c, const void* xi,
                                     const void* vbar, void* dvals, void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(xi, "xi") | need(vbar, "vbar") | need(dvals, "dvals"));
     GPB2_SHARDED(p, c, Shard<float>::grad_vals(p, c, CF32(xi), CF32(vbar), F32(dvals), s),
                  Shard<double>::grad_vals(p, c, CF64(xi), CF64(vbar), F64(dvals), s));
@@ -1328,6 +1347,7 @@ int gpb2_generate_logdet_sharded(gpb2_problem* p, gpb2_comm* c, double* out, voi
 
 int gpb2_generate_logdet_grad_vals_sharded(gpb2_problem* p, gpb2_comm* c, void* dvals,
                                            double* ld, void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(dvals, "dvals"));
     GPB2_SHARDED(p, c, Shard<float>::logdet_grad(p, c, F32(dvals), ld, s),
                  Shard<double>::logdet_grad(p, c, F64(dvals), ld, s));
@@ -1335,6 +1355,7 @@ int gpb2_generate_logdet_grad_vals_sharded(gpb2_problem* p, gpb2_comm* c, void* 
 
 int gpb2_generate_inv_loss_grad_vals_sharded(gpb2_problem* p, gpb2_comm* c, const void* data,
                                              void* dvals, double* loss, void* stream) {
+    GPB2_TRY(iso_only(p, __func__));
     GPB2_TRY(need(data, "data") | need(dvals, "dvals"));
     GPB2_SHARDED(p, c, Shard<float>::inv_loss_grad(p, c, CF32(data), F32(dvals), loss, s),
                  Shard<double>::inv_loss_grad(p, c, CF64(data), F64(dvals), loss, s));

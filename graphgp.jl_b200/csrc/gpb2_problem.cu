@@ -270,7 +270,7 @@ static void free_problem(gpb2_problem* p) {
                     p->Ldr,    p->Dinv,  p->Wtri, p->Ainv,  p->sh_v, p->sh_vb,
                     p->sh_xg,  p->sh_own, p->perm_stage, p->perm_pos_g, p->perm_q_g,
                     p->perm_pos_s, p->perm_q_s, p->perm_from_g, p->perm_from_s, p->lib_tree, p->fc_L, p->fc_t, p->fc_lo,
-                    p->rev_off, p->rev_mj, p->rev_w, p->dpts};
+                    p->rev_off, p->rev_mj, p->rev_w, p->dpts, p->an_sb, p->an_zb, p->an_grid};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (p->solver) cusolverDnDestroy(p->solver);
@@ -288,6 +288,14 @@ static void free_problem(gpb2_problem* p) {
 }  // namespace gpb2
 
 using namespace gpb2;
+
+namespace gpb2 {
+// aniso_lookup(0, 0): the diagonal of an anisotropic covariance, for the dense jitter ladder.
+template <typename T>
+__global__ void k_aniso_diag(AnisoView<T> av, double* out) {
+    *out = (double)av.lookup(T(0), T(0));
+}
+}  // namespace gpb2
 
 extern "C" {
 
@@ -542,6 +550,61 @@ int gpb2_problem_set_factor_cache(gpb2_problem* p, int mode) {
         p->fc_valid = false;
         p->fc_sh_valid = false;
     }
+    return GPB2_OK;
+}
+
+int gpb2_problem_set_aniso(gpb2_problem* p, const void* spatial_bins_dev, int64_t ns,
+                           const void* z_bins_dev, int64_t nz, const void* grid_dev,
+                           double alpha, void* stream) {
+    clear_error();
+    if (!p || !spatial_bins_dev || !z_bins_dev || !grid_dev)
+        return set_error(GPB2_ERR_INVALID_ARG, "gpb2_problem_set_aniso: NULL");
+    if (ns < 1 || nz < 1 || ns > (1 << 20) || nz > (1 << 20) || !(alpha > 0.0))
+        return set_error(GPB2_ERR_INVALID_ARG,
+                         "gpb2_problem_set_aniso: ns %lld, nz %lld, alpha %g", (long long)ns,
+                         (long long)nz, alpha);
+    DeviceGuard dg(p->device);
+    if (!dg.ok) return set_error(GPB2_ERR_NO_DEVICE, "cudaSetDevice(%d) failed", p->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t ts = tsize(p);
+    GPB2_CUDA_TRY(cudaStreamSynchronize(s));  // earlier work may still read the old arrays
+    for (void** b : {&p->an_sb, &p->an_zb, &p->an_grid})
+        if (*b) {
+            cudaFree(*b);
+            *b = nullptr;
+        }
+    GPB2_TRY(ensure_alloc(&p->an_sb, ts * ns));
+    GPB2_TRY(ensure_alloc(&p->an_zb, ts * nz));
+    GPB2_TRY(ensure_alloc(&p->an_grid, ts * ns * nz));
+    GPB2_CUDA_TRY(cudaMemcpyAsync(p->an_sb, spatial_bins_dev, ts * ns, cudaMemcpyDeviceToDevice, s));
+    GPB2_CUDA_TRY(cudaMemcpyAsync(p->an_zb, z_bins_dev, ts * nz, cudaMemcpyDeviceToDevice, s));
+    GPB2_CUDA_TRY(
+        cudaMemcpyAsync(p->an_grid, grid_dev, ts * ns * nz, cudaMemcpyDeviceToDevice, s));
+    p->an_ns = (int)ns;
+    p->an_nz = (int)nz;
+    p->an_alpha = alpha;
+    // The ladder's diagonal value, aniso_lookup(0, 0), evaluated on the device.
+    double* d0 = nullptr;
+    GPB2_TRY(ensure_alloc(reinterpret_cast<void**>(&d0), sizeof(double)));
+    if (p->dtype == GPB2_F32)
+        k_aniso_diag<float><<<1, 1, 0, s>>>(aniso_view<float>(p), d0);
+    else
+        k_aniso_diag<double><<<1, 1, 0, s>>>(aniso_view<double>(p), d0);
+    double h0 = 0;
+    cudaMemcpyAsync(&h0, d0, sizeof(double), cudaMemcpyDeviceToHost, s);
+    const cudaError_t e = cudaStreamSynchronize(s);
+    cudaFree(d0);
+    GPB2_CUDA_TRY(e);
+    p->an_diag = h0;
+    // Every factor belongs to the previous covariance.
+    p->dense_valid = false;
+    p->dense_launched = false;
+    p->ladder_hint = -1;
+    p->factor_valid = false;
+    p->sh_factor_valid = false;
+    p->fc_valid = false;
+    p->fc_sh_valid = false;
+    p->rev_w_valid = false;
     return GPB2_OK;
 }
 

@@ -55,6 +55,14 @@ struct gpb2_problem {
     bool fc_valid = false;       // the cache holds the current table's factors of all points
     bool fc_sh_valid = false;    // ... of the points of this rank's level-sharded forward ranges
 
+    // Anisotropic covariance (src/aniso.jl), when set: the forward operations assemble from it
+    // instead of the table (bins/vals stay as given and unused).  (ns), (nz), (ns, nz) T.
+    void* an_sb = nullptr;
+    void* an_zb = nullptr;
+    void* an_grid = nullptr;
+    int an_ns = 0, an_nz = 0;
+    double an_alpha = 1.0, an_diag = 0.0;  // alpha; aniso_lookup(0, 0) (the ladder's diagonal)
+
     // Transposed graph of the pull-form reverse sweep (gpb2_rev.cu): rev_off (N + 1) delimits
     // each point's incoming edges in rev_mj (child m * K + slot j, in the serial sweep's order)
     // and rev_w (that slot's mean_vec, per table).  Mode 0: atomic push; 1: pull; 2 (default):
@@ -186,8 +194,23 @@ TableView<T> table_view(const gpb2_problem* p) {
 enum class FcUse { None, Fill, Read, ReadShard };
 
 template <typename T>
+AnisoView<T> aniso_view(const gpb2_problem* p) {
+    AnisoView<T> av;
+    if (p->an_grid) {
+        av.sb = static_cast<const T*>(p->an_sb);
+        av.zb = static_cast<const T*>(p->an_zb);
+        av.grid = static_cast<const T*>(p->an_grid);
+        av.ns = p->an_ns;
+        av.nz = p->an_nz;
+        av.alpha = (T)p->an_alpha;
+    }
+    return av;
+}
+
+template <typename T>
 PointArgs<T> point_args(const gpb2_problem* p, FcUse fc = FcUse::None) {
     PointArgs<T> a;
+    a.an = aniso_view<T>(p);
     a.tab = table_view<T>(p);
     a.coords = p->coords;
     a.nbrs = p->nbrs;

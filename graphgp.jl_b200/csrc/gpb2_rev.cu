@@ -74,8 +74,20 @@ size_t rev_graph_bytes(const gpb2_problem* p) {
     return E * (4 + ts) + 4 * ((size_t)p->n + 1);
 }
 
+// Mode 2 pulls from this many refined points up (GPB2_PULL_MIN overrides): below it the pushed
+// sweep is faster (small batches leave the pull's two dependent loads per point exposed; the
+// measured crossover on B200 is at about 2e7 points).
+static int64_t pull_min() {
+    static const int64_t v = [] {
+        const char* e = std::getenv("GPB2_PULL_MIN");
+        return e ? (int64_t)std::atoll(e) : (int64_t)20000000;
+    }();
+    return v;
+}
+
 int ensure_rev_graph(gpb2_problem* p, cudaStream_t s) {
     if (p->rev_off || p->rev_mode == 0 || p->m <= 0) return GPB2_OK;
+    if (p->rev_mode == 2 && p->m < pull_min()) return GPB2_OK;
     const int64_t N = p->n, M = p->m, K = p->k, E = M * K;
     if (E >= ((int64_t)1 << 31) || N >= ((int64_t)1 << 32) - 1) return GPB2_OK;  // 32-bit CSR
     const size_t ts = p->dtype == GPB2_F32 ? 4 : 8;

@@ -15,7 +15,8 @@ from .api import (check_graph, generate, generate_grad_vals, generate_grad_xi, g
                   refine_logdet_grad_points, refine_logdet_grad_vals,
                   refine_logdet_grad_vals_noalloc, refine_logdet_terms, set_synchronous)
 from .autodiff import generate_of_vals, generate_t, inv_quadratic_loss_of_vals, logdet_of_vals
-from .extras import hyperparam_grad, make_cov_bins, matern_kernel, rbf_kernel
+from .extras import (AnisoCov, build_anisotropic_covariance, hyperparam_grad, make_cov_bins,
+                     matern_kernel, rbf_kernel)
 from .graph import build_graph, build_graph_arrays, build_graph_device, cached_graph
 from .problem import GraphGPProblem, set_vals, to_backend
 

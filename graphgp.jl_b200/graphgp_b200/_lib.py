@@ -85,6 +85,7 @@ _SIGNATURES = {
     "gpb2_problem_prefactor": (I32, [P, P]),
     "gpb2_problem_info": (I32, [P, PI64, PI64, PI64, PI64, PI64]),
     "gpb2_problem_set_factor_cache": (I32, [P, I32]),
+    "gpb2_problem_set_aniso": (I32, [P, P, I64, P, I64, P, C.c_double, P]),
     "gpb2_problem_set_reverse_mode": (I32, [P, I32]),
     "gpb2_problem_reverse_mode": (I32, [P, C.POINTER(I32), C.POINTER(I32), PI64]),
     "gpb2_problem_factor_cache": (I32, [P, C.POINTER(I32), C.POINTER(I32), PI64]),

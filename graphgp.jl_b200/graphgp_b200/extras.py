@@ -86,3 +86,27 @@ def hyperparam_grad(grad_cov_vals, make_kernel, hyperparams):
 
     J = torch.autograd.functional.jacobian(f, hp)
     return (J.T @ g).numpy()
+
+
+class AnisoCov:
+    """Anisotropic covariance K(d_spatial, d_z) (src/types.jl:15-20): a 2-D table
+    ``grid[i, j] = K(spatial_bins[i], z_bins[j])`` bilinear in the fractional bin indices;
+    points carry the radial coordinate last (alpha * z), the first D - 1 spatial."""
+
+    def __init__(self, spatial_bins, z_bins, grid, alpha):
+        self.spatial_bins = spatial_bins
+        self.z_bins = z_bins
+        self.grid = grid
+        self.alpha = float(alpha)
+
+
+def build_anisotropic_covariance(spatial_bins, z_bins, grid, alpha, jitter=0.0, dtype=None):
+    """``build_anisotropic_covariance`` (src/aniso.jl:20-39): grid (ns, nz), increasing axes
+    starting at 0; ``grid[0, 0]`` inflated by ``1 + jitter`` (in the grid's type)."""
+    g = np.array(grid, dtype=dtype if dtype is not None else np.asarray(grid).dtype, copy=True)
+    if g.shape != (len(spatial_bins), len(z_bins)):
+        raise ValueError("grid must be (len(spatial_bins), len(z_bins))")
+    t = g.dtype.type
+    g[0, 0] = g[0, 0] * (t(1) + t(jitter))
+    return AnisoCov(np.asarray(spatial_bins, g.dtype), np.asarray(z_bins, g.dtype), g,
+                    alpha)

@@ -49,10 +49,21 @@ def _destroy(handle_value: int) -> None:
 
 
 class GraphGPProblem:
-    """GraphGPProblem(coords, neighbors, offsets, n0, scale, bins, vals, indices=None)."""
+    """GraphGPProblem(coords, neighbors, offsets, n0, scale, bins, vals, indices=None), or with
+    an anisotropic covariance ``GraphGPProblem.anisotropic(coords, neighbors, offsets, n0,
+    scale, cov, indices=None)`` (src/types.jl:62-68; forward operations only)."""
+
+    @classmethod
+    def anisotropic(cls, coords, neighbors, offsets, n0, scale, cov, indices=None, **kw):
+        # The table holds the covariance's axes as placeholders, as in the reference.
+        prob = cls(coords, neighbors, offsets, n0, scale, cov.spatial_bins, cov.z_bins, indices,
+                   dtype=kw.pop("dtype", cov.grid.dtype), **kw)
+        prob.cov = cov
+        return prob
 
     def __init__(self, coords, neighbors, offsets, n0, scale, bins, vals, indices=None, *,
                  dtype=None, device=None, neighbor_base: int = 0):
+        self.cov = None
         dt = np.dtype(dtype) if dtype is not None else _np_dtype(vals)
         if dt not in _DT:
             raise TypeError(f"vals must be float32 or float64 (got {dt})")
@@ -160,6 +171,19 @@ class GraphGPProblem:
                                            None if idx is None else idx.ctypes.data_as(_lib.PI64),
                                            0, C.c_void_p(stream))
             _lib.check(st, "GraphGPProblem upload")
+            if self.cov is not None:
+                cv = self.cov
+                sb = self._dev(cv.spatial_bins, self.torch_dtype)
+                zb = self._dev(cv.z_bins, self.torch_dtype)
+                # (ns, nz) column-major, as the reference's Matrix.
+                g = self._dev(np.asarray(cv.grid).ravel(order="F"), self.torch_dtype)
+                st = L.gpb2_problem_set_aniso(h, C.c_void_p(sb.data_ptr()), sb.numel(),
+                                              C.c_void_p(zb.data_ptr()), zb.numel(),
+                                              C.c_void_p(g.data_ptr()), float(cv.alpha),
+                                              C.c_void_p(stream))
+                if st != 0:
+                    L.gpb2_problem_destroy(h)
+                    _lib.check(st, "GraphGPProblem anisotropic covariance")
         return h
 
     def update_vals(self, vals) -> "GraphGPProblem":
@@ -209,8 +233,9 @@ class GraphGPProblem:
 
     def set_reverse_mode(self, mode: int) -> "GraphGPProblem":
         """Reverse sweep form: 0 atomic push (sums in no fixed order), 1 pull through the
-        transposed graph (the serial sweep's sums bit for bit), 2 (default) pull when the graph
-        fits in free device memory with a margin."""
+        transposed graph (the serial sweep's sums bit for bit), 2 (default) pull from 2e7
+        refined points up (below, the push is faster) when the graph fits in free device
+        memory with a margin."""
         _lib.check(_lib.lib().gpb2_problem_set_reverse_mode(self.handle, int(mode)),
                    "set_reverse_mode")
         return self

@@ -76,6 +76,20 @@ function _create(prob::GraphGPProblem{T}) where {T}
             idxv === nothing ? Ptr{Int64}(C_NULL) : pointer(idxv), Cint(1), _stream())
         _check(rc, "gpb2_problem_create")
     end
+    # An anisotropic covariance (src/types.jl:37, src/aniso.jl): the forward operations
+    # assemble from its grid; its CuArrays are copied into the handle.
+    if prob.cov !== nothing
+        cov = prob.cov
+        rc = ccall(_sym(:gpb2_problem_set_aniso), Cint,
+            (Ptr{Cvoid}, CuPtr{Cvoid}, Int64, CuPtr{Cvoid}, Int64, CuPtr{Cvoid}, Cdouble,
+             Ptr{Cvoid}),
+            out[], _ptr(cov.spatial_bins), length(cov.spatial_bins), _ptr(cov.z_bins),
+            length(cov.z_bins), _ptr(cov.grid), Float64(cov.alpha), _stream())
+        if rc != 0
+            ccall(_sym(:gpb2_problem_destroy), Cint, (Ptr{Cvoid},), out[])
+            _check(rc, "gpb2_problem_set_aniso")
+        end
+    end
     h = Handle(out[], prob.vals)
     finalizer(h) do hh
         ccall(_sym(:gpb2_problem_destroy), Cint, (Ptr{Cvoid},), hh.ptr)

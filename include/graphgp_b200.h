@@ -110,6 +110,21 @@ int gpb2_problem_set_vals(gpb2_problem* prob, const void* vals_dev, void* stream
  * factorises the dense block) is reported by the next operation that uses the factor. */
 int gpb2_problem_prefactor(gpb2_problem* prob, void* stream);
 
+/* Anisotropic covariance K(d_spatial, d_z) (src/aniso.jl; the problem constructor of
+ * src/types.jl:62-68 with an AnisoCov): a 2-D table grid[i + j*ns] = K(spatial_bins[i],
+ * z_bins[j]) ((ns, nz) column-major, as the reference's Matrix; the caller applies the
+ * jitter to grid[0], as build_anisotropic_covariance does), bilinear interpolation at the
+ * fractional bin indices (aniso_lookup, src/aniso.jl:67-85) of d_spatial = |x_a - x_b| over
+ * the first D - 1 coordinates and d_z = |z_a - z_b| / alpha over the last (times scale).  From
+ * this call on, the forward operations (generate, generate_inv, generate_logdet, refine*, and
+ * generate_grad_xi, their adjoint) assemble every covariance -- the dense block's included --
+ * from it; the vals and position gradients return GPB2_ERR_INVALID_ARG (the reference's
+ * anisotropic path is forward-only).  All arrays are the problem's T, on the device; they are
+ * copied. */
+int gpb2_problem_set_aniso(gpb2_problem* prob, const void* spatial_bins_dev, int64_t ns,
+                           const void* z_bins_dev, int64_t nz, const void* grid_dev, double alpha,
+                           void* stream);
+
 /* Per-point factor cache: the packed (K+1)x(K+1) Cholesky factor of every refined point and
  * the interpolation segment and fraction of each of its K(K+1)/2 pair radii, kept in device
  * memory (M * (NT*sizeof(T) + NR*(sizeof(T)+2)) bytes, NT = (K+1)(K+2)/2, NR = NT - K - 1;
@@ -134,7 +149,8 @@ int gpb2_problem_factor_cache(const gpb2_problem* prob, int* mode, int* valid, i
  * order) -- sums bit for bit those of the serial reference sweep and reproducible -- at the
  * cost of (4 + sizeof(T)) bytes per edge plus 4 per point of device memory (the graph is built
  * once, its weights once per table).  2 (default; GPB2_REVERSE_MODE in the environment sets the
- * default of new handles): 1 when it fits with a margin of free memory, else 0.  The per-batch
+ * default of new handles): 1 from 2e7 refined points up (GPB2_PULL_MIN overrides; below it the
+ * push is faster) when the graph fits with a margin of free memory, else 0.  The per-batch
  * sweep modes and the level-sharded operations always push.  No reference counterpart. */
 int gpb2_problem_set_reverse_mode(gpb2_problem* prob, int mode);
 /* The mode, whether the transposed graph is built, and its size in bytes. */

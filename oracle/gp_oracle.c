@@ -95,6 +95,77 @@ static inline int64_t cov_lookup_weights(T r, const T* bins, int64_t n, T* wlo, 
     return lo;
 }
 
+/* Anisotropic covariance (src/aniso.jl), consulted by assemble_cov and gpo_dense_cov while set
+ * by gpo_set_aniso (this checker handles one problem at a time). */
+static struct {
+    const T* sb;
+    int64_t ns;
+    const T* zb;
+    int64_t nz;
+    const T* grid; /* (ns, nz) column-major */
+    T alpha;
+    int on;
+} g_an;
+
+int SFX(gpo_set_aniso)(const T* sb, int64_t ns, const T* zb, int64_t nz, const T* grid,
+                       T alpha, int on) {
+    g_an.sb = sb;
+    g_an.ns = ns;
+    g_an.zb = zb;
+    g_an.nz = nz;
+    g_an.grid = grid;
+    g_an.alpha = alpha;
+    g_an.on = on;
+    return 0;
+}
+
+/* _frac_index (src/aniso.jl:42-57): 0-based, clamped to [0, n - 1]. */
+static inline T frac_index(T d, const T* bins, int64_t n) {
+    if (d <= bins[0]) return (T)0;
+    if (d >= bins[n - 1]) return (T)(n - 1);
+    int64_t lo = 0, hi = n - 1;
+    while (hi - lo > 1) {
+        int64_t mid = (lo + hi) >> 1;
+        if (bins[mid] <= d) lo = mid; else hi = mid;
+    }
+    T x0 = bins[lo], x1 = bins[lo + 1];
+    return (T)lo + (d - x0) / (x1 - x0);
+}
+
+/* aniso_lookup (src/aniso.jl:67-85). */
+static inline T aniso_lookup(T ds, T dz) {
+    T fx = frac_index(ds, g_an.sb, g_an.ns), fz = frac_index(dz, g_an.zb, g_an.nz);
+    int64_t i0 = (int64_t)fx, j0 = (int64_t)fz;
+    int64_t i1 = i0 + 1 < g_an.ns ? i0 + 1 : g_an.ns - 1;
+    int64_t j1 = j0 + 1 < g_an.nz ? j0 + 1 : g_an.nz - 1;
+    T tx = fx - (T)i0, tz = fz - (T)j0;
+    const T* g = g_an.grid;
+    int64_t ns = g_an.ns;
+    T g00 = g[i0 + j0 * ns], g10 = g[i1 + j0 * ns], g01 = g[i0 + j1 * ns], g11 = g[i1 + j1 * ns];
+    return (g00 * ((T)1 - tx) + g10 * tx) * ((T)1 - tz) + (g01 * ((T)1 - tx) + g11 * tx) * tz;
+}
+
+/* aniso_lookup on arrays (the model set by gpo_set_aniso). */
+int SFX(gpo_aniso_lookup)(const T* ds, const T* dz, int64_t n, T* out) {
+    for (int64_t i = 0; i < n; i++) out[i] = aniso_lookup(ds[i], dz[i]);
+    return 0;
+}
+
+/* The pair's covariance under the anisotropic model (src/aniso.jl:88-105): spatial distance
+ * over the first D - 1 coordinates, radial |dz| * scale / alpha over the last. */
+static inline T aniso_pair(const uint32_t* a, const uint32_t* b, int D, T scale) {
+    int64_t sqs = 0;
+    for (int d = 0; d < D - 1; d++) {
+        int64_t di = (int64_t)a[d] - (int64_t)b[d];
+        sqs += di * di;
+    }
+    int64_t dzi = (int64_t)a[D - 1] - (int64_t)b[D - 1];
+    T dsp = SQRT_T((T)sqs) * scale;
+    T tz = (T)dzi;
+    T dz = (tz < 0 ? -tz : tz) * scale / g_an.alpha;
+    return aniso_lookup(dsp, dz);
+}
+
 /* Radius between two lattice points: exact Int64 squared distance, then T(sq), sqrt, * scale
  * (src/linalg.jl:19-24). */
 static inline T lattice_radius(const uint32_t* a, const uint32_t* b, int D, T scale) {
@@ -118,6 +189,14 @@ static inline void gather_joint(uint32_t* jc, const uint32_t* coords, const int6
 /* src/linalg.jl:15-29.  A is KP1 x KP1 row-major; only the lower triangle is written. */
 static inline void assemble_cov(T* A, const uint32_t* jc, int KP1, int D, T scale,
                                 const T* bins, const T* vals, int64_t nb) {
+    if (g_an.on) { /* assemble_cov! of src/aniso.jl:88-105 */
+        T diag = aniso_lookup((T)0, (T)0);
+        for (int a = 0; a < KP1; a++) {
+            A[a * KP1 + a] = diag;
+            for (int b = 0; b < a; b++) A[a * KP1 + b] = aniso_pair(jc + a * D, jc + b * D, D, scale);
+        }
+        return;
+    }
     for (int a = 0; a < KP1; a++) {
         A[a * KP1 + a] = cov_lookup((T)0, bins, vals, nb);
         for (int b = 0; b < a; b++) {
@@ -586,12 +665,18 @@ int SFX(gpo_refine_inv_loss_grad_vals)(double* dv_out, double* loss_out, const T
  * independent, so the columns are spread over the host threads. */
 int SFX(gpo_dense_cov)(T* K, const uint32_t* coords, int64_t n, int D, T scale, const T* bins,
                        const T* vals, int64_t nb) {
+    /* _assemble_dense_cov_aniso (src/aniso.jl:218-244) while the anisotropic model is set. */
 #pragma omp parallel for schedule(dynamic, 16)
     for (int64_t j = 0; j < n; j++) {
-        K[j * n + j] = cov_lookup((T)0, bins, vals, nb);
+        K[j * n + j] = g_an.on ? aniso_lookup((T)0, (T)0) : cov_lookup((T)0, bins, vals, nb);
         for (int64_t i = j + 1; i < n; i++) {
-            T r = lattice_radius(coords + i * D, coords + j * D, D, scale);
-            T v = cov_lookup(r, bins, vals, nb);
+            T v;
+            if (g_an.on) {
+                v = aniso_pair(coords + i * D, coords + j * D, D, scale);
+            } else {
+                T r = lattice_radius(coords + i * D, coords + j * D, D, scale);
+                v = cov_lookup(r, bins, vals, nb);
+            }
             K[i * n + j] = v;
             K[j * n + i] = v;
         }

@@ -220,10 +220,50 @@ def dense_cov(p, n=None):
     return Km
 
 
+_ANISO = None  # the anisotropic covariance in force (see `anisotropic`), or None
+
+
+class anisotropic:
+    """Context in which the assembly functions of the C restatement use an anisotropic
+    covariance (src/aniso.jl) instead of the table: ``with anisotropic(p, cov): generate(p, xi)``.
+    cov has spatial_bins (ns), z_bins (nz), grid (ns, nz) and alpha, in the problem's type."""
+
+    def __init__(self, p, cov):
+        self.p = p
+        dt = p.dtype
+        self.sb = np.ascontiguousarray(cov.spatial_bins, dt)
+        self.zb = np.ascontiguousarray(cov.z_bins, dt)
+        self.g = np.ascontiguousarray(np.asarray(cov.grid, dt).ravel(order="F"))
+        self.alpha = float(cov.alpha)
+
+    def __enter__(self):
+        global _ANISO
+        _fn("gpo_set_aniso", self.p.dtype)(_p(self.sb), I64(self.sb.size), _p(self.zb),
+                                            I64(self.zb.size), _p(self.g),
+                                            _ct(self.p.dtype)(self.alpha), I32(1))
+        _ANISO = hash((self.sb.tobytes(), self.zb.tobytes(), self.g.tobytes(), self.alpha))
+        return self
+
+    def __exit__(self, *exc):
+        global _ANISO
+        _fn("gpo_set_aniso", self.p.dtype)(None, I64(0), None, I64(0), None,
+                                            _ct(self.p.dtype)(1.0), I32(0))
+        _ANISO = None
+
+
+def aniso_lookup(p, ds, dz):
+    """aniso_lookup (src/aniso.jl:67-85) of the model in force, on arrays."""
+    ds = np.ascontiguousarray(np.atleast_1d(ds), p.dtype)
+    dz = np.ascontiguousarray(np.atleast_1d(dz), p.dtype)
+    out = np.empty_like(ds)
+    _fn("gpo_aniso_lookup", p.dtype)(_p(ds), _p(dz), I64(ds.size), _p(out))
+    return out
+
+
 def dense_chol(p):
     """_dense_chol_L (src/dense.jl:46-67) -> (L, jitter_used).  The factor is kept on the
     problem object for its table (a large first layer takes minutes on the host)."""
-    key = hash(p.vals.tobytes())
+    key = hash((p.vals.tobytes(), _ANISO))
     cached = getattr(p, "_dense_cache", None)
     if cached is not None and cached[0] == key:
         return cached[1], cached[2]

@@ -2,7 +2,8 @@
 
 The reference (yipihey/GraphGP.jl) pins its refine path with JAX/Python-generated fixtures:
 ``test/reference/small.npz`` and ``medium.npz`` (written by ``test/dump_reference.py``) and
-``test/reference/generate_parity.npz`` (written by ``test/python_parity_generate.py``).  This
+``test/reference/generate_parity.npz`` (written by ``test/python_parity_generate.py``), and its
+anisotropic path with ``test/reference/aniso_parity.npz`` (``test/python_parity_aniso.py``).  This
 script copies their arrays, unchanged, into compressed ``.npz`` files here so the tests can run
 where the reference tree is absent (the GPU box).  Run it where the reference is mounted:
 
@@ -14,7 +15,7 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-NAMES = ("small", "medium", "generate_parity")
+NAMES = ("small", "medium", "generate_parity", "aniso_parity")
 
 
 def main(ref_root: str) -> None:

@@ -8,7 +8,10 @@ of side sqrt(1e6/1e9)) and the same lattice step relative to the point spacing (
 over the window instead of 21 over the unit square), so the per-point factorisations meet the
 near-singular covariances and lattice collisions of the full configuration; the clamp counts
 are reported with the errors.  Tolerances are those of the drop-in target: 1e-5 norm-relative
-in float32 (test/python_parity_generate.jl:26-36 measures the same way).
+in float32 (test/python_parity_generate.jl:26-36 measures the same way).  The reverse sweep runs
+in its pull form (set_reverse_mode(1); automatic only from 2e7 points up, where it is also the
+faster form), whose sums follow the serial reference sweep's order: generate_grad_xi is then the
+oracle's bit for bit at every configuration.
 """
 import numpy as np
 import pytest
@@ -32,6 +35,7 @@ def _problems(c, pts=None, n0=None, lattice_bits=21):
     dt = c.dtype
     prob = gp.GraphGPProblem(g["coords"], g["neighbors"], g["offsets"], g["n0"], dt(g["scale"]),
                              bins, vals, g["indices"], dtype=dt)
+    prob.set_reverse_mode(1)
     orc = O.make_problem(g["coords"], g["neighbors"], g["offsets"], g["n0"], dt(g["scale"]),
                          bins, vals, g["indices"], dt)
     return prob, orc, g
