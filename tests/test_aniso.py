@@ -86,6 +86,7 @@ def test_aniso_gpu(cuda_device, dt):
     # mat-vecs) are the checker's bit for bit; generate_inv's dense layer multiplies by the kept
     # inverse of the factor (not the checker's forward substitution), and the log-determinant is
     # summed in another order, so those two agree to the tolerance, as in the isotropic tests.
+    # The reverse sweep runs in its pull form, whose sums follow the serial sweep's order.
     import graphgp_b200 as gp
     tol = 1e-12 if dt == np.float64 else 1e-5
     d, p, cov = _fixture_problem(dt)
@@ -93,6 +94,7 @@ def test_aniso_gpu(cuda_device, dt):
                        np.asarray(cov.grid, dt), cov.alpha)
     prob = gp.GraphGPProblem.anisotropic(d["coords"], d["neighbors"], d["offsets"], int(d["n0"]),
                                          dt(d["scale"]), acov, d["indices"], dtype=dt)
+    prob.set_reverse_mode(1)
     xi = d["xi"].astype(dt)
     vals = d["values"].astype(dt)
     vb = np.random.default_rng(4).standard_normal(len(xi)).astype(dt)
