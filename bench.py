@@ -648,11 +648,14 @@ def c2_step(args, dev, stream, timed):
             "unit": UNIT, "ms_per_step": t, "l2": "flushed between timed steps (256 MB write)"}
 
 
-# DRAM bytes (read + write) per launch of the step's kernels, from one ncu capture of
-# `python bench.py --ncu-case --points 10000000` scaled to a 1e8-point launch (profiles/).
-# Measured, not computed here: the bench itself never runs under a profiler.
-NCU_TRAFFIC = {}
-NCU_SOURCE = "profiles/ (ncu capture at 1e7 points, scaled by points per launch)"
+# DRAM bytes (read + write) per launch, from one ncu capture of
+# `GPB2_REVERSE_MODE=1 python bench.py --ncu-case --points 10000000` (5.356e9 bytes for
+# 9.995e6 refined points) scaled to the 99,995,000 refined points of a 1e8-point launch
+# (profiles/traffic_c4_1e7_step.md).  Only the streaming kernel is listed: the sweeps' neighbour
+# reads partly hit L2 at 1e7 points, so their bytes do not scale with the points.  Measured,
+# not computed here: the bench itself never runs under a profiler.
+NCU_TRAFFIC = {"grad_vals_cached": 5.3563e9 * 99_995_000 / 9_995_000}
+NCU_SOURCE = "profiles/traffic_c4_1e7_step.md (ncu at 1e7 points, scaled by refined points)"
 
 
 def main():
