@@ -59,6 +59,22 @@ template <> struct Num<float> {
         const bool safe = (ea - 31u) < 130u && (eb - 97u) < 60u;  // |a| in [2^-96, 2^34), b in [2^-30, 2^30)
         return safe ? q : __fdiv_rn(a, b);
     }
+    // The corrected quotient of div_r without its per-operation range check, for callers that
+    // check a whole point's operands at once (DivChecked): exact when quot_a_ok(a) and b and 2b
+    // pass quot_b_ok, div_r's window.
+    static __device__ __forceinline__ float div_q(float a, float b, float r) {
+        const float q0 = __fmul_rn(a, r);
+        const float e = __fmaf_rn(-q0, b, a);
+        return __fmaf_rn(e, r, q0);
+    }
+    static __device__ __forceinline__ bool quot_a_ok(float a) {
+        return (((__float_as_uint(a) >> 23) & 0xffu) - 31u) < 130u;
+    }
+    static __device__ __forceinline__ bool quot_b_ok(float b) {
+        return (((__float_as_uint(b) >> 23) & 0xffu) - 97u) < 60u;
+    }
+    // RN(1 / a): the same bits as div(1, a).
+    static __device__ __forceinline__ float rcp(float a) { return __frcp_rn(a); }
     static __device__ __forceinline__ float log(float a) { return logf(a); }
     static __device__ __forceinline__ float from_i64(long long x) { return __ll2float_rn(x); }
     static __device__ __forceinline__ U bits(float x) { return __float_as_uint(x); }
@@ -86,6 +102,20 @@ template <> struct Num<double> {
         const bool safe = (ea - 223u) < 1024u && (eb - 923u) < 200u;  // |a| in [2^-800, 2^224), b in [2^-100, 2^100)
         return safe ? q : __ddiv_rn(a, b);
     }
+    static __device__ __forceinline__ double div_q(double a, double b, double r) {
+        const double q0 = __dmul_rn(a, r);
+        const double e = __fma_rn(-q0, b, a);
+        return __fma_rn(e, r, q0);
+    }
+    static __device__ __forceinline__ bool quot_a_ok(double a) {
+        const unsigned long long u = (unsigned long long)__double_as_longlong(a);
+        return ((unsigned)((u >> 52) & 0x7ffu) - 223u) < 1024u;
+    }
+    static __device__ __forceinline__ bool quot_b_ok(double b) {
+        const unsigned long long u = (unsigned long long)__double_as_longlong(b);
+        return ((unsigned)((u >> 52) & 0x7ffu) - 923u) < 200u;
+    }
+    static __device__ __forceinline__ double rcp(double a) { return __drcp_rn(a); }
     static __device__ __forceinline__ double log(double a) { return ::log(a); }
     static __device__ __forceinline__ double from_i64(long long x) { return __ll2double_rn(x); }
     static __device__ __forceinline__ U bits(double x) {
@@ -420,6 +450,36 @@ __device__ __forceinline__ void sfor_down(F&& f) {
 }
 #define GPB2_CI(name) constexpr int name = decltype(name##_)::value
 
+// Division policies of the adjoint arithmetic (forward_subst, pullback), both giving the
+// correctly rounded quotient a / b from r = RN(1/b).  DivExact: div_r, whose range check and IEEE
+// fallback come with every division.  DivChecked: the bare corrected quotient (div_q), each
+// dividend's exponent tested against div_r's window into one flag; ok() then adds the pivots
+// (the divisors L[j][j] and 2 L[j][j]) and says whether every operation of the point lay in the
+// window where div_q is exact.  A point that fails is redone with DivExact (rare: clamped
+// pivots, zero or extreme cotangents), so the results are DivExact's bit for bit.  The window
+// is tested on the exponent bits, exactly as div_r tests it.
+template <typename T>
+struct DivExact {
+    __device__ __forceinline__ T operator()(T a, T b, T r) { return Num<T>::div_r(a, b, r); }
+};
+template <typename T>
+struct DivChecked {
+    bool bad = false;
+    __device__ __forceinline__ T operator()(T a, T b, T r) {
+        bad |= !Num<T>::quot_a_ok(a);
+        return Num<T>::div_q(a, b, r);
+    }
+    template <int KP1, int NT>
+    __device__ __forceinline__ bool ok(const T (&L)[NT]) const {
+        bool pb = false;
+        sfor<0, KP1>([&](auto j_) {
+            GPB2_CI(j);
+            pb |= !Num<T>::quot_b_ok(L[tri(j, j)]) || !Num<T>::quot_b_ok(Num<T>::mul(T(2), L[tri(j, j)]));
+        });
+        return !bad && !pb;
+    }
+};
+
 template <typename T, int K, int D>
 struct PointMath {
     using N = Num<T>;
@@ -512,7 +572,7 @@ struct PointMath {
             L[tri(j, j)] = d;
             // t / d for the column's entries: the correctly rounded quotients, from one rounded
             // reciprocal of the pivot (div_r), the same bits as the IEEE divisions.
-            const T rd = N::div(T(1), d);
+            const T rd = N::rcp(d);
             sfor<j + 1, KP1>([&](auto i_) {
                 GPB2_CI(i);
                 T t = L[tri(i, j)];
@@ -545,7 +605,7 @@ struct PointMath {
     static __device__ __forceinline__ void pivot_recips(T (&rp)[KP1], const T (&L)[NT]) {
         sfor<0, KP1>([&](auto j_) {
             GPB2_CI(j);
-            rp[j] = N::div(T(1), L[tri(j, j)]);
+            rp[j] = N::rcp(L[tri(j, j)]);
         });
     }
 
@@ -555,9 +615,10 @@ struct PointMath {
     // operation order with every operation rounded to nearest, as the forward's: each division
     // by a pivot is the correctly rounded quotient (div_r, from the pivot's reciprocal), so a
     // point's cotangents equal the CPU restatement's bit for bit.
-    template <bool GUARD>
+    template <bool GUARD, typename Div = DivExact<T>>
     static __device__ __forceinline__ void forward_subst(T (&z)[K], const T (&L)[NT],
-                                                         const T (&rp)[KP1], T pivfloor) {
+                                                         const T (&rp)[KP1], T pivfloor,
+                                                         Div&& div = Div()) {
         sfor<0, K>([&](auto i_) {
             GPB2_CI(i);
             T s = z[i];
@@ -566,9 +627,9 @@ struct PointMath {
                 s = N::sub(s, N::mul(L[tri(i, q)], z[q]));
             });
             if constexpr (GUARD)
-                z[i] = L[tri(i, i)] > pivfloor ? N::div_r(s, L[tri(i, i)], rp[i]) : T(0);
+                z[i] = L[tri(i, i)] > pivfloor ? div(s, L[tri(i, i)], rp[i]) : T(0);
             else
-                z[i] = N::div_r(s, L[tri(i, i)], rp[i]);
+                z[i] = div(s, L[tri(i, i)], rp[i]);
         });
     }
 
@@ -589,8 +650,9 @@ struct PointMath {
     // chol_pullback! (src/linalg.jl:112-134), in place: on entry B holds L-bar (lower), on
     // exit B holds A-bar.  Each L-bar[i][j] is last read exactly where A-bar[i][j] is written,
     // so one array serves both.
+    template <typename Div = DivExact<T>>
     static __device__ __forceinline__ void pullback(T (&B)[NT], const T (&L)[NT],
-                                                    const T (&rp)[KP1]) {
+                                                    const T (&rp)[KP1], Div&& div = Div()) {
         sfor_down<0, KP1>([&](auto j_) {
             GPB2_CI(j);
             const T ljj = L[tri(j, j)];
@@ -598,8 +660,8 @@ struct PointMath {
             sfor_down<j + 1, KP1>([&](auto i_) {
                 GPB2_CI(i);
                 const T lbij = B[tri(i, j)];
-                const T tbar = N::div_r(lbij, ljj, rj);
-                B[tri(j, j)] = N::sub(B[tri(j, j)], N::div_r(N::mul(lbij, L[tri(i, j)]), ljj, rj));
+                const T tbar = div(lbij, ljj, rj);
+                B[tri(j, j)] = N::sub(B[tri(j, j)], div(N::mul(lbij, L[tri(i, j)]), ljj, rj));
                 B[tri(i, j)] = tbar;
                 sfor<0, j>([&](auto p_) {
                     GPB2_CI(p);
@@ -608,7 +670,7 @@ struct PointMath {
                 });
             });
             // 1 / (2 ljj) rounded is rj / 2 exactly (a power-of-two scaling).
-            const T sbar = N::div_r(B[tri(j, j)], N::mul(T(2), ljj), N::mul(T(0.5), rj));
+            const T sbar = div(B[tri(j, j)], N::mul(T(2), ljj), N::mul(T(0.5), rj));
             B[tri(j, j)] = sbar;
             const T s2 = N::mul(T(2), sbar);
             sfor<0, j>([&](auto p_) {

@@ -311,10 +311,10 @@ __device__ __forceinline__ void flush_hist(double* __restrict__ gacc, const doub
     }
 }
 
-// refine_logdet_and_grad_hist_kernel! (src/kernels_adjoint.jl:117-152), seed 1.
-// Block shape of the histogram kernels (k_logdet_grad, k_grad_vals, k_inv_loss_grad): 320 threads, two blocks per SM (20 warps, within both the register
-// file at <= 102 registers and shared memory), when the interpolation weights of 320 threads fit
-// in 72 KB; else the flat kernels' 128 threads.
+// Block shape of the histogram kernels (k_logdet_grad, k_grad_vals, k_inv_loss_grad): 320
+// threads, two blocks per SM (20 warps, within both the register file at <= 102 registers and
+// shared memory), when the interpolation weights of 320 threads fit in 72 KB; else the flat
+// kernels' 128 threads.
 template <typename T, int K, int D>
 struct GradShape {
     static constexpr int kWide = 320;
@@ -359,12 +359,180 @@ __device__ __forceinline__ void grad_factor(F& f, const PointArgs<T>& a, const S
     }
 }
 
+// Each histogram kernel handles a point in two forms: FAST (DivChecked: the adjoint's divisions
+// without per-operation range checks, then one check of the point's operands) and exact
+// (DivExact, the same arithmetic with div_r's check and IEEE fallback in every division).  The
+// FAST form does the whole point and returns true, or, when an operand lay outside the window,
+// returns false having written nothing; the kernel then calls the exact form, kept out of line
+// (point_exact) so that the rare path does not enlarge the hot loop.  Both give the same bits
+// wherever the FAST form accepts a point.
+
+// One point of k_logdet_grad: the log-pivot (its term, into *s) and the Abar scatter.
+template <typename T, int K, int D, bool CACHED, bool FAST>
+__device__ __forceinline__ bool logdet_grad_point(const PointArgs<T>& a, const SmemTable<T>& tab,
+                                                  unsigned char* rbase, int64_t m, double* hist,
+                                                  double& bin0, T* terms, double& s) {
+    using N = Num<T>;
+    using PM = PointMath<T, K, D>;
+    typename GradShape<T, K, D>::template Factor<CACHED> f;
+    grad_factor<T, K, D, CACHED>(f, a, tab, rbase, m);
+    T B[PM::NT];
+    sfor<0, PM::NT>([&](auto i_) {
+        GPB2_CI(i);
+        B[i] = T(0);
+    });
+    T rp[PM::KP1];
+    PM::pivot_recips(rp, f.L);
+    B[tri(K, K)] = rp[K];  // chol_logdet_pullback! seed 1/L[K][K] (src/linalg.jl:137-146)
+    if constexpr (FAST) {
+        DivChecked<T> dv;
+        PM::pullback(B, f.L, rp, dv);
+        if (!dv.template ok<PM::KP1>(f.L)) return false;
+    } else {
+        PM::pullback(B, f.L, rp);
+    }
+    const T t = N::log(f.L[tri(K, K)]);
+    if (terms) terms[m] = t;
+    s += (double)t;
+    scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
+    return true;
+}
+
+// One point of k_grad_vals.
+template <typename T, int K, int D, bool CACHED, bool FAST>
+__device__ __forceinline__ bool grad_vals_point(const PointArgs<T>& a, const SmemTable<T>& tab,
+                                                unsigned char* rbase, int64_t m,
+                                                const T* __restrict__ v, const T* __restrict__ xih,
+                                                const T* __restrict__ vb,
+                                                const T* __restrict__ mv, double* hist,
+                                                double& bin0) {
+    using N = Num<T>;
+    using PM = PointMath<T, K, D>;
+    const int64_t p = a.n0 + m;
+    const T vbp = vb[p];
+    typename GradShape<T, K, D>::template Factor<CACHED> f;
+    grad_factor<T, K, D, CACHED>(f, a, tab, rbase, m);
+    const T pivfloor = N::mul(a.tab.pivc, f.L[0]);
+    T B[PM::NT];
+    sfor<0, PM::NT>([&](auto i_) {
+        GPB2_CI(i);
+        B[i] = T(0);
+    });
+    B[tri(K, K)] = N::mul(vbp, xih[p]);
+    T z[K];
+    sfor<0, K>([&](auto j_) {
+        GPB2_CI(j);
+        z[j] = N::mul(vbp, v[f.nb[j]]);
+    });
+    T rp[PM::KP1];
+    PM::pivot_recips(rp, f.L);
+    T x[K];  // mean_vec of the point: k_factor's output, the same solve bit for bit
+    sfor<0, K>([&](auto j_) {
+        GPB2_CI(j);
+        x[j] = mv[m * K + j];
+    });
+    if constexpr (FAST) {
+        DivChecked<T> dv;
+        PM::template forward_subst<true>(z, f.L, rp, pivfloor, dv);
+        PM::seed_from_solve(B, z, x);
+        PM::pullback(B, f.L, rp, dv);
+        if (!dv.template ok<PM::KP1>(f.L)) return false;
+    } else {
+        PM::template forward_subst<true>(z, f.L, rp, pivfloor);
+        PM::seed_from_solve(B, z, x);
+        PM::pullback(B, f.L, rp);
+    }
+    scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
+    return true;
+}
+
+// One point of k_inv_loss_grad: its xi (into xi_out), its loss term (into *ls), the scatter.
+template <typename T, int K, int D, bool CACHED, bool FAST>
+__device__ __forceinline__ bool inv_loss_grad_point(const PointArgs<T>& a,
+                                                    const SmemTable<T>& tab, unsigned char* rbase,
+                                                    int64_t m, const T* __restrict__ values,
+                                                    double* hist, double& bin0, T* xi_out,
+                                                    double& ls) {
+    using N = Num<T>;
+    using PM = PointMath<T, K, D>;
+    typename GradShape<T, K, D>::template Factor<CACHED> f;
+    grad_factor<T, K, D, CACHED>(f, a, tab, rbase, m);
+    T x[K];
+    PM::solve(x, f.L, a.tab.pivc);
+    const T sd = f.L[tri(K, K)];
+    T vn[K];
+    T mean = T(0);
+    sfor<0, K>([&](auto j_) {
+        GPB2_CI(j);
+        vn[j] = values[f.nb[j]];
+        mean = N::add(mean, N::mul(x[j], vn[j]));
+    });
+    const T xim = N::div(N::sub(values[a.n0 + m], mean), sd);
+    T B[PM::NT];
+    sfor<0, PM::NT>([&](auto i_) {
+        GPB2_CI(i);
+        B[i] = T(0);
+    });
+    B[tri(K, K)] = N::div(N::mul(-xim, xim), sd);
+    T z[K];
+    sfor<0, K>([&](auto j_) {
+        GPB2_CI(j);
+        z[j] = N::div(N::mul(-xim, vn[j]), sd);
+    });
+    T rp[PM::KP1];
+    PM::pivot_recips(rp, f.L);
+    if constexpr (FAST) {
+        DivChecked<T> dv;
+        PM::template forward_subst<false>(z, f.L, rp, T(0), dv);
+        PM::seed_from_solve(B, z, x);
+        PM::pullback(B, f.L, rp, dv);
+        if (!dv.template ok<PM::KP1>(f.L)) return false;
+    } else {
+        PM::template forward_subst<false>(z, f.L, rp, T(0));
+        PM::seed_from_solve(B, z, x);
+        PM::pullback(B, f.L, rp);
+    }
+    if (xi_out) xi_out[m] = xim;
+    ls += (double)N::div(N::mul(xim, xim), T(2));
+    scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
+    return true;
+}
+
+// The exact forms, out of line: each returns its point's contributions to the thread's
+// bin-0 share and scalar accumulator through the two-element array acc.
+template <typename T, int K, int D, bool CACHED>
+__device__ __noinline__ void logdet_grad_exact(PointArgs<T> a, SmemTable<T> tab,
+                                               unsigned char* rbase, int64_t m, double* hist,
+                                               T* terms, double* acc) {
+    double b0 = 0.0, s = 0.0;
+    logdet_grad_point<T, K, D, CACHED, false>(a, tab, rbase, m, hist, b0, terms, s);
+    acc[0] = b0;
+    acc[1] = s;
+}
+template <typename T, int K, int D, bool CACHED>
+__device__ __noinline__ double grad_vals_exact(PointArgs<T> a, SmemTable<T> tab,
+                                               unsigned char* rbase, int64_t m, const T* v,
+                                               const T* xih, const T* vb, const T* mv,
+                                               double* hist) {
+    double b0 = 0.0;
+    grad_vals_point<T, K, D, CACHED, false>(a, tab, rbase, m, v, xih, vb, mv, hist, b0);
+    return b0;
+}
+template <typename T, int K, int D, bool CACHED>
+__device__ __noinline__ void inv_loss_grad_exact(PointArgs<T> a, SmemTable<T> tab,
+                                                 unsigned char* rbase, int64_t m, const T* values,
+                                                 double* hist, T* xi_out, double* acc) {
+    double b0 = 0.0, ls = 0.0;
+    inv_loss_grad_point<T, K, D, CACHED, false>(a, tab, rbase, m, values, hist, b0, xi_out, ls);
+    acc[0] = b0;
+    acc[1] = ls;
+}
+
+// refine_logdet_and_grad_hist_kernel! (src/kernels_adjoint.jl:117-152), seed 1.
 template <typename T, int K, int D, bool CACHED>
 __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
 k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld_acc,
               T* __restrict__ terms, int64_t m0, int64_t cnt, const int* __restrict__ mlist) {
-    using N = Num<T>;
-    using PM = PointMath<T, K, D>;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ double red[32];
     SmemTable<T> tab;
@@ -378,22 +546,12 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
     for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
          it += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = point_of(it, m0, mlist);
-        typename GradShape<T, K, D>::template Factor<CACHED> f;
-        grad_factor<T, K, D, CACHED>(f, a, tab, rbase, m);
-        const T lkk = f.L[tri(K, K)];
-        const T t = N::log(lkk);
-        if (terms) terms[m] = t;
-        s += (double)t;
-        T B[PM::NT];
-        sfor<0, PM::NT>([&](auto i_) {
-            GPB2_CI(i);
-            B[i] = T(0);
-        });
-        T rp[PM::KP1];
-        PM::pivot_recips(rp, f.L);
-        B[tri(K, K)] = rp[K];  // chol_logdet_pullback! seed 1/L[K][K] (src/linalg.jl:137-146)
-        PM::pullback(B, f.L, rp);
-        scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
+        if (!logdet_grad_point<T, K, D, CACHED, true>(a, tab, rbase, m, hist, bin0, terms, s)) {
+            double acc[2];
+            logdet_grad_exact<T, K, D, CACHED>(a, tab, rbase, m, hist, terms, acc);
+            bin0 += acc[0];
+            s += acc[1];
+        }
     }
     s = block_sum_double(s, red);
     if (threadIdx.x == 0 && ld_acc) atomicAdd(ld_acc, s);
@@ -412,8 +570,6 @@ __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, 
 k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
             const T* __restrict__ vb, const T* __restrict__ mv, double* __restrict__ gacc,
             int64_t m0, int64_t cnt, const int* __restrict__ mlist) {
-    using N = Num<T>;
-    using PM = PointMath<T, K, D>;
     extern __shared__ __align__(16) unsigned char smem[];
     SmemTable<T> tab;
     double* hist;
@@ -425,33 +581,8 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
     for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
          it += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = point_of(it, m0, mlist);
-        const int64_t p = a.n0 + m;
-        const T vbp = vb[p];
-        typename GradShape<T, K, D>::template Factor<CACHED> f;
-        grad_factor<T, K, D, CACHED>(f, a, tab, rbase, m);
-        const T pivfloor = N::mul(a.tab.pivc, f.L[0]);
-        T B[PM::NT];
-        sfor<0, PM::NT>([&](auto i_) {
-            GPB2_CI(i);
-            B[i] = T(0);
-        });
-        B[tri(K, K)] = N::mul(vbp, xih[p]);
-        T z[K];
-        sfor<0, K>([&](auto j_) {
-            GPB2_CI(j);
-            z[j] = N::mul(vbp, v[f.nb[j]]);
-        });
-        T rp[PM::KP1];
-        PM::pivot_recips(rp, f.L);
-        PM::template forward_subst<true>(z, f.L, rp, pivfloor);
-        T x[K];  // mean_vec of the point: k_factor's output, the same solve bit for bit
-        sfor<0, K>([&](auto j_) {
-            GPB2_CI(j);
-            x[j] = mv[m * K + j];
-        });
-        PM::seed_from_solve(B, z, x);
-        PM::pullback(B, f.L, rp);
-        scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
+        if (!grad_vals_point<T, K, D, CACHED, true>(a, tab, rbase, m, v, xih, vb, mv, hist, bin0))
+            bin0 += grad_vals_exact<T, K, D, CACHED>(a, tab, rbase, m, v, xih, vb, mv, hist);
     }
     atomicAdd(&hist[0], bin0);
     __syncthreads();
@@ -465,8 +596,6 @@ __global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, 
 k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict__ gacc,
                 double* __restrict__ loss_acc, T* __restrict__ xi_out, int64_t m0, int64_t cnt,
                 const int* __restrict__ mlist) {
-    using N = Num<T>;
-    using PM = PointMath<T, K, D>;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ double red[32];
     SmemTable<T> tab;
@@ -480,38 +609,13 @@ k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict
     for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < cnt;
          it += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = point_of(it, m0, mlist);
-        typename GradShape<T, K, D>::template Factor<CACHED> f;
-        grad_factor<T, K, D, CACHED>(f, a, tab, rbase, m);
-        T x[K];
-        PM::solve(x, f.L, a.tab.pivc);
-        const T sd = f.L[tri(K, K)];
-        T vn[K];
-        T mean = T(0);
-        sfor<0, K>([&](auto j_) {
-            GPB2_CI(j);
-            vn[j] = values[f.nb[j]];
-            mean = N::add(mean, N::mul(x[j], vn[j]));
-        });
-        const T xim = N::div(N::sub(values[a.n0 + m], mean), sd);
-        if (xi_out) xi_out[m] = xim;
-        ls += (double)N::div(N::mul(xim, xim), T(2));
-        T B[PM::NT];
-        sfor<0, PM::NT>([&](auto i_) {
-            GPB2_CI(i);
-            B[i] = T(0);
-        });
-        B[tri(K, K)] = N::div(N::mul(-xim, xim), sd);
-        T z[K];
-        sfor<0, K>([&](auto j_) {
-            GPB2_CI(j);
-            z[j] = N::div(N::mul(-xim, vn[j]), sd);
-        });
-        T rp[PM::KP1];
-        PM::pivot_recips(rp, f.L);
-        PM::template forward_subst<false>(z, f.L, rp, T(0));
-        PM::seed_from_solve(B, z, x);
-        PM::pullback(B, f.L, rp);
-        scatter_hist<T, K, D>(hist, bin0, B, f.R, tab);
+        if (!inv_loss_grad_point<T, K, D, CACHED, true>(a, tab, rbase, m, values, hist, bin0,
+                                                        xi_out, ls)) {
+            double acc[2];
+            inv_loss_grad_exact<T, K, D, CACHED>(a, tab, rbase, m, values, hist, xi_out, acc);
+            bin0 += acc[0];
+            ls += acc[1];
+        }
     }
     ls = block_sum_double(ls, red);
     if (threadIdx.x == 0 && loss_acc) atomicAdd(loss_acc, ls);

@@ -48,7 +48,10 @@ cudaError_t prepare_kernel_smem(const void* kernel, size_t smem) {
     if (smem > 48 * 1024 && smem > ki.smem_set) {
         cudaError_t e =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
+        if (e != cudaSuccess) {
+            cudaGetLastError();  // reported here: no later call may find it pending
+            return e;
+        }
         ki.smem_set = smem;
         ki.blocks_per_sm = 0;
     }
