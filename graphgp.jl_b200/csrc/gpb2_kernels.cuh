@@ -322,6 +322,16 @@ struct GradShape {
         (size_t)PointMath<T, K, D>::NR * kWide * (sizeof(T) + sizeof(uint16_t)) <= 72 * 1024;
     static constexpr int kThreads = kUse ? kWide : kFlatThreads;
     static constexpr int kMinBlocks = kUse ? 2 : 1;
+    // The factor-cache form keeps no pair weights in shared memory and its loop is latency-bound:
+    // more resident warps pay more than the registers they cost.  Measured at C4 (f32, K = 8,
+    // 2e7 points): k_grad_vals 7.1 ms at 256 threads x 3 blocks per SM against 7.9 ms at the
+    // 320 x 2 shape; k_logdet_grad 5.6 ms at 256 x 4 against 7.5 ms.  Other shapes keep the
+    // recompute form's block.
+    static constexpr bool kCachedWide = kUse && std::is_same<T, float>::value;
+    static constexpr int kCachedThreads = kCachedWide ? 256 : kThreads;
+    static constexpr int kCachedBlocks = kCachedWide ? 3 : kMinBlocks;        // grad_vals, inv_loss
+    static constexpr int kCachedBlocksLogdet = kCachedWide ? 4 : kMinBlocks;  // logdet_grad
+    static constexpr int threads(bool cached) { return cached ? kCachedThreads : kThreads; }
     using Store = RadiusStore<T, K, D, kThreads, kUse ? 72 * 1024 : 36 * 1024>;
     // The point factor of a histogram kernel: recomputed (pair weights in Store), or read from
     // the factor cache (pair weights in its slabs).
@@ -530,7 +540,9 @@ __device__ __noinline__ void inv_loss_grad_exact(PointArgs<T> a, SmemTable<T> ta
 
 // refine_logdet_and_grad_hist_kernel! (src/kernels_adjoint.jl:117-152), seed 1.
 template <typename T, int K, int D, bool CACHED>
-__global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
+__global__ void __launch_bounds__(GradShape<T, K, D>::threads(CACHED),
+                                  CACHED ? GradShape<T, K, D>::kCachedBlocksLogdet
+                                         : GradShape<T, K, D>::kMinBlocks)
 k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld_acc,
               T* __restrict__ terms, int64_t m0, int64_t cnt, const int* __restrict__ mlist) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -566,7 +578,9 @@ k_logdet_grad(PointArgs<T> a, double* __restrict__ gacc, double* __restrict__ ld
 // pullback needs nothing else, so the batches need not be visited in order.
 
 template <typename T, int K, int D, bool CACHED>
-__global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
+__global__ void __launch_bounds__(GradShape<T, K, D>::threads(CACHED),
+                                  CACHED ? GradShape<T, K, D>::kCachedBlocks
+                                         : GradShape<T, K, D>::kMinBlocks)
 k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
             const T* __restrict__ vb, const T* __restrict__ mv, double* __restrict__ gacc,
             int64_t m0, int64_t cnt, const int* __restrict__ mlist) {
@@ -592,7 +606,9 @@ k_grad_vals(PointArgs<T> a, const T* __restrict__ v, const T* __restrict__ xih,
 // refine_inv_loss_grad_hist_kernel! (src/kernels_adjoint.jl:155-221): loss 0.5*sum(xi^2) and its
 // vals-gradient; the z-bar solve has no pivot guard, as in the reference.
 template <typename T, int K, int D, bool CACHED>
-__global__ void __launch_bounds__(GradShape<T, K, D>::kThreads, GradShape<T, K, D>::kMinBlocks)
+__global__ void __launch_bounds__(GradShape<T, K, D>::threads(CACHED),
+                                  CACHED ? GradShape<T, K, D>::kCachedBlocks
+                                         : GradShape<T, K, D>::kMinBlocks)
 k_inv_loss_grad(PointArgs<T> a, const T* __restrict__ values, double* __restrict__ gacc,
                 double* __restrict__ loss_acc, T* __restrict__ xi_out, int64_t m0, int64_t cnt,
                 const int* __restrict__ mlist) {
@@ -1164,10 +1180,11 @@ struct Launch {
                                    : flat_smem(a, true) + G::Store::bytes;
         cudaError_t e = prepare_kernel_smem(kern, smem);
         if (e != cudaSuccess) return e;
-        const int grid = flat_grid(kern, G::kThreads, smem, work);
+        const int threads = G::threads(cached);
+        const int grid = flat_grid(kern, threads, smem, work);
         if (cached)
-            return launch_prof(name, kc, dim3(grid), dim3(G::kThreads), smem, s, a, args...);
-        return launch_prof(name, kr, dim3(grid), dim3(G::kThreads), smem, s, a, args...);
+            return launch_prof(name, kc, dim3(grid), dim3(threads), smem, s, a, args...);
+        return launch_prof(name, kr, dim3(grid), dim3(threads), smem, s, a, args...);
     }
     static cudaError_t inv(const PointArgs<T>& a, const T* values, T* xi, Pts r,
                            cudaStream_t s) {
