@@ -649,12 +649,12 @@ def c2_step(args, dev, stream, timed):
 
 
 # DRAM bytes (read + write) per launch, from one ncu capture of
-# `GPB2_REVERSE_MODE=1 python bench.py --ncu-case --points 10000000` (5.356e9 bytes for
+# `GPB2_REVERSE_MODE=1 python bench.py --ncu-case --points 10000000` (6.062e9 bytes for
 # 9.995e6 refined points) scaled to the 99,995,000 refined points of a 1e8-point launch
 # (profiles/traffic_c4_1e7_step.md).  Only the streaming kernel is listed: the sweeps' neighbour
 # reads partly hit L2 at 1e7 points, so their bytes do not scale with the points.  Measured,
 # not computed here: the bench itself never runs under a profiler.
-NCU_TRAFFIC = {"grad_vals_cached": 5.3563e9 * 99_995_000 / 9_995_000}
+NCU_TRAFFIC = {"grad_vals_cached": 6.0621e9 * 99_995_000 / 9_995_000}
 NCU_SOURCE = "profiles/traffic_c4_1e7_step.md (ncu at 1e7 points, scaled by refined points)"
 
 
