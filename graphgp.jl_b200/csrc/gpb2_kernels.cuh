@@ -860,6 +860,9 @@ struct SweepShape {
 
 // The incoming terms of point p in the pull-form reverse sweep, in edge order (the serial
 // sweep's order): acc = vb[p] + w_0 vb[c_0] + w_1 vb[c_1] + ..., eight edges' loads in flight.
+// The children's cotangents are final (written in earlier steps, or by earlier launches) and
+// are read through L1 (ld.global.ca), where a child shared by several parents of the CTA hits:
+// see the forward gathers in sweep_pipe for why the L1 holds no stale line.
 template <typename T, int K>
 __device__ __forceinline__ T pull_sum(T acc, const RevGraph<T>& rg, const T* __restrict__ vb,
                                       int64_t n0, uint32_t e, uint32_t end) {
@@ -874,11 +877,11 @@ __device__ __forceinline__ T pull_sum(T acc, const RevGraph<T>& rg, const T* __r
             w[u] = __ldg(rg.w + e + u);
         }
 #pragma unroll
-        for (int u = 0; u < U; u++) v[u] = __ldcg(vb + n0 + mj[u] / K);
+        for (int u = 0; u < U; u++) v[u] = __ldca(vb + n0 + mj[u] / K);
 #pragma unroll
         for (int u = 0; u < U; u++) acc = N::add(acc, N::mul(w[u], v[u]));
     }
-    for (; e < end; e++) acc = N::add(acc, N::mul(__ldg(rg.w + e), __ldcg(vb + n0 + __ldg(rg.mj + e) / K)));
+    for (; e < end; e++) acc = N::add(acc, N::mul(__ldg(rg.w + e), __ldca(vb + n0 + __ldg(rg.mj + e) / K)));
     return acc;
 }
 
@@ -952,10 +955,17 @@ __device__ __forceinline__ void sweep_pipe(T* __restrict__ values, const T* __re
             }
             if (F && fwd) {
                 const int64_t p = f0 + k * gsz;
+                // The neighbours' values were written in earlier steps, by other CTAs.  They are
+                // read through L1 (ld.global.ca: neighbours shared by the CTA's points hit there,
+                // -19 % sweep time at C4 1e8): each step begins after grid_sync, whose acquire
+                // load (thread 0) and block barrier order these loads after every earlier
+                // step's writes, so no stale L1 line is read; lines written during this step
+                // hold only this batch's values, which no point of the step reads (batch-mates
+                // never neighbour each other).
                 T v[K];
                 sfor<0, K>([&](auto j_) {
                     GPB2_CI(j);
-                    v[j] = __ldcg(values + cur.nb[j]);
+                    v[j] = __ldca(values + cur.nb[j]);
                 });
                 if (nvalid) load(nxt, nfwd, nk);
                 T acc = N::mul(cur.sd, cur.xi);
